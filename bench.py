@@ -1,0 +1,440 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized-FFN hot path (BASELINE.json metric: FFN GEMV achieved HBM GB/s
+and FFN tokens/s).
+
+Default workload: Llama-3-8B-shaped FFN stack, 32 layers resident
+in HBM, gate/up Q4_K, down Q6_K, batch-1 decode, x <- x + FFN_l(x).  One step = one token
+through all 32 layers.  Weights are seeded N(0, 0.02^2) quantized on the device with the
+reference's Q4_K quantizer (and this project's Q6_K quantizer); activations N(0, 1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
+
+Multi-GPU (torchrun, one rank per GPU): configs 1-3 do not shard, so every rank runs an
+independent replica ("weak" scaling, no collective on the data path); value = all ranks'
+bytes / max-over-ranks time.
+
+--impl reference times the reference's CPU implementation of the path (the C restatement
+in oracle/, the Rust reference cannot be built here) on this host's cores, on a bounded
+sample of the same workload (one layer per step), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "FFN GEMV achieved HBM GB/s (fraction of 8 TB/s) and FFN tokens/sec at 1/2/4/8 B200"
+
+# ---------------------------------------------------------------- workloads
+Q4_K, Q6_K, Q8_0 = 12, 14, 8
+BLK = {Q4_K: (256, 144), Q6_K: (256, 210), Q8_0: (32, 34)}
+
+
+def mat_bytes(t, m, n):
+    qk, bs = BLK[t]
+    return m * n // qk * bs
+
+
+CONFIGS = {
+    # name: (layers, d_model, k_in, d_ff, gate/up type, down type, description)
+    "llama8b": dict(layers=32, d_model=4096, k_in=4096, d_ff=14336, tg=Q4_K, td=Q6_K,
+                    workload="Llama-3-8B FFN stack x32, gate/up Q4_K, down Q6_K, batch-1 decode"),
+    "smollm": dict(layers=256, d_model=576, k_in=768, d_ff=1536, tg=Q4_K, td=Q4_K,
+                   workload="SmolLM2-135M FFN layer (Q4_K x3, K 576 zero-padded to 768), 256 distinct "
+                            "resident copies streamed as a stack (HBM figure; one copy fits in L2)"),
+    "llama8b-q8": dict(layers=8, d_model=4096, k_in=4096, d_ff=14336, tg=Q8_0, td=Q8_0,
+                       workload="Llama-3-8B FFN shape, Q8_0 x3, stack of 8 distinct layers"),
+    "llama70b": dict(layers=80, d_model=8192, k_in=8192, d_ff=28672, tg=Q4_K, td=Q6_K,
+                     workload="Llama-3-70B FFN stack x80, gate/up Q4_K, down Q6_K, TP=1"),
+}
+
+
+def layer_bytes(c):
+    return 2 * mat_bytes(c["tg"], c["d_ff"], c["k_in"]) + mat_bytes(c["td"], c["d_model"], c["d_ff"])
+
+
+# ---------------------------------------------------------------- clocks sampler
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [v.strip() for v in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                smax.append(float(p[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- helpers
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def committed_traffic(kernel_key: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(kernel_key)
+    except (OSError, ValueError):
+        return None
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(v: float, world: int, dev) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle port)
+def cpu_baseline(c, layers_raw, x0, seconds: float):
+    """Time the oracle's FFN on all host cores over the sampled layers, for ~`seconds`."""
+    import numpy as np
+
+    import oracle
+
+    cores = oracle.get_threads()
+    x = x0.copy()
+    lb = layer_bytes(c)
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        g, u, d = layers_raw[done % len(layers_raw)]
+        y = oracle.ffn_swiglu(c["tg"], g, c["tg"], u, c["td"], d, c["k_in"], c["d_ff"], c["d_model"], x)
+        x[:c["d_model"]] += y
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and done >= 2:
+            break
+    gbs = lb * done / el / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+            "tokens_per_s": round(done / c["layers"] / el, 4),
+            "sample": f"{done} FFN layers ({len(layers_raw)} distinct, {lb / 1e6:.1f} MB each) on the C "
+                      f"restatement of the reference CPU path, {el:.1f} s, {cores} OpenMP threads"}, np.isfinite(x).all()
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args):
+    world, rank, local = dist_setup(args)
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    import oracle
+    from hayai_b200 import _build
+
+    _build.build_oracle()
+    c = CONFIGS[args.config]
+    cores = oracle.get_threads()
+    # a few distinct layers of the same shapes, generated on the host with the oracle
+    S = 3
+    layers = []
+    for l in range(S):
+        g = oracle.quantize(c["tg"], oracle.normal(1000 + 3 * l, c["d_ff"] * c["k_in"], 0.0, 0.02))
+        u = oracle.quantize(c["tg"], oracle.normal(1001 + 3 * l, c["d_ff"] * c["k_in"], 0.0, 0.02))
+        d = oracle.quantize(c["td"], oracle.normal(1002 + 3 * l, c["d_model"] * c["d_ff"], 0.0, 0.02))
+        layers.append((g, u, d))
+    x = np.zeros(c["k_in"], np.float32)
+    x[:c["d_model"]] = oracle.normal(7, c["d_model"])
+    lb = layer_bytes(c)
+
+    def step(i):
+        g, u, d = layers[i % S]
+        y = oracle.ffn_swiglu(c["tg"], g, c["tg"], u, c["td"], d, c["k_in"], c["d_ff"], c["d_model"], x)
+        x[:c["d_model"]] = x0[:c["d_model"]] + y
+
+    x0 = x.copy()
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(i)
+    el = time.perf_counter() - t0
+    gbs = lb * args.steps / el / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": c_dtype(c),
+        "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) activations)",
+        "config": {"workload": c["workload"] + f"; reference arm step = 1 FFN layer ({lb / 1e6:.1f} MB)",
+                   "batch": 1, "layers": c["layers"], "parallelism": "replicas"},
+        "tokens_per_s": round(args.steps / c["layers"] / el, 4),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"1 FFN layer per step, {S} distinct layers rotated, {cores} OpenMP threads; "
+                                   "C restatement of the reference Rust CPU path (no Rust toolchain here)"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def c_dtype(c):
+    return {Q4_K: "q4_k/f32", Q6_K: "q6_k/f32", Q8_0: "q8_0/f32"}[c["tg"]] + (
+        "+" + {Q4_K: "q4_k", Q6_K: "q6_k", Q8_0: "q8_0"}[c["td"]] if c["td"] != c["tg"] else "")
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    import hayai_b200 as hb
+
+    c = CONFIGS[args.config]
+    L, dm, kin, ff, tg, td = c["layers"], c["d_model"], c["k_in"], c["d_ff"], c["tg"], c["td"]
+    B = args.batch
+    eng = hb.CudaEngine(local)
+    stream = torch.cuda.current_stream(dev)
+    eng.set_stream(stream)
+
+    # ---- resident weights, generated and quantized on the device
+    scratch = torch.empty(max(ff * kin, dm * ff), dtype=torch.float32, device=dev)
+    want_cpu = (rank == 0 and world == 1 and not args.no_cpu_baseline)
+    S_cpu = 3 if want_cpu else 0
+    G, U, D, raw = [], [], [], []
+    seed0 = 1_000_003 * (rank + 1)
+
+    padded = torch.zeros(ff, kin, dtype=torch.float32, device=dev) if kin != dm else None
+
+    def synth(t, m, n, seed, keep, n_real=None):
+        """Seeded N(0, 0.02^2) m x n_real weights, zero-padded to n columns, quantized on device."""
+        qk, bs = BLK[t]
+        n_real = n_real or n
+        src = scratch[:m * n_real]
+        eng.synth_normal_dev(seed, src, 0.0, 0.02)
+        if n_real != n:  # zero-padded K (SmolLM 576 -> 768): pad sub-blocks quantize to exact zeros
+            padded[:, :n_real] = src.view(m, n_real)
+            src = padded.view(-1)
+        q = torch.empty(m * n // qk * bs, dtype=torch.uint8, device=dev)
+        eng.quantize_dev(t, src, q)
+        rw = eng.upload_from_device(t, m, n, q)
+        host = q.cpu().numpy() if keep else None
+        del q
+        return rw, host
+
+    for l in range(L):
+        keep = l < S_cpu
+        g, gh = synth(tg, ff, kin, seed0 + 3 * l, keep, dm)
+        u, uh = synth(tg, ff, kin, seed0 + 3 * l + 1, keep, dm)
+        d, dh = synth(td, dm, ff, seed0 + 3 * l + 2, keep)
+        G.append(g)
+        U.append(u)
+        D.append(d)
+        if keep:
+            raw.append((gh, uh, dh))
+    del scratch, padded
+    x0 = torch.zeros(B, kin, dtype=torch.float32, device=dev)
+    xs = torch.empty(B * dm, dtype=torch.float32, device=dev)
+    eng.synth_normal_dev(7 + rank, xs, 0.0, 1.0)
+    x0[:, :dm] = xs.view(B, dm)
+    x = x0.clone()
+    torch.cuda.synchronize(dev)
+
+    def step():
+        x.copy_(x0)
+        eng.ffn_stack_dev(G, U, D, x, B)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    t_local = ev0.elapsed_time(ev1) / 1e3
+    eng.sync()  # surfaces any device-side error flag
+    t = max_over_ranks(t_local, world, dev)
+    barrier(world)
+    tok_bytes = L * layer_bytes(c)
+    value = world * args.steps * tok_bytes / t / 1e9
+    tokens_per_s = world * args.steps * B / t
+
+    # ---- roofline: the dominant kernel (fused gate/up) timed alone, rotating over layers
+    h = torch.empty(B, ff, dtype=torch.float32, device=dev)
+    reps = 3 * L if L >= 8 else 96
+    for i in range(L):
+        eng.ffn_gateup_dev(G[i % L], U[i % L], x0, h, B)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for i in range(reps):
+        eng.ffn_gateup_dev(G[i % L], U[i % L], x0, h, B)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    gu_time = e0.elapsed_time(e1) / 1e3 / reps
+    gu_bytes = 2 * mat_bytes(tg, ff, kin)
+    peak, peak_kind = measured_peak()
+    achieved = gu_bytes / gu_time / 1e9
+    kkey = f"gateup_{args.config}_b{B}"
+    roofline = {"bound": "hbm", "kernel": "gemv_mma_kernel<FmtQ4K,1,true> (fused gate/up + SiLU*up)"
+                if tg == Q4_K else f"gemv_mma_kernel (fused gate/up, type {tg})",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback 6.65 TB/s",
+                "traffic": committed_traffic(kkey), "algorithmic_bytes_per_launch": gu_bytes,
+                "avg_launch_us": round(gu_time * 1e6, 2)}
+
+    # ---- e2e through the host C-ABI call: pinned host x in, result out, every step
+    n_e2e = min(args.steps, 200)
+    x_in = torch.empty(B * kin, dtype=torch.float32).pin_memory()
+    x_in.copy_(x0.view(-1).cpu())
+    x_out = torch.empty_like(x_in).pin_memory()
+    xi, xo = x_in.numpy(), x_out.numpy()
+    for _ in range(3):
+        eng.ffn_stack(G, U, D, xi, B)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(n_e2e):
+        xo[:] = eng.ffn_stack(G, U, D, xi, B)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
+    e2e = {"value": round(world * n_e2e * tok_bytes / t_e2e / 1e9, 2), "unit": "GB/s",
+           "tokens_per_s": round(world * n_e2e * B / t_e2e, 2), "steps": n_e2e,
+           "h2d_bytes_per_step": B * kin * 4, "d2h_bytes_per_step": B * kin * 4,
+           "api": "hc_ffn_stack (host buffers)"}
+    assert np.isfinite(xo).all()
+
+    cpu = None
+    if want_cpu:
+        x_np = x0[0].cpu().numpy()
+        cpu, ok = cpu_baseline(c, raw, x_np, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": c_dtype(c),
+            "data": "synthetic (seeded N(0,0.02^2) weights quantized on device, N(0,1) activations)",
+            "config": {"workload": c["workload"], "batch": B, "layers": L, "d_model": dm, "d_ff": ff,
+                       "bytes_per_token": tok_bytes, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (weights per step %.2f GB > 126 MB)" % (tok_bytes / 1e9)},
+            "tokens_per_s": round(tokens_per_s, 2),
+            "frac_of_8tbs": round(value / world / 8000.0, 4),
+            "roofline": roofline, "e2e": e2e, "clocks": clocks,
+            "gpu_launches": args.steps * 2 * L,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    for w in G + U + D:
+        w.free()
+    eng.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="llama8b")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,746 @@
+// capi.cu -- the C ABI (include/hayai_cuda.h): engine, resident weights, GEMV and FFN
+// entry points.  Host logic mirrors hayai-opencl's OpenClEngine
+// (crates/hayai-opencl/src/compute.rs, async_gemv.rs): the same validation and error
+// behaviour, with CUDA streams and one-time resident uploads instead of per-call
+// buffer creation.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/hayai_cuda.h"
+#include "common.cuh"
+#include "engine.h"
+#include "gemv_launch.h"
+#include "gemv_mma.cuh"
+
+using namespace hc;
+
+// ------------------------------------------------------------------ errors
+static thread_local std::string g_last_error;
+
+int hc_set_error(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int hc_cuda_error(cudaError_t e, const char* what) {
+    return hc_set_error(HC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define HC_CUDA(call)                                              \
+    do {                                                           \
+        cudaError_t _e = (call);                                   \
+        if (_e != cudaSuccess) return hc_cuda_error(_e, #call);    \
+    } while (0)
+
+extern "C" const char* hc_last_error(void) { return g_last_error.c_str(); }
+
+// ------------------------------------------------------------------ labels / row bytes
+const char* hc_type_label(int t) {
+    switch (t) {
+        case T_F32: return "f32";
+        case T_Q8_0: return "q8_0";
+        case T_Q4_K: return "q4_k";
+        case T_Q6_K: return "q6_k";
+        case T_IQ2_XXS: return "iq2_xxs";
+        case T_IQ2_XS: return "iq2_xs";
+        case T_IQ2_S: return "iq2_s";
+        case T_IQ3_XXS: return "iq3_xxs";
+        case T_IQ3_S: return "iq3_s";
+        default: return "unknown";
+    }
+}
+
+static int block_elems(int t) {
+    switch (t) {
+        case T_F32: return 1;
+        case T_Q8_0: return 32;
+        case T_Q4_K: case T_Q6_K: case T_IQ2_XXS: case T_IQ2_XS: case T_IQ2_S: case T_IQ3_XXS: case T_IQ3_S:
+            return 256;
+        default: return 0;
+    }
+}
+
+// gemv_row_bytes (compute.rs:877-907) restricted to the formats with a kernel here.
+extern "C" int hc_gemv_row_bytes(int ggml_type, size_t n, size_t* out) {
+    const int qk = block_elems(ggml_type);
+    if (qk == 0) return hc_set_error(HC_ERR_UNSUPPORTED, "CUDA GEMV missing for ggml type %d", ggml_type);
+    if (n % (size_t)qk != 0)
+        return hc_set_error(HC_ERR_INVALID, "ggml_gemv_%s: n=%zu is not a valid column count for this layout",
+                            hc_type_label(ggml_type), n);
+    if (out) *out = raw_row_bytes(ggml_type, (int)n);
+    return HC_OK;
+}
+
+// validate_gemv_shape (compute.rs:937-951)
+int hc_validate_shape(int type, size_t m, size_t n) {
+    if (block_elems(type) == 0) return hc_set_error(HC_ERR_UNSUPPORTED, "CUDA GEMV missing for ggml type %d", type);
+    if (m == 0 || n == 0)
+        return hc_set_error(HC_ERR_INVALID, "ggml_gemv_%s: empty shape m=%zu n=%zu", hc_type_label(type), m, n);
+    if (m > (size_t)INT32_MAX || n > (size_t)INT32_MAX)
+        return hc_set_error(HC_ERR_INVALID, "ggml_gemv_%s: shape too large m=%zu n=%zu", hc_type_label(type), m, n);
+    if (n % (size_t)block_elems(type) != 0)
+        return hc_set_error(HC_ERR_INVALID,
+                            "ggml_gemv_%s: n=%zu is not a valid column count (multiple of the block size)",
+                            hc_type_label(type), n);
+    return HC_OK;
+}
+
+// validate_gemv_weights (compute.rs:912-933)
+int hc_validate_weights(int type, size_t m, size_t n, size_t len) {
+    int rc = hc_validate_shape(type, m, n);
+    if (rc) return rc;
+    const size_t row = raw_row_bytes(type, (int)n);
+    if (row != 0 && m > SIZE_MAX / row)
+        return hc_set_error(HC_ERR_INVALID, "ggml_gemv_%s: weight size overflow for %zux%zu", hc_type_label(type), m, n);
+    const size_t expected = m * row;
+    if (len < expected)
+        return hc_set_error(HC_ERR_INVALID, "ggml_gemv_%s: weight buffer %zu B < %zu B required for %zux%zu",
+                            hc_type_label(type), len, expected, m, n);
+    return HC_OK;
+}
+
+// ------------------------------------------------------------------ engine
+int DevBuf::ensure(size_t n) {
+    if (n <= cap) return HC_OK;
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+    cudaError_t e = cudaMalloc(&p, n);
+    if (e != cudaSuccess) {
+        p = nullptr;
+        return hc_cuda_error(e, "workspace cudaMalloc");
+    }
+    cap = n;
+    return HC_OK;
+}
+
+void DevBuf::release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+}
+
+int HostBuf::ensure(size_t n) {
+    if (n <= cap) return HC_OK;
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    cap = 0;
+    cudaError_t e = cudaMallocHost(&p, n);
+    if (e != cudaSuccess) {
+        p = nullptr;
+        return hc_cuda_error(e, "pinned cudaMallocHost");
+    }
+    cap = n;
+    return HC_OK;
+}
+
+void HostBuf::release() {
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    cap = 0;
+}
+
+int hc_engine_activate(hc_engine* e) {
+    if (!e) return hc_set_error(HC_ERR_INVALID, "null engine");
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != e->device) HC_CUDA(cudaSetDevice(e->device));
+    return HC_OK;
+}
+
+extern "C" int hc_device_count(int* out) {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        if (out) *out = 0;
+        return hc_cuda_error(e, "cudaGetDeviceCount");
+    }
+    if (out) *out = n;
+    return HC_OK;
+}
+
+extern "C" int hc_engine_init(int device, hc_engine** out) {
+    if (!out) return hc_set_error(HC_ERR_INVALID, "null out pointer");
+    *out = nullptr;
+    int n = 0;
+    HC_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return hc_set_error(HC_ERR_INVALID, "device %d out of range (%d devices)", device, n);
+    HC_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    HC_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10)
+        return hc_set_error(HC_ERR_UNSUPPORTED, "device %d (%s, sm_%d%d) is not an sm_100 part", device, prop.name,
+                            prop.major, prop.minor);
+    hc_engine* e = new hc_engine();
+    e->device = device;
+    e->num_sms = prop.multiProcessorCount;
+    e->smem_optin = (int)prop.sharedMemPerBlockOptin;
+    cudaError_t ce = cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking);
+    if (ce != cudaSuccess) {
+        delete e;
+        return hc_cuda_error(ce, "cudaStreamCreate");
+    }
+    e->stream = e->own_stream;
+    ce = cudaMalloc(&e->d_err, 16);
+    if (ce == cudaSuccess) ce = cudaMemset(e->d_err, 0, 16);
+    if (ce != cudaSuccess) {
+        cudaStreamDestroy(e->own_stream);
+        delete e;
+        return hc_cuda_error(ce, "error flag allocation");
+    }
+    *out = e;
+    return HC_OK;
+}
+
+extern "C" int hc_engine_free(hc_engine* e) {
+    if (!e) return HC_OK;
+    hc_engine_activate(e);
+    cudaStreamSynchronize(e->stream);
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+    for (auto& kv : e->ptr_tables) cudaFree(kv.second);
+    e->ptr_tables.clear();
+    e->ws_raw.release();
+    e->ws_gpu.release();
+    e->ws_x.release();
+    e->ws_y.release();
+    e->ws_h.release();
+    e->ws_g.release();
+    e->ws_u.release();
+    e->ws_misc.release();
+    e->hs_out.release();
+    if (e->d_err) cudaFree(e->d_err);
+    if (e->own_stream) cudaStreamDestroy(e->own_stream);
+    delete e;
+    return HC_OK;
+}
+
+extern "C" int hc_engine_set_stream(hc_engine* e, void* stream) {
+    if (!e) return hc_set_error(HC_ERR_INVALID, "null engine");
+    e->stream = stream ? (cudaStream_t)stream : e->own_stream;
+    return HC_OK;
+}
+
+extern "C" int hc_engine_get_stream(hc_engine* e, void** stream) {
+    if (!e || !stream) return hc_set_error(HC_ERR_INVALID, "null argument");
+    *stream = (void*)e->stream;
+    return HC_OK;
+}
+
+// Read (and clear) the device error flag.  Call only after the stream is synchronised.
+int hc_check_device_error(hc_engine* e) {
+    int flag = 0;
+    HC_CUDA(cudaMemcpy(&flag, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (flag) {
+        HC_CUDA(cudaMemset(e->d_err, 0, sizeof(int)));
+        if (flag & 1)
+            return hc_set_error(HC_ERR_RANGE,
+                                "an activation magnitude reached 65504 (outside the f16 range of the tensor-core split)");
+        if (flag & 2) return hc_set_error(HC_ERR_TIMEOUT, "a bounded device wait expired");
+        return hc_set_error(HC_ERR_CUDA, "device error flag 0x%x", flag);
+    }
+    return HC_OK;
+}
+
+extern "C" int hc_sync(hc_engine* e) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    HC_CUDA(cudaStreamSynchronize(e->stream));
+    return hc_check_device_error(e);
+}
+
+// ------------------------------------------------------------------ weights
+static int weights_make(hc_engine* e, int type, size_t m, size_t n, const void* src, size_t len, bool from_host,
+                        hc_weights** out) {
+    if (!out) return hc_set_error(HC_ERR_INVALID, "null out pointer");
+    *out = nullptr;
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    rc = hc_validate_weights(type, m, n, len);
+    if (rc) return rc;
+    if (!src) return hc_set_error(HC_ERR_INVALID, "null weight bytes");
+    const size_t raw_rb = raw_row_bytes(type, (int)n);
+    const size_t gpu_rb = gpu_row_stride(type, (int)n);
+    const size_t raw_bytes = m * raw_rb, gpu_bytes = m * gpu_rb;
+    hc_weights* w = new hc_weights();
+    w->type = type;
+    w->m = m;
+    w->n = n;
+    w->stride = gpu_rb;
+    w->bytes = gpu_bytes;
+    w->device = e->device;
+    cudaError_t ce = cudaMalloc(&w->dev, gpu_bytes + 16);
+    if (ce != cudaSuccess) {
+        delete w;
+        return hc_cuda_error(ce, "weights cudaMalloc");
+    }
+    const uint8_t* raw_dev = nullptr;
+    void* tmp = nullptr;
+    const bool same_layout = raw_rb == gpu_rb && (type != T_Q6_K && type != T_Q8_0);
+    if (from_host) {
+        if (same_layout) {
+            ce = cudaMemcpyAsync(w->dev, src, raw_bytes, cudaMemcpyHostToDevice, e->stream);
+        } else {
+            ce = cudaMalloc(&tmp, raw_bytes);
+            if (ce == cudaSuccess) ce = cudaMemcpyAsync(tmp, src, raw_bytes, cudaMemcpyHostToDevice, e->stream);
+            raw_dev = (const uint8_t*)tmp;
+        }
+    } else {
+        raw_dev = (const uint8_t*)src;
+        if (same_layout) ce = cudaMemcpyAsync(w->dev, src, raw_bytes, cudaMemcpyDeviceToDevice, e->stream);
+    }
+    if (ce == cudaSuccess && !same_layout) ce = launch_repack(type, raw_dev, (uint8_t*)w->dev, (int)m, (int)n, e->stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->stream);
+    if (tmp) cudaFree(tmp);
+    if (ce != cudaSuccess) {
+        cudaFree(w->dev);
+        delete w;
+        return hc_cuda_error(ce, "weights upload");
+    }
+    *out = w;
+    return HC_OK;
+}
+
+extern "C" int hc_weights_upload(hc_engine* e, int type, size_t m, size_t n, const void* host, size_t len,
+                                 hc_weights** out) {
+    return weights_make(e, type, m, n, host, len, true, out);
+}
+
+extern "C" int hc_weights_from_device(hc_engine* e, int type, size_t m, size_t n, const void* dev, size_t len,
+                                      hc_weights** out) {
+    return weights_make(e, type, m, n, dev, len, false, out);
+}
+
+extern "C" int hc_weights_free(hc_weights* w) {
+    if (!w) return HC_OK;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != w->device) cudaSetDevice(w->device);
+    cudaFree(w->dev);
+    delete w;
+    return HC_OK;
+}
+
+extern "C" int hc_weights_info(const hc_weights* w, int* type, size_t* m, size_t* n, size_t* bytes) {
+    if (!w) return hc_set_error(HC_ERR_INVALID, "null weights");
+    if (type) *type = w->type;
+    if (m) *m = w->m;
+    if (n) *n = w->n;
+    if (bytes) *bytes = w->bytes;
+    return HC_OK;
+}
+
+// ------------------------------------------------------------------ GEMV core
+int hc_launch_gemv(hc_engine* e, const hc_weights* w, const float* x, size_t ldx, float* y, size_t ldy,
+                   const float* resid, size_t ldr, size_t nvec) {
+    if (!w || !x || !y) return hc_set_error(HC_ERR_INVALID, "null argument");
+    if (w->device != e->device) return hc_set_error(HC_ERR_INVALID, "weights live on device %d, engine on %d", w->device, e->device);
+    if (nvec == 0) return HC_OK;
+    if (ldx < w->n || ldy < w->m || (resid && ldr < w->m))
+        return hc_set_error(HC_ERR_INVALID, "leading dimension smaller than the row length");
+    if (((uintptr_t)x & 15) || (ldx & 3))
+        return hc_set_error(HC_ERR_INVALID, "x must be 16-byte aligned with ldx a multiple of 4");
+    cudaError_t ce;
+    if (gemv_mma_supported(w->type)) {
+        GemvArgs a{};
+        a.w = (const uint8_t*)w->dev;
+        a.row_stride = (long long)w->stride;
+        a.M = (int)w->m;
+        a.K = (int)w->n;
+        a.x = x;
+        a.ldx = (int)ldx;
+        a.y = y;
+        a.ldy = (int)ldy;
+        a.resid = resid;
+        a.ldr = (int)ldr;
+        a.w2 = nullptr;
+        a.err = e->d_err;
+        ce = launch_gemv_mma(w->type, a, (int)nvec, false, e->num_sms, e->smem_optin, e->stream);
+    } else if (gemv_simple_supported(w->type)) {
+        ce = launch_gemv_simple(w->type, (const uint8_t*)w->dev, w->stride, (int)w->m, (int)w->n, x, (int)ldx, y,
+                                (int)ldy, resid, (int)ldr, (int)nvec, e->stream);
+    } else {
+        return hc_set_error(HC_ERR_UNSUPPORTED, "CUDA GEMV missing for %s", hc_type_label(w->type));
+    }
+    if (ce != cudaSuccess) return hc_cuda_error(ce, "gemv launch");
+    return HC_OK;
+}
+
+extern "C" int hc_gemv_dev(hc_engine* e, const hc_weights* w, const float* x, size_t ldx, float* y, size_t ldy,
+                           const float* resid, size_t ldr, size_t nvec) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    return hc_launch_gemv(e, w, x, ldx, y, ldy, resid, ldr, nvec);
+}
+
+// Blocking host-buffer GEMV through resident weights.
+static int gemv_host(hc_engine* e, const hc_weights* w, const float* in, float* out, size_t nvec) {
+    if (!w || !in || !out) return hc_set_error(HC_ERR_INVALID, "null argument");
+    const size_t n = w->n, m = w->m;
+    int rc = e->ws_x.ensure(nvec * n * 4);
+    if (!rc) rc = e->ws_y.ensure(nvec * m * 4);
+    if (rc) return rc;
+    HC_CUDA(cudaMemcpyAsync(e->ws_x.p, in, nvec * n * 4, cudaMemcpyHostToDevice, e->stream));
+    rc = hc_launch_gemv(e, w, (const float*)e->ws_x.p, n, (float*)e->ws_y.p, m, nullptr, 0, nvec);
+    if (rc) return rc;
+    HC_CUDA(cudaMemcpyAsync(out, e->ws_y.p, nvec * m * 4, cudaMemcpyDeviceToHost, e->stream));
+    HC_CUDA(cudaStreamSynchronize(e->stream));
+    return hc_check_device_error(e);
+}
+
+extern "C" int hc_ggml_gemv_bound(hc_engine* e, const hc_weights* w, const float* in, float* out) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    return gemv_host(e, w, in, out, 1);
+}
+
+extern "C" int hc_ggml_gemv_batched(hc_engine* e, const hc_weights* w, const float* in, float* out, size_t batch) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    if (batch == 0) return HC_OK;
+    return gemv_host(e, w, in, out, batch);
+}
+
+// ggml_gemv_dispatch: host weights are staged into the engine workspace every call
+// (the reference does the same with its GemvSyncWorkspace, compute.rs:302-333).
+extern "C" int hc_ggml_gemv_dispatch(hc_engine* e, int type, size_t m, size_t n, const uint8_t* weights, size_t len,
+                                     const float* in, float* out) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    rc = hc_validate_weights(type, m, n, len);
+    if (rc) return rc;
+    if (!weights || !in || !out) return hc_set_error(HC_ERR_INVALID, "null argument");
+    const size_t raw_bytes = m * raw_row_bytes(type, (int)n), gpu_rb = gpu_row_stride(type, (int)n);
+    rc = e->ws_raw.ensure(raw_bytes);
+    if (!rc) rc = e->ws_gpu.ensure(m * gpu_rb + 16);
+    if (rc) return rc;
+    HC_CUDA(cudaMemcpyAsync(e->ws_raw.p, weights, raw_bytes, cudaMemcpyHostToDevice, e->stream));
+    cudaError_t ce = launch_repack(type, (const uint8_t*)e->ws_raw.p, (uint8_t*)e->ws_gpu.p, (int)m, (int)n, e->stream);
+    if (ce != cudaSuccess) return hc_cuda_error(ce, "repack");
+    hc_weights tmp;
+    tmp.type = type;
+    tmp.m = m;
+    tmp.n = n;
+    tmp.stride = gpu_rb;
+    tmp.bytes = m * gpu_rb;
+    tmp.dev = e->ws_gpu.p;
+    tmp.device = e->device;
+    return gemv_host(e, &tmp, in, out, 1);
+}
+
+// ------------------------------------------------------------------ async
+struct hc_pending {
+    hc_engine* eng = nullptr;
+    void* d_x = nullptr;
+    float* d_y = nullptr;
+    float* h_y = nullptr;
+    size_t m = 0;
+    cudaEvent_t done = nullptr;
+    bool waited = false;
+};
+
+extern "C" int hc_ggml_gemv_async(hc_engine* e, const hc_weights* w, const float* in, hc_pending** out) {
+    if (!out) return hc_set_error(HC_ERR_INVALID, "null out pointer");
+    *out = nullptr;
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    if (!w || !in) return hc_set_error(HC_ERR_INVALID, "null argument");
+    hc_pending* p = new hc_pending();
+    p->eng = e;
+    p->m = w->m;
+    cudaError_t ce = cudaMalloc(&p->d_x, w->n * 4);
+    if (ce == cudaSuccess) ce = cudaMalloc((void**)&p->d_y, w->m * 4);
+    if (ce == cudaSuccess) ce = cudaMallocHost((void**)&p->h_y, w->m * 4);
+    if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&p->done, cudaEventDisableTiming);
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(p->d_x, in, w->n * 4, cudaMemcpyHostToDevice, e->stream);
+    if (ce != cudaSuccess) {
+        hc_pending_free(p);
+        return hc_cuda_error(ce, "async gemv setup");
+    }
+    rc = hc_launch_gemv(e, w, (const float*)p->d_x, w->n, p->d_y, w->m, nullptr, 0, 1);
+    if (rc) {
+        hc_pending_free(p);
+        return rc;
+    }
+    ce = cudaMemcpyAsync(p->h_y, p->d_y, w->m * 4, cudaMemcpyDeviceToHost, e->stream);
+    if (ce == cudaSuccess) ce = cudaEventRecord(p->done, e->stream);
+    if (ce != cudaSuccess) {
+        hc_pending_free(p);
+        return hc_cuda_error(ce, "async gemv enqueue");
+    }
+    *out = p;
+    return HC_OK;
+}
+
+extern "C" int hc_pending_wait(hc_pending* p, float* output, size_t m) {
+    if (!p) return hc_set_error(HC_ERR_INVALID, "null pending");
+    int rc = hc_engine_activate(p->eng);
+    if (rc) return rc;
+    if (!p->waited) {
+        HC_CUDA(cudaEventSynchronize(p->done));
+        p->waited = true;
+        rc = hc_check_device_error(p->eng);
+        if (rc) return rc;
+    }
+    if (output) {
+        if (m < p->m) return hc_set_error(HC_ERR_INVALID, "output holds %zu floats, GEMV produced %zu", m, p->m);
+        memcpy(output, p->h_y, p->m * 4);
+    }
+    return HC_OK;
+}
+
+extern "C" int hc_pending_free(hc_pending* p) {
+    if (!p) return HC_OK;
+    if (p->eng) hc_engine_activate(p->eng);
+    // never free buffers a copy may still target (PendingGemv::drop, async_gemv.rs:48-57)
+    if (p->done && !p->waited) cudaEventSynchronize(p->done);
+    if (p->done) cudaEventDestroy(p->done);
+    if (p->d_x) cudaFree(p->d_x);
+    if (p->d_y) cudaFree(p->d_y);
+    if (p->h_y) cudaFreeHost(p->h_y);
+    delete p;
+    return HC_OK;
+}
+
+// ------------------------------------------------------------------ LUT-Q4
+extern "C" int hc_lut_matmul_q4_dev(hc_engine* e, size_t m, size_t n, const uint8_t* w, const float* lut16,
+                                    const float* x, float* y) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    if (m == 0 || n == 0 || n % 2) return hc_set_error(HC_ERR_INVALID, "lut_matmul_q4: N must be even and non-zero");
+    if (!w || !lut16 || !x || !y) return hc_set_error(HC_ERR_INVALID, "null argument");
+    cudaError_t ce = launch_lut_matmul_q4(w, (int)m, (int)n, lut16, x, y, e->stream);
+    if (ce != cudaSuccess) return hc_cuda_error(ce, "lut_matmul_q4 launch");
+    return HC_OK;
+}
+
+extern "C" int hc_lut_matmul_q4(hc_engine* e, size_t m, size_t n, const uint8_t* w, const float* lut16,
+                                const float* x, float* y) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    if (m == 0 || n == 0 || n % 2) return hc_set_error(HC_ERR_INVALID, "lut_matmul_q4: N must be even and non-zero");
+    if (!w || !lut16 || !x || !y) return hc_set_error(HC_ERR_INVALID, "null argument");
+    const size_t wb = m * (n / 2);
+    rc = e->ws_raw.ensure(wb + 64);
+    if (!rc) rc = e->ws_x.ensure(n * 4);
+    if (!rc) rc = e->ws_y.ensure(m * 4);
+    if (rc) return rc;
+    uint8_t* dw = (uint8_t*)e->ws_raw.p;
+    float* dlut = (float*)(dw + (wb + 15) / 16 * 16);
+    if ((wb + 15) / 16 * 16 + 64 > e->ws_raw.cap) {
+        rc = e->ws_raw.ensure((wb + 15) / 16 * 16 + 64);
+        if (rc) return rc;
+        dw = (uint8_t*)e->ws_raw.p;
+        dlut = (float*)(dw + (wb + 15) / 16 * 16);
+    }
+    HC_CUDA(cudaMemcpyAsync(dw, w, wb, cudaMemcpyHostToDevice, e->stream));
+    HC_CUDA(cudaMemcpyAsync(dlut, lut16, 64, cudaMemcpyHostToDevice, e->stream));
+    HC_CUDA(cudaMemcpyAsync(e->ws_x.p, x, n * 4, cudaMemcpyHostToDevice, e->stream));
+    cudaError_t ce = launch_lut_matmul_q4(dw, (int)m, (int)n, dlut, (const float*)e->ws_x.p, (float*)e->ws_y.p, e->stream);
+    if (ce != cudaSuccess) return hc_cuda_error(ce, "lut_matmul_q4 launch");
+    HC_CUDA(cudaMemcpyAsync(y, e->ws_y.p, m * 4, cudaMemcpyDeviceToHost, e->stream));
+    HC_CUDA(cudaStreamSynchronize(e->stream));
+    return HC_OK;
+}
+
+// ------------------------------------------------------------------ FFN
+static int check_ffn(const hc_weights* g, const hc_weights* u, const hc_weights* d) {
+    if (!g || !u || !d) return hc_set_error(HC_ERR_INVALID, "null FFN weights");
+    if (g->m != u->m || g->n != u->n)
+        return hc_set_error(HC_ERR_INVALID, "gate %zux%zu and up %zux%zu shapes differ", g->m, g->n, u->m, u->n);
+    if (d->n != g->m)
+        return hc_set_error(HC_ERR_INVALID, "down has %zu columns, gate/up produce %zu", d->n, g->m);
+    if (d->m > g->n) return hc_set_error(HC_ERR_INVALID, "down rows %zu exceed the FFN input width %zu", d->m, g->n);
+    if (g->device != d->device || u->device != d->device)
+        return hc_set_error(HC_ERR_INVALID, "FFN weights live on different devices");
+    return HC_OK;
+}
+
+// h[v][d_ff] = silu(gate x[v]) * (up x[v])
+int hc_launch_gateup(hc_engine* e, const hc_weights* g, const hc_weights* u, const float* x, size_t ldx, float* h,
+                     size_t nvec) {
+    if (g->type == u->type && gemv_mma_supported(g->type)) {
+        if (((uintptr_t)x & 15) || (ldx & 3))
+            return hc_set_error(HC_ERR_INVALID, "x must be 16-byte aligned with ldx a multiple of 4");
+        GemvArgs a{};
+        a.w = (const uint8_t*)g->dev;
+        a.w2 = (const uint8_t*)u->dev;
+        a.row_stride = (long long)g->stride;
+        a.M = (int)g->m;
+        a.K = (int)g->n;
+        a.x = x;
+        a.ldx = (int)ldx;
+        a.y = h;
+        a.ldy = (int)g->m;
+        a.resid = nullptr;
+        a.err = e->d_err;
+        cudaError_t ce = launch_gemv_mma(g->type, a, (int)nvec, true, e->num_sms, e->smem_optin, e->stream);
+        if (ce != cudaSuccess) return hc_cuda_error(ce, "gate/up launch");
+        return HC_OK;
+    }
+    const size_t ff = g->m;
+    int rc = e->ws_g.ensure(nvec * ff * 4);
+    if (!rc) rc = e->ws_u.ensure(nvec * ff * 4);
+    if (!rc) rc = hc_launch_gemv(e, g, x, ldx, (float*)e->ws_g.p, ff, nullptr, 0, nvec);
+    if (!rc) rc = hc_launch_gemv(e, u, x, ldx, (float*)e->ws_u.p, ff, nullptr, 0, nvec);
+    if (rc) return rc;
+    cudaError_t ce = launch_swiglu((const float*)e->ws_g.p, (const float*)e->ws_u.p, h, nvec * ff, e->stream);
+    if (ce != cudaSuccess) return hc_cuda_error(ce, "swiglu launch");
+    return HC_OK;
+}
+
+int hc_launch_ffn(hc_engine* e, const hc_weights* g, const hc_weights* u, const hc_weights* d, const float* x,
+                  size_t ldx, float* y, size_t ldy, const float* resid, size_t ldr, float* h_ws, size_t nvec) {
+    int rc = check_ffn(g, u, d);
+    if (rc) return rc;
+    if (!h_ws) {
+        rc = e->ws_h.ensure(nvec * g->m * 4);
+        if (rc) return rc;
+        h_ws = (float*)e->ws_h.p;
+    }
+    rc = hc_launch_gateup(e, g, u, x, ldx, h_ws, nvec);
+    if (rc) return rc;
+    return hc_launch_gemv(e, d, h_ws, g->m, y, ldy, resid, ldr, nvec);
+}
+
+extern "C" int hc_ffn_swiglu_dev(hc_engine* e, const hc_weights* g, const hc_weights* u, const hc_weights* d,
+                                 const float* x, float* y, const float* resid, float* h_ws, size_t nvec) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    rc = check_ffn(g, u, d);
+    if (rc) return rc;
+    return hc_launch_ffn(e, g, u, d, x, g->n, y, d->m, resid, d->m, h_ws, nvec);
+}
+
+extern "C" int hc_ffn_gateup_dev(hc_engine* e, const hc_weights* g, const hc_weights* u, const float* x, float* h,
+                                 size_t nvec) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    if (!g || !u || !x || !h) return hc_set_error(HC_ERR_INVALID, "null argument");
+    if (g->m != u->m || g->n != u->n)
+        return hc_set_error(HC_ERR_INVALID, "gate %zux%zu and up %zux%zu shapes differ", g->m, g->n, u->m, u->n);
+    if (nvec == 0) return HC_OK;
+    return hc_launch_gateup(e, g, u, x, g->n, h, nvec);
+}
+
+extern "C" int hc_ffn_swiglu(hc_engine* e, const hc_weights* g, const hc_weights* u, const hc_weights* d,
+                             const float* x, float* y, size_t nvec) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    rc = check_ffn(g, u, d);
+    if (rc) return rc;
+    if (!x || !y) return hc_set_error(HC_ERR_INVALID, "null argument");
+    if (nvec == 0) return HC_OK;
+    rc = e->ws_x.ensure(nvec * g->n * 4);
+    if (!rc) rc = e->ws_y.ensure(nvec * d->m * 4);
+    if (rc) return rc;
+    HC_CUDA(cudaMemcpyAsync(e->ws_x.p, x, nvec * g->n * 4, cudaMemcpyHostToDevice, e->stream));
+    rc = hc_launch_ffn(e, g, u, d, (const float*)e->ws_x.p, g->n, (float*)e->ws_y.p, d->m, nullptr, 0, nullptr, nvec);
+    if (rc) return rc;
+    HC_CUDA(cudaMemcpyAsync(y, e->ws_y.p, nvec * d->m * 4, cudaMemcpyDeviceToHost, e->stream));
+    HC_CUDA(cudaStreamSynchronize(e->stream));
+    return hc_check_device_error(e);
+}
+
+// ------------------------------------------------------------------ FFN stack (+ CUDA graph)
+static uint64_t mix(uint64_t h, uint64_t v) {
+    h ^= v + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+    return h;
+}
+
+static int stack_enqueue(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
+                         const hc_weights* const* d, size_t L, float* x, size_t nvec, float* h) {
+    const size_t k_in = g[0]->n;
+    for (size_t l = 0; l < L; ++l) {
+        // in place: each element of x is read (residual) and written by the same thread
+        int rc = hc_launch_ffn(e, g[l], u[l], d[l], x, k_in, x, k_in, x, k_in, h, nvec);
+        if (rc) return rc;
+    }
+    return HC_OK;
+}
+
+static int stack_check(const hc_weights* const* g, const hc_weights* const* u, const hc_weights* const* d, size_t L) {
+    if (!g || !u || !d || L == 0) return hc_set_error(HC_ERR_INVALID, "empty FFN stack");
+    for (size_t l = 0; l < L; ++l) {
+        int rc = check_ffn(g[l], u[l], d[l]);
+        if (rc) return rc;
+        if (g[l]->n != g[0]->n || d[l]->m != d[0]->m)
+            return hc_set_error(HC_ERR_INVALID, "layer %zu changes the model width", l);
+    }
+    return HC_OK;
+}
+
+extern "C" int hc_ffn_stack_dev(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
+                                const hc_weights* const* d, size_t L, float* x, size_t nvec) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    rc = stack_check(g, u, d, L);
+    if (rc) return rc;
+    if (!x) return hc_set_error(HC_ERR_INVALID, "null x");
+    if (nvec == 0) return HC_OK;
+    size_t ffmax = 0;
+    for (size_t l = 0; l < L; ++l) ffmax = g[l]->m > ffmax ? g[l]->m : ffmax;
+    rc = e->ws_h.ensure(nvec * ffmax * 4);
+    if (rc) return rc;
+    float* h = (float*)e->ws_h.p;
+    if (!e->use_graphs) return stack_enqueue(e, g, u, d, L, x, nvec, h);
+
+    uint64_t key = mix(mix(mix(0, (uint64_t)(uintptr_t)x), nvec), L);
+    key = mix(key, (uint64_t)(uintptr_t)h);
+    key = mix(key, (uint64_t)(uintptr_t)e->stream);
+    for (size_t l = 0; l < L; ++l) {
+        key = mix(key, (uint64_t)(uintptr_t)g[l]->dev);
+        key = mix(key, (uint64_t)(uintptr_t)u[l]->dev);
+        key = mix(key, (uint64_t)(uintptr_t)d[l]->dev);
+        key = mix(key, ((uint64_t)g[l]->type << 32) ^ g[l]->m ^ (g[l]->n << 20) ^ ((uint64_t)d[l]->type << 40));
+    }
+    auto it = e->graphs.find(key);
+    if (it == e->graphs.end()) {
+        cudaGraph_t graph;
+        HC_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeRelaxed));
+        rc = stack_enqueue(e, g, u, d, L, x, nvec, h);
+        cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
+        if (rc) {
+            if (ce == cudaSuccess) cudaGraphDestroy(graph);
+            return rc;
+        }
+        if (ce != cudaSuccess) return hc_cuda_error(ce, "stack capture");
+        cudaGraphExec_t exec;
+        ce = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ce != cudaSuccess) return hc_cuda_error(ce, "stack graph instantiate");
+        it = e->graphs.emplace(key, exec).first;
+    }
+    HC_CUDA(cudaGraphLaunch(it->second, e->stream));
+    return HC_OK;
+}
+
+extern "C" int hc_ffn_stack(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
+                            const hc_weights* const* d, size_t L, const float* x_in, float* x_out, size_t nvec) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    rc = stack_check(g, u, d, L);
+    if (rc) return rc;
+    if (!x_in || !x_out) return hc_set_error(HC_ERR_INVALID, "null argument");
+    const size_t bytes = nvec * g[0]->n * 4;
+    rc = e->ws_x.ensure(bytes);
+    if (rc) return rc;
+    HC_CUDA(cudaMemcpyAsync(e->ws_x.p, x_in, bytes, cudaMemcpyHostToDevice, e->stream));
+    rc = hc_ffn_stack_dev(e, g, u, d, L, (float*)e->ws_x.p, nvec);
+    if (rc) return rc;
+    HC_CUDA(cudaMemcpyAsync(x_out, e->ws_x.p, bytes, cudaMemcpyDeviceToHost, e->stream));
+    HC_CUDA(cudaStreamSynchronize(e->stream));
+    return hc_check_device_error(e);
+}

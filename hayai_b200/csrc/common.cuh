@@ -1,0 +1,123 @@
+// common.cuh -- device helpers shared by the hayai_b200 kernels (sm_100a only).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#ifndef __CUDACC__
+#error "common.cuh is CUDA-only"
+#endif
+
+namespace hc {
+
+// GgmlType ids (reference: crates/hayai-model/src/gguf_types.rs:43-77).
+enum GgmlType : int {
+    T_F32 = 0,
+    T_Q8_0 = 8,
+    T_Q4_K = 12,
+    T_Q6_K = 14,
+    T_IQ2_XXS = 16,
+    T_IQ2_XS = 17,
+    T_IQ3_XXS = 18,
+    T_IQ3_S = 21,
+    T_IQ2_S = 22,
+};
+
+constexpr int QK_K = 256;
+
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+
+// ---------------------------------------------------------------- loads
+// Weights are streamed once per call: do not let them evict the activation
+// working set from L1.
+__device__ __forceinline__ uint4 ldg_stream128(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t ldg_stream32(const void* p) {
+    uint32_t r;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint16_t ldg_u16(const void* p) {
+    uint16_t r;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint2 ldg_u2(const void* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
+
+// ---------------------------------------------------------------- f16 packing
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    return h2_as_u32(__floats2half2_rn(lo, hi));
+}
+
+// x = hi + lo * 2^-11 with hi, lo in f16: hi = f16(x), lo = f16((x - hi) * 2^11).
+// The residual is pre-scaled by 2^11 so it stays a normal f16 whenever x does,
+// which gives ~22 significant bits for |x| < 65504.
+__device__ __forceinline__ void split_f16(float x, __half& hi, __half& lo) {
+    hi = __float2half_rn(x);
+    lo = __float2half_rn((x - __half2float(hi)) * 2048.0f);
+}
+
+// ---------------------------------------------------------------- byte tricks
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t orv) {
+    // (a & mask) | orv  as one LOP3
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(mask), "r"(orv));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+    return h2_as_u32(__hfma2(u32_as_h2(a), u32_as_h2(b), u32_as_h2(c)));
+}
+
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+    return h2_as_u32(__hsub2(u32_as_h2(a), u32_as_h2(b)));
+}
+
+// ---------------------------------------------------------------- tensor core
+// D = A(16x16 f16, row) * B(16x8 f16, col) + C, f32 accumulate.
+// Fragment layout (PTX ISA, mma.m16n8k16): lane = 4*g + t;
+//   A regs: {row g, k 2t..2t+1}, {row g+8, k 2t..2t+1}, {row g, k 2t+8..}, {row g+8, k 2t+8..}
+//   B regs: {k 2t..2t+1, col g}, {k 2t+8..2t+9, col g}
+//   C regs: (row g, col 2t), (row g, col 2t+1), (row g+8, col 2t), (row g+8, col 2t+1)
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---------------------------------------------------------------- misc
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    // crates/hayai-core/src/stream_infer.rs:3836-3840: (g / (1 + exp(-g))) * u
+    return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))) * u;
+}
+
+}  // namespace hc

@@ -1,0 +1,61 @@
+// engine.h -- internal definitions of the C-ABI objects (not part of the public header).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <unordered_map>
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    int ensure(size_t n);
+    void release();
+};
+
+struct HostBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    int ensure(size_t n);
+    void release();
+};
+
+// One GPU + stream: the counterpart of OpenClEngine (crates/hayai-opencl/src/context.rs:23).
+struct hc_engine {
+    int device = 0;
+    int num_sms = 0;
+    int smem_optin = 0;
+    cudaStream_t stream = nullptr;      // stream all work is enqueued on
+    cudaStream_t own_stream = nullptr;  // the engine's own stream
+    int* d_err = nullptr;               // device error flags (bit 0: f16 range, bit 1: wait timeout)
+    bool use_graphs = true;
+    // grow-on-demand workspaces (the reference's GemvSyncWorkspace, compute.rs:10-17)
+    DevBuf ws_raw, ws_gpu, ws_x, ws_y, ws_h, ws_g, ws_u, ws_misc;
+    HostBuf hs_out;
+    std::unordered_map<uint64_t, cudaGraphExec_t> graphs;  // captured FFN stacks
+    std::unordered_map<uint64_t, void*> ptr_tables;        // device tables of expert pointers
+};
+
+// A resident weight matrix in the GPU layout of its format.
+struct hc_weights {
+    int type = 0;
+    size_t m = 0, n = 0;
+    size_t stride = 0;  // bytes per row in the GPU layout
+    size_t bytes = 0;
+    void* dev = nullptr;
+    int device = 0;
+};
+
+// internal helpers shared by the translation units of the C ABI
+int hc_set_error(int code, const char* fmt, ...);
+int hc_cuda_error(cudaError_t e, const char* what);
+int hc_engine_activate(hc_engine* e);
+int hc_check_device_error(hc_engine* e);
+int hc_launch_gemv(hc_engine* e, const hc_weights* w, const float* x, size_t ldx, float* y, size_t ldy,
+                   const float* resid, size_t ldr, size_t nvec);
+int hc_launch_gateup(hc_engine* e, const hc_weights* g, const hc_weights* u, const float* x, size_t ldx, float* h,
+                     size_t nvec);
+int hc_launch_ffn(hc_engine* e, const hc_weights* g, const hc_weights* u, const hc_weights* d, const float* x,
+                  size_t ldx, float* y, size_t ldy, const float* resid, size_t ldr, float* h_ws, size_t nvec);
+const char* hc_type_label(int t);

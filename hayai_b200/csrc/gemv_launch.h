@@ -1,0 +1,35 @@
+// gemv_launch.h -- host-side entry points of the kernel translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace hc {
+
+struct GemvArgs;
+
+// Tensor-core GEMV / fused SwiGLU gate-up for Q4_K, Q6_K, Q8_0 (weights in the GPU layout).
+cudaError_t launch_gemv_mma(int type, const GemvArgs& a, int nvec, bool fused, int num_sms, int smem_limit,
+                            cudaStream_t stream);
+bool gemv_mma_supported(int type);
+
+// CUDA-core GEMV on the raw GGUF layout for F32 and the IQ2/IQ3 codebook formats.
+cudaError_t launch_gemv_simple(int type, const uint8_t* w, size_t row_bytes, int M, int K, const float* x,
+                               int ldx, float* y, int ldy, const float* resid, int ldr, int nvec,
+                               cudaStream_t stream);
+bool gemv_simple_supported(int type);
+
+// Toy LUT-Q4 matmul (16-entry LUT, two nibbles per byte, low nibble first).
+cudaError_t launch_lut_matmul_q4(const uint8_t* w, int M, int N, const float* lut16, const float* x, float* y,
+                                 cudaStream_t stream);
+
+// Elementwise SwiGLU h = silu(g) * u, with an optional residual for out = resid + ...
+cudaError_t launch_swiglu(const float* g, const float* u, float* h, size_t n, cudaStream_t stream);
+
+// Upload repack: raw GGUF rows -> GPU layout (Q6_K, Q8_0); returns the GPU row stride.
+size_t gpu_row_stride(int type, int K);
+size_t raw_row_bytes(int type, int K);
+cudaError_t launch_repack(int type, const uint8_t* raw, uint8_t* gpu, int M, int K, cudaStream_t stream);
+
+}  // namespace hc

@@ -1,0 +1,99 @@
+// gemv_mma.cuh -- batch-1..4 quantized GEMV on tensor-core tiles (sm_100a).
+//
+// y[v][r] = resid[v][r] + sum_k W[r][k] * x[v][k]   for the packed formats Q4_K, Q6_K, Q8_0.
+//
+// Design (one warp = one 16-row tile over a range of super-blocks):
+//  * Weights are dequantized in registers straight into the A fragment of
+//    mma.m16n8k16 (f16 in, f32 accumulate).  Integer codes are exact in f16.
+//    Q4_K folds its 6-bit sub-block scale into the same HFMA2 that removes the
+//    f16 magic offset (q*sc <= 945 is exact in f16), so one MMA may span
+//    several sub-blocks; Q6_K and Q8_0 apply their scale per MMA in f32.
+//  * Activations are split as x = hi + lo * 2^-11 (both f16), occupying two
+//    columns of the B operand, so the tensor-core product carries ~22 bits of
+//    x -- enough for the reference's f32 contract (rel-L2 <= 1e-4).  Columns
+//    2v / 2v+1 hold vector v, so up to 4 vectors share one MMA for free.
+//  * The B fragments of the whole K range are built once per CTA into shared
+//    memory in exactly the order the lanes consume them (one LDS.64 per MMA).
+//  * CTAs are persistent; the warps of a CTA split K of the same row tile and
+//    reduce through shared memory, so each output is written once (no atomics).
+#pragma once
+
+#include "common.cuh"
+
+namespace hc {
+
+// Layout of the per-CTA shared memory: [xt table][Sx (Q4_K)][Q4_K scale LUT][reduction]
+struct GemvSmem {
+    int table_bytes;
+    int sx_bytes;
+    int lut_bytes;
+    int red_bytes;
+    __host__ __device__ int total() const { return table_bytes + sx_bytes + lut_bytes + red_bytes; }
+};
+
+struct GemvArgs {
+    const uint8_t* w;    // weights in the GPU layout of the format
+    long long row_stride;  // bytes per row in that layout
+    int M, K;            // rows, columns
+    const float* x;      // [nvec][ldx]
+    int ldx;
+    float* y;            // [nvec][ldy]
+    int ldy;
+    const float* resid;  // optional [nvec][ldr], added to y
+    int ldr;
+    int wk;              // warps splitting K for one row tile (1, 2, 4, 8)
+    // fused SwiGLU: second matrix (up) with the same layout; y receives silu(W x) * (W2 x)
+    const uint8_t* w2;
+    int* err;            // device error flag (activation outside the f16 range)
+};
+
+// ------------------------------------------------------------------ formats
+struct FmtQ4K {
+    static constexpr int kType = T_Q4_K;
+    static constexpr int kBlockElems = 256;
+    static constexpr int kMmaPerBlock = 16;
+    // element index (within the block) of lane t's k-slot j of MMA `mi`:
+    // byte p = 32t + 4wi + j of qs; low nibble -> 64t + 4wi + j, high -> +32
+    __device__ static int base(int mi, int t) { return 64 * t + 4 * (mi >> 1) + 32 * (mi & 1); }
+    static constexpr bool kNeedSx = true;
+};
+
+struct FmtQ6K {
+    static constexpr int kType = T_Q6_K;
+    static constexpr int kBlockElems = 256;
+    static constexpr int kMmaPerBlock = 16;
+    // mi = 8h + 4lh + q covers scale group (h, q, lh): elements 128h + 32q + 16lh + [0,16)
+    __device__ static int base(int mi, int t) {
+        int h = mi >> 3, lh = (mi >> 2) & 1, q = mi & 3;
+        return 128 * h + 32 * q + 16 * lh + 4 * t;
+    }
+    static constexpr bool kNeedSx = false;
+};
+
+// Q8_0 kernels work on groups of 4 Q8_0 blocks (128 elements, 8 MMAs); mi = 2*blk + half.
+struct FmtQ80 {
+    static constexpr int kType = T_Q8_0;
+    static constexpr int kBlockElems = 128;
+    static constexpr int kMmaPerBlock = 8;
+    __device__ static int base(int mi, int t) { return 16 * mi + 4 * t; }
+    static constexpr bool kNeedSx = false;
+};
+
+template <class F>
+__host__ __device__ constexpr int table_entries_per_block(int nv) {
+    return F::kMmaPerBlock * 2 * nv * 4;
+}
+
+// ------------------------------------------------------------------ host-side sizing
+template <class F>
+__host__ __device__ inline GemvSmem gemv_smem_layout(int K, int nv, bool fused) {
+    GemvSmem s;
+    int nb = (K + F::kBlockElems - 1) / F::kBlockElems;
+    s.table_bytes = nb * table_entries_per_block<F>(nv) * 8;
+    s.sx_bytes = F::kNeedSx ? ((nv * (K / 32) * 4 + 15) / 16) * 16 : 0;
+    s.lut_bytes = F::kType == T_Q4_K ? 64 * 2 * 8 : 0;
+    s.red_bytes = 8 * 16 * nv * 4 * (fused ? 2 : 1);
+    return s;
+}
+
+}  // namespace hc

@@ -1,0 +1,49 @@
+"""Test helpers: seeded synthetic weights in every format, parity metrics."""
+from __future__ import annotations
+
+import numpy as np
+
+import oracle
+
+QK = {oracle.F32: 1, oracle.Q8_0: 32, oracle.Q4_K: 256, oracle.Q6_K: 256, oracle.IQ2_XXS: 256,
+      oracle.IQ2_XS: 256, oracle.IQ2_S: 256, oracle.IQ3_XXS: 256, oracle.IQ3_S: 256}
+IQ_TYPES = [oracle.IQ2_XXS, oracle.IQ2_XS, oracle.IQ2_S, oracle.IQ3_XXS, oracle.IQ3_S]
+# byte offsets of the f16 scales inside a block, per IQ type (d at 0)
+F16_AT = {oracle.Q4_K: (0, 2), oracle.Q6_K: (208,), oracle.Q8_0: (0,), oracle.IQ2_XXS: (0,), oracle.IQ2_XS: (0,),
+          oracle.IQ2_S: (0,), oracle.IQ3_XXS: (0,), oracle.IQ3_S: (0,)}
+
+
+def quantized(ggml_type: int, m: int, n: int, seed: int, std: float = 0.02) -> np.ndarray:
+    """Seeded weights: N(0, std^2) quantized (Q4_K with the reference quantizer), or
+    random valid blocks with d in [0.002, 0.02] for the IQ formats."""
+    if ggml_type == oracle.F32:
+        return oracle.normal(seed, m * n, 0.0, std).view(np.uint8).copy()
+    if ggml_type in (oracle.Q4_K, oracle.Q6_K, oracle.Q8_0):
+        w = oracle.normal(seed, m * n, 0.0, std)
+        return oracle.quantize(ggml_type, w)
+    qk, bs = oracle.BLOCK[ggml_type]
+    nblk = m * n // qk
+    b = oracle.random_bytes(seed, nblk * bs).reshape(nblk, bs)
+    u = oracle.normal(seed ^ 0x5EED, nblk, 0.0, 1.0)
+    d = (0.002 + 0.018 * (0.5 + 0.5 * np.tanh(u))).astype(np.float16)
+    for off in F16_AT[ggml_type]:
+        b[:, off:off + 2] = d.view(np.uint8).reshape(nblk, 2)
+    return b.reshape(-1).copy()
+
+
+def metrics(ref: np.ndarray, got: np.ndarray) -> tuple[float, float]:
+    ref = np.asarray(ref, dtype=np.float64).reshape(-1)
+    got = np.asarray(got, dtype=np.float64).reshape(-1)
+    err = got - ref
+    rel = float(np.linalg.norm(err) / max(np.linalg.norm(ref), 1e-30))
+    return rel, float(np.abs(err).max()) if err.size else 0.0
+
+
+# The parity contract: rel-L2 <= 1e-4 and max-abs <= 1e-3 on FP32 outputs.
+REL_L2 = 1e-4
+MAX_ABS = 1e-3
+
+
+def assert_parity(ref, got, rel_tol: float = REL_L2, abs_tol: float = MAX_ABS, what: str = "") -> None:
+    rel, mx = metrics(ref, got)
+    assert rel <= rel_tol and mx <= abs_tol, f"{what}: rel-L2 {rel:.3e} (tol {rel_tol}), max-abs {mx:.3e} (tol {abs_tol})"

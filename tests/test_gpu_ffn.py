@@ -1,0 +1,116 @@
+"""GPU parity of the SwiGLU FFN block and the layer stack against the oracle (C ABI).
+
+Shapes follow BASELINE.json: SmolLM2-135M (Q4_K x3, K=576 zero-padded to 768),
+Llama-3-8B (gate/up Q4_K, down Q6_K) and the Q8_0 variant.  Tolerance: rel-L2 <= 1e-4,
+max-abs <= 1e-3.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.helpers import assert_parity, quantized
+
+pytestmark = pytest.mark.gpu
+
+
+def ffn_weights(tg, td, d_model, d_ff, seed, k_in=None):
+    """gate/up d_ff x k_in (rows zero-padded from d_model), down d_model x d_ff."""
+    k_in = k_in or d_model
+    if tg == oracle.Q4_K and k_in != d_model:
+        wg32 = np.zeros((d_ff, k_in), np.float32)
+        wu32 = np.zeros((d_ff, k_in), np.float32)
+        wg32[:, :d_model] = oracle.normal(seed, d_ff * d_model, 0, 0.02).reshape(d_ff, d_model)
+        wu32[:, :d_model] = oracle.normal(seed + 1, d_ff * d_model, 0, 0.02).reshape(d_ff, d_model)
+        wg, wu = oracle.quantize(tg, wg32), oracle.quantize(tg, wu32)
+    else:
+        wg, wu = quantized(tg, d_ff, k_in, seed), quantized(tg, d_ff, k_in, seed + 1)
+    wd = quantized(td, d_model, d_ff, seed + 2)
+    return wg, wu, wd
+
+
+def run_ffn(engine, tg, td, d_model, d_ff, seed, nvec=1, k_in=None):
+    k_in = k_in or d_model
+    wg, wu, wd = ffn_weights(tg, td, d_model, d_ff, seed, k_in)
+    x = np.zeros((nvec, k_in), np.float32)
+    x[:, :d_model] = oracle.normal(seed + 3, nvec * d_model).reshape(nvec, d_model)
+    G, U, D = engine.upload(tg, d_ff, k_in, wg), engine.upload(tg, d_ff, k_in, wu), engine.upload(td, d_model, d_ff, wd)
+    got = engine.ffn_swiglu(G, U, D, x, nvec).reshape(nvec, d_model)
+    ref = np.stack([oracle.ffn_swiglu(tg, wg, tg, wu, td, wd, k_in, d_ff, d_model, x[v]) for v in range(nvec)])
+    return ref, got
+
+
+def test_ffn_smollm_layer(engine):
+    ref, got = run_ffn(engine, oracle.Q4_K, oracle.Q4_K, 576, 1536, 100, k_in=768)
+    assert_parity(ref, got, what="smollm ffn")
+
+
+def test_ffn_llama8b_layer(engine):
+    ref, got = run_ffn(engine, oracle.Q4_K, oracle.Q6_K, 4096, 14336, 200)
+    assert_parity(ref, got, what="llama-8b ffn")
+
+
+@pytest.mark.parametrize("nvec", [1, 3, 8])
+def test_ffn_q8_0(engine, nvec):
+    ref, got = run_ffn(engine, oracle.Q8_0, oracle.Q8_0, 1024, 2816, 300, nvec=nvec)
+    assert_parity(ref, got, what=f"q8_0 ffn nvec={nvec}")
+
+
+def test_ffn_mixed_types_falls_back_to_unfused(engine):
+    ref, got = run_ffn(engine, oracle.IQ3_S, oracle.Q4_K, 512, 1024, 400)
+    assert_parity(ref, got, what="iq3_s/q4_k ffn")
+
+
+def make_stack(engine, L, tg, td, d_model, d_ff, seed):
+    layers = [ffn_weights(tg, td, d_model, d_ff, seed + 10 * l) for l in range(L)]
+    res = [(engine.upload(tg, d_ff, d_model, g), engine.upload(tg, d_ff, d_model, u),
+            engine.upload(td, d_model, d_ff, d)) for g, u, d in layers]
+    return layers, res
+
+
+def oracle_stack(layers, tg, td, d_model, d_ff, x):
+    x = x.copy()
+    for g, u, d in layers:
+        x = (x + oracle.ffn_swiglu(tg, g, tg, u, td, d, d_model, d_ff, d_model, x)).astype(np.float32)
+    return x
+
+
+def test_stack_parity(engine):
+    L, dm, ff = 6, 1024, 2816
+    layers, res = make_stack(engine, L, oracle.Q4_K, oracle.Q6_K, dm, ff, 500)
+    x = oracle.normal(501, dm)
+    ref = oracle_stack(layers, oracle.Q4_K, oracle.Q6_K, dm, ff, x)
+    got = engine.ffn_stack([r[0] for r in res], [r[1] for r in res], [r[2] for r in res], x)
+    assert_parity(ref, got, what="stack")
+
+
+def test_stack_graph_equals_eager_layers(engine):
+    L, dm, ff = 4, 4096, 14336
+    layers, res = make_stack(engine, L, oracle.Q4_K, oracle.Q6_K, dm, ff, 600)
+    x = oracle.normal(601, dm)
+    xd = torch.from_numpy(x).cuda()
+    engine.set_stream(torch.cuda.current_stream())
+    try:
+        engine.ffn_stack_dev([r[0] for r in res], [r[1] for r in res], [r[2] for r in res], xd)
+        torch.cuda.synchronize()
+        y_graph = xd.cpu().numpy()
+        xe = torch.from_numpy(x).cuda()
+        for g, u, d in res:
+            ye = torch.empty_like(xe)
+            engine.ffn_swiglu_dev(g, u, d, xe, ye, resid=xe)
+            xe = ye
+        torch.cuda.synchronize()
+    finally:
+        engine.set_stream(None)
+    assert np.array_equal(y_graph, xe.cpu().numpy())
+    ref = oracle_stack(layers, oracle.Q4_K, oracle.Q6_K, dm, ff, x)
+    assert_parity(ref, y_graph, what="8b stack x4")
+
+
+def test_stack_rejects_mismatched_layers(engine):
+    import hayai_b200 as hb
+
+    _, a = make_stack(engine, 1, oracle.Q4_K, oracle.Q4_K, 512, 1024, 700)
+    _, b = make_stack(engine, 1, oracle.Q4_K, oracle.Q4_K, 768, 1024, 710)
+    with pytest.raises(hb.CudaError):
+        engine.ffn_stack([a[0][0], b[0][0]], [a[0][1], b[0][1]], [a[0][2], b[0][2]], np.zeros(512, np.float32))

@@ -1,0 +1,213 @@
+"""GPU parity of the GEMV kernels against the oracle, through the C ABI.
+
+Tolerance (the parity contract): rel-L2 <= 1e-4 and max-abs <= 1e-3 on FP32 outputs.
+Fixtures include the reference's own OpenCL parity patterns
+(crates/hayai-opencl/src/compute.rs:1034-1245, 1370-1496, 1648-1670).
+"""
+import numpy as np
+import pytest
+import torch
+
+import hayai_b200 as hb
+import oracle
+from tests.helpers import IQ_TYPES, MAX_ABS, REL_L2, assert_parity, quantized
+
+pytestmark = pytest.mark.gpu
+
+ALL = [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, oracle.F32, *IQ_TYPES]
+LUT = np.array([-0.5, -0.4, -0.3, -0.2, -0.1, 0.0, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 1.0], np.float32)
+
+
+@pytest.mark.parametrize("t", ALL)
+@pytest.mark.parametrize("m,n", [(32, 256), (100, 1024), (576, 1536), (1536, 768), (8, 4096)])
+def test_gemv_seeded(engine, t, m, n):
+    w = quantized(t, m, n, seed=1000 * t + m + n)
+    x = oracle.normal(7 + m + n, n)
+    ref = oracle.gemv(t, m, n, w, x)
+    got = engine.ggml_gemv_dispatch(t, m, n, w, x)
+    assert_parity(ref, got, what=f"{hb.TYPE_LABELS[t]} {m}x{n}")
+
+
+def test_q8_0_k_not_multiple_of_128(engine):
+    m, n = 64, 32 * 7  # 7 blocks: the GPU layout pads the last group of 4
+    w = quantized(oracle.Q8_0, m, n, 5)
+    x = oracle.normal(6, n)
+    assert_parity(oracle.gemv(oracle.Q8_0, m, n, w, x), engine.ggml_gemv_q8_0(m, n, w, x))
+
+
+def test_reference_q4_k_fixture(engine):
+    m, n = 32, 256
+    w = np.zeros((m, 144), np.uint8)
+    for row in range(m):
+        w[row, 0:2] = [0x00, 0x3C]
+        w[row, 4:16] = 1
+        w[row, 16:144] = (row + np.arange(16, 144)) % 256
+    x = (np.arange(n, dtype=np.float32) * np.float32(0.005) - np.float32(0.2)).astype(np.float32)
+    ref = oracle.gemv(oracle.Q4_K, m, n, w, x)
+    assert np.abs(ref - engine.ggml_gemv_q4_k(m, n, w, x)).max() < 1e-3
+
+
+def test_reference_q6_k_fixture(engine):
+    m, n = 32, 256
+    w = np.zeros((m, 210), np.uint8)
+    for row in range(m):
+        w[row, 0:128] = (row + np.arange(128)) % 256
+        w[row, 128:192] = (row * 3 + np.arange(128, 192)) % 256
+        w[row, 192:208] = 1
+        w[row, 208:210] = [0x00, 0x3C]
+    x = (np.arange(n, dtype=np.float32) * np.float32(0.005) - np.float32(0.2)).astype(np.float32)
+    ref = oracle.gemv(oracle.Q6_K, m, n, w, x)
+    assert np.abs(ref - engine.ggml_gemv_q6_k(m, n, w, x)).max() < 1e-3
+
+
+def test_reference_q8_0_fixture(engine):
+    m, n = 32, 256
+    w = np.zeros((m, 8, 34), np.uint8)
+    for row in range(m):
+        for b in range(8):
+            w[row, b, 0:2] = [0x66, 0x2E]
+            w[row, b, 2:34] = (row + b + np.arange(32)) % 256
+    x = (np.arange(n, dtype=np.float32) * np.float32(0.01) - np.float32(0.4)).astype(np.float32)
+    ref = oracle.gemv(oracle.Q8_0, m, n, w, x)
+    assert np.abs(ref - engine.ggml_gemv_q8_0(m, n, w, x)).max() < 1e-3
+
+
+@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, *IQ_TYPES])
+def test_reference_gemv_parity_pattern(engine, t):
+    # gemv_parity (compute.rs:1370-1396): bytes (i*131+17)&0x1F, input i*0.003-0.2, m32 n256
+    m, n = 32, 256
+    nbytes = m * hb.row_bytes(t, n)
+    w = ((np.arange(nbytes) * 131 + 17) & 0x1F).astype(np.uint8)
+    x = (np.arange(n, dtype=np.float32) * np.float32(0.003) - np.float32(0.2)).astype(np.float32)
+    ref = oracle.gemv(t, m, n, w, x)
+    got = engine.ggml_gemv_dispatch(t, m, n, w, x)
+    assert np.abs(ref - got).max() < 1e-3
+
+
+def test_reference_batched_q4_k(engine):
+    # compute.rs:1648-1670
+    m, n, batch = 32, 256, 3
+    w = ((np.arange(m * 144) * 131 + 17) & 0x1F).astype(np.uint8)
+    inputs = (np.arange(batch * n, dtype=np.float32) * np.float32(0.003) - np.float32(0.2)).astype(np.float32)
+    outputs = np.zeros(batch * m, np.float32)
+    engine.ggml_gemv_batched_q4_k(m, n, w, inputs, outputs, batch)
+    expected = np.concatenate([oracle.gemv(oracle.Q4_K, m, n, w, inputs[b * n:(b + 1) * n]) for b in range(batch)])
+    assert np.abs(expected - outputs).max() < 1e-3
+
+
+@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, oracle.IQ2_S, oracle.F32])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 8])
+def test_batched_all_types(engine, t, batch):
+    m, n = 80, 1024
+    w = quantized(t, m, n, seed=31 + t)
+    xs = oracle.normal(32 + batch, batch * n)
+    rw = engine.upload(t, m, n, w)
+    got = engine.ggml_gemv_batched(rw, xs, batch)
+    ref = np.concatenate([oracle.gemv(t, m, n, w, xs[b * n:(b + 1) * n]) for b in range(batch)])
+    assert_parity(ref, got, what=f"{hb.TYPE_LABELS[t]} batch {batch}")
+
+
+@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0])
+def test_dispatch_bound_dev_async_agree(engine, t):
+    m, n = 256, 2048
+    w = quantized(t, m, n, seed=77)
+    x = oracle.normal(78, n)
+    a = engine.ggml_gemv_dispatch(t, m, n, w, x)
+    rw = engine.upload(t, m, n, w)
+    b = engine.ggml_gemv_dispatch_bound(rw, x)
+    c = engine.ggml_gemv_async(rw, x).wait()
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty(m, device="cuda")
+    engine.set_stream(torch.cuda.current_stream())
+    engine.gemv_dev(rw, xd, yd)
+    torch.cuda.synchronize()
+    engine.set_stream(None)
+    d = yd.cpu().numpy()
+    assert np.array_equal(a, b) and np.array_equal(b, c) and np.array_equal(c, d)
+
+
+def test_gemv_dev_residual(engine):
+    m, n = 512, 1024
+    w = quantized(oracle.Q4_K, m, n, 3)
+    x = oracle.normal(4, n)
+    r = oracle.normal(5, m)
+    rw = engine.upload(oracle.Q4_K, m, n, w)
+    xd, rd = torch.from_numpy(x).cuda(), torch.from_numpy(r).cuda()
+    yd = torch.empty(m, device="cuda")
+    engine.set_stream(torch.cuda.current_stream())
+    engine.gemv_dev(rw, xd, yd, resid=rd)
+    torch.cuda.synchronize()
+    engine.set_stream(None)
+    assert_parity(oracle.gemv(oracle.Q4_K, m, n, w, x) + r, yd.cpu().numpy())
+
+
+def test_upload_from_device_matches_host_upload(engine):
+    m, n = 128, 512
+    w = quantized(oracle.Q6_K, m, n, 9)
+    x = oracle.normal(10, n)
+    a = engine.ggml_gemv_dispatch_bound(engine.upload(oracle.Q6_K, m, n, w), x)
+    b = engine.ggml_gemv_dispatch_bound(engine.upload_from_device(oracle.Q6_K, m, n, torch.from_numpy(w).cuda()), x)
+    assert np.array_equal(a, b)
+
+
+def test_lut_reference_fixture(engine):
+    # compute.rs:1034-1061
+    m, n = 64, 128
+    w = ((np.arange(m * n // 2) * 17) % 256).astype(np.uint8)
+    x = (np.arange(n, dtype=np.float32) * np.float32(0.01) - np.float32(0.5)).astype(np.float32)
+    assert np.abs(oracle.lut_matmul_q4(m, n, w, LUT, x) - engine.lut_matmul_q4(m, n, w, LUT, x)).max() < 1e-4
+
+
+def test_lut_bench_and_validate_workloads(engine):
+    m, n = 1536, 576  # `hayai bench` (main.rs:601-646)
+    w = np.full(m * n // 2, 0xAB, np.uint8)
+    x = np.ones(n, np.float32)
+    assert np.abs(oracle.lut_matmul_q4(m, n, w, LUT, x) - engine.lut_matmul_q4(m, n, w, LUT, x)).max() < 1e-4
+    m, n = 128, 256  # `hayai validate` (main.rs:648-696)
+    w = ((np.arange(m * n // 2) * 31) % 256).astype(np.uint8)
+    x = (np.arange(n, dtype=np.float32) * np.float32(0.01) - np.float32(0.25)).astype(np.float32)
+    assert np.abs(oracle.lut_matmul_q4(m, n, w, LUT, x) - engine.lut_matmul_q4(m, n, w, LUT, x)).max() < 1e-4
+
+
+def test_invalid_shapes_rejected(engine):
+    with pytest.raises(hb.CudaError) as e:
+        engine.ggml_gemv_dispatch(oracle.Q4_K, 4, 576, np.zeros(4 * 3 * 144, np.uint8), np.zeros(576, np.float32))
+    assert e.value.code == 1
+    with pytest.raises(hb.CudaError) as e:
+        engine.ggml_gemv_dispatch(oracle.Q4_K, 4, 256, np.zeros(3 * 144, np.uint8), np.zeros(256, np.float32))
+    assert "weight buffer" in str(e.value)
+    with pytest.raises(hb.CudaError) as e:
+        engine.ggml_gemv_dispatch(2, 4, 256, np.zeros(4 * 144, np.uint8), np.zeros(256, np.float32))
+    assert e.value.code == 2
+
+
+def test_activation_out_of_f16_range_is_reported(engine):
+    m, n = 16, 256
+    w = quantized(oracle.Q4_K, m, n, 1)
+    x = np.zeros(n, np.float32)
+    x[3] = 1e6
+    with pytest.raises(hb.CudaError) as e:
+        engine.ggml_gemv_q4_k(m, n, w, x)
+    assert e.value.code == 4
+    # the engine stays usable and the flag is cleared
+    x[3] = 1.0
+    assert_parity(oracle.gemv(oracle.Q4_K, m, n, w, x), engine.ggml_gemv_q4_k(m, n, w, x))
+
+
+def test_zero_and_tiny_inputs(engine):
+    m, n = 64, 512
+    w = quantized(oracle.Q4_K, m, n, 2)
+    assert np.all(engine.ggml_gemv_q4_k(m, n, w, np.zeros(n, np.float32)) == 0.0)
+    x = oracle.normal(3, n) * np.float32(1e-6)
+    assert_parity(oracle.gemv(oracle.Q4_K, m, n, w, x), engine.ggml_gemv_q4_k(m, n, w, x), abs_tol=MAX_ABS,
+                  rel_tol=REL_L2)
+
+
+def test_deterministic(engine):
+    m, n = 4096, 4096
+    w = quantized(oracle.Q4_K, m, n, 12)
+    rw = engine.upload(oracle.Q4_K, m, n, w)
+    x = oracle.normal(13, n)
+    a = engine.ggml_gemv_dispatch_bound(rw, x)
+    b = engine.ggml_gemv_dispatch_bound(rw, x)
+    assert np.array_equal(a, b)

@@ -161,6 +161,38 @@ def barrier(world: int):
 
 
 # ---------------------------------------------------------------- CPU baseline (oracle port)
+EPS = 1e-5
+
+
+def oracle_layer(c, g, u, d, nw, x):
+    """One FFN sublayer on the CPU path: FFN(rms_norm(x)) (stream_infer.rs:2166-2170, :3752-3864)."""
+    import numpy as np
+
+    import oracle
+
+    dm = c["d_model"]
+    xn = np.zeros(c["k_in"], np.float32)
+    xn[:dm] = oracle.rms_norm(x[:dm], nw, EPS)
+    return oracle.ffn_swiglu(c["tg"], g, c["tg"], u, c["td"], d, c["k_in"], c["d_ff"], dm, xn)
+
+
+def host_layer(c, seed):
+    """Seeded layer generated on the host with the oracle (zero-padded K where needed)."""
+    import numpy as np
+
+    import oracle
+
+    dm, kin, ff = c["d_model"], c["k_in"], c["d_ff"]
+
+    def gu(s):
+        w = np.zeros((ff, kin), np.float32)
+        w[:, :dm] = oracle.normal(s, ff * dm, 0.0, 0.02).reshape(ff, dm)
+        return oracle.quantize(c["tg"], w)
+
+    d = oracle.quantize(c["td"], oracle.normal(seed + 2, dm * ff, 0.0, 0.02))
+    return gu(seed), gu(seed + 1), d, oracle.normal(seed + 3, dm, 1.0, 0.1)
+
+
 def cpu_baseline(c, layers_raw, x0, seconds: float):
     """Time the oracle's FFN on all host cores over the sampled layers, for ~`seconds`."""
     import numpy as np
@@ -173,9 +205,7 @@ def cpu_baseline(c, layers_raw, x0, seconds: float):
     done = 0
     t0 = time.perf_counter()
     while True:
-        g, u, d = layers_raw[done % len(layers_raw)]
-        y = oracle.ffn_swiglu(c["tg"], g, c["tg"], u, c["td"], d, c["k_in"], c["d_ff"], c["d_model"], x)
-        x[:c["d_model"]] += y
+        x[:c["d_model"]] += oracle_layer(c, *layers_raw[done % len(layers_raw)], x)
         done += 1
         el = time.perf_counter() - t0
         if el >= seconds and done >= 2:
@@ -202,20 +232,13 @@ def run_reference(args):
     cores = oracle.get_threads()
     # a few distinct layers of the same shapes, generated on the host with the oracle
     S = 3
-    layers = []
-    for l in range(S):
-        g = oracle.quantize(c["tg"], oracle.normal(1000 + 3 * l, c["d_ff"] * c["k_in"], 0.0, 0.02))
-        u = oracle.quantize(c["tg"], oracle.normal(1001 + 3 * l, c["d_ff"] * c["k_in"], 0.0, 0.02))
-        d = oracle.quantize(c["td"], oracle.normal(1002 + 3 * l, c["d_model"] * c["d_ff"], 0.0, 0.02))
-        layers.append((g, u, d))
+    layers = [host_layer(c, 1000 + 4 * l) for l in range(S)]
     x = np.zeros(c["k_in"], np.float32)
     x[:c["d_model"]] = oracle.normal(7, c["d_model"])
     lb = layer_bytes(c)
 
     def step(i):
-        g, u, d = layers[i % S]
-        y = oracle.ffn_swiglu(c["tg"], g, c["tg"], u, c["td"], d, c["k_in"], c["d_ff"], c["d_model"], x)
-        x[:c["d_model"]] = x0[:c["d_model"]] + y
+        x[:c["d_model"]] = x0[:c["d_model"]] + oracle_layer(c, *layers[i % S], x)
 
     x0 = x.copy()
     for i in range(args.warmup):
@@ -267,7 +290,8 @@ def run_ours(args):
     L, dm, kin, ff, tg, td = c["layers"], c["d_model"], c["k_in"], c["d_ff"], c["tg"], c["td"]
     B = args.batch
     eng = hb.CudaEngine(local)
-    stream = torch.cuda.current_stream(dev)
+    stream = torch.cuda.Stream(dev)  # one stream for torch's copies, our kernels and the CUDA events
+    torch.cuda.set_stream(stream)
     eng.set_stream(stream)
 
     # ---- resident weights, generated and quantized on the device
@@ -295,16 +319,20 @@ def run_ours(args):
         del q
         return rw, host
 
+    NW = []  # per-layer RMSNorm weights (ffn_norm), N(1, 0.1^2)
     for l in range(L):
         keep = l < S_cpu
-        g, gh = synth(tg, ff, kin, seed0 + 3 * l, keep, dm)
-        u, uh = synth(tg, ff, kin, seed0 + 3 * l + 1, keep, dm)
-        d, dh = synth(td, dm, ff, seed0 + 3 * l + 2, keep)
+        g, gh = synth(tg, ff, kin, seed0 + 4 * l, keep, dm)
+        u, uh = synth(tg, ff, kin, seed0 + 4 * l + 1, keep, dm)
+        d, dh = synth(td, dm, ff, seed0 + 4 * l + 2, keep)
+        nw = torch.empty(dm, dtype=torch.float32, device=dev)
+        eng.synth_normal_dev(seed0 + 4 * l + 3, nw, 1.0, 0.1)
         G.append(g)
         U.append(u)
         D.append(d)
+        NW.append(nw)
         if keep:
-            raw.append((gh, uh, dh))
+            raw.append((gh, uh, dh, nw.cpu().numpy()))
     del scratch, padded
     x0 = torch.zeros(B, kin, dtype=torch.float32, device=dev)
     xs = torch.empty(B * dm, dtype=torch.float32, device=dev)
@@ -315,7 +343,7 @@ def run_ours(args):
 
     def step():
         x.copy_(x0)
-        eng.ffn_stack_dev(G, U, D, x, B)
+        eng.ffn_stack_dev(G, U, D, x, B, norms=NW, eps=EPS)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -345,12 +373,12 @@ def run_ours(args):
     h = torch.empty(B, ff, dtype=torch.float32, device=dev)
     reps = 3 * L if L >= 8 else 96
     for i in range(L):
-        eng.ffn_gateup_dev(G[i % L], U[i % L], x0, h, B)
+        eng.ffn_gateup_dev(G[i % L], U[i % L], x0, h, B, norm=NW[i % L], norm_len=dm, eps=EPS)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize(dev)
     e0.record(stream)
     for i in range(reps):
-        eng.ffn_gateup_dev(G[i % L], U[i % L], x0, h, B)
+        eng.ffn_gateup_dev(G[i % L], U[i % L], x0, h, B, norm=NW[i % L], norm_len=dm, eps=EPS)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     gu_time = e0.elapsed_time(e1) / 1e3 / reps
@@ -373,12 +401,12 @@ def run_ours(args):
     x_out = torch.empty_like(x_in).pin_memory()
     xi, xo = x_in.numpy(), x_out.numpy()
     for _ in range(3):
-        eng.ffn_stack(G, U, D, xi, B)
+        eng.ffn_stack(G, U, D, xi, B, norms=NW, eps=EPS)
     barrier(world)
     torch.cuda.synchronize(dev)
     e0.record(stream)
     for _ in range(n_e2e):
-        xo[:] = eng.ffn_stack(G, U, D, xi, B)
+        xo[:] = eng.ffn_stack(G, U, D, xi, B, norms=NW, eps=EPS)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     t_e2e = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)

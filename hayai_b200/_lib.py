@@ -36,6 +36,7 @@ SIGNATURES: dict[str, list] = {
     "hc_engine_init": [_I, _PP],
     "hc_engine_free": [_P],
     "hc_engine_set_stream": [_P, _P],
+    "hc_engine_use_own_stream": [_P],
     "hc_engine_get_stream": [_P, _PP],
     "hc_sync": [_P],
     "hc_gemv_row_bytes": [_I, _S, ctypes.POINTER(_S)],
@@ -54,9 +55,9 @@ SIGNATURES: dict[str, list] = {
     "hc_lut_matmul_q4_dev": [_P, _S, _S, _P, _P, _P, _P],
     "hc_ffn_swiglu": [_P, _P, _P, _P, _P, _P, _S],
     "hc_ffn_swiglu_dev": [_P, _P, _P, _P, _P, _P, _P, _P, _S],
-    "hc_ffn_gateup_dev": [_P, _P, _P, _P, _P, _S],
-    "hc_ffn_stack_dev": [_P, _P, _P, _P, _S, _P, _S],
-    "hc_ffn_stack": [_P, _P, _P, _P, _S, _P, _P, _S],
+    "hc_ffn_gateup_dev": [_P, _P, _P, _P, _P, _S, _P, _S, _F],
+    "hc_ffn_stack_dev": [_P, _P, _P, _P, _P, _F, _S, _P, _S],
+    "hc_ffn_stack": [_P, _P, _P, _P, _P, _F, _S, _P, _P, _S],
     "hc_route_experts_dev": [_P, _P, _P, _S, _S, _S, _S, _S, _I, _I, _F, _P, _P],
     "hc_router_scores_dev": [_P, _P, _S, _S, _P, _S, _P],
     "hc_moe_ffn_dev": [_P, _P, _S, _S, _I, _F, _P, _P, _P, _P, _S, _P, _P, _P],

@@ -229,7 +229,14 @@ extern "C" int hc_engine_free(hc_engine* e) {
 
 extern "C" int hc_engine_set_stream(hc_engine* e, void* stream) {
     if (!e) return hc_set_error(HC_ERR_INVALID, "null engine");
-    e->stream = stream ? (cudaStream_t)stream : e->own_stream;
+    // NULL is CUDA's legacy default stream (the stream torch calls "default"), used as is
+    e->stream = stream ? (cudaStream_t)stream : cudaStreamLegacy;
+    return HC_OK;
+}
+
+extern "C" int hc_engine_use_own_stream(hc_engine* e) {
+    if (!e) return hc_set_error(HC_ERR_INVALID, "null engine");
+    e->stream = e->own_stream;
     return HC_OK;
 }
 
@@ -568,12 +575,15 @@ static int check_ffn(const hc_weights* g, const hc_weights* u, const hc_weights*
     return HC_OK;
 }
 
-// h[v][d_ff] = silu(gate x[v]) * (up x[v])
+// h[v][d_ff] = silu(gate xn[v]) * (up xn[v]), xn = rms_norm(x) when norm_w is given
+// (over the first norm_len entries of each row) else x.
 int hc_launch_gateup(hc_engine* e, const hc_weights* g, const hc_weights* u, const float* x, size_t ldx, float* h,
-                     size_t nvec) {
+                     size_t nvec, const float* norm_w, size_t norm_len, float eps) {
+    if (((uintptr_t)x & 15) || (ldx & 3))
+        return hc_set_error(HC_ERR_INVALID, "x must be 16-byte aligned with ldx a multiple of 4");
+    if (norm_w && (norm_len == 0 || norm_len > g->n))
+        return hc_set_error(HC_ERR_INVALID, "norm length %zu must be in [1, %zu]", norm_len, g->n);
     if (g->type == u->type && gemv_mma_supported(g->type)) {
-        if (((uintptr_t)x & 15) || (ldx & 3))
-            return hc_set_error(HC_ERR_INVALID, "x must be 16-byte aligned with ldx a multiple of 4");
         GemvArgs a{};
         a.w = (const uint8_t*)g->dev;
         a.w2 = (const uint8_t*)u->dev;
@@ -586,15 +596,31 @@ int hc_launch_gateup(hc_engine* e, const hc_weights* g, const hc_weights* u, con
         a.ldy = (int)g->m;
         a.resid = nullptr;
         a.err = e->d_err;
+        a.norm_w = norm_w;
+        a.norm_len = (int)norm_len;
+        a.norm_eps = eps;
         cudaError_t ce = launch_gemv_mma(g->type, a, (int)nvec, true, e->num_sms, e->smem_optin, e->stream);
         if (ce != cudaSuccess) return hc_cuda_error(ce, "gate/up launch");
         return HC_OK;
     }
-    const size_t ff = g->m;
+    // unfused: (norm) -> gate GEMV, up GEMV -> SwiGLU
+    const size_t ff = g->m, K = g->n;
     int rc = e->ws_g.ensure(nvec * ff * 4);
     if (!rc) rc = e->ws_u.ensure(nvec * ff * 4);
-    if (!rc) rc = hc_launch_gemv(e, g, x, ldx, (float*)e->ws_g.p, ff, nullptr, 0, nvec);
-    if (!rc) rc = hc_launch_gemv(e, u, x, ldx, (float*)e->ws_u.p, ff, nullptr, 0, nvec);
+    if (rc) return rc;
+    const float* xin = x;
+    size_t ldin = ldx;
+    if (norm_w) {
+        rc = e->ws_misc.ensure(nvec * K * 4);
+        if (rc) return rc;
+        cudaError_t ce = launch_rms_norm(x, (int)ldx, norm_w, (int)norm_len, (int)K, eps, (float*)e->ws_misc.p,
+                                         (int)K, (int)nvec, e->stream);
+        if (ce != cudaSuccess) return hc_cuda_error(ce, "rms_norm launch");
+        xin = (const float*)e->ws_misc.p;
+        ldin = K;
+    }
+    rc = hc_launch_gemv(e, g, xin, ldin, (float*)e->ws_g.p, ff, nullptr, 0, nvec);
+    if (!rc) rc = hc_launch_gemv(e, u, xin, ldin, (float*)e->ws_u.p, ff, nullptr, 0, nvec);
     if (rc) return rc;
     cudaError_t ce = launch_swiglu((const float*)e->ws_g.p, (const float*)e->ws_u.p, h, nvec * ff, e->stream);
     if (ce != cudaSuccess) return hc_cuda_error(ce, "swiglu launch");
@@ -602,7 +628,8 @@ int hc_launch_gateup(hc_engine* e, const hc_weights* g, const hc_weights* u, con
 }
 
 int hc_launch_ffn(hc_engine* e, const hc_weights* g, const hc_weights* u, const hc_weights* d, const float* x,
-                  size_t ldx, float* y, size_t ldy, const float* resid, size_t ldr, float* h_ws, size_t nvec) {
+                  size_t ldx, float* y, size_t ldy, const float* resid, size_t ldr, float* h_ws, size_t nvec,
+                  const float* norm_w, size_t norm_len, float eps) {
     int rc = check_ffn(g, u, d);
     if (rc) return rc;
     if (!h_ws) {
@@ -610,7 +637,7 @@ int hc_launch_ffn(hc_engine* e, const hc_weights* g, const hc_weights* u, const 
         if (rc) return rc;
         h_ws = (float*)e->ws_h.p;
     }
-    rc = hc_launch_gateup(e, g, u, x, ldx, h_ws, nvec);
+    rc = hc_launch_gateup(e, g, u, x, ldx, h_ws, nvec, norm_w, norm_len, eps);
     if (rc) return rc;
     return hc_launch_gemv(e, d, h_ws, g->m, y, ldy, resid, ldr, nvec);
 }
@@ -621,18 +648,19 @@ extern "C" int hc_ffn_swiglu_dev(hc_engine* e, const hc_weights* g, const hc_wei
     if (rc) return rc;
     rc = check_ffn(g, u, d);
     if (rc) return rc;
-    return hc_launch_ffn(e, g, u, d, x, g->n, y, d->m, resid, d->m, h_ws, nvec);
+    if (!x || !y) return hc_set_error(HC_ERR_INVALID, "null argument");
+    return hc_launch_ffn(e, g, u, d, x, g->n, y, d->m, resid, d->m, h_ws, nvec, nullptr, 0, 0.f);
 }
 
 extern "C" int hc_ffn_gateup_dev(hc_engine* e, const hc_weights* g, const hc_weights* u, const float* x, float* h,
-                                 size_t nvec) {
+                                 size_t nvec, const float* norm_w, size_t norm_len, float eps) {
     int rc = hc_engine_activate(e);
     if (rc) return rc;
     if (!g || !u || !x || !h) return hc_set_error(HC_ERR_INVALID, "null argument");
     if (g->m != u->m || g->n != u->n)
         return hc_set_error(HC_ERR_INVALID, "gate %zux%zu and up %zux%zu shapes differ", g->m, g->n, u->m, u->n);
     if (nvec == 0) return HC_OK;
-    return hc_launch_gateup(e, g, u, x, g->n, h, nvec);
+    return hc_launch_gateup(e, g, u, x, g->n, h, nvec, norm_w, norm_len, eps);
 }
 
 extern "C" int hc_ffn_swiglu(hc_engine* e, const hc_weights* g, const hc_weights* u, const hc_weights* d,
@@ -647,7 +675,8 @@ extern "C" int hc_ffn_swiglu(hc_engine* e, const hc_weights* g, const hc_weights
     if (!rc) rc = e->ws_y.ensure(nvec * d->m * 4);
     if (rc) return rc;
     HC_CUDA(cudaMemcpyAsync(e->ws_x.p, x, nvec * g->n * 4, cudaMemcpyHostToDevice, e->stream));
-    rc = hc_launch_ffn(e, g, u, d, (const float*)e->ws_x.p, g->n, (float*)e->ws_y.p, d->m, nullptr, 0, nullptr, nvec);
+    rc = hc_launch_ffn(e, g, u, d, (const float*)e->ws_x.p, g->n, (float*)e->ws_y.p, d->m, nullptr, 0, nullptr,
+                       nvec, nullptr, 0, 0.f);
     if (rc) return rc;
     HC_CUDA(cudaMemcpyAsync(y, e->ws_y.p, nvec * d->m * 4, cudaMemcpyDeviceToHost, e->stream));
     HC_CUDA(cudaStreamSynchronize(e->stream));
@@ -660,57 +689,64 @@ static uint64_t mix(uint64_t h, uint64_t v) {
     return h;
 }
 
-static int stack_enqueue(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
-                         const hc_weights* const* d, size_t L, float* x, size_t nvec, float* h) {
-    const size_t k_in = g[0]->n;
-    for (size_t l = 0; l < L; ++l) {
+struct StackArgs {
+    const hc_weights* const* g;
+    const hc_weights* const* u;
+    const hc_weights* const* d;
+    const float* const* norm;  // per-layer RMSNorm weights (device) or nullptr
+    size_t L;
+    float eps;
+};
+
+static int stack_enqueue(hc_engine* e, const StackArgs& s, float* x, size_t nvec, float* h) {
+    const size_t k_in = s.g[0]->n, dm = s.d[0]->m;
+    for (size_t l = 0; l < s.L; ++l) {
         // in place: each element of x is read (residual) and written by the same thread
-        int rc = hc_launch_ffn(e, g[l], u[l], d[l], x, k_in, x, k_in, x, k_in, h, nvec);
+        int rc = hc_launch_ffn(e, s.g[l], s.u[l], s.d[l], x, k_in, x, k_in, x, k_in, h, nvec,
+                               s.norm ? s.norm[l] : nullptr, dm, s.eps);
         if (rc) return rc;
     }
     return HC_OK;
 }
 
-static int stack_check(const hc_weights* const* g, const hc_weights* const* u, const hc_weights* const* d, size_t L) {
-    if (!g || !u || !d || L == 0) return hc_set_error(HC_ERR_INVALID, "empty FFN stack");
-    for (size_t l = 0; l < L; ++l) {
-        int rc = check_ffn(g[l], u[l], d[l]);
+static int stack_check(const StackArgs& s) {
+    if (!s.g || !s.u || !s.d || s.L == 0) return hc_set_error(HC_ERR_INVALID, "empty FFN stack");
+    for (size_t l = 0; l < s.L; ++l) {
+        int rc = check_ffn(s.g[l], s.u[l], s.d[l]);
         if (rc) return rc;
-        if (g[l]->n != g[0]->n || d[l]->m != d[0]->m)
+        if (s.g[l]->n != s.g[0]->n || s.d[l]->m != s.d[0]->m)
             return hc_set_error(HC_ERR_INVALID, "layer %zu changes the model width", l);
+        if (s.norm && !s.norm[l]) return hc_set_error(HC_ERR_INVALID, "layer %zu has no norm weight", l);
     }
     return HC_OK;
 }
 
-extern "C" int hc_ffn_stack_dev(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
-                                const hc_weights* const* d, size_t L, float* x, size_t nvec) {
-    int rc = hc_engine_activate(e);
-    if (rc) return rc;
-    rc = stack_check(g, u, d, L);
-    if (rc) return rc;
-    if (!x) return hc_set_error(HC_ERR_INVALID, "null x");
-    if (nvec == 0) return HC_OK;
+static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
     size_t ffmax = 0;
-    for (size_t l = 0; l < L; ++l) ffmax = g[l]->m > ffmax ? g[l]->m : ffmax;
-    rc = e->ws_h.ensure(nvec * ffmax * 4);
+    for (size_t l = 0; l < s.L; ++l) ffmax = s.g[l]->m > ffmax ? s.g[l]->m : ffmax;
+    int rc = e->ws_h.ensure(nvec * ffmax * 4);
     if (rc) return rc;
     float* h = (float*)e->ws_h.p;
-    if (!e->use_graphs) return stack_enqueue(e, g, u, d, L, x, nvec, h);
+    if (!e->use_graphs) return stack_enqueue(e, s, x, nvec, h);
 
-    uint64_t key = mix(mix(mix(0, (uint64_t)(uintptr_t)x), nvec), L);
+    uint64_t key = mix(mix(mix(0, (uint64_t)(uintptr_t)x), nvec), s.L);
     key = mix(key, (uint64_t)(uintptr_t)h);
     key = mix(key, (uint64_t)(uintptr_t)e->stream);
-    for (size_t l = 0; l < L; ++l) {
-        key = mix(key, (uint64_t)(uintptr_t)g[l]->dev);
-        key = mix(key, (uint64_t)(uintptr_t)u[l]->dev);
-        key = mix(key, (uint64_t)(uintptr_t)d[l]->dev);
-        key = mix(key, ((uint64_t)g[l]->type << 32) ^ g[l]->m ^ (g[l]->n << 20) ^ ((uint64_t)d[l]->type << 40));
+    uint32_t eb;
+    memcpy(&eb, &s.eps, 4);
+    key = mix(key, eb);
+    for (size_t l = 0; l < s.L; ++l) {
+        key = mix(key, (uint64_t)(uintptr_t)s.g[l]->dev);
+        key = mix(key, (uint64_t)(uintptr_t)s.u[l]->dev);
+        key = mix(key, (uint64_t)(uintptr_t)s.d[l]->dev);
+        key = mix(key, (uint64_t)(uintptr_t)(s.norm ? s.norm[l] : nullptr));
+        key = mix(key, ((uint64_t)s.g[l]->type << 32) ^ s.g[l]->m ^ (s.g[l]->n << 20) ^ ((uint64_t)s.d[l]->type << 40));
     }
     auto it = e->graphs.find(key);
     if (it == e->graphs.end()) {
         cudaGraph_t graph;
         HC_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeRelaxed));
-        rc = stack_enqueue(e, g, u, d, L, x, nvec, h);
+        rc = stack_enqueue(e, s, x, nvec, h);
         cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
         if (rc) {
             if (ce == cudaSuccess) cudaGraphDestroy(graph);
@@ -727,18 +763,34 @@ extern "C" int hc_ffn_stack_dev(hc_engine* e, const hc_weights* const* g, const 
     return HC_OK;
 }
 
-extern "C" int hc_ffn_stack(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
-                            const hc_weights* const* d, size_t L, const float* x_in, float* x_out, size_t nvec) {
+extern "C" int hc_ffn_stack_dev(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
+                                const hc_weights* const* d, const float* const* norm_w, float eps, size_t L, float* x,
+                                size_t nvec) {
     int rc = hc_engine_activate(e);
     if (rc) return rc;
-    rc = stack_check(g, u, d, L);
+    StackArgs s{g, u, d, norm_w, L, eps};
+    rc = stack_check(s);
+    if (rc) return rc;
+    if (!x) return hc_set_error(HC_ERR_INVALID, "null x");
+    if (nvec == 0) return HC_OK;
+    return stack_run(e, s, x, nvec);
+}
+
+extern "C" int hc_ffn_stack(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
+                            const hc_weights* const* d, const float* const* norm_w, float eps, size_t L,
+                            const float* x_in, float* x_out, size_t nvec) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    StackArgs s{g, u, d, norm_w, L, eps};
+    rc = stack_check(s);
     if (rc) return rc;
     if (!x_in || !x_out) return hc_set_error(HC_ERR_INVALID, "null argument");
+    if (nvec == 0) return HC_OK;
     const size_t bytes = nvec * g[0]->n * 4;
     rc = e->ws_x.ensure(bytes);
     if (rc) return rc;
     HC_CUDA(cudaMemcpyAsync(e->ws_x.p, x_in, bytes, cudaMemcpyHostToDevice, e->stream));
-    rc = hc_ffn_stack_dev(e, g, u, d, L, (float*)e->ws_x.p, nvec);
+    rc = stack_run(e, s, (float*)e->ws_x.p, nvec);
     if (rc) return rc;
     HC_CUDA(cudaMemcpyAsync(x_out, e->ws_x.p, bytes, cudaMemcpyDeviceToHost, e->stream));
     HC_CUDA(cudaStreamSynchronize(e->stream));

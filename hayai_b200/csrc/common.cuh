@@ -33,7 +33,7 @@ __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 // working set from L1.
 __device__ __forceinline__ uint4 ldg_stream128(const void* p) {
     uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(p));
     return r;
@@ -41,13 +41,13 @@ __device__ __forceinline__ uint4 ldg_stream128(const void* p) {
 
 __device__ __forceinline__ uint32_t ldg_stream32(const void* p) {
     uint32_t r;
-    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
     return r;
 }
 
 __device__ __forceinline__ uint16_t ldg_u16(const void* p) {
     uint16_t r;
-    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+    asm("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
     return r;
 }
 
@@ -101,7 +101,7 @@ __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
 //   C regs: (row g, col 2t), (row g, col 2t+1), (row g+8, col 2t), (row g+8, col 2t+1)
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(  // pure: no memory side effects, free to be scheduled around the loads
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])

@@ -55,7 +55,8 @@ int hc_check_device_error(hc_engine* e);
 int hc_launch_gemv(hc_engine* e, const hc_weights* w, const float* x, size_t ldx, float* y, size_t ldy,
                    const float* resid, size_t ldr, size_t nvec);
 int hc_launch_gateup(hc_engine* e, const hc_weights* g, const hc_weights* u, const float* x, size_t ldx, float* h,
-                     size_t nvec);
+                     size_t nvec, const float* norm_w, size_t norm_len, float eps);
 int hc_launch_ffn(hc_engine* e, const hc_weights* g, const hc_weights* u, const hc_weights* d, const float* x,
-                  size_t ldx, float* y, size_t ldy, const float* resid, size_t ldr, float* h_ws, size_t nvec);
+                  size_t ldx, float* y, size_t ldy, const float* resid, size_t ldr, float* h_ws, size_t nvec,
+                  const float* norm_w, size_t norm_len, float eps);
 const char* hc_type_label(int t);

@@ -24,6 +24,10 @@ bool gemv_simple_supported(int type);
 cudaError_t launch_lut_matmul_q4(const uint8_t* w, int M, int N, const float* lut16, const float* x, float* y,
                                  cudaStream_t stream);
 
+// RMSNorm rows: out[v][i] = (x[v][i] * inv_v) * w[i] for i < len, 0 for len <= i < K.
+cudaError_t launch_rms_norm(const float* x, int ldx, const float* w, int len, int K, float eps, float* out, int ldo,
+                            int nvec, cudaStream_t stream);
+
 // Elementwise SwiGLU h = silu(g) * u, with an optional residual for out = resid + ...
 cudaError_t launch_swiglu(const float* g, const float* u, float* h, size_t n, cudaStream_t stream);
 

@@ -21,8 +21,9 @@ __global__ void __launch_bounds__(256) gemv_mma_kernel(GemvArgs a, int nvec) {
     uint2* lut = reinterpret_cast<uint2*>(smem + L.table_bytes + L.sx_bytes);
     float* red = reinterpret_cast<float*>(smem + L.table_bytes + L.sx_bytes + L.lut_bytes);
 
-    build_table<F, NV>(xt, a.x, a.ldx, a.K, nvec, a.err);
-    if constexpr (F::kNeedSx) build_sx<NV>(sx, a.x, a.ldx, a.K, nvec);
+    __shared__ float s_red[32];
+    const NormArgs nrm{a.norm_w, a.norm_len, a.norm_eps};
+    build_prologue<F, NV>(xt, sx, a.x, a.ldx, a.K, nvec, nrm, s_red, a.err);
     if constexpr (F::kType == T_Q4_K) build_q4k_lut(lut);
     __syncthreads();
 
@@ -32,8 +33,16 @@ __global__ void __launch_bounds__(256) gemv_mma_kernel(GemvArgs a, int nvec) {
     const int nbw = (nb + WK - 1) / WK;
     const int kb0 = min(nb, wk * nbw), kb1 = min(nb, kb0 + nbw);
     const int ntiles = (a.M + 15) / 16;
-    const int sxs = a.K / 32;
     constexpr int kMats = FUSED ? 2 : 1;
+    LaneCtx<NV> ctx;
+    ctx.xt = xt + g * 4 + t;
+    ctx.sx = sx;
+    ctx.lut = lut;
+    ctx.sxs = a.K / 32;
+    ctx.nb = nb;
+    ctx.g = g;
+    ctx.t = t;
+    ctx.has_b = g < 2 * NV;
 
     for (int tb = blockIdx.x * groups; tb < ntiles; tb += gridDim.x * groups) {
         const int tile = tb + grp;
@@ -41,12 +50,15 @@ __global__ void __launch_bounds__(256) gemv_mma_kernel(GemvArgs a, int nvec) {
 #pragma unroll
         for (int mt = 0; mt < kMats; ++mt) yA[mt] = yB[mt] = 0.f;
         if (tile < ntiles) {
-            const int rA = min(tile * 16 + g, a.M - 1), rB = min(tile * 16 + g + 8, a.M - 1);
-#pragma unroll
-            for (int mt = 0; mt < kMats; ++mt) {
-                const uint8_t* w = mt == 0 ? a.w : a.w2;
-                rows_dispatch<F, NV>(w + (size_t)rA * a.row_stride, w + (size_t)rB * a.row_stride, kb0, kb1, nb, xt,
-                                     sx, sxs, lut, g, t, yA[mt], yB[mt]);
+            const size_t rA = (size_t)min(tile * 16 + g, a.M - 1), rB = (size_t)min(tile * 16 + g + 8, a.M - 1);
+            if constexpr (FUSED) {
+                const uint8_t* const pa[2] = {a.w + rA * a.row_stride, a.w2 + rA * a.row_stride};
+                const uint8_t* const pb[2] = {a.w + rB * a.row_stride, a.w2 + rB * a.row_stride};
+                stream_tile<F, NV, 2>(pa, pb, kb0, kb1, ctx, yA, yB);
+            } else {
+                const uint8_t* const pa[1] = {a.w + rA * a.row_stride};
+                const uint8_t* const pb[1] = {a.w + rB * a.row_stride};
+                stream_tile<F, NV, 1>(pa, pb, kb0, kb1, ctx, yA, yB);
             }
         }
         if (t < NV) {

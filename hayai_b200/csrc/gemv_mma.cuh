@@ -45,6 +45,9 @@ struct GemvArgs {
     // fused SwiGLU: second matrix (up) with the same layout; y receives silu(W x) * (W2 x)
     const uint8_t* w2;
     int* err;            // device error flag (activation outside the f16 range)
+    const float* norm_w; // optional RMSNorm weight applied to x first (nullptr = none)
+    int norm_len;        // normalized length (<= K)
+    float norm_eps;
 };
 
 // ------------------------------------------------------------------ formats

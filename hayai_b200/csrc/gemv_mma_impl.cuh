@@ -1,5 +1,14 @@
 // gemv_mma_impl.cuh -- device building blocks of the tensor-core GEMV, shared by the
 // dense kernels (gemv_mma.cu) and the expert-routed kernels (moe.cu).
+//
+// Two phases per CTA:
+//  1. prologue: the activation rows (optionally RMS-normalised) are turned into the
+//     B-fragment table in shared memory.  Every thread issues all its float4 loads up
+//     front (no dependent load chain), maps each 4-element chunk to its table slot with
+//     the format's inverse index, and writes the hi and lo f16 halves.
+//  2. main loop: each warp streams the code blocks of its 16-row tile with 128-bit
+//     non-allocating loads, double-buffered (the next block's loads are in flight while
+//     the current block is dequantised into mma.m16n8k16 A fragments).
 #pragma once
 
 #include "gemv_mma.cuh"
@@ -9,56 +18,124 @@ namespace hc {
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr float kLoScale = 1.0f / 2048.0f;
 
-// ------------------------------------------------------------------ prologue
-// B-fragment table: entry e = ((block * kMmaPerBlock + mi) * 2NV + g) * 4 + t holds
-// {pack(x[e0], x[e2]), pack(x[e1], x[e3])} of vector g/2, part g&1 (hi / lo*2^11),
-// where e_j = block*kBlockElems + F::base(mi, t) + j.
-template <class F, int NV>
-__device__ void build_table(uint2* __restrict__ xt, const float* __restrict__ x, int ldx, int K, int nvec,
-                            int* err) {
-    const int nb = (K + F::kBlockElems - 1) / F::kBlockElems;
-    const int total = nb * F::kMmaPerBlock * 2 * NV * 4;
-    bool bad = false;
-    for (int e = threadIdx.x; e < total; e += blockDim.x) {
-        const int t = e & 3;
-        const int g = (e >> 2) % (2 * NV);
-        const int mall = e / (8 * NV);
-        const int kb = mall / F::kMmaPerBlock, mi = mall % F::kMmaPerBlock;
-        const int v = g >> 1, part = g & 1;
-        const int b = kb * F::kBlockElems + F::base(mi, t);
-        float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (v < nvec && b < K) xv = __ldg(reinterpret_cast<const float4*>(x + (size_t)v * ldx + b));
-        float xs[4] = {xv.x, xv.y, xv.z, xv.w};
-        __half p[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            if (fabsf(xs[j]) >= 65504.0f && isfinite(xs[j])) bad = true;
-            __half hi, lo;
-            split_f16(xs[j], hi, lo);
-            p[j] = part ? lo : hi;
-        }
-        xt[e] = make_uint2(h2_as_u32(__halves2half2(p[0], p[2])), h2_as_u32(__halves2half2(p[1], p[3])));
-    }
-    if (bad && err) atomicOr(err, 1);
+// ------------------------------------------------------------------ inverse maps
+// Element offset within a kernel block -> (mma index mi, lane-in-group t) such that
+// F::base(mi, t) == offset.  Offsets are multiples of 4.
+__device__ __forceinline__ void inv_q4k(int e, int& mi, int& t) {
+    t = e >> 6;  // 64t + 4wi + 32part
+    const int r = e & 63;
+    mi = 2 * ((r & 31) >> 2) + (r >> 5);
+}
+__device__ __forceinline__ void inv_q6k(int e, int& mi, int& t) {
+    const int h = e >> 7, r = e & 127, q = r >> 5, r2 = r & 31, lh = r2 >> 4;
+    t = (r2 & 15) >> 2;  // 128h + 32q + 16lh + 4t
+    mi = 8 * h + 4 * lh + q;
+}
+__device__ __forceinline__ void inv_q80(int e, int& mi, int& t) {
+    mi = e >> 4;  // 16mi + 4t
+    t = (e & 15) >> 2;
 }
 
-// Sub-block sums of x (for the Q4_K min term), [NV][K/32].
-template <int NV>
-__device__ void build_sx(float* __restrict__ sx, const float* __restrict__ x, int ldx, int K, int nvec) {
-    const int ns = K / 32;
-    for (int i = threadIdx.x; i < NV * ns; i += blockDim.x) {
-        const int v = i / ns, j = i % ns;
-        float s = 0.f;
-        if (v < nvec) {
-            const float4* p = reinterpret_cast<const float4*>(x + (size_t)v * ldx + 32 * j);
+template <class F>
+__device__ __forceinline__ void inv_map(int e, int& mi, int& t) {
+    if constexpr (F::kType == T_Q4_K) inv_q4k(e, mi, t);
+    else if constexpr (F::kType == T_Q6_K) inv_q6k(e, mi, t);
+    else inv_q80(e, mi, t);
+}
+
+// ------------------------------------------------------------------ prologue
+// Optional RMSNorm of the activation rows, applied while the fragment table is built:
+// xn[i] = (x[i] * inv[v]) * w[i] for i < len (rms_norm, crates/hayai-cpu/src/attention.rs:142-147).
+struct NormArgs {
+    const float* w;  // [len] norm weight, nullptr = no normalization
+    int len;         // normalized length (<= K, multiple of 4; elements beyond it are zero padding)
+    float eps;
+};
+
+__device__ __forceinline__ float block_sum(float s, float* scratch) {
+    s = warp_sum(s);
+    __syncthreads();  // scratch may still be read by a previous call
+    if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = s;
+    __syncthreads();
+    float t = 0.f;
+    const int nw = blockDim.x >> 5;
+    for (int i = 0; i < nw; ++i) t += scratch[i];
+    return t;
+}
+
+// Builds the B-fragment table (entry e = ((block * kMmaPerBlock + mi) * 2NV + g) * 4 + t holds
+// {pack(x[e0], x[e2]), pack(x[e1], x[e3])} of vector g/2, part g&1 (hi / lo*2^11), with
+// e_j = block*kBlockElems + F::base(mi, t) + j) and, for Q4_K, the 32-element sub-block sums.
+template <class F, int NV>
+__device__ void build_prologue(uint2* __restrict__ xt, float* __restrict__ sx, const float* __restrict__ x, int ldx,
+                               int K, int nvec, const NormArgs& nrm, float* scratch, int* err) {
+    const int nb = (K + F::kBlockElems - 1) / F::kBlockElems;
+    const int nchunk = K >> 2;                         // real float4 chunks
+    const int ntab = (nb * F::kBlockElems) >> 2;       // chunks covered by the table (zero padded)
+    const int rounds = (ntab + blockDim.x - 1) / blockDim.x;
+    bool bad = false;
+    for (int v = 0; v < NV; ++v) {
+        const float* xv = x + (size_t)v * ldx;
+        const bool live = v < nvec;
+        float inv = 1.0f;
+        if (nrm.w) {
+            float s = 0.f;
+            if (live) {
+                const int nc = nrm.len >> 2;
+#pragma unroll 4
+                for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+                    const float4 a = __ldg(reinterpret_cast<const float4*>(xv) + c);
+                    s += (a.x * a.x + a.y * a.y) + (a.z * a.z + a.w * a.w);
+                }
+            }
+            const float tot = block_sum(s, scratch);
+            inv = 1.0f / sqrtf(tot / (float)nrm.len + nrm.eps);
+        }
+#pragma unroll 4
+        for (int r = 0; r < rounds; ++r) {
+            const int c = threadIdx.x + r * blockDim.x;
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (live && c < nchunk) {
+                a = __ldg(reinterpret_cast<const float4*>(xv) + c);
+                if (nrm.w) {
+                    if (4 * c < nrm.len) {
+                        const float4 w = __ldg(reinterpret_cast<const float4*>(nrm.w) + c);
+                        a.x = a.x * inv * w.x;
+                        a.y = a.y * inv * w.y;
+                        a.z = a.z * inv * w.z;
+                        a.w = a.w * inv * w.w;
+                    } else {
+                        a = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+            }
+            if (c < ntab) {
+                const float xs[4] = {a.x, a.y, a.z, a.w};
+                __half hi[4], lo[4];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                float4 a = __ldg(p + q);
-                s += (a.x + a.y) + (a.z + a.w);
+                for (int j = 0; j < 4; ++j) {
+                    if (fabsf(xs[j]) >= 65504.0f && isfinite(xs[j])) bad = true;
+                    split_f16(xs[j], hi[j], lo[j]);
+                }
+                const int e = 4 * c, kb = e / F::kBlockElems;
+                int mi, t;
+                inv_map<F>(e - kb * F::kBlockElems, mi, t);
+                const int base = ((kb * F::kMmaPerBlock + mi) * 2 * NV + 2 * v) * 4 + t;
+                xt[base] = make_uint2(h2_as_u32(__halves2half2(hi[0], hi[2])), h2_as_u32(__halves2half2(hi[1], hi[3])));
+                xt[base + 4] =
+                    make_uint2(h2_as_u32(__halves2half2(lo[0], lo[2])), h2_as_u32(__halves2half2(lo[1], lo[3])));
+            }
+            if constexpr (F::kNeedSx) {
+                // 8 consecutive chunks (= consecutive lanes) form one 32-element sub-block
+                float s = (a.x + a.y) + (a.z + a.w);
+                s += __shfl_xor_sync(kFull, s, 1);
+                s += __shfl_xor_sync(kFull, s, 2);
+                s += __shfl_xor_sync(kFull, s, 4);
+                if ((threadIdx.x & 7) == 0 && c < ntab) sx[v * (ntab >> 3) + (c >> 3)] = s;
             }
         }
-        sx[i] = s;
     }
+    if (bad && err) atomicOr(err, 1);
 }
 
 // Q4_K scale LUT: [sc] -> {mul (sc,sc), add (-1024 sc)} for low nibbles (value 1024+n),
@@ -70,6 +147,18 @@ __device__ inline void build_q4k_lut(uint2* lut) {
         lut[64 + i] = make_uint2(pack_h2(sc * 0.0625f, sc * 0.0625f), pack_h2(-64.f * sc, -64.f * sc));
     }
 }
+
+// Per-lane context of the main loop.
+template <int NV>
+struct LaneCtx {
+    const uint2* xt;   // table + g*4 + t
+    const float* sx;   // Q4_K sub-block sums
+    const uint2* lut;  // Q4_K scale LUT
+    int sxs;           // Q4_K: K/32
+    int nb;            // kernel blocks per row (Q6_K/Q8_0: d plane offset)
+    int g, t;
+    bool has_b;
+};
 
 // ------------------------------------------------------------------ Q4_K
 // 6-bit (scale, min) pairs of sub-blocks 2t and 2t+1 (get_scale_min_k4, q4k.rs:34-43),
@@ -90,61 +179,64 @@ __device__ __forceinline__ void q4k_scales(const uint4& h, int t, int& sc0, int&
     }
 }
 
+struct Q4KBlk {
+    uint4 h, q0, q1;
+};
+
+__device__ __forceinline__ void q4k_load(Q4KBlk& b, const uint8_t* row, int kb, int t) {
+    const uint8_t* p = row + kb * 144;
+    b.h = ldg_stream128(p);
+    b.q0 = ldg_stream128(p + 16 + 32 * t);
+    b.q1 = ldg_stream128(p + 32 + 32 * t);
+}
+
+// Contribution of one super-block to rows g (dA) and g+8 (dB), for vector t (lanes t < NV).
 template <int NV>
-__device__ __forceinline__ void q4k_rows(const uint8_t* __restrict__ pA, const uint8_t* __restrict__ pB, int kb0,
-                                         int kb1, const uint2* __restrict__ xt, const float* __restrict__ sx, int sxs,
-                                         const uint2* __restrict__ lut, int g, int t, float& yA, float& yB) {
+__device__ __forceinline__ void q4k_block(const Q4KBlk& A, const Q4KBlk& B, int kb, const LaneCtx<NV>& c,
+                                          float& dA, float& dB) {
     constexpr int kEnt = 16 * 2 * NV * 4;
-    const bool has_b = g < 2 * NV;
-#pragma unroll 1
-    for (int kb = kb0; kb < kb1; ++kb) {
-        const uint8_t* bA = pA + kb * 144;
-        const uint8_t* bB = pB + kb * 144;
-        const uint4 hA = ldg_stream128(bA), hB = ldg_stream128(bB);
-        const uint4 qA0 = ldg_stream128(bA + 16 + 32 * t), qA1 = ldg_stream128(bA + 32 + 32 * t);
-        const uint4 qB0 = ldg_stream128(bB + 16 + 32 * t), qB1 = ldg_stream128(bB + 32 + 32 * t);
-        int scA0, mA0, scA1, mA1, scB0, mB0, scB1, mB1;
-        q4k_scales(hA, t, scA0, mA0, scA1, mA1);
-        q4k_scales(hB, t, scB0, mB0, scB1, mB1);
-        const uint2 loA = lut[scA0], hiA = lut[64 + scA1], loB = lut[scB0], hiB = lut[64 + scB1];
-        const uint2* xb = xt + kb * kEnt + g * 4 + t;
-        const uint32_t wA[8] = {qA0.x, qA0.y, qA0.z, qA0.w, qA1.x, qA1.y, qA1.z, qA1.w};
-        const uint32_t wB[8] = {qB0.x, qB0.y, qB0.z, qB0.w, qB1.x, qB1.y, qB1.z, qB1.w};
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
+    const int t = c.t;
+    int scA0, mA0, scA1, mA1, scB0, mB0, scB1, mB1;
+    q4k_scales(A.h, t, scA0, mA0, scA1, mA1);
+    q4k_scales(B.h, t, scB0, mB0, scB1, mB1);
+    const uint2 loA = c.lut[scA0], hiA = c.lut[64 + scA1], loB = c.lut[scB0], hiB = c.lut[64 + scB1];
+    const uint2* xb = c.xt + kb * kEnt;
+    const uint32_t wA[8] = {A.q0.x, A.q0.y, A.q0.z, A.q0.w, A.q1.x, A.q1.y, A.q1.z, A.q1.w};
+    const uint32_t wB[8] = {B.q0.x, B.q0.y, B.q0.z, B.q0.w, B.q1.x, B.q1.y, B.q1.z, B.q1.w};
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int wi = 0; wi < 8; ++wi) {
-            const uint32_t a = wA[wi], b = wB[wi], a8 = a >> 8, b8 = b >> 8;
-            const uint2 fl = has_b ? xb[(2 * wi) * (2 * NV * 4)] : make_uint2(0u, 0u);
-            const uint2 fh = has_b ? xb[(2 * wi + 1) * (2 * NV * 4)] : make_uint2(0u, 0u);
-            mma16816(c, hfma2_u32(lop3_and_or(a, 0x000F000Fu, 0x64006400u), loA.x, loA.y),
-                     hfma2_u32(lop3_and_or(b, 0x000F000Fu, 0x64006400u), loB.x, loB.y),
-                     hfma2_u32(lop3_and_or(a8, 0x000F000Fu, 0x64006400u), loA.x, loA.y),
-                     hfma2_u32(lop3_and_or(b8, 0x000F000Fu, 0x64006400u), loB.x, loB.y), fl.x, fl.y);
-            mma16816(c, hfma2_u32(lop3_and_or(a, 0x00F000F0u, 0x64006400u), hiA.x, hiA.y),
-                     hfma2_u32(lop3_and_or(b, 0x00F000F0u, 0x64006400u), hiB.x, hiB.y),
-                     hfma2_u32(lop3_and_or(a8, 0x00F000F0u, 0x64006400u), hiA.x, hiA.y),
-                     hfma2_u32(lop3_and_or(b8, 0x00F000F0u, 0x64006400u), hiB.x, hiB.y), fh.x, fh.y);
-        }
-        const float2 ddA = __half22float2(u32_as_h2(hA.x));
-        const float2 ddB = __half22float2(u32_as_h2(hB.x));
-        float mpA = 0.f, mpB = 0.f;
-#pragma unroll
-        for (int v = 0; v < NV; ++v) {
-            const float s0 = sx[v * sxs + kb * 8 + 2 * t], s1 = sx[v * sxs + kb * 8 + 2 * t + 1];
-            float pa = (float)mA0 * s0 + (float)mA1 * s1;
-            float pb = (float)mB0 * s0 + (float)mB1 * s1;
-            pa += __shfl_xor_sync(kFull, pa, 1);
-            pb += __shfl_xor_sync(kFull, pb, 1);
-            pa += __shfl_xor_sync(kFull, pa, 2);
-            pb += __shfl_xor_sync(kFull, pb, 2);
-            if (t == v) {
-                mpA = pa;
-                mpB = pb;
-            }
-        }
-        yA += ddA.x * (c[0] + c[1] * kLoScale) - ddA.y * mpA;
-        yB += ddB.x * (c[2] + c[3] * kLoScale) - ddB.y * mpB;
+    for (int wi = 0; wi < 8; ++wi) {
+        const uint32_t a = wA[wi], b = wB[wi], a8 = a >> 8, b8 = b >> 8;
+        const uint2 fl = c.has_b ? xb[(2 * wi) * (2 * NV * 4)] : make_uint2(0u, 0u);
+        const uint2 fh = c.has_b ? xb[(2 * wi + 1) * (2 * NV * 4)] : make_uint2(0u, 0u);
+        mma16816(acc, hfma2_u32(lop3_and_or(a, 0x000F000Fu, 0x64006400u), loA.x, loA.y),
+                 hfma2_u32(lop3_and_or(b, 0x000F000Fu, 0x64006400u), loB.x, loB.y),
+                 hfma2_u32(lop3_and_or(a8, 0x000F000Fu, 0x64006400u), loA.x, loA.y),
+                 hfma2_u32(lop3_and_or(b8, 0x000F000Fu, 0x64006400u), loB.x, loB.y), fl.x, fl.y);
+        mma16816(acc, hfma2_u32(lop3_and_or(a, 0x00F000F0u, 0x64006400u), hiA.x, hiA.y),
+                 hfma2_u32(lop3_and_or(b, 0x00F000F0u, 0x64006400u), hiB.x, hiB.y),
+                 hfma2_u32(lop3_and_or(a8, 0x00F000F0u, 0x64006400u), hiA.x, hiA.y),
+                 hfma2_u32(lop3_and_or(b8, 0x00F000F0u, 0x64006400u), hiB.x, hiB.y), fh.x, fh.y);
     }
+    const float2 ddA = __half22float2(u32_as_h2(A.h.x));
+    const float2 ddB = __half22float2(u32_as_h2(B.h.x));
+    float mpA = 0.f, mpB = 0.f;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+        const float s0 = c.sx[v * c.sxs + kb * 8 + 2 * t], s1 = c.sx[v * c.sxs + kb * 8 + 2 * t + 1];
+        float pa = (float)mA0 * s0 + (float)mA1 * s1;
+        float pb = (float)mB0 * s0 + (float)mB1 * s1;
+        pa += __shfl_xor_sync(kFull, pa, 1);
+        pb += __shfl_xor_sync(kFull, pb, 1);
+        pa += __shfl_xor_sync(kFull, pa, 2);
+        pb += __shfl_xor_sync(kFull, pb, 2);
+        if (t == v) {
+            mpA = pa;
+            mpB = pb;
+        }
+    }
+    dA = ddA.x * (acc[0] + acc[1] * kLoScale) - ddA.y * mpA;
+    dB = ddB.x * (acc[2] + acc[3] * kLoScale) - ddB.y * mpB;
 }
 
 // ------------------------------------------------------------------ Q6_K (GPU layout)
@@ -153,124 +245,184 @@ __device__ __forceinline__ void q4k_rows(const uint8_t* __restrict__ pA, const u
 // holds original ql bytes 64h + 32qq + 16lh + 4t..+3; qh word wh = 2h + lh holds
 // qh bytes 32h + 16lh + 4t..+3 (q6k.rs:26-57 layout).
 __device__ __forceinline__ float i8_to_f32(uint32_t word, int byte) {
-    const uint32_t sel = 0x8880u | (uint32_t)byte | ((0x8u | (uint32_t)byte) << 4) | ((0x8u | (uint32_t)byte) << 8) |
-                         ((0x8u | (uint32_t)byte) << 12);
-    const int s = (int)prmt(word, 0u, sel & 0xFFFFu);
-    return (float)s;
+    const uint32_t b = (uint32_t)byte;
+    const uint32_t sel = b | ((0x8u | b) << 4) | ((0x8u | b) << 8) | ((0x8u | b) << 12);
+    return (float)(int)prmt(word, 0u, sel);
+}
+
+struct Q6KBlk {
+    uint4 l0, l1, qh, sc;
+    uint16_t d;
+};
+
+__device__ __forceinline__ void q6k_load(Q6KBlk& b, const uint8_t* row, int kb, int t, int nb) {
+    const uint8_t* p = row + kb * 208;
+    b.l0 = ldg_stream128(p + 32 * t);
+    b.l1 = ldg_stream128(p + 32 * t + 16);
+    b.qh = ldg_stream128(p + 128 + 16 * t);
+    b.sc = ldg_stream128(p + 192);
+    b.d = ldg_u16(row + (size_t)nb * 208 + 2 * kb);
 }
 
 template <int NV>
-__device__ __forceinline__ void q6k_rows(const uint8_t* __restrict__ pA, const uint8_t* __restrict__ pB, int kb0,
-                                         int kb1, int nb, const uint2* __restrict__ xt, int g, int t, float& yA,
-                                         float& yB) {
+__device__ __forceinline__ void q6k_block(const Q6KBlk& A, const Q6KBlk& B, int kb, const LaneCtx<NV>& c,
+                                          float& dA, float& dB) {
     constexpr int kEnt = 16 * 2 * NV * 4;
-    const bool has_b = g < 2 * NV;
-    const uint8_t* dpA = pA + (size_t)nb * 208;
-    const uint8_t* dpB = pB + (size_t)nb * 208;
     const uint32_t kOff = 0x64206420u;  // (1056, 1056) in f16: 1024 magic + 32 code offset
-#pragma unroll 1
-    for (int kb = kb0; kb < kb1; ++kb) {
-        const uint8_t* bA = pA + kb * 208;
-        const uint8_t* bB = pB + kb * 208;
-        const uint4 lA0 = ldg_stream128(bA + 32 * t), lA1 = ldg_stream128(bA + 32 * t + 16);
-        const uint4 lB0 = ldg_stream128(bB + 32 * t), lB1 = ldg_stream128(bB + 32 * t + 16);
-        const uint4 hA = ldg_stream128(bA + 128 + 16 * t), hB = ldg_stream128(bB + 128 + 16 * t);
-        const uint4 sA = ldg_stream128(bA + 192), sB = ldg_stream128(bB + 192);
-        const float dA = h2f(ldg_u16(dpA + 2 * kb)), dB = h2f(ldg_u16(dpB + 2 * kb));
-        const uint32_t LA[8] = {lA0.x, lA0.y, lA0.z, lA0.w, lA1.x, lA1.y, lA1.z, lA1.w};
-        const uint32_t LB[8] = {lB0.x, lB0.y, lB0.z, lB0.w, lB1.x, lB1.y, lB1.z, lB1.w};
-        const uint32_t QHA[4] = {hA.x, hA.y, hA.z, hA.w};
-        const uint32_t QHB[4] = {hB.x, hB.y, hB.z, hB.w};
-        const uint32_t SA[4] = {sA.x, sA.y, sA.z, sA.w};
-        const uint32_t SB[4] = {sB.x, sB.y, sB.z, sB.w};
-        const uint2* xb = xt + kb * kEnt + g * 4 + t;
+    const float fdA = h2f(A.d), fdB = h2f(B.d);
+    const uint32_t LA[8] = {A.l0.x, A.l0.y, A.l0.z, A.l0.w, A.l1.x, A.l1.y, A.l1.z, A.l1.w};
+    const uint32_t LB[8] = {B.l0.x, B.l0.y, B.l0.z, B.l0.w, B.l1.x, B.l1.y, B.l1.z, B.l1.w};
+    const uint32_t QHA[4] = {A.qh.x, A.qh.y, A.qh.z, A.qh.w};
+    const uint32_t QHB[4] = {B.qh.x, B.qh.y, B.qh.z, B.qh.w};
+    const uint32_t SA[4] = {A.sc.x, A.sc.y, A.sc.z, A.sc.w};
+    const uint32_t SB[4] = {B.sc.x, B.sc.y, B.sc.z, B.sc.w};
+    const uint2* xb = c.xt + kb * kEnt;
+    float sumA = 0.f, sumB = 0.f;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < 2; ++h) {
 #pragma unroll
-            for (int lh = 0; lh < 2; ++lh) {
-                const uint32_t QA = QHA[2 * h + lh], QB = QHB[2 * h + lh];
-                const uint32_t qa[4] = {(QA << 4) & 0x30303030u, (QA << 2) & 0x30303030u, QA & 0x30303030u,
-                                        (QA >> 2) & 0x30303030u};
-                const uint32_t qb[4] = {(QB << 4) & 0x30303030u, (QB << 2) & 0x30303030u, QB & 0x30303030u,
-                                        (QB >> 2) & 0x30303030u};
+        for (int lh = 0; lh < 2; ++lh) {
+            const uint32_t QA = QHA[2 * h + lh], QB = QHB[2 * h + lh];
+            const uint32_t qa[4] = {(QA << 4) & 0x30303030u, (QA << 2) & 0x30303030u, QA & 0x30303030u,
+                                    (QA >> 2) & 0x30303030u};
+            const uint32_t qb[4] = {(QB << 4) & 0x30303030u, (QB << 2) & 0x30303030u, QB & 0x30303030u,
+                                    (QB >> 2) & 0x30303030u};
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int qq = q & 1;
-                    const uint32_t la = LA[4 * h + 2 * qq + lh], lb = LB[4 * h + 2 * qq + lh];
-                    const uint32_t ua = lop3_and_or(q < 2 ? la : (la >> 4), 0x0F0F0F0Fu, qa[q]);
-                    const uint32_t ub = lop3_and_or(q < 2 ? lb : (lb >> 4), 0x0F0F0F0Fu, qb[q]);
-                    const int m = 8 * h + 4 * lh + q;
-                    const uint2 f = has_b ? xb[m * (2 * NV * 4)] : make_uint2(0u, 0u);
-                    float c[4] = {0.f, 0.f, 0.f, 0.f};
-                    mma16816(c, hsub2_u32(prmt(ua, 0x64646464u, 0x4240u), kOff),
-                             hsub2_u32(prmt(ub, 0x64646464u, 0x4240u), kOff),
-                             hsub2_u32(prmt(ua, 0x64646464u, 0x4341u), kOff),
-                             hsub2_u32(prmt(ub, 0x64646464u, 0x4341u), kOff), f.x, f.y);
-                    const int si = 8 * h + 2 * q + lh;  // scale index = element / 16
-                    const float sa = dA * i8_to_f32(SA[si >> 2], si & 3);
-                    const float sb = dB * i8_to_f32(SB[si >> 2], si & 3);
-                    yA += sa * (c[0] + c[1] * kLoScale);
-                    yB += sb * (c[2] + c[3] * kLoScale);
-                }
+            for (int q = 0; q < 4; ++q) {
+                const int qq = q & 1;
+                const uint32_t la = LA[4 * h + 2 * qq + lh], lb = LB[4 * h + 2 * qq + lh];
+                const uint32_t ua = lop3_and_or(q < 2 ? la : (la >> 4), 0x0F0F0F0Fu, qa[q]);
+                const uint32_t ub = lop3_and_or(q < 2 ? lb : (lb >> 4), 0x0F0F0F0Fu, qb[q]);
+                const int m = 8 * h + 4 * lh + q;
+                const uint2 f = c.has_b ? xb[m * (2 * NV * 4)] : make_uint2(0u, 0u);
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16816(acc, hsub2_u32(prmt(ua, 0x64646464u, 0x4240u), kOff),
+                         hsub2_u32(prmt(ub, 0x64646464u, 0x4240u), kOff),
+                         hsub2_u32(prmt(ua, 0x64646464u, 0x4341u), kOff),
+                         hsub2_u32(prmt(ub, 0x64646464u, 0x4341u), kOff), f.x, f.y);
+                const int si = 8 * h + 2 * q + lh;  // scale index = element / 16
+                sumA += i8_to_f32(SA[si >> 2], si & 3) * (acc[0] + acc[1] * kLoScale);
+                sumB += i8_to_f32(SB[si >> 2], si & 3) * (acc[2] + acc[3] * kLoScale);
             }
         }
     }
+    dA = fdA * sumA;
+    dB = fdB * sumB;
 }
 
 // ------------------------------------------------------------------ Q8_0 (GPU layout)
 // Row: ng groups of 128 B {qs_perm[4 lanes][8 words]} (group = 4 Q8_0 blocks = 128
 // elements), then the f16 d plane (4 entries per group, padded to 16 B).  Word w of
 // lane t holds codes 16*(w&1) + 4t..+3 of block w/2 of the group.
+struct Q80Blk {
+    uint4 q0, q1;
+    uint2 d;
+};
+
+__device__ __forceinline__ void q80_load(Q80Blk& b, const uint8_t* row, int kg, int t, int ng) {
+    b.q0 = ldg_stream128(row + kg * 128 + 32 * t);
+    b.q1 = ldg_stream128(row + kg * 128 + 32 * t + 16);
+    b.d = ldg_u2(row + (size_t)ng * 128 + kg * 8);
+}
+
 template <int NV>
-__device__ __forceinline__ void q80_rows(const uint8_t* __restrict__ pA, const uint8_t* __restrict__ pB, int kb0,
-                                         int kb1, int ng, const uint2* __restrict__ xt, int g, int t, float& yA,
-                                         float& yB) {
+__device__ __forceinline__ void q80_block(const Q80Blk& A, const Q80Blk& B, int kg, const LaneCtx<NV>& c, float& dA,
+                                          float& dB) {
     constexpr int kEnt = 8 * 2 * NV * 4;
-    const bool has_b = g < 2 * NV;
-    const uint8_t* dpA = pA + (size_t)ng * 128;
-    const uint8_t* dpB = pB + (size_t)ng * 128;
     const uint32_t kOff = 0x64806480u;  // (1152, 1152): 1024 magic + 128 sign flip
-#pragma unroll 1
-    for (int kg = kb0; kg < kb1; ++kg) {
-        const uint4 qA0 = ldg_stream128(pA + kg * 128 + 32 * t), qA1 = ldg_stream128(pA + kg * 128 + 32 * t + 16);
-        const uint4 qB0 = ldg_stream128(pB + kg * 128 + 32 * t), qB1 = ldg_stream128(pB + kg * 128 + 32 * t + 16);
-        const uint2 dwA = ldg_u2(dpA + kg * 8), dwB = ldg_u2(dpB + kg * 8);
-        const uint32_t WA[8] = {qA0.x, qA0.y, qA0.z, qA0.w, qA1.x, qA1.y, qA1.z, qA1.w};
-        const uint32_t WB[8] = {qB0.x, qB0.y, qB0.z, qB0.w, qB1.x, qB1.y, qB1.z, qB1.w};
-        const float2 dA01 = __half22float2(u32_as_h2(dwA.x)), dA23 = __half22float2(u32_as_h2(dwA.y));
-        const float2 dB01 = __half22float2(u32_as_h2(dwB.x)), dB23 = __half22float2(u32_as_h2(dwB.y));
-        const float dA[4] = {dA01.x, dA01.y, dA23.x, dA23.y};
-        const float dB[4] = {dB01.x, dB01.y, dB23.x, dB23.y};
-        const uint2* xb = xt + kg * kEnt + g * 4 + t;
+    const uint32_t WA[8] = {A.q0.x, A.q0.y, A.q0.z, A.q0.w, A.q1.x, A.q1.y, A.q1.z, A.q1.w};
+    const uint32_t WB[8] = {B.q0.x, B.q0.y, B.q0.z, B.q0.w, B.q1.x, B.q1.y, B.q1.z, B.q1.w};
+    const float2 dA01 = __half22float2(u32_as_h2(A.d.x)), dA23 = __half22float2(u32_as_h2(A.d.y));
+    const float2 dB01 = __half22float2(u32_as_h2(B.d.x)), dB23 = __half22float2(u32_as_h2(B.d.y));
+    const float fa[4] = {dA01.x, dA01.y, dA23.x, dA23.y};
+    const float fb[4] = {dB01.x, dB01.y, dB23.x, dB23.y};
+    const uint2* xb = c.xt + kg * kEnt;
+    float sA = 0.f, sB = 0.f;
 #pragma unroll
-        for (int blk = 0; blk < 4; ++blk) {
-            float c[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int blk = 0; blk < 4; ++blk) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const int w = 2 * blk + half;
-                const uint32_t ua = WA[w] ^ 0x80808080u, ub = WB[w] ^ 0x80808080u;
-                const uint2 f = has_b ? xb[w * (2 * NV * 4)] : make_uint2(0u, 0u);
-                mma16816(c, hsub2_u32(prmt(ua, 0x64646464u, 0x4240u), kOff),
-                         hsub2_u32(prmt(ub, 0x64646464u, 0x4240u), kOff),
-                         hsub2_u32(prmt(ua, 0x64646464u, 0x4341u), kOff),
-                         hsub2_u32(prmt(ub, 0x64646464u, 0x4341u), kOff), f.x, f.y);
-            }
-            yA += dA[blk] * (c[0] + c[1] * kLoScale);
-            yB += dB[blk] * (c[2] + c[3] * kLoScale);
+        for (int half = 0; half < 2; ++half) {
+            const int w = 2 * blk + half;
+            const uint32_t ua = WA[w] ^ 0x80808080u, ub = WB[w] ^ 0x80808080u;
+            const uint2 f = c.has_b ? xb[w * (2 * NV * 4)] : make_uint2(0u, 0u);
+            mma16816(acc, hsub2_u32(prmt(ua, 0x64646464u, 0x4240u), kOff),
+                     hsub2_u32(prmt(ub, 0x64646464u, 0x4240u), kOff),
+                     hsub2_u32(prmt(ua, 0x64646464u, 0x4341u), kOff),
+                     hsub2_u32(prmt(ub, 0x64646464u, 0x4341u), kOff), f.x, f.y);
         }
+        sA += fa[blk] * (acc[0] + acc[1] * kLoScale);
+        sB += fb[blk] * (acc[2] + acc[3] * kLoScale);
     }
+    dA = sA;
+    dB = sB;
+}
+
+// ------------------------------------------------------------------ tile streaming
+template <class F>
+struct BlkOf;
+template <>
+struct BlkOf<FmtQ4K> {
+    using T = Q4KBlk;
+};
+template <>
+struct BlkOf<FmtQ6K> {
+    using T = Q6KBlk;
+};
+template <>
+struct BlkOf<FmtQ80> {
+    using T = Q80Blk;
+};
+
+template <class F>
+__device__ __forceinline__ void blk_load(typename BlkOf<F>::T& b, const uint8_t* row, int kb, int t, int nb) {
+    if constexpr (F::kType == T_Q4_K) q4k_load(b, row, kb, t);
+    else if constexpr (F::kType == T_Q6_K) q6k_load(b, row, kb, t, nb);
+    else q80_load(b, row, kb, t, nb);
 }
 
 template <class F, int NV>
-__device__ __forceinline__ void rows_dispatch(const uint8_t* pA, const uint8_t* pB, int kb0, int kb1, int nb,
-                                              const uint2* xt, const float* sx, int sxs, const uint2* lut, int g,
-                                              int t, float& yA, float& yB) {
-    if constexpr (F::kType == T_Q4_K) {
-        q4k_rows<NV>(pA, pB, kb0, kb1, xt, sx, sxs, lut, g, t, yA, yB);
-    } else if constexpr (F::kType == T_Q6_K) {
-        q6k_rows<NV>(pA, pB, kb0, kb1, nb, xt, g, t, yA, yB);
-    } else {
-        q80_rows<NV>(pA, pB, kb0, kb1, nb, xt, g, t, yA, yB);
+__device__ __forceinline__ void blk_compute(const typename BlkOf<F>::T& A, const typename BlkOf<F>::T& B, int kb,
+                                            const LaneCtx<NV>& c, float& dA, float& dB) {
+    if constexpr (F::kType == T_Q4_K) q4k_block<NV>(A, B, kb, c, dA, dB);
+    else if constexpr (F::kType == T_Q6_K) q6k_block<NV>(A, B, kb, c, dA, dB);
+    else q80_block<NV>(A, B, kb, c, dA, dB);
+}
+
+// Streams blocks [kb0, kb1) of NMAT matrices (rows rA/rB of each) through the tensor cores,
+// one block ahead: yA[m] / yB[m] accumulate the outputs of rows g / g+8 for vector t.
+template <class F, int NV, int NMAT>
+__device__ __forceinline__ void stream_tile(const uint8_t* const (&rowA)[NMAT], const uint8_t* const (&rowB)[NMAT],
+                                            int kb0, int kb1, const LaneCtx<NV>& c, float (&yA)[NMAT],
+                                            float (&yB)[NMAT]) {
+    using B = typename BlkOf<F>::T;
+    const int nk = kb1 - kb0;
+    const int total = NMAT * nk;
+    if (total <= 0) return;
+    B curA, curB, nxtA, nxtB;
+    blk_load<F>(curA, rowA[0], kb0, c.t, c.nb);
+    blk_load<F>(curB, rowB[0], kb0, c.t, c.nb);
+#pragma unroll 1
+    for (int i = 0; i < total; ++i) {
+        const int m = NMAT == 1 ? 0 : i / nk;
+        const int kb = kb0 + (i - m * nk);
+        if (i + 1 < total) {
+            const int m1 = NMAT == 1 ? 0 : (i + 1) / nk;
+            const int kbn = kb0 + (i + 1 - m1 * nk);
+            blk_load<F>(nxtA, rowA[m1], kbn, c.t, c.nb);
+            blk_load<F>(nxtB, rowB[m1], kbn, c.t, c.nb);
+        }
+        float dA, dB;
+        blk_compute<F, NV>(curA, curB, kb, c, dA, dB);
+        if (NMAT == 1 || m == 0) {
+            yA[0] += dA;
+            yB[0] += dB;
+        } else {
+            yA[NMAT - 1] += dA;
+            yB[NMAT - 1] += dB;
+        }
+        curA = nxtA;
+        curB = nxtB;
     }
 }
 

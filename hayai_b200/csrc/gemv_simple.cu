@@ -212,6 +212,32 @@ cudaError_t launch_lut_matmul_q4(const uint8_t* w, int M, int N, const float* lu
     return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------ RMSNorm rows
+// out[v][i] = (x[v][i] * inv_v) * w[i] for i < len, zero padding up to K
+// (rms_norm, crates/hayai-cpu/src/attention.rs:142-147; one CTA per row).
+__global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__ x, int ldx,
+                                                       const float* __restrict__ w, int len, int K, float eps,
+                                                       float* __restrict__ out, int ldo) {
+    __shared__ float red[8];
+    const float* xr = x + (size_t)blockIdx.x * ldx;
+    float s = 0.f;
+    for (int i = threadIdx.x; i < len; i += blockDim.x) s += xr[i] * xr[i];
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+    const float inv = 1.0f / sqrtf(t / (float)len + eps);
+    float* o = out + (size_t)blockIdx.x * ldo;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) o[i] = i < len ? xr[i] * inv * w[i] : 0.f;
+}
+
+cudaError_t launch_rms_norm(const float* x, int ldx, const float* w, int len, int K, float eps, float* out, int ldo,
+                            int nvec, cudaStream_t stream) {
+    rms_norm_kernel<<<nvec, 256, 0, stream>>>(x, ldx, w, len, K, eps, out, ldo);
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ SwiGLU combine
 __global__ void swiglu_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ h,
                               size_t n) {

@@ -202,8 +202,9 @@ __global__ void __launch_bounds__(256) moe_gemv_kernel(MoeStage s) {
     const int p = blockIdx.x / s.items_per_pair, j = blockIdx.x % s.items_per_pair;
     const int e = s.ids[p];
     const float* x = s.x + (size_t)(p / s.x_div) * s.ldx;
-    build_table<F, 1>(xt, x, s.ldx, s.K, 1, s.err);
-    if constexpr (F::kNeedSx) build_sx<1>(sx, x, s.ldx, s.K, 1);
+    __shared__ float s_red[32];
+    const NormArgs nrm{nullptr, 0, 0.f};
+    build_prologue<F, 1>(xt, sx, x, s.ldx, s.K, 1, nrm, s_red, s.err);
     if constexpr (F::kType == T_Q4_K) build_q4k_lut(lut);
     __syncthreads();
     if (e < 0) return;  // no expert (cannot happen for validated routing)
@@ -219,18 +220,30 @@ __global__ void __launch_bounds__(256) moe_gemv_kernel(MoeStage s) {
     const uint8_t* W2 = FUSED ? s.w2[e] : nullptr;
     float* y = s.y + (size_t)p * s.ldy;
     constexpr int kMats = FUSED ? 2 : 1;
+    LaneCtx<1> ctx;
+    ctx.xt = xt + g * 4 + t;
+    ctx.sx = sx;
+    ctx.lut = lut;
+    ctx.sxs = s.K / 32;
+    ctx.nb = nb;
+    ctx.g = g;
+    ctx.t = t;
+    ctx.has_b = g < 2;
     for (int tb = 0; tb < ntiles; tb += groups) {
         const int tile = tb + grp;
         float yA[kMats], yB[kMats];
 #pragma unroll
         for (int mt = 0; mt < kMats; ++mt) yA[mt] = yB[mt] = 0.f;
         if (tile < ntiles) {
-            const int rA = min(r0 + tile * 16 + g, r1 - 1), rB = min(r0 + tile * 16 + g + 8, r1 - 1);
-#pragma unroll
-            for (int mt = 0; mt < kMats; ++mt) {
-                const uint8_t* w = mt == 0 ? W : W2;
-                rows_dispatch<F, 1>(w + (size_t)rA * s.row_stride, w + (size_t)rB * s.row_stride, kb0, kb1, nb, xt,
-                                    sx, s.K / 32, lut, g, t, yA[mt], yB[mt]);
+            const size_t rA = (size_t)min(r0 + tile * 16 + g, r1 - 1), rB = (size_t)min(r0 + tile * 16 + g + 8, r1 - 1);
+            if constexpr (FUSED) {
+                const uint8_t* const pa[2] = {W + rA * s.row_stride, W2 + rA * s.row_stride};
+                const uint8_t* const pb[2] = {W + rB * s.row_stride, W2 + rB * s.row_stride};
+                stream_tile<F, 1, 2>(pa, pb, kb0, kb1, ctx, yA, yB);
+            } else {
+                const uint8_t* const pa[1] = {W + rA * s.row_stride};
+                const uint8_t* const pb[1] = {W + rB * s.row_stride};
+                stream_tile<F, 1, 1>(pa, pb, kb0, kb1, ctx, yA, yB);
             }
         }
         if (t == 0) {

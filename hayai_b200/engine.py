@@ -134,6 +134,13 @@ def _handles(ws: Sequence[ResidentWeights]):
     return arr
 
 
+def _norm_ptrs(norms):
+    """Array of device pointers of per-layer RMSNorm weights (torch CUDA tensors), or NULL."""
+    if norms is None:
+        return None
+    return (ctypes.c_void_p * len(norms))(*[_tptr(t) for t in norms])
+
+
 class CudaEngine:
     """One GPU + stream (OpenClEngine, crates/hayai-opencl/src/context.rs:23)."""
 
@@ -156,13 +163,12 @@ class CudaEngine:
 
     # ---------------------------------------------------------------- streams
     def set_stream(self, stream) -> None:
-        """Enqueue on a caller stream (a torch.cuda.Stream, a raw handle, or None for the engine's own)."""
+        """Enqueue on a caller stream (a torch.cuda.Stream or a raw cudaStream_t handle; handle 0 is the
+        legacy default stream), or on the engine's own stream when ``stream`` is None."""
         if stream is None:
-            ptr = 0
-        elif isinstance(stream, int):
-            ptr = stream
-        else:
-            ptr = stream.cuda_stream
+            _check(lib().hc_engine_use_own_stream(self.handle))
+            return
+        ptr = stream if isinstance(stream, int) else stream.cuda_stream
         _check(lib().hc_engine_set_stream(self.handle, ctypes.c_void_p(ptr)))
 
     def stream_handle(self) -> int:
@@ -272,11 +278,13 @@ class CudaEngine:
                                    y.ctypes.data, nvec))
         return y
 
-    def ffn_stack(self, gates, ups, downs, x, nvec: int = 1) -> np.ndarray:
+    def ffn_stack(self, gates, ups, downs, x, nvec: int = 1, norms=None, eps: float = 1e-5) -> np.ndarray:
+        """x <- x + FFN_l(rms_norm(x, norms[l])) for every layer (host buffers in and out).
+        ``norms`` is a list of float32 CUDA tensors (or None for no normalization)."""
         xv = _f32(x)
         out = np.empty_like(xv)
-        _check(lib().hc_ffn_stack(self.handle, _handles(gates), _handles(ups), _handles(downs), len(gates),
-                                  xv.ctypes.data, out.ctypes.data, nvec))
+        _check(lib().hc_ffn_stack(self.handle, _handles(gates), _handles(ups), _handles(downs), _norm_ptrs(norms),
+                                  eps, len(gates), xv.ctypes.data, out.ctypes.data, nvec))
         return out
 
     # ---------------------------------------------------------------- device tensors
@@ -296,13 +304,14 @@ class CudaEngine:
                                        ctypes.c_void_p(_tptr(y)), ctypes.c_void_p(_tptr(resid)),
                                        ctypes.c_void_p(_tptr(h_ws)), nvec))
 
-    def ffn_gateup_dev(self, gate, up, x, h, nvec: int = 1) -> None:
+    def ffn_gateup_dev(self, gate, up, x, h, nvec: int = 1, norm=None, norm_len: int = 0, eps: float = 1e-5) -> None:
         _check(lib().hc_ffn_gateup_dev(self.handle, gate.handle, up.handle, ctypes.c_void_p(_tptr(x)),
-                                       ctypes.c_void_p(_tptr(h)), nvec))
+                                       ctypes.c_void_p(_tptr(h)), nvec, ctypes.c_void_p(_tptr(norm)),
+                                       norm_len if norm is not None else 0, eps))
 
-    def ffn_stack_dev(self, gates, ups, downs, x, nvec: int = 1) -> None:
-        _check(lib().hc_ffn_stack_dev(self.handle, _handles(gates), _handles(ups), _handles(downs), len(gates),
-                                      ctypes.c_void_p(_tptr(x)), nvec))
+    def ffn_stack_dev(self, gates, ups, downs, x, nvec: int = 1, norms=None, eps: float = 1e-5) -> None:
+        _check(lib().hc_ffn_stack_dev(self.handle, _handles(gates), _handles(ups), _handles(downs), _norm_ptrs(norms),
+                                      eps, len(gates), ctypes.c_void_p(_tptr(x)), nvec))
 
     def synth_normal_dev(self, seed: int, out, mean: float = 0.0, std: float = 1.0) -> None:
         """Fill a float32 CUDA tensor with seeded N(mean, std^2) values."""

@@ -58,8 +58,10 @@ int hc_device_count(int* out);
 int hc_engine_init(int device, hc_engine** out);
 int hc_engine_free(hc_engine* eng);
 
-/* Use the caller's CUDA stream (cudaStream_t as void*) instead of the engine's own. */
+/* Enqueue on the caller's CUDA stream (cudaStream_t as void*; NULL = the legacy default
+ * stream), or go back to the engine's own non-blocking stream. */
 int hc_engine_set_stream(hc_engine* eng, void* stream);
+int hc_engine_use_own_stream(hc_engine* eng);
 int hc_engine_get_stream(hc_engine* eng, void** stream);
 
 /* Wait for all work on the engine stream and report any device-side error. */
@@ -134,21 +136,28 @@ int hc_ffn_swiglu(hc_engine* eng, const hc_weights* gate, const hc_weights* up, 
 int hc_ffn_swiglu_dev(hc_engine* eng, const hc_weights* gate, const hc_weights* up, const hc_weights* down,
                       const float* x, float* y, const float* resid, float* h_ws, size_t nvec);
 
-/* The fused first half of the block alone: h[v] = silu(W_gate x[v]) * (W_up x[v]), one
+/* The fused first half of the block alone: h[v] = silu(W_gate xn[v]) * (W_up xn[v]), one
  * kernel reading both matrices (ffn_begin_gate_up_scratch + the SiLU*up combine,
- * stream_infer.rs:3752-3840).  h is [nvec][d_ff]. */
+ * stream_infer.rs:3752-3840).  xn = rms_norm(x, norm_w, eps) over the first norm_len
+ * entries of each row (crates/hayai-cpu/src/attention.rs:142-147) when norm_w (device,
+ * norm_len floats) is non-NULL, else x.  h is [nvec][d_ff]. */
 int hc_ffn_gateup_dev(hc_engine* eng, const hc_weights* gate, const hc_weights* up, const float* x, float* h,
-                      size_t nvec);
+                      size_t nvec, const float* norm_w, size_t norm_len, float eps);
 
-/* Stack of n_layers FFN blocks with residual: x <- x + FFN_l(x) for l = 0..n_layers-1
- * (the decode-step loop of stream_infer.rs:2166 and :3752-3864, FFN only).  x is
- * [nvec][k_in] with k_in >= n_out (rows are zero-padded for K-quant block alignment;
- * the residual is added to the first n_out entries).  _dev works in place on device
- * memory; the host version copies x in and the result out (timed end to end). */
+/* Stack of n_layers FFN sublayers with pre-norm and residual, as in a decode step
+ * (stream_infer.rs:2166-2170 rms_norm(x, ffn_norm) then :3752-3864):
+ *     x <- x + FFN_l(rms_norm(x, norm_w[l], eps))        for l = 0..n_layers-1
+ * norm_w is an array of n_layers device pointers (n_out floats each), or NULL for no
+ * normalization.  x is [nvec][k_in] with k_in >= n_out (rows zero-padded for K-quant
+ * block alignment; norm and residual cover the first n_out entries).  _dev works in place
+ * on device memory (captured once into a CUDA graph and replayed); the host version
+ * copies x in and the result out. */
 int hc_ffn_stack_dev(hc_engine* eng, const hc_weights* const* gate, const hc_weights* const* up,
-                     const hc_weights* const* down, size_t n_layers, float* x, size_t nvec);
+                     const hc_weights* const* down, const float* const* norm_w, float eps, size_t n_layers,
+                     float* x, size_t nvec);
 int hc_ffn_stack(hc_engine* eng, const hc_weights* const* gate, const hc_weights* const* up,
-                 const hc_weights* const* down, size_t n_layers, const float* x_in, float* x_out, size_t nvec);
+                 const hc_weights* const* down, const float* const* norm_w, float eps, size_t n_layers,
+                 const float* x_in, float* x_out, size_t nvec);
 
 /* ---- MoE ---------------------------------------------------------------------------
  * Routing of route_experts (crates/hayai-core/src/moe_infer.rs:868-935, with

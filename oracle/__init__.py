@@ -76,6 +76,8 @@ def _declare(L: ctypes.CDLL) -> None:
     L.or_moe_ffn.argtypes = [_P, _P, _S, _S, ctypes.c_int, ctypes.c_float,
                              ctypes.c_int, _P, _S, ctypes.c_int, _P, _S, ctypes.c_int, _P, _S,
                              _S, _S, _S, _P, _P, _P, _P]
+    L.or_rms_norm.restype = None
+    L.or_rms_norm.argtypes = [_P, _P, _S, ctypes.c_float, _P]
     L.or_set_threads.restype = None
     L.or_set_threads.argtypes = [ctypes.c_int]
     L.or_get_threads.restype = ctypes.c_int
@@ -178,6 +180,16 @@ def swiglu(g: np.ndarray, u: np.ndarray) -> np.ndarray:
     h = np.empty_like(g)
     lib().or_swiglu(_ptr(g), _ptr(u), _ptr(h), g.size)
     return h
+
+
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """rms_norm (crates/hayai-cpu/src/attention.rs:142-147), out of place."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    assert x.size == w.size
+    out = np.empty_like(x)
+    lib().or_rms_norm(_ptr(x), _ptr(w), x.size, eps, _ptr(out))
+    return out
 
 
 def ffn_swiglu(tg: int, wg: np.ndarray, tu: int, wu: np.ndarray, td: int, wd: np.ndarray,

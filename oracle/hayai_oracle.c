@@ -728,6 +728,31 @@ void or_fp32_matmul(size_t m, size_t n, const float* w, const float* input, floa
 }
 
 /* ------------------------------------------------------------------------ */
+/* RMSNorm                                                                   */
+/* ------------------------------------------------------------------------ */
+
+/* crates/hayai-cpu/src/simd_ops.rs:10-25 (simd_mean_square): eight f32 lanes accumulate
+ * v*v over chunks of 8, ordered reduce_sum, then the scalar tail, then / len. */
+float or_mean_square(const float* x, size_t n) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    size_t i = 0;
+    for (; i + 8 <= n; i += 8)
+        for (int l = 0; l < 8; l++) acc[l] += x[i + l] * x[i + l];
+    float ms = 0.0f;
+    for (int l = 0; l < 8; l++) ms += acc[l];
+    for (; i < n; i++) ms += x[i] * x[i];
+    return ms / (float)n;
+}
+
+/* crates/hayai-cpu/src/attention.rs:142-147 (rms_norm) with simd_scale_mul
+ * (simd_ops.rs:28-42): x[i] = (x[i] * inv) * w[i], inv = 1 / sqrt(ms + eps).  Out of place. */
+void or_rms_norm(const float* x, const float* w, size_t n, float eps, float* out) {
+    float ms = or_mean_square(x, n);
+    float inv = 1.0f / sqrtf(ms + eps);
+    for (size_t i = 0; i < n; i++) out[i] = x[i] * inv * w[i];
+}
+
+/* ------------------------------------------------------------------------ */
 /* SwiGLU FFN block                                                          */
 /* ------------------------------------------------------------------------ */
 

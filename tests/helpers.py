@@ -8,6 +8,9 @@ import oracle
 QK = {oracle.F32: 1, oracle.Q8_0: 32, oracle.Q4_K: 256, oracle.Q6_K: 256, oracle.IQ2_XXS: 256,
       oracle.IQ2_XS: 256, oracle.IQ2_S: 256, oracle.IQ3_XXS: 256, oracle.IQ3_S: 256}
 IQ_TYPES = [oracle.IQ2_XXS, oracle.IQ2_XS, oracle.IQ2_S, oracle.IQ3_XXS, oracle.IQ3_S]
+# typical |decoded value| / d for random codes: block scale factor x mean grid value
+IQ_SCALE = {oracle.IQ2_XXS: 50.0, oracle.IQ2_XS: 50.0, oracle.IQ2_S: 50.0, oracle.IQ3_XXS: 120.0,
+            oracle.IQ3_S: 130.0}
 # byte offsets of the f16 scales inside a block, per IQ type (d at 0)
 F16_AT = {oracle.Q4_K: (0, 2), oracle.Q6_K: (208,), oracle.Q8_0: (0,), oracle.IQ2_XXS: (0,), oracle.IQ2_XS: (0,),
           oracle.IQ2_S: (0,), oracle.IQ3_XXS: (0,), oracle.IQ3_S: (0,)}
@@ -25,7 +28,9 @@ def quantized(ggml_type: int, m: int, n: int, seed: int, std: float = 0.02) -> n
     nblk = m * n // qk
     b = oracle.random_bytes(seed, nblk * bs).reshape(nblk, bs)
     u = oracle.normal(seed ^ 0x5EED, nblk, 0.0, 1.0)
-    d = (0.002 + 0.018 * (0.5 + 0.5 * np.tanh(u))).astype(np.float16)
+    # d chosen so the decoded weights have a realistic magnitude (~std): a typical
+    # |value| is about d * IQ_SCALE[type] for random codes
+    d = (std / IQ_SCALE[ggml_type] * (0.5 + 0.5 * (1.0 + np.tanh(u)))).astype(np.float16)
     for off in F16_AT[ggml_type]:
         b[:, off:off + 2] = d.view(np.uint8).reshape(nblk, 2)
     return b.reshape(-1).copy()

@@ -61,56 +61,93 @@ def test_ffn_mixed_types_falls_back_to_unfused(engine):
     assert_parity(ref, got, what="iq3_s/q4_k ffn")
 
 
-def make_stack(engine, L, tg, td, d_model, d_ff, seed):
-    layers = [ffn_weights(tg, td, d_model, d_ff, seed + 10 * l) for l in range(L)]
-    res = [(engine.upload(tg, d_ff, d_model, g), engine.upload(tg, d_ff, d_model, u),
+EPS = 1e-5
+
+
+def make_stack(engine, L, tg, td, d_model, d_ff, seed, k_in=None):
+    k_in = k_in or d_model
+    layers = [ffn_weights(tg, td, d_model, d_ff, seed + 10 * l, k_in) for l in range(L)]
+    res = [(engine.upload(tg, d_ff, k_in, g), engine.upload(tg, d_ff, k_in, u),
             engine.upload(td, d_model, d_ff, d)) for g, u, d in layers]
-    return layers, res
+    norms = [oracle.normal(seed + 10 * l + 7, d_model, 1.0, 0.1) for l in range(L)]
+    return layers, res, norms
 
 
-def oracle_stack(layers, tg, td, d_model, d_ff, x):
+def oracle_stack(layers, norms, tg, td, d_model, d_ff, x, k_in=None):
+    """x <- x + FFN(rms_norm(x)) per layer (stream_infer.rs:2166-2170, :3752-3864)."""
+    k_in = k_in or d_model
     x = x.copy()
-    for g, u, d in layers:
-        x = (x + oracle.ffn_swiglu(tg, g, tg, u, td, d, d_model, d_ff, d_model, x)).astype(np.float32)
+    for (g, u, d), nw in zip(layers, norms):
+        xn = np.zeros(k_in, np.float32)
+        xn[:d_model] = oracle.rms_norm(x[:d_model], nw, EPS)
+        x[:d_model] = (x[:d_model] + oracle.ffn_swiglu(tg, g, tg, u, td, d, k_in, d_ff, d_model, xn)).astype(np.float32)
     return x
+
+
+def split(res):
+    return [r[0] for r in res], [r[1] for r in res], [r[2] for r in res]
 
 
 def test_stack_parity(engine):
     L, dm, ff = 6, 1024, 2816
-    layers, res = make_stack(engine, L, oracle.Q4_K, oracle.Q6_K, dm, ff, 500)
+    layers, res, norms = make_stack(engine, L, oracle.Q4_K, oracle.Q6_K, dm, ff, 500)
     x = oracle.normal(501, dm)
-    ref = oracle_stack(layers, oracle.Q4_K, oracle.Q6_K, dm, ff, x)
-    got = engine.ffn_stack([r[0] for r in res], [r[1] for r in res], [r[2] for r in res], x)
+    ref = oracle_stack(layers, norms, oracle.Q4_K, oracle.Q6_K, dm, ff, x)
+    got = engine.ffn_stack(*split(res), x, norms=[torch.from_numpy(n).cuda() for n in norms], eps=EPS)
     assert_parity(ref, got, what="stack")
+
+
+def test_stack_padded_k(engine):
+    # SmolLM shape: K 576 zero-padded to 768 for Q4_K; norm and residual cover 576 entries
+    L, dm, kin, ff = 3, 576, 768, 1536
+    layers, res, norms = make_stack(engine, L, oracle.Q4_K, oracle.Q4_K, dm, ff, 550, k_in=kin)
+    x = np.zeros(kin, np.float32)
+    x[:dm] = oracle.normal(551, dm)
+    ref = oracle_stack(layers, norms, oracle.Q4_K, oracle.Q4_K, dm, ff, x, k_in=kin)
+    got = engine.ffn_stack(*split(res), x, norms=[torch.from_numpy(n).cuda() for n in norms], eps=EPS)
+    assert np.all(got[dm:] == 0.0)
+    assert_parity(ref, got, what="padded stack")
+
+
+def test_stack_unfused_types(engine):
+    L, dm, ff = 2, 512, 1024
+    layers, res, norms = make_stack(engine, L, oracle.IQ3_S, oracle.Q8_0, dm, ff, 560)
+    x = oracle.normal(561, dm)
+    ref = oracle_stack(layers, norms, oracle.IQ3_S, oracle.Q8_0, dm, ff, x)
+    got = engine.ffn_stack(*split(res), x, norms=[torch.from_numpy(n).cuda() for n in norms], eps=EPS)
+    assert_parity(ref, got, what="unfused stack")
 
 
 def test_stack_graph_equals_eager_layers(engine):
     L, dm, ff = 4, 4096, 14336
-    layers, res = make_stack(engine, L, oracle.Q4_K, oracle.Q6_K, dm, ff, 600)
+    layers, res, norms = make_stack(engine, L, oracle.Q4_K, oracle.Q6_K, dm, ff, 600)
     x = oracle.normal(601, dm)
+    nd = [torch.from_numpy(n).cuda() for n in norms]
     xd = torch.from_numpy(x).cuda()
     engine.set_stream(torch.cuda.current_stream())
     try:
-        engine.ffn_stack_dev([r[0] for r in res], [r[1] for r in res], [r[2] for r in res], xd)
+        engine.ffn_stack_dev(*split(res), xd, norms=nd, eps=EPS)
         torch.cuda.synchronize()
         y_graph = xd.cpu().numpy()
         xe = torch.from_numpy(x).cuda()
-        for g, u, d in res:
+        h = torch.empty(ff, device="cuda")
+        for (g, u, d), n in zip(res, nd):
+            engine.ffn_gateup_dev(g, u, xe, h, norm=n, norm_len=dm, eps=EPS)
             ye = torch.empty_like(xe)
-            engine.ffn_swiglu_dev(g, u, d, xe, ye, resid=xe)
+            engine.gemv_dev(d, h, ye, resid=xe)
             xe = ye
         torch.cuda.synchronize()
     finally:
         engine.set_stream(None)
     assert np.array_equal(y_graph, xe.cpu().numpy())
-    ref = oracle_stack(layers, oracle.Q4_K, oracle.Q6_K, dm, ff, x)
+    ref = oracle_stack(layers, norms, oracle.Q4_K, oracle.Q6_K, dm, ff, x)
     assert_parity(ref, y_graph, what="8b stack x4")
 
 
 def test_stack_rejects_mismatched_layers(engine):
     import hayai_b200 as hb
 
-    _, a = make_stack(engine, 1, oracle.Q4_K, oracle.Q4_K, 512, 1024, 700)
-    _, b = make_stack(engine, 1, oracle.Q4_K, oracle.Q4_K, 768, 1024, 710)
+    _, a, _ = make_stack(engine, 1, oracle.Q4_K, oracle.Q4_K, 512, 1024, 700)
+    _, b, _ = make_stack(engine, 1, oracle.Q4_K, oracle.Q4_K, 768, 1024, 710)
     with pytest.raises(hb.CudaError):
         engine.ffn_stack([a[0][0], b[0][0]], [a[0][1], b[0][1]], [a[0][2], b[0][2]], np.zeros(512, np.float32))

@@ -159,10 +159,13 @@ def test_lut_reference_fixture(engine):
 
 
 def test_lut_bench_and_validate_workloads(engine):
-    m, n = 1536, 576  # `hayai bench` (main.rs:601-646)
+    m, n = 1536, 576  # `hayai bench` (main.rs:601-646): outputs ~317, where the oracle's own
+    # sequential f32 sum drifts ~9e-4 from the exact 316.8, so the contract tolerance applies
     w = np.full(m * n // 2, 0xAB, np.uint8)
     x = np.ones(n, np.float32)
-    assert np.abs(oracle.lut_matmul_q4(m, n, w, LUT, x) - engine.lut_matmul_q4(m, n, w, LUT, x)).max() < 1e-4
+    got = engine.lut_matmul_q4(m, n, w, LUT, x)
+    assert_parity(oracle.lut_matmul_q4(m, n, w, LUT, x), got, what="lut bench")
+    assert np.abs(got - 316.8).max() < 1e-3
     m, n = 128, 256  # `hayai validate` (main.rs:648-696)
     w = ((np.arange(m * n // 2) * 31) % 256).astype(np.uint8)
     x = (np.arange(n, dtype=np.float32) * np.float32(0.01) - np.float32(0.25)).astype(np.float32)

@@ -92,6 +92,17 @@ def test_cli_validate():
     assert np.abs(oracle.fp32_matmul(m, n, dense, x) - oracle.lut_matmul_q4(m, n, w, LUT, x)).max() < 1e-4
 
 
+# ----------------------------------------------------------------------------- rms_norm
+def test_rms_norm_matches_formula():
+    x = oracle.normal(21, 1000)  # not a multiple of 8: exercises the scalar tail
+    w = oracle.normal(22, 1000, 1.0, 0.1)
+    ref = x.astype(np.float64) / np.sqrt(np.mean(x.astype(np.float64) ** 2) + 1e-5) * w
+    got = oracle.rms_norm(x, w, 1e-5)
+    assert np.abs(got - ref).max() < 1e-5
+    assert np.allclose(oracle.rms_norm(np.array([3, 4], np.float32), np.ones(2, np.float32), 0.0),
+                       [3 / np.sqrt(12.5), 4 / np.sqrt(12.5)], rtol=1e-6)
+
+
 # ----------------------------------------------------------------------------- moe_infer.rs tests
 def test_top_k_picks_highest_scores():
     s = np.array([0.1, 0.9, 0.5, -0.2, 0.7], np.float32)

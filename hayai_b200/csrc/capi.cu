@@ -208,8 +208,9 @@ extern "C" int hc_engine_free(hc_engine* e) {
     if (!e) return HC_OK;
     hc_engine_activate(e);
     cudaStreamSynchronize(e->stream);
-    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
-    e->graphs.clear();
+    hc_drop_graphs(e);
+    e->sk_ws.release();
+    e->sk_cnt.release();
     for (auto& kv : e->ptr_tables) cudaFree(kv.second);
     e->ptr_tables.clear();
     e->ws_raw.release();
@@ -224,6 +225,34 @@ extern "C" int hc_engine_free(hc_engine* e) {
     if (e->d_err) cudaFree(e->d_err);
     if (e->own_stream) cudaStreamDestroy(e->own_stream);
     delete e;
+    return HC_OK;
+}
+
+void hc_drop_graphs(hc_engine* e) {
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+}
+
+int hc_sk_prepare(hc_engine* e, int type, size_t M, size_t K, bool fused, float** ws, int** cnt) {
+    size_t nws = 0, ncnt = 0;
+    gemv_sk_workspace(type, (int)M, (int)K, fused, e->num_sms, &nws, &ncnt);
+    nws *= sizeof(float);
+    ncnt *= sizeof(int);
+    if (nws > e->sk_ws.cap || ncnt > e->sk_cnt.cap) {
+        // graphs captured earlier hold the old addresses
+        cudaStreamSynchronize(e->stream);
+        hc_drop_graphs(e);
+        const size_t want_ws = nws > e->sk_ws.cap ? nws : e->sk_ws.cap;
+        const size_t want_cnt = ncnt > e->sk_cnt.cap ? ncnt : e->sk_cnt.cap;
+        e->sk_ws.release();
+        e->sk_cnt.release();
+        int rc = e->sk_ws.ensure(want_ws);
+        if (!rc) rc = e->sk_cnt.ensure(want_cnt);
+        if (rc) return rc;
+        HC_CUDA(cudaMemset(e->sk_cnt.p, 0, e->sk_cnt.cap));
+    }
+    *ws = (float*)e->sk_ws.p;
+    *cnt = (int*)e->sk_cnt.p;
     return HC_OK;
 }
 
@@ -374,6 +403,8 @@ int hc_launch_gemv(hc_engine* e, const hc_weights* w, const float* x, size_t ldx
         a.ldr = (int)ldr;
         a.w2 = nullptr;
         a.err = e->d_err;
+        int rc = hc_sk_prepare(e, w->type, w->m, w->n, false, &a.sk_ws, &a.sk_cnt);
+        if (rc) return rc;
         ce = launch_gemv_mma(w->type, a, (int)nvec, false, e->num_sms, e->smem_optin, e->stream);
     } else if (gemv_simple_supported(w->type)) {
         ce = launch_gemv_simple(w->type, (const uint8_t*)w->dev, w->stride, (int)w->m, (int)w->n, x, (int)ldx, y,
@@ -599,6 +630,8 @@ int hc_launch_gateup(hc_engine* e, const hc_weights* g, const hc_weights* u, con
         a.norm_w = norm_w;
         a.norm_len = (int)norm_len;
         a.norm_eps = eps;
+        int rc = hc_sk_prepare(e, g->type, g->m, g->n, true, &a.sk_ws, &a.sk_cnt);
+        if (rc) return rc;
         cudaError_t ce = launch_gemv_mma(g->type, a, (int)nvec, true, e->num_sms, e->smem_optin, e->stream);
         if (ce != cudaSuccess) return hc_cuda_error(ce, "gate/up launch");
         return HC_OK;
@@ -724,14 +757,37 @@ static int stack_check(const StackArgs& s) {
 static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
     size_t ffmax = 0;
     for (size_t l = 0; l < s.L; ++l) ffmax = s.g[l]->m > ffmax ? s.g[l]->m : ffmax;
+    void* old_h = e->ws_h.p;
     int rc = e->ws_h.ensure(nvec * ffmax * 4);
     if (rc) return rc;
+    if (old_h && old_h != e->ws_h.p) hc_drop_graphs(e);
     float* h = (float*)e->ws_h.p;
+    // size every workspace before a capture (no allocation may happen inside it)
+    for (size_t l = 0; l < s.L; ++l) {
+        float* ws;
+        int* cnt;
+        if (s.g[l]->type == s.u[l]->type && gemv_mma_supported(s.g[l]->type)) {
+            rc = hc_sk_prepare(e, s.g[l]->type, s.g[l]->m, s.g[l]->n, true, &ws, &cnt);
+        } else {
+            rc = e->ws_g.ensure(nvec * s.g[l]->m * 4);
+            if (!rc) rc = e->ws_u.ensure(nvec * s.g[l]->m * 4);
+            if (!rc && s.norm) rc = e->ws_misc.ensure(nvec * s.g[l]->n * 4);
+            if (!rc && gemv_mma_supported(s.g[l]->type))
+                rc = hc_sk_prepare(e, s.g[l]->type, s.g[l]->m, s.g[l]->n, false, &ws, &cnt);
+            if (!rc && gemv_mma_supported(s.u[l]->type))
+                rc = hc_sk_prepare(e, s.u[l]->type, s.u[l]->m, s.u[l]->n, false, &ws, &cnt);
+        }
+        if (!rc && gemv_mma_supported(s.d[l]->type))
+            rc = hc_sk_prepare(e, s.d[l]->type, s.d[l]->m, s.d[l]->n, false, &ws, &cnt);
+        if (rc) return rc;
+    }
     if (!e->use_graphs) return stack_enqueue(e, s, x, nvec, h);
 
     uint64_t key = mix(mix(mix(0, (uint64_t)(uintptr_t)x), nvec), s.L);
     key = mix(key, (uint64_t)(uintptr_t)h);
-    key = mix(key, (uint64_t)(uintptr_t)e->stream);
+    key = mix(key, (uint64_t)(uintptr_t)e->ws_g.p);
+    key = mix(key, (uint64_t)(uintptr_t)e->ws_u.p);
+    key = mix(key, (uint64_t)(uintptr_t)e->ws_misc.p);
     uint32_t eb;
     memcpy(&eb, &s.eps, 4);
     key = mix(key, eb);
@@ -744,10 +800,19 @@ static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
     }
     auto it = e->graphs.find(key);
     if (it == e->graphs.end()) {
+        // capture on the engine's private stream (the caller's may be the legacy default
+        // stream, which cannot be captured); the graph is then launched on the caller's
         cudaGraph_t graph;
-        HC_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeRelaxed));
+        cudaStream_t caller = e->stream;
+        e->stream = e->own_stream;
+        cudaError_t ce = cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeRelaxed);
+        if (ce != cudaSuccess) {
+            e->stream = caller;
+            return hc_cuda_error(ce, "stack capture begin");
+        }
         rc = stack_enqueue(e, s, x, nvec, h);
-        cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
+        ce = cudaStreamEndCapture(e->stream, &graph);
+        e->stream = caller;
         if (rc) {
             if (ce == cudaSuccess) cudaGraphDestroy(graph);
             return rc;

@@ -32,6 +32,8 @@ struct hc_engine {
     bool use_graphs = true;
     // grow-on-demand workspaces (the reference's GemvSyncWorkspace, compute.rs:10-17)
     DevBuf ws_raw, ws_gpu, ws_x, ws_y, ws_h, ws_g, ws_u, ws_misc;
+    // stream-K partial sums and per-tile counters (counters zeroed once; kernels re-arm them)
+    DevBuf sk_ws, sk_cnt;
     HostBuf hs_out;
     std::unordered_map<uint64_t, cudaGraphExec_t> graphs;  // captured FFN stacks
     std::unordered_map<uint64_t, void*> ptr_tables;        // device tables of expert pointers
@@ -60,3 +62,7 @@ int hc_launch_ffn(hc_engine* e, const hc_weights* g, const hc_weights* u, const 
                   size_t ldx, float* y, size_t ldy, const float* resid, size_t ldr, float* h_ws, size_t nvec,
                   const float* norm_w, size_t norm_len, float eps);
 const char* hc_type_label(int t);
+// Make the stream-K workspace large enough for an M x K launch of `type`; a reallocation
+// drops the captured CUDA graphs (they hold the old addresses).
+int hc_sk_prepare(hc_engine* e, int type, size_t M, size_t K, bool fused, float** ws, int** cnt);
+void hc_drop_graphs(hc_engine* e);

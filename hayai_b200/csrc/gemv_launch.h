@@ -13,6 +13,8 @@ struct GemvArgs;
 cudaError_t launch_gemv_mma(int type, const GemvArgs& a, int nvec, bool fused, int num_sms, int smem_limit,
                             cudaStream_t stream);
 bool gemv_mma_supported(int type);
+// Workspace of the stream-K split for an M x K launch: partial-sum floats and tile counters.
+void gemv_sk_workspace(int type, int M, int K, bool fused, int num_sms, size_t* ws_floats, size_t* counters);
 
 // CUDA-core GEMV on the raw GGUF layout for F32 and the IQ2/IQ3 codebook formats.
 cudaError_t launch_gemv_simple(int type, const uint8_t* w, size_t row_bytes, int M, int K, const float* x,

@@ -48,6 +48,12 @@ struct GemvArgs {
     const float* norm_w; // optional RMSNorm weight applied to x first (nullptr = none)
     int norm_len;        // normalized length (<= K)
     float norm_eps;
+    // stream-K split: partial sums of tiles shared by several warps + per-tile arrival
+    // counters (zero between launches); filled by the launcher
+    float* sk_ws;
+    int* sk_cnt;
+    int sk_slots;
+    int stages;          // depth of each warp's cp.async ring
 };
 
 // ------------------------------------------------------------------ formats

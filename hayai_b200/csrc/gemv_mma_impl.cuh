@@ -203,7 +203,8 @@ __device__ __forceinline__ void q4k_block(const Q4KBlk& A, const Q4KBlk& B, int 
     const uint2* xb = c.xt + kb * kEnt;
     const uint32_t wA[8] = {A.q0.x, A.q0.y, A.q0.z, A.q0.w, A.q1.x, A.q1.y, A.q1.z, A.q1.w};
     const uint32_t wB[8] = {B.q0.x, B.q0.y, B.q0.z, B.q0.w, B.q1.x, B.q1.y, B.q1.z, B.q1.w};
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    // two accumulator chains (low / high nibbles) halve the dependent MMA latency
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int wi = 0; wi < 8; ++wi) {
         const uint32_t a = wA[wi], b = wB[wi], a8 = a >> 8, b8 = b >> 8;
@@ -213,11 +214,13 @@ __device__ __forceinline__ void q4k_block(const Q4KBlk& A, const Q4KBlk& B, int 
                  hfma2_u32(lop3_and_or(b, 0x000F000Fu, 0x64006400u), loB.x, loB.y),
                  hfma2_u32(lop3_and_or(a8, 0x000F000Fu, 0x64006400u), loA.x, loA.y),
                  hfma2_u32(lop3_and_or(b8, 0x000F000Fu, 0x64006400u), loB.x, loB.y), fl.x, fl.y);
-        mma16816(acc, hfma2_u32(lop3_and_or(a, 0x00F000F0u, 0x64006400u), hiA.x, hiA.y),
+        mma16816(acc2, hfma2_u32(lop3_and_or(a, 0x00F000F0u, 0x64006400u), hiA.x, hiA.y),
                  hfma2_u32(lop3_and_or(b, 0x00F000F0u, 0x64006400u), hiB.x, hiB.y),
                  hfma2_u32(lop3_and_or(a8, 0x00F000F0u, 0x64006400u), hiA.x, hiA.y),
                  hfma2_u32(lop3_and_or(b8, 0x00F000F0u, 0x64006400u), hiB.x, hiB.y), fh.x, fh.y);
     }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] += acc2[i];
     const float2 ddA = __half22float2(u32_as_h2(A.h.x));
     const float2 ddB = __half22float2(u32_as_h2(B.h.x));
     float mpA = 0.f, mpB = 0.f;
@@ -237,6 +240,80 @@ __device__ __forceinline__ void q4k_block(const Q4KBlk& A, const Q4KBlk& B, int 
     }
     dA = ddA.x * (acc[0] + acc[1] * kLoScale) - ddA.y * mpA;
     dB = ddB.x * (acc[2] + acc[3] * kLoScale) - ddB.y * mpB;
+}
+
+// Q4_K, scale-per-lane variant.  Lane t's codes are chunk t of the super-block: the low
+// nibbles are sub-block 2t, the high nibbles sub-block 2t+1.  B holds lane t's x only in
+// columns 2t (hi part) and 2t+1 (lo part), so in every MMA lane t's k-slots meet only its
+// own columns and the accumulator comes back per sub-block, already distributed over the
+// lanes: C[row][2t] = sum over sub-block (2t+G) of A * x_hi.  Codes enter as
+// f16(1 + n/64) (magic 0x3C00, nibble at bits 4-7: one LOP3 per two codes), so
+//     sum n*x = 64 * (C - Sx_j)
+// and the 6-bit scale, d, dmin and the min term are applied once per sub-block per lane in
+// f32.  pA/pB receive lane t's share of rows g / g+8 (summed over t at the end of a tile).
+template <int NV, int NMAT>
+__device__ __forceinline__ void q4k_unit_dist(const Q4KBlk (&A)[NMAT], const Q4KBlk (&B)[NMAT], int kb,
+                                              const LaneCtx<NV>& c, float (&pA)[NMAT][NV], float (&pB)[NMAT][NV]) {
+    constexpr int kEnt = 16 * 2 * NV * 4;  // table entries of one super-block
+    const int t = c.t, g = c.g;
+    const bool mine = (g >> 1) == t;
+    // entry ((mma * 2NV + 2v + part) * 4 + t); c.xt points at g*4 + t, rebase to part*4 + t
+    const uint2* xb = c.xt - g * 4 + (g & 1) * 4 + kb * kEnt;
+    float acc[NMAT][NV][2][4];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int v = 0; v < NV; ++v)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[m][v][0][i] = acc[m][v][1][i] = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < 8; ++wi) {
+        uint2 blo[NV], bhi[NV];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            blo[v] = mine ? xb[((2 * wi) * 2 * NV + 2 * v) * 4] : make_uint2(0u, 0u);
+            bhi[v] = mine ? xb[((2 * wi + 1) * 2 * NV + 2 * v) * 4] : make_uint2(0u, 0u);
+        }
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+            const uint32_t qa[8] = {A[m].q0.x, A[m].q0.y, A[m].q0.z, A[m].q0.w, A[m].q1.x, A[m].q1.y, A[m].q1.z, A[m].q1.w};
+            const uint32_t qb[8] = {B[m].q0.x, B[m].q0.y, B[m].q0.z, B[m].q0.w, B[m].q1.x, B[m].q1.y, B[m].q1.z, B[m].q1.w};
+            const uint32_t a = qa[wi], b = qb[wi];
+            const uint32_t lo02a = lop3_and_or(a << 4, 0x00F000F0u, 0x3C003C00u);
+            const uint32_t lo13a = lop3_and_or(a >> 4, 0x00F000F0u, 0x3C003C00u);
+            const uint32_t hi02a = lop3_and_or(a, 0x00F000F0u, 0x3C003C00u);
+            const uint32_t hi13a = lop3_and_or(a >> 8, 0x00F000F0u, 0x3C003C00u);
+            const uint32_t lo02b = lop3_and_or(b << 4, 0x00F000F0u, 0x3C003C00u);
+            const uint32_t lo13b = lop3_and_or(b >> 4, 0x00F000F0u, 0x3C003C00u);
+            const uint32_t hi02b = lop3_and_or(b, 0x00F000F0u, 0x3C003C00u);
+            const uint32_t hi13b = lop3_and_or(b >> 8, 0x00F000F0u, 0x3C003C00u);
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                mma16816(acc[m][v][0], lo02a, lo02b, lo13a, lo13b, blo[v].x, blo[v].y);
+                mma16816(acc[m][v][1], hi02a, hi02b, hi13a, hi13b, bhi[v].x, bhi[v].y);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+        int scA0, mA0, scA1, mA1, scB0, mB0, scB1, mB1;
+        q4k_scales(A[m].h, t, scA0, mA0, scA1, mA1);
+        q4k_scales(B[m].h, t, scB0, mB0, scB1, mB1);
+        const float2 ddA = __half22float2(u32_as_h2(A[m].h.x));  // (d, dmin)
+        const float2 ddB = __half22float2(u32_as_h2(B[m].h.x));
+        const float cA0 = 64.f * ddA.x * (float)scA0, cA1 = 64.f * ddA.x * (float)scA1;
+        const float cB0 = 64.f * ddB.x * (float)scB0, cB1 = 64.f * ddB.x * (float)scB1;
+        const float kA0 = cA0 + ddA.y * (float)mA0, kA1 = cA1 + ddA.y * (float)mA1;
+        const float kB0 = cB0 + ddB.y * (float)mB0, kB1 = cB1 + ddB.y * (float)mB1;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            const float s0 = c.sx[v * c.sxs + kb * 8 + 2 * t], s1 = c.sx[v * c.sxs + kb * 8 + 2 * t + 1];
+            const float* a0 = acc[m][v][0];
+            const float* a1 = acc[m][v][1];
+            pA[m][v] += cA0 * (a0[0] + a0[1] * kLoScale) - s0 * kA0 + cA1 * (a1[0] + a1[1] * kLoScale) - s1 * kA1;
+            pB[m][v] += cB0 * (a0[2] + a0[3] * kLoScale) - s0 * kB0 + cB1 * (a1[2] + a1[3] * kLoScale) - s1 * kB1;
+        }
+    }
 }
 
 // ------------------------------------------------------------------ Q6_K (GPU layout)

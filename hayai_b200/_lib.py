@@ -51,6 +51,7 @@ SIGNATURES: dict[str, list] = {
     "hc_pending_wait": [_P, _P, _S],
     "hc_pending_free": [_P],
     "hc_gemv_dev": [_P, _P, _P, _S, _P, _S, _P, _S, _S],
+    "hc_gemv_dev_noalloc": [_P, _P, _P, _S, _P, _S, _P, _S, _S],
     "hc_lut_matmul_q4": [_P, _S, _S, _P, _P, _P, _P],
     "hc_lut_matmul_q4_dev": [_P, _S, _S, _P, _P, _P, _P],
     "hc_ffn_swiglu": [_P, _P, _P, _P, _P, _P, _S],

@@ -116,6 +116,20 @@ int hc_pending_free(hc_pending* p);
 int hc_gemv_dev(hc_engine* eng, const hc_weights* w, const float* x, size_t ldx, float* y, size_t ldy,
                 const float* resid, size_t ldr, size_t nvec);
 
+/* hc_gemv_dev for Q4_K, Q6_K and Q8_0 weights that allocates nothing.  No counterpart in
+ * the reference: it exists for callers that cannot let a library call cudaMalloc -- hosts
+ * whose device memory belongs to their own pool allocator, and decode loops that cannot
+ * absorb the device synchronisation a cudaMalloc/cudaFree may cause.  The scratch the
+ * stream-K split needs comes from a static device array of the library (4 MiB of partial
+ * sums + 16384 tile counters per GPU, held until exit); a matrix that needs more is
+ * rejected with HC_ERR_INVALID (every Llama-3 8B/70B FFN matrix and a 128256 x 4096 output
+ * projection fit; M above 262144 never does).  The first call on
+ * a device looks the array's address up (cudaGetSymbolAddress): make that first call
+ * before any stream capture.  All calls on a device share the array, so calls that overlap
+ * on the GPU race: serialise them.  Other formats return HC_ERR_UNSUPPORTED. */
+int hc_gemv_dev_noalloc(hc_engine* eng, const hc_weights* w, const float* x, size_t ldx, float* y, size_t ldy,
+                        const float* resid, size_t ldr, size_t nvec);
+
 /* Toy 16-entry LUT-Q4 matmul (two nibbles per byte, low nibble first); blocking.
  * Replaces OpenClEngine::lut_matmul_q4 (compute.rs:45-128) and
  * EngineOrchestrator::execute_lut_matmul (orchestrator.rs:198-218). */

@@ -308,8 +308,8 @@ static int weights_make(hc_engine* e, int type, size_t m, size_t n, const void* 
     if (rc) return rc;
     if (!src) return hc_set_error(HC_ERR_INVALID, "null weight bytes");
     const size_t raw_rb = raw_row_bytes(type, (int)n);
-    const size_t gpu_rb = gpu_row_stride(type, (int)n);
-    const size_t raw_bytes = m * raw_rb, gpu_bytes = m * gpu_rb;
+    const size_t gpu_rb = gpu_stride(type, (int)n);
+    const size_t raw_bytes = m * raw_rb, gpu_bytes = gpu_weight_bytes(type, (int)m, (int)n);
     hc_weights* w = new hc_weights();
     w->type = type;
     w->m = m;
@@ -324,7 +324,7 @@ static int weights_make(hc_engine* e, int type, size_t m, size_t n, const void* 
     }
     const uint8_t* raw_dev = nullptr;
     void* tmp = nullptr;
-    const bool same_layout = raw_rb == gpu_rb && (type != T_Q6_K && type != T_Q8_0);
+    const bool same_layout = !tiled_type(type);
     if (from_host) {
         if (same_layout) {
             ce = cudaMemcpyAsync(w->dev, src, raw_bytes, cudaMemcpyHostToDevice, e->stream);
@@ -460,9 +460,10 @@ extern "C" int hc_ggml_gemv_dispatch(hc_engine* e, int type, size_t m, size_t n,
     rc = hc_validate_weights(type, m, n, len);
     if (rc) return rc;
     if (!weights || !in || !out) return hc_set_error(HC_ERR_INVALID, "null argument");
-    const size_t raw_bytes = m * raw_row_bytes(type, (int)n), gpu_rb = gpu_row_stride(type, (int)n);
+    const size_t raw_bytes = m * raw_row_bytes(type, (int)n), gpu_rb = gpu_stride(type, (int)n);
+    const size_t gpu_bytes = gpu_weight_bytes(type, (int)m, (int)n);
     rc = e->ws_raw.ensure(raw_bytes);
-    if (!rc) rc = e->ws_gpu.ensure(m * gpu_rb + 16);
+    if (!rc) rc = e->ws_gpu.ensure(gpu_bytes + 16);
     if (rc) return rc;
     HC_CUDA(cudaMemcpyAsync(e->ws_raw.p, weights, raw_bytes, cudaMemcpyHostToDevice, e->stream));
     cudaError_t ce = launch_repack(type, (const uint8_t*)e->ws_raw.p, (uint8_t*)e->ws_gpu.p, (int)m, (int)n, e->stream);
@@ -472,7 +473,7 @@ extern "C" int hc_ggml_gemv_dispatch(hc_engine* e, int type, size_t m, size_t n,
     tmp.m = m;
     tmp.n = n;
     tmp.stride = gpu_rb;
-    tmp.bytes = m * gpu_rb;
+    tmp.bytes = gpu_bytes;
     tmp.dev = e->ws_gpu.p;
     tmp.device = e->device;
     return gemv_host(e, &tmp, in, out, 1);

@@ -33,8 +33,12 @@ cudaError_t launch_rms_norm(const float* x, int ldx, const float* w, int len, in
 // Elementwise SwiGLU h = silu(g) * u, with an optional residual for out = resid + ...
 cudaError_t launch_swiglu(const float* g, const float* u, float* h, size_t n, cudaStream_t stream);
 
-// Upload repack: raw GGUF rows -> GPU layout (Q6_K, Q8_0); returns the GPU row stride.
-size_t gpu_row_stride(int type, int K);
+// Upload repack: raw GGUF rows -> GPU layout.  Q4_K, Q6_K and Q8_0 become tile-major
+// (16-row tiles of contiguous tile-block images); the other formats keep their rows.
+bool tiled_type(int type);
+size_t tile_block_bytes(int type);                 // bytes of one 16-row x kernel-block image
+size_t gpu_stride(int type, int K);                // bytes per tile (tiled) or per row
+size_t gpu_weight_bytes(int type, int M, int K);   // bytes of the whole GPU image
 size_t raw_row_bytes(int type, int K);
 cudaError_t launch_repack(int type, const uint8_t* raw, uint8_t* gpu, int M, int K, cudaStream_t stream);
 

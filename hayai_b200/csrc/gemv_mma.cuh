@@ -32,8 +32,8 @@ struct GemvSmem {
 };
 
 struct GemvArgs {
-    const uint8_t* w;    // weights in the GPU layout of the format
-    long long row_stride;  // bytes per row in that layout
+    const uint8_t* w;    // weights in the tile-major GPU layout of the format
+    long long row_stride;  // bytes per 16-row tile in that layout
     int M, K;            // rows, columns
     const float* x;      // [nvec][ldx]
     int ldx;
@@ -57,8 +57,11 @@ struct GemvArgs {
 };
 
 // ------------------------------------------------------------------ formats
+// Tile-block images (16 rows x one kernel block) of the GPU layout: byte offsets of the
+// regions; a lane's 16-byte piece of row r sits at region + 16 * (4r + t).
 struct FmtQ4K {
     static constexpr int kType = T_Q4_K;
+    static constexpr int kTile = 2304, kHdr = 0, kQ0 = 256, kQ1 = 1280;
     static constexpr int kBlockElems = 256;
     static constexpr int kMmaPerBlock = 16;
     // element index (within the block) of lane t's k-slot j of MMA `mi`:
@@ -69,6 +72,7 @@ struct FmtQ4K {
 
 struct FmtQ6K {
     static constexpr int kType = T_Q6_K;
+    static constexpr int kTile = 3360, kL0 = 0, kL1 = 1024, kQh = 2048, kSc = 3072, kD = 3328;
     static constexpr int kBlockElems = 256;
     static constexpr int kMmaPerBlock = 16;
     // mi = 8h + 4lh + q covers scale group (h, q, lh): elements 128h + 32q + 16lh + [0,16)
@@ -82,6 +86,7 @@ struct FmtQ6K {
 // Q8_0 kernels work on groups of 4 Q8_0 blocks (128 elements, 8 MMAs); mi = 2*blk + half.
 struct FmtQ80 {
     static constexpr int kType = T_Q8_0;
+    static constexpr int kTile = 2176, kQ0 = 0, kQ1 = 1024, kD = 2048;
     static constexpr int kBlockElems = 128;
     static constexpr int kMmaPerBlock = 8;
     __device__ static int base(int mi, int t) { return 16 * mi + 4 * t; }

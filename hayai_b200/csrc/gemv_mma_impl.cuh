@@ -1,14 +1,13 @@
 // gemv_mma_impl.cuh -- device building blocks of the tensor-core GEMV, shared by the
-// dense kernels (gemv_mma.cu) and the expert-routed kernels (moe.cu).
+// dense kernel (gemv_tma.cu) and the expert-routed kernels (moe.cu).
 //
-// Two phases per CTA:
 //  1. prologue: the activation rows (optionally RMS-normalised) are turned into the
 //     B-fragment table in shared memory.  Every thread issues all its float4 loads up
 //     front (no dependent load chain), maps each 4-element chunk to its table slot with
 //     the format's inverse index, and writes the hi and lo f16 halves.
-//  2. main loop: each warp streams the code blocks of its 16-row tile with 128-bit
-//     non-allocating loads, double-buffered (the next block's loads are in flight while
-//     the current block is dequantised into mma.m16n8k16 A fragments).
+//  2. per kernel block: a warp takes rows g and g+8 of one tile-block image (from shared
+//     memory, or streamed from global memory one block ahead) and dequantises them
+//     straight into mma.m16n8k16 A fragments.
 #pragma once
 
 #include "gemv_mma.cuh"
@@ -52,13 +51,15 @@ struct NormArgs {
     float eps;
 };
 
-__device__ __forceinline__ float block_sum(float s, float* scratch) {
+// Sum over the first nthr threads of the CTA (whole warps), synchronised on named barrier
+// `bar` (bar 0 with nthr == blockDim.x is __syncthreads).
+__device__ __forceinline__ float block_sum(float s, float* scratch, int nthr, int bar) {
     s = warp_sum(s);
-    __syncthreads();  // scratch may still be read by a previous call
+    named_bar_sync(bar, nthr);  // scratch may still be read by a previous call
     if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = s;
-    __syncthreads();
+    named_bar_sync(bar, nthr);
     float t = 0.f;
-    const int nw = blockDim.x >> 5;
+    const int nw = nthr >> 5;
     for (int i = 0; i < nw; ++i) t += scratch[i];
     return t;
 }
@@ -66,13 +67,15 @@ __device__ __forceinline__ float block_sum(float s, float* scratch) {
 // Builds the B-fragment table (entry e = ((block * kMmaPerBlock + mi) * 2NV + g) * 4 + t holds
 // {pack(x[e0], x[e2]), pack(x[e1], x[e3])} of vector g/2, part g&1 (hi / lo*2^11), with
 // e_j = block*kBlockElems + F::base(mi, t) + j) and, for Q4_K, the 32-element sub-block sums.
+// Run by threads [0, nthr) of the CTA (all of it by default); `bar` is the named barrier they
+// synchronise on.
 template <class F, int NV>
 __device__ void build_prologue(uint2* __restrict__ xt, float* __restrict__ sx, const float* __restrict__ x, int ldx,
-                               int K, int nvec, const NormArgs& nrm, float* scratch, int* err) {
+                               int K, int nvec, const NormArgs& nrm, float* scratch, int* err, int nthr, int bar) {
     const int nb = (K + F::kBlockElems - 1) / F::kBlockElems;
     const int nchunk = K >> 2;                         // real float4 chunks
     const int ntab = (nb * F::kBlockElems) >> 2;       // chunks covered by the table (zero padded)
-    const int rounds = (ntab + blockDim.x - 1) / blockDim.x;
+    const int rounds = (ntab + nthr - 1) / nthr;
     bool bad = false;
     for (int v = 0; v < NV; ++v) {
         const float* xv = x + (size_t)v * ldx;
@@ -83,17 +86,17 @@ __device__ void build_prologue(uint2* __restrict__ xt, float* __restrict__ sx, c
             if (live) {
                 const int nc = nrm.len >> 2;
 #pragma unroll 4
-                for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+                for (int c = threadIdx.x; c < nc; c += nthr) {
                     const float4 a = __ldg(reinterpret_cast<const float4*>(xv) + c);
                     s += (a.x * a.x + a.y * a.y) + (a.z * a.z + a.w * a.w);
                 }
             }
-            const float tot = block_sum(s, scratch);
+            const float tot = block_sum(s, scratch, nthr, bar);
             inv = 1.0f / sqrtf(tot / (float)nrm.len + nrm.eps);
         }
 #pragma unroll 4
         for (int r = 0; r < rounds; ++r) {
-            const int c = threadIdx.x + r * blockDim.x;
+            const int c = threadIdx.x + r * nthr;
             float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
             if (live && c < nchunk) {
                 a = __ldg(reinterpret_cast<const float4*>(xv) + c);
@@ -136,6 +139,12 @@ __device__ void build_prologue(uint2* __restrict__ xt, float* __restrict__ sx, c
         }
     }
     if (bad && err) atomicOr(err, 1);
+}
+
+template <class F, int NV>
+__device__ void build_prologue(uint2* __restrict__ xt, float* __restrict__ sx, const float* __restrict__ x, int ldx,
+                               int K, int nvec, const NormArgs& nrm, float* scratch, int* err) {
+    build_prologue<F, NV>(xt, sx, x, ldx, K, nvec, nrm, scratch, err, (int)blockDim.x, 0);
 }
 
 // Q4_K scale LUT: [sc] -> {mul (sc,sc), add (-1024 sc)} for low nibbles (value 1024+n),
@@ -182,13 +191,6 @@ __device__ __forceinline__ void q4k_scales(const uint4& h, int t, int& sc0, int&
 struct Q4KBlk {
     uint4 h, q0, q1;
 };
-
-__device__ __forceinline__ void q4k_load(Q4KBlk& b, const uint8_t* row, int kb, int t) {
-    const uint8_t* p = row + kb * 144;
-    b.h = ldg_stream128(p);
-    b.q0 = ldg_stream128(p + 16 + 32 * t);
-    b.q1 = ldg_stream128(p + 32 + 32 * t);
-}
 
 // Contribution of one super-block to rows g (dA) and g+8 (dB), for vector t (lanes t < NV).
 template <int NV>
@@ -332,15 +334,6 @@ struct Q6KBlk {
     uint16_t d;
 };
 
-__device__ __forceinline__ void q6k_load(Q6KBlk& b, const uint8_t* row, int kb, int t, int nb) {
-    const uint8_t* p = row + kb * 208;
-    b.l0 = ldg_stream128(p + 32 * t);
-    b.l1 = ldg_stream128(p + 32 * t + 16);
-    b.qh = ldg_stream128(p + 128 + 16 * t);
-    b.sc = ldg_stream128(p + 192);
-    b.d = ldg_u16(row + (size_t)nb * 208 + 2 * kb);
-}
-
 template <int NV>
 __device__ __forceinline__ void q6k_block(const Q6KBlk& A, const Q6KBlk& B, int kb, const LaneCtx<NV>& c,
                                           float& dA, float& dB) {
@@ -396,12 +389,6 @@ struct Q80Blk {
     uint2 d;
 };
 
-__device__ __forceinline__ void q80_load(Q80Blk& b, const uint8_t* row, int kg, int t, int ng) {
-    b.q0 = ldg_stream128(row + kg * 128 + 32 * t);
-    b.q1 = ldg_stream128(row + kg * 128 + 32 * t + 16);
-    b.d = ldg_u2(row + (size_t)ng * 128 + kg * 8);
-}
-
 template <int NV>
 __device__ __forceinline__ void q80_block(const Q80Blk& A, const Q80Blk& B, int kg, const LaneCtx<NV>& c, float& dA,
                                           float& dB) {
@@ -451,11 +438,54 @@ struct BlkOf<FmtQ80> {
     using T = Q80Blk;
 };
 
-template <class F>
-__device__ __forceinline__ void blk_load(typename BlkOf<F>::T& b, const uint8_t* row, int kb, int t, int nb) {
-    if constexpr (F::kType == T_Q4_K) q4k_load(b, row, kb, t);
-    else if constexpr (F::kType == T_Q6_K) q6k_load(b, row, kb, t, nb);
-    else q80_load(b, row, kb, t, nb);
+template <bool kShared>
+__device__ __forceinline__ uint4 ld_piece(const uint8_t* p) {
+    if constexpr (kShared) return *reinterpret_cast<const uint4*>(p);
+    else return ldg_stream128(p);
+}
+
+// Rows g (A) and g+8 (B) of one tile-block image (see repack.cu for the layout), from
+// shared memory (kShared) or streamed from global memory.
+template <class F, bool kShared>
+__device__ __forceinline__ void tile_load(typename BlkOf<F>::T& A, typename BlkOf<F>::T& B, const uint8_t* tb, int g,
+                                          int t) {
+    const int pa = 16 * (4 * g + t), pb = pa + 512;
+    if constexpr (F::kType == T_Q4_K) {
+        A.h = ld_piece<kShared>(tb + F::kHdr + 16 * g);
+        B.h = ld_piece<kShared>(tb + F::kHdr + 16 * (g + 8));
+        A.q0 = ld_piece<kShared>(tb + F::kQ0 + pa);
+        B.q0 = ld_piece<kShared>(tb + F::kQ0 + pb);
+        A.q1 = ld_piece<kShared>(tb + F::kQ1 + pa);
+        B.q1 = ld_piece<kShared>(tb + F::kQ1 + pb);
+    } else if constexpr (F::kType == T_Q6_K) {
+        A.l0 = ld_piece<kShared>(tb + F::kL0 + pa);
+        B.l0 = ld_piece<kShared>(tb + F::kL0 + pb);
+        A.l1 = ld_piece<kShared>(tb + F::kL1 + pa);
+        B.l1 = ld_piece<kShared>(tb + F::kL1 + pb);
+        A.qh = ld_piece<kShared>(tb + F::kQh + pa);
+        B.qh = ld_piece<kShared>(tb + F::kQh + pb);
+        A.sc = ld_piece<kShared>(tb + F::kSc + 16 * g);
+        B.sc = ld_piece<kShared>(tb + F::kSc + 16 * (g + 8));
+        if constexpr (kShared) {
+            A.d = *reinterpret_cast<const uint16_t*>(tb + F::kD + 2 * g);
+            B.d = *reinterpret_cast<const uint16_t*>(tb + F::kD + 2 * (g + 8));
+        } else {
+            A.d = ldg_u16(tb + F::kD + 2 * g);
+            B.d = ldg_u16(tb + F::kD + 2 * (g + 8));
+        }
+    } else {
+        A.q0 = ld_piece<kShared>(tb + F::kQ0 + pa);
+        B.q0 = ld_piece<kShared>(tb + F::kQ0 + pb);
+        A.q1 = ld_piece<kShared>(tb + F::kQ1 + pa);
+        B.q1 = ld_piece<kShared>(tb + F::kQ1 + pb);
+        if constexpr (kShared) {
+            A.d = *reinterpret_cast<const uint2*>(tb + F::kD + 8 * g);
+            B.d = *reinterpret_cast<const uint2*>(tb + F::kD + 8 * (g + 8));
+        } else {
+            A.d = ldg_u2(tb + F::kD + 8 * g);
+            B.d = ldg_u2(tb + F::kD + 8 * (g + 8));
+        }
+    }
 }
 
 template <class F, int NV>
@@ -466,19 +496,18 @@ __device__ __forceinline__ void blk_compute(const typename BlkOf<F>::T& A, const
     else q80_block<NV>(A, B, kb, c, dA, dB);
 }
 
-// Streams blocks [kb0, kb1) of NMAT matrices (rows rA/rB of each) through the tensor cores,
-// one block ahead: yA[m] / yB[m] accumulate the outputs of rows g / g+8 for vector t.
+// Streams blocks [kb0, kb1) of one 16-row tile of NMAT matrices (tile images at tb[m])
+// through the tensor cores, one block ahead: yA[m] / yB[m] accumulate the outputs of rows
+// g / g+8 for vector t.
 template <class F, int NV, int NMAT>
-__device__ __forceinline__ void stream_tile(const uint8_t* const (&rowA)[NMAT], const uint8_t* const (&rowB)[NMAT],
-                                            int kb0, int kb1, const LaneCtx<NV>& c, float (&yA)[NMAT],
-                                            float (&yB)[NMAT]) {
+__device__ __forceinline__ void stream_tile(const uint8_t* const (&tb)[NMAT], int kb0, int kb1, const LaneCtx<NV>& c,
+                                            float (&yA)[NMAT], float (&yB)[NMAT]) {
     using B = typename BlkOf<F>::T;
     const int nk = kb1 - kb0;
     const int total = NMAT * nk;
     if (total <= 0) return;
     B curA, curB, nxtA, nxtB;
-    blk_load<F>(curA, rowA[0], kb0, c.t, c.nb);
-    blk_load<F>(curB, rowB[0], kb0, c.t, c.nb);
+    tile_load<F, false>(curA, curB, tb[0] + (size_t)kb0 * F::kTile, c.g, c.t);
 #pragma unroll 1
     for (int i = 0; i < total; ++i) {
         const int m = NMAT == 1 ? 0 : i / nk;
@@ -486,8 +515,7 @@ __device__ __forceinline__ void stream_tile(const uint8_t* const (&rowA)[NMAT], 
         if (i + 1 < total) {
             const int m1 = NMAT == 1 ? 0 : (i + 1) / nk;
             const int kbn = kb0 + (i + 1 - m1 * nk);
-            blk_load<F>(nxtA, rowA[m1], kbn, c.t, c.nb);
-            blk_load<F>(nxtB, rowB[m1], kbn, c.t, c.nb);
+            tile_load<F, false>(nxtA, nxtB, tb[m1] + (size_t)kbn * F::kTile, c.g, c.t);
         }
         float dA, dB;
         blk_compute<F, NV>(curA, curB, kb, c, dA, dB);

@@ -180,7 +180,7 @@ struct MoeStage {
     const int32_t* ids;        // [P] expert of pair p
     const uint8_t* const* w;   // [E] expert matrix (gate or down), GPU layout
     const uint8_t* const* w2;  // [E] up matrix (fused stage)
-    long long row_stride;
+    long long row_stride;  // bytes per 16-row tile of the tile-major layout
     int M, K;
     const float* x;  // rows: token (x_div = top_k) or pair (x_div = 1)
     int x_div, ldx;
@@ -235,15 +235,13 @@ __global__ void __launch_bounds__(256) moe_gemv_kernel(MoeStage s) {
 #pragma unroll
         for (int mt = 0; mt < kMats; ++mt) yA[mt] = yB[mt] = 0.f;
         if (tile < ntiles) {
-            const size_t rA = (size_t)min(r0 + tile * 16 + g, r1 - 1), rB = (size_t)min(r0 + tile * 16 + g + 8, r1 - 1);
+            const size_t toff = (size_t)(r0 / 16 + tile) * s.row_stride;  // r0 is a multiple of 16
             if constexpr (FUSED) {
-                const uint8_t* const pa[2] = {W + rA * s.row_stride, W2 + rA * s.row_stride};
-                const uint8_t* const pb[2] = {W + rB * s.row_stride, W2 + rB * s.row_stride};
-                stream_tile<F, 1, 2>(pa, pb, kb0, kb1, ctx, yA, yB);
+                const uint8_t* const tb[2] = {W + toff, W2 + toff};
+                stream_tile<F, 1, 2>(tb, kb0, kb1, ctx, yA, yB);
             } else {
-                const uint8_t* const pa[1] = {W + rA * s.row_stride};
-                const uint8_t* const pb[1] = {W + rB * s.row_stride};
-                stream_tile<F, 1, 1>(pa, pb, kb0, kb1, ctx, yA, yB);
+                const uint8_t* const tb[1] = {W + toff};
+                stream_tile<F, 1, 1>(tb, kb0, kb1, ctx, yA, yB);
             }
         }
         if (t == 0) {

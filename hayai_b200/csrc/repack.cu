@@ -1,26 +1,34 @@
 // repack.cu -- one-time upload transform from raw GGUF rows to the GPU layouts.
 //
-// GGUF Q6_K (210 B) and Q8_0 (34 B) blocks are only 2-byte aligned inside a row, which
-// rules out 128-bit loads.  At upload the rows are rewritten (same byte count, or a
-// few bytes of padding per row) so that every lane of the tensor-core GEMV reads its
-// codes with 16-byte vector loads:
+// Q4_K, Q6_K and Q8_0 are stored tile-major: the matrix is cut into 16-row tiles, and the
+// 16 rows x one kernel block (256 elements; 128 for Q8_0) of a tile form one contiguous
+// "tile-block" image.  The blocks of a tile follow one another, so any run of blocks of a
+// tile is a single contiguous range: the GEMV moves a whole pipeline stage with one TMA
+// bulk copy per matrix.  Inside an image, every 16-byte piece a lane reads sits at
+// (4 * row + lane_in_group) * 16 within its region, so the 32 lanes of a warp read 32
+// consecutive pieces (conflict-free shared-memory reads) and 128-bit loads are always
+// aligned.  Rows past M are zero.
 //
-//  Q6_K row:  nb x 208 B {ql_perm[4][8 words] | qh_perm[4][4 words] | scales[16]}
-//             + d plane (nb f16, padded to 16 B).
-//             ql word (t, wq=4h+2qq+lh) = ql bytes 64h+32qq+16lh+4t..+3
-//             qh word (t, wh=2h+lh)     = qh bytes 32h+16lh+4t..+3
-//  Q8_0 row:  ng = ceil(nb/4) groups x 128 B {qs_perm[4][8 words]} + d plane (4 f16 per
-//             group, padded to 16 B).  word (t, w) = codes 16(w&1)+4t..+3 of block 4G+w/2;
-//             missing blocks of the last group are zero (d = 0).
-//  Q4_K, F32, IQ*: raw layout (Q4_K's 144 B blocks are already 16-byte aligned).
+//  Q4_K image (2304 B):  [hdr: row r at 16r, the block's first 16 bytes (d, dmin, scales)]
+//                        [q0: (r,t) at 256 + 16(4r+t) = qs bytes 32t..32t+15]
+//                        [q1: (r,t) at 1280 + 16(4r+t) = qs bytes 32t+16..32t+31]
+//  Q6_K image (3360 B):  [l0: (r,t) at 16(4r+t)][l1: at 1024 + 16(4r+t)][qh: at 2048 + 16(4r+t)]
+//                        [sc: row r at 3072 + 16r][d: row r at 3328 + 2r]
+//                        l0 word j (j < 4) of lane t / l1 word j: ql word wq = j / 4 + j of the
+//                        lane-t view, which holds ql bytes 64h + 32qq + 16lh + 4t..+3 for
+//                        wq = 4h + 2qq + lh; qh word wh = 2h + lh holds qh bytes 32h + 16lh + 4t..+3
+//  Q8_0 image (2176 B), one group = 4 GGUF blocks = 128 elements:
+//                        [q0: (r,t) at 16(4r+t)][q1: at 1024 + 16(4r+t)][d: row r at 2048 + 8r]
+//                        word wi of lane t (q0: wi < 4, q1: wi - 4) = codes 16(wi & 1) + 4t..+3 of
+//                        block 4G + wi / 2; d = the group's 4 f16 scales; missing blocks are zero.
+//  F32, IQ*: raw GGUF rows.
 //
-// Layout of the GGUF blocks: q6k.rs:26-57 (ql/qh/scales/d), quant.rs:598-615 (Q8_0).
+// Layout of the GGUF blocks: q4k.rs:11-43 (Q4_K), q6k.rs:26-57 (ql/qh/scales/d),
+// quant.rs:598-615 (Q8_0).
 #include "common.cuh"
 #include "gemv_launch.h"
 
 namespace hc {
-
-static inline size_t pad16(size_t b) { return (b + 15) / 16 * 16; }
 
 size_t raw_row_bytes(int type, int K) {
     switch (type) {
@@ -37,96 +45,127 @@ size_t raw_row_bytes(int type, int K) {
     }
 }
 
-size_t gpu_row_stride(int type, int K) {
-    if (type == T_Q6_K) {
-        const size_t nb = (size_t)K / 256;
-        return nb * 208 + pad16(nb * 2);
+bool tiled_type(int type) { return type == T_Q4_K || type == T_Q6_K || type == T_Q8_0; }
+
+size_t tile_block_bytes(int type) {
+    switch (type) {
+        case T_Q4_K: return 2304;
+        case T_Q6_K: return 3360;
+        case T_Q8_0: return 2176;
+        default: return 0;
     }
-    if (type == T_Q8_0) {
-        const size_t ng = ((size_t)K / 32 + 3) / 4;
-        return ng * 128 + pad16(ng * 8);
-    }
+}
+
+// kernel blocks per row: 256-element super-blocks, or 128-element groups for Q8_0
+static size_t kernel_blocks(int type, int K) {
+    return type == T_Q8_0 ? ((size_t)K / 32 + 3) / 4 : (size_t)K / 256;
+}
+
+size_t gpu_stride(int type, int K) {
+    if (tiled_type(type)) return kernel_blocks(type, K) * tile_block_bytes(type);
     return raw_row_bytes(type, K);
+}
+
+size_t gpu_weight_bytes(int type, int M, int K) {
+    if (tiled_type(type)) return (size_t)((M + 15) / 16) * gpu_stride(type, K);
+    return (size_t)M * raw_row_bytes(type, K);
 }
 
 __device__ __forceinline__ uint32_t rd4(const uint8_t* p) {
     return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
 }
+__device__ __forceinline__ uint32_t rd2(const uint8_t* p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
 
-// one thread per destination 32-bit word of the block area, plus one per d entry
-__global__ void repack_q6k_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ gpu, int M, int nb,
-                                  size_t raw_rb, size_t gpu_rb) {
-    const size_t total = (size_t)M * nb * 53;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const int w = (int)(i % 53);
-        const size_t rb = i / 53;
-        const int b = (int)(rb % nb);
-        const size_t row = rb / nb;
-        const uint8_t* src = raw + row * raw_rb + (size_t)b * 210;
-        uint8_t* dst = gpu + row * gpu_rb + (size_t)b * 208;
-        if (w < 32) {
-            const int t = w >> 3, wq = w & 7, h = wq >> 2, qq = (wq >> 1) & 1, lh = wq & 1;
-            *reinterpret_cast<uint32_t*>(dst + 32 * t + 4 * wq) = rd4(src + 64 * h + 32 * qq + 16 * lh + 4 * t);
-        } else if (w < 48) {
-            const int j = w - 32, t = j >> 2, wh = j & 3, h = wh >> 1, lh = wh & 1;
-            *reinterpret_cast<uint32_t*>(dst + 128 + 16 * t + 4 * wh) = rd4(src + 128 + 32 * h + 16 * lh + 4 * t);
-        } else if (w < 52) {
-            const int j = w - 48;
-            *reinterpret_cast<uint32_t*>(dst + 192 + 4 * j) = rd4(src + 192 + 4 * j);
+// One thread per 32-bit word of the tiled image.  Word w of tile-block (tile, kb); the
+// source row is tile * 16 + r (zero when >= M).
+template <int kType>
+__device__ __forceinline__ uint32_t tiled_word(const uint8_t* __restrict__ raw, size_t raw_rb, int M, int nb, int tile,
+                                               int kb, int w) {
+    if constexpr (kType == T_Q4_K) {
+        int r, off;
+        if (w < 64) {
+            r = w >> 2;
+            off = 4 * (w & 3);
         } else {
-            uint8_t* dp = gpu + row * gpu_rb + (size_t)nb * 208 + 2 * b;
-            dp[0] = src[208];
-            dp[1] = src[209];
+            const int q = w >= 320, p = (w - (q ? 320 : 64)) >> 2, j = w & 3, t = p & 3;
+            r = p >> 2;
+            off = 16 + 32 * t + 16 * q + 4 * j;
         }
+        const int row = tile * 16 + r;
+        return row < M ? rd4(raw + (size_t)row * raw_rb + (size_t)kb * 144 + off) : 0u;
+    } else if constexpr (kType == T_Q6_K) {
+        if (w >= 832) {  // d of rows 2k, 2k+1
+            const int k = w - 832;
+            uint32_t v = 0;
+            for (int h = 0; h < 2; ++h) {
+                const int row = tile * 16 + 2 * k + h;
+                if (row < M) v |= rd2(raw + (size_t)row * raw_rb + (size_t)kb * 210 + 208) << (16 * h);
+            }
+            return v;
+        }
+        int r, off;
+        if (w < 768) {
+            const int reg = w >> 8, p = (w & 255) >> 2, j = w & 3, t = p & 3;
+            r = p >> 2;
+            if (reg < 2) {
+                const int wq = 4 * reg + j, h = wq >> 2, qq = (wq >> 1) & 1, lh = wq & 1;
+                off = 64 * h + 32 * qq + 16 * lh + 4 * t;
+            } else {
+                const int h = j >> 1, lh = j & 1;
+                off = 128 + 32 * h + 16 * lh + 4 * t;
+            }
+        } else {
+            r = (w - 768) >> 2;
+            off = 192 + 4 * (w & 3);
+        }
+        const int row = tile * 16 + r;
+        return row < M ? rd4(raw + (size_t)row * raw_rb + (size_t)kb * 210 + off) : 0u;
+    } else {  // Q8_0, kb = group of 4 blocks
+        if (w >= 512) {  // d: row r = k / 2, blocks 4G + 2(k & 1) + {0, 1}
+            const int k = w - 512, row = tile * 16 + (k >> 1);
+            uint32_t v = 0;
+            for (int h = 0; h < 2; ++h) {
+                const int blk = 4 * kb + 2 * (k & 1) + h;
+                if (row < M && blk < nb) v |= rd2(raw + (size_t)row * raw_rb + (size_t)blk * 34) << (16 * h);
+            }
+            return v;
+        }
+        const int q = w >= 256, p = (w & 255) >> 2, j = w & 3, t = p & 3, r = p >> 2;
+        const int wi = 4 * q + j, blk = 4 * kb + (wi >> 1), half = wi & 1;
+        const int row = tile * 16 + r;
+        return (row < M && blk < nb) ? rd4(raw + (size_t)row * raw_rb + (size_t)blk * 34 + 2 + 16 * half + 4 * t)
+                                     : 0u;
     }
 }
 
-__global__ void repack_q80_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ gpu, int M, int nb, int ng,
-                                  size_t raw_rb, size_t gpu_rb) {
-    const size_t total = (size_t)M * ng * 36;
+template <int kType>
+__global__ void repack_tiled_kernel(const uint8_t* __restrict__ raw, uint32_t* __restrict__ gpu, int M, int nb,
+                                    int nkb, size_t raw_rb, int words) {
+    const int ntiles = (M + 15) / 16;
+    const size_t total = (size_t)ntiles * nkb * words;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const int w = (int)(i % 36);
-        const size_t rg = i / 36;
-        const int G = (int)(rg % ng);
-        const size_t row = rg / ng;
-        const uint8_t* srow = raw + row * raw_rb;
-        uint8_t* drow = gpu + row * gpu_rb;
-        if (w < 32) {
-            const int t = w >> 3, wi = w & 7, blk = 4 * G + (wi >> 1), half = wi & 1;
-            uint32_t v = 0;
-            if (blk < nb) v = rd4(srow + (size_t)blk * 34 + 2 + 16 * half + 4 * t);
-            *reinterpret_cast<uint32_t*>(drow + (size_t)G * 128 + 32 * t + 4 * wi) = v;
-        } else {
-            const int blk = 4 * G + (w - 32);
-            uint8_t* dp = drow + (size_t)ng * 128 + 2 * blk;
-            dp[0] = blk < nb ? srow[(size_t)blk * 34] : 0;
-            dp[1] = blk < nb ? srow[(size_t)blk * 34 + 1] : 0;
-        }
+        const int w = (int)(i % words);
+        const size_t tb = i / words;
+        const int kb = (int)(tb % nkb), tile = (int)(tb / nkb);
+        gpu[i] = tiled_word<kType>(raw, raw_rb, M, nb, tile, kb, w);
     }
 }
 
 cudaError_t launch_repack(int type, const uint8_t* raw, uint8_t* gpu, int M, int K, cudaStream_t stream) {
-    const size_t rrb = raw_row_bytes(type, K), grb = gpu_row_stride(type, K);
-    if (type == T_Q6_K) {
-        const int nb = K / 256;
-        // zero the d-plane padding first
-        cudaError_t e = cudaMemsetAsync(gpu, 0, (size_t)M * grb, stream);
-        if (e != cudaSuccess) return e;
-        const size_t total = (size_t)M * nb * 53;
-        const unsigned blocks = (unsigned)((total + 255) / 256 < 65535 * 8 ? (total + 255) / 256 : 65535 * 8);
-        repack_q6k_kernel<<<blocks, 256, 0, stream>>>(raw, gpu, M, nb, rrb, grb);
-        return cudaGetLastError();
+    const size_t rrb = raw_row_bytes(type, K);
+    if (!tiled_type(type)) return cudaMemcpyAsync(gpu, raw, (size_t)M * rrb, cudaMemcpyDeviceToDevice, stream);
+    const int nb = type == T_Q8_0 ? K / 32 : K / 256;
+    const int nkb = (int)kernel_blocks(type, K);
+    const int words = (int)(tile_block_bytes(type) / 4);
+    const size_t total = (size_t)((M + 15) / 16) * nkb * words;
+    const unsigned blocks = (unsigned)((total + 255) / 256 < 65535 * 8 ? (total + 255) / 256 : 65535 * 8);
+    uint32_t* out = reinterpret_cast<uint32_t*>(gpu);
+    switch (type) {
+        case T_Q4_K: repack_tiled_kernel<T_Q4_K><<<blocks, 256, 0, stream>>>(raw, out, M, nb, nkb, rrb, words); break;
+        case T_Q6_K: repack_tiled_kernel<T_Q6_K><<<blocks, 256, 0, stream>>>(raw, out, M, nb, nkb, rrb, words); break;
+        default: repack_tiled_kernel<T_Q8_0><<<blocks, 256, 0, stream>>>(raw, out, M, nb, nkb, rrb, words); break;
     }
-    if (type == T_Q8_0) {
-        const int nb = K / 32, ng = (nb + 3) / 4;
-        cudaError_t e = cudaMemsetAsync(gpu, 0, (size_t)M * grb, stream);
-        if (e != cudaSuccess) return e;
-        const size_t total = (size_t)M * ng * 36;
-        const unsigned blocks = (unsigned)((total + 255) / 256 < 65535 * 8 ? (total + 255) / 256 : 65535 * 8);
-        repack_q80_kernel<<<blocks, 256, 0, stream>>>(raw, gpu, M, nb, ng, rrb, grb);
-        return cudaGetLastError();
-    }
-    return cudaMemcpyAsync(gpu, raw, (size_t)M * rrb, cudaMemcpyDeviceToDevice, stream);
+    return cudaGetLastError();
 }
 
 }  // namespace hc

@@ -22,13 +22,13 @@
 
 namespace hc {
 
-// Layout of the per-CTA shared memory: [xt table][Sx (Q4_K)][Q4_K scale LUT][reduction]
+// Layout of the per-CTA shared memory: [xt table][zero block][Sx (Q4_K)][reduction]
 struct GemvSmem {
     int table_bytes;
+    int zero_bytes;  // one zeroed block of table entries (B fragments of empty columns)
     int sx_bytes;
-    int lut_bytes;
     int red_bytes;
-    __host__ __device__ int total() const { return table_bytes + sx_bytes + lut_bytes + red_bytes; }
+    __host__ __device__ int total() const { return table_bytes + zero_bytes + sx_bytes + red_bytes; }
 };
 
 struct GemvArgs {
@@ -68,6 +68,13 @@ struct FmtQ4K {
     // byte p = 32t + 4wi + j of qs; low nibble -> 64t + 4wi + j, high -> +32
     __device__ static int base(int mi, int t) { return 64 * t + 4 * (mi >> 1) + 32 * (mi & 1); }
     static constexpr bool kNeedSx = true;
+    // table slot (within a block) of the hi part of MMA mi = 2 wi + nib, vector v, lane t:
+    // the lo- and hi-nibble fragments of one word sit side by side (one 128-bit load)
+    template <int NV>
+    __device__ static int tab(int mi, int v, int t) {
+        return (((mi >> 1) * 2 * NV + 2 * v) * 4 + t) * 2 + (mi & 1);
+    }
+    static constexpr int kLoOff = 8;  // lo part of the same slot
 };
 
 struct FmtQ6K {
@@ -81,6 +88,11 @@ struct FmtQ6K {
         return 128 * h + 32 * q + 16 * lh + 4 * t;
     }
     static constexpr bool kNeedSx = false;
+    template <int NV>
+    __device__ static int tab(int mi, int v, int t) {
+        return (mi * 2 * NV + 2 * v) * 4 + t;
+    }
+    static constexpr int kLoOff = 4;
 };
 
 // Q8_0 kernels work on groups of 4 Q8_0 blocks (128 elements, 8 MMAs); mi = 2*blk + half.
@@ -91,6 +103,11 @@ struct FmtQ80 {
     static constexpr int kMmaPerBlock = 8;
     __device__ static int base(int mi, int t) { return 16 * mi + 4 * t; }
     static constexpr bool kNeedSx = false;
+    template <int NV>
+    __device__ static int tab(int mi, int v, int t) {
+        return (mi * 2 * NV + 2 * v) * 4 + t;
+    }
+    static constexpr int kLoOff = 4;
 };
 
 template <class F>
@@ -104,8 +121,8 @@ __host__ __device__ inline GemvSmem gemv_smem_layout(int K, int nv, bool fused) 
     GemvSmem s;
     int nb = (K + F::kBlockElems - 1) / F::kBlockElems;
     s.table_bytes = nb * table_entries_per_block<F>(nv) * 8;
+    s.zero_bytes = table_entries_per_block<F>(nv) * 8;
     s.sx_bytes = F::kNeedSx ? ((nv * (K / 32) * 4 + 15) / 16) * 16 : 0;
-    s.lut_bytes = F::kType == T_Q4_K ? 64 * 2 * 8 : 0;
     s.red_bytes = 8 * 16 * nv * 4 * (fused ? 2 : 1);
     return s;
 }

@@ -123,9 +123,9 @@ __device__ void build_prologue(uint2* __restrict__ xt, float* __restrict__ sx, c
                 const int e = 4 * c, kb = e / F::kBlockElems;
                 int mi, t;
                 inv_map<F>(e - kb * F::kBlockElems, mi, t);
-                const int base = ((kb * F::kMmaPerBlock + mi) * 2 * NV + 2 * v) * 4 + t;
+                const int base = kb * table_entries_per_block<F>(NV) + F::template tab<NV>(mi, v, t);
                 xt[base] = make_uint2(h2_as_u32(__halves2half2(hi[0], hi[2])), h2_as_u32(__halves2half2(hi[1], hi[3])));
-                xt[base + 4] =
+                xt[base + F::kLoOff] =
                     make_uint2(h2_as_u32(__halves2half2(lo[0], lo[2])), h2_as_u32(__halves2half2(lo[1], lo[3])));
             }
             if constexpr (F::kNeedSx) {
@@ -147,140 +147,103 @@ __device__ void build_prologue(uint2* __restrict__ xt, float* __restrict__ sx, c
     build_prologue<F, NV>(xt, sx, x, ldx, K, nvec, nrm, scratch, err, (int)blockDim.x, 0);
 }
 
-// Q4_K scale LUT: [sc] -> {mul (sc,sc), add (-1024 sc)} for low nibbles (value 1024+n),
-// [64+sc] -> {mul (sc/16), add (-64 sc)} for high nibbles (value 1024+16n).  All exact in f16.
-__device__ inline void build_q4k_lut(uint2* lut) {
-    for (int i = threadIdx.x; i < 64; i += blockDim.x) {
-        const float sc = (float)i;
-        lut[i] = make_uint2(pack_h2(sc, sc), pack_h2(-1024.f * sc, -1024.f * sc));
-        lut[64 + i] = make_uint2(pack_h2(sc * 0.0625f, sc * 0.0625f), pack_h2(-64.f * sc, -64.f * sc));
-    }
-}
-
-// Per-lane context of the main loop.
+// Per-lane context of the main loop.  The B fragments of kernel block kb are read at
+// xb0 + kb * xstride; a lane whose B columns are zero for the format (no vector there, or
+// a Q4_K column owned by another lane) points at a zeroed block of the table instead
+// (xstride 0), so every fragment load is unconditional.
 template <int NV>
 struct LaneCtx {
-    const uint2* xt;   // table + g*4 + t
-    const float* sx;   // Q4_K sub-block sums
-    const uint2* lut;  // Q4_K scale LUT
-    int sxs;           // Q4_K: K/32
-    int nb;            // kernel blocks per row (Q6_K/Q8_0: d plane offset)
+    const uint2* xb0;
+    int xstride;      // table entries per kernel block, or 0
+    const float* sx;  // Q4_K sub-block sums
+    int sxs;          // Q4_K: K/32
     int g, t;
-    bool has_b;
 };
 
-// ------------------------------------------------------------------ Q4_K
-// 6-bit (scale, min) pairs of sub-blocks 2t and 2t+1 (get_scale_min_k4, q4k.rs:34-43),
-// from the 12 scale bytes held in h.y, h.z, h.w.
-__device__ __forceinline__ void q4k_scales(const uint4& h, int t, int& sc0, int& m0, int& sc1, int& m1) {
-    const int sh = 16 * (t & 1);
-    const uint32_t Y = h.y >> sh, Z = h.z >> sh, W = h.w >> sh;
-    if (t < 2) {
-        sc0 = Y & 63;
-        m0 = Z & 63;
-        sc1 = (Y >> 8) & 63;
-        m1 = (Z >> 8) & 63;
+// Lane context for format F: xt = fragment table, zero = a zeroed block of it.
+template <class F, int NV>
+__device__ __forceinline__ LaneCtx<NV> make_ctx(const uint2* xt, const uint2* zero, const float* sx, int K, int lane) {
+    LaneCtx<NV> c;
+    c.g = lane >> 2;
+    c.t = lane & 3;
+    c.sx = sx;
+    c.sxs = K / 32;
+    int off;
+    bool live;
+    if constexpr (F::kType == T_Q4_K) {
+        off = ((c.g & 1) * 4 + c.t) * 2;  // part g&1 of owner lane g>>1, lane t
+        live = (c.g >> 1) == c.t;
     } else {
-        sc0 = (W & 0xF) | ((Y >> 2) & 0x30);
-        m0 = ((W >> 4) & 0xF) | ((Z >> 2) & 0x30);
-        sc1 = ((W >> 8) & 0xF) | ((Y >> 10) & 0x30);
-        m1 = ((W >> 12) & 0xF) | ((Z >> 10) & 0x30);
+        off = c.g * 4 + c.t;
+        live = c.g < 2 * NV;
+        if (!live) off = c.t;
     }
+    c.xb0 = (live ? xt : zero) + off;
+    c.xstride = live ? table_entries_per_block<F>(NV) : 0;
+    return c;
 }
 
+// ------------------------------------------------------------------ Q4_K
 struct Q4KBlk {
     uint4 h, q0, q1;
 };
 
-// Contribution of one super-block to rows g (dA) and g+8 (dB), for vector t (lanes t < NV).
-template <int NV>
-__device__ __forceinline__ void q4k_block(const Q4KBlk& A, const Q4KBlk& B, int kb, const LaneCtx<NV>& c,
-                                          float& dA, float& dB) {
-    constexpr int kEnt = 16 * 2 * NV * 4;
-    const int t = c.t;
-    int scA0, mA0, scA1, mA1, scB0, mB0, scB1, mB1;
-    q4k_scales(A.h, t, scA0, mA0, scA1, mA1);
-    q4k_scales(B.h, t, scB0, mB0, scB1, mB1);
-    const uint2 loA = c.lut[scA0], hiA = c.lut[64 + scA1], loB = c.lut[scB0], hiB = c.lut[64 + scB1];
-    const uint2* xb = c.xt + kb * kEnt;
-    const uint32_t wA[8] = {A.q0.x, A.q0.y, A.q0.z, A.q0.w, A.q1.x, A.q1.y, A.q1.z, A.q1.w};
-    const uint32_t wB[8] = {B.q0.x, B.q0.y, B.q0.z, B.q0.w, B.q1.x, B.q1.y, B.q1.z, B.q1.w};
-    // two accumulator chains (low / high nibbles) halve the dependent MMA latency
-    float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int wi = 0; wi < 8; ++wi) {
-        const uint32_t a = wA[wi], b = wB[wi], a8 = a >> 8, b8 = b >> 8;
-        const uint2 fl = c.has_b ? xb[(2 * wi) * (2 * NV * 4)] : make_uint2(0u, 0u);
-        const uint2 fh = c.has_b ? xb[(2 * wi + 1) * (2 * NV * 4)] : make_uint2(0u, 0u);
-        mma16816(acc, hfma2_u32(lop3_and_or(a, 0x000F000Fu, 0x64006400u), loA.x, loA.y),
-                 hfma2_u32(lop3_and_or(b, 0x000F000Fu, 0x64006400u), loB.x, loB.y),
-                 hfma2_u32(lop3_and_or(a8, 0x000F000Fu, 0x64006400u), loA.x, loA.y),
-                 hfma2_u32(lop3_and_or(b8, 0x000F000Fu, 0x64006400u), loB.x, loB.y), fl.x, fl.y);
-        mma16816(acc2, hfma2_u32(lop3_and_or(a, 0x00F000F0u, 0x64006400u), hiA.x, hiA.y),
-                 hfma2_u32(lop3_and_or(b, 0x00F000F0u, 0x64006400u), hiB.x, hiB.y),
-                 hfma2_u32(lop3_and_or(a8, 0x00F000F0u, 0x64006400u), hiA.x, hiA.y),
-                 hfma2_u32(lop3_and_or(b8, 0x00F000F0u, 0x64006400u), hiB.x, hiB.y), fh.x, fh.y);
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) acc[i] += acc2[i];
-    const float2 ddA = __half22float2(u32_as_h2(A.h.x));
-    const float2 ddB = __half22float2(u32_as_h2(B.h.x));
-    float mpA = 0.f, mpB = 0.f;
-#pragma unroll
-    for (int v = 0; v < NV; ++v) {
-        const float s0 = c.sx[v * c.sxs + kb * 8 + 2 * t], s1 = c.sx[v * c.sxs + kb * 8 + 2 * t + 1];
-        float pa = (float)mA0 * s0 + (float)mA1 * s1;
-        float pb = (float)mB0 * s0 + (float)mB1 * s1;
-        pa += __shfl_xor_sync(kFull, pa, 1);
-        pb += __shfl_xor_sync(kFull, pb, 1);
-        pa += __shfl_xor_sync(kFull, pa, 2);
-        pb += __shfl_xor_sync(kFull, pb, 2);
-        if (t == v) {
-            mpA = pa;
-            mpB = pb;
-        }
-    }
-    dA = ddA.x * (acc[0] + acc[1] * kLoScale) - ddA.y * mpA;
-    dB = ddB.x * (acc[2] + acc[3] * kLoScale) - ddB.y * mpB;
+// Q4_K (sc, m) of sub-blocks 2t, 2t+1 of one row, folded into the per-sub-block factors
+// c = 64 d sc and k = c + dmin m (branch-free over t: t < 2 reads the plain 6-bit fields,
+// t >= 2 the split ones).
+__device__ __forceinline__ void q4k_factors(const uint4& h, int t, float& c0, float& k0, float& c1, float& k1) {
+    const int sh = 16 * (t & 1);
+    const uint32_t Y = h.y >> sh, Z = h.z >> sh, W = h.w >> sh;
+    const uint32_t psc = t < 2 ? (Y & 0x3F3Fu) : ((W & 0x0F0Fu) | ((Y >> 2) & 0x3030u));
+    const uint32_t pm = t < 2 ? (Z & 0x3F3Fu) : (((W >> 4) & 0x0F0Fu) | ((Z >> 2) & 0x3030u));
+    const float2 dd = __half22float2(u32_as_h2(h.x));
+    const float d64 = 64.f * dd.x;
+    c0 = d64 * (float)(psc & 0xFFu);
+    c1 = d64 * (float)(psc >> 8);
+    k0 = fmaf(dd.y, (float)(pm & 0xFFu), c0);
+    k1 = fmaf(dd.y, (float)(pm >> 8), c1);
 }
 
-// Q4_K, scale-per-lane variant.  Lane t's codes are chunk t of the super-block: the low
-// nibbles are sub-block 2t, the high nibbles sub-block 2t+1.  B holds lane t's x only in
-// columns 2t (hi part) and 2t+1 (lo part), so in every MMA lane t's k-slots meet only its
-// own columns and the accumulator comes back per sub-block, already distributed over the
-// lanes: C[row][2t] = sum over sub-block (2t+G) of A * x_hi.  Codes enter as
+// One Q4_K unit, lane-distributed sub-blocks.  Lane t's codes are chunk t of the super-block
+// (q0, q1): the low nibbles are sub-block 2t, the high nibbles sub-block 2t+1.  B holds lane
+// t's x only in columns 2t (hi part) and 2t+1 (lo part), so in every MMA lane t's k-slots
+// meet only its own columns and the accumulator comes back per sub-block, already spread
+// over the lanes: C[row][2t] = sum over the sub-block of A * x_hi.  Codes enter as
 // f16(1 + n/64) (magic 0x3C00, nibble at bits 4-7: one LOP3 per two codes), so
 //     sum n*x = 64 * (C - Sx_j)
-// and the 6-bit scale, d, dmin and the min term are applied once per sub-block per lane in
-// f32.  pA/pB receive lane t's share of rows g / g+8 (summed over t at the end of a tile).
-template <int NV, int NMAT>
-__device__ __forceinline__ void q4k_unit_dist(const Q4KBlk (&A)[NMAT], const Q4KBlk (&B)[NMAT], int kb,
-                                              const LaneCtx<NV>& c, float (&pA)[NMAT][NV], float (&pB)[NMAT][NV]) {
-    constexpr int kEnt = 16 * 2 * NV * 4;  // table entries of one super-block
-    const int t = c.t, g = c.g;
-    const bool mine = (g >> 1) == t;
-    // entry ((mma * 2NV + 2v + part) * 4 + t); c.xt points at g*4 + t, rebase to part*4 + t
-    const uint2* xb = c.xt - g * 4 + (g & 1) * 4 + kb * kEnt;
-    float acc[NMAT][NV][2][4];
+// and the 6-bit scale, d, dmin and the min term (get_scale_min_k4, q4k.rs:34-43; the
+// dequantisation q4k.rs:206-256) are applied once per sub-block per lane in f32.  pA/pB
+// receive lane t's share of rows g / g+8 of each of the NMAT matrices (the caller sums the
+// shares over t).  The table holds, per 8-code word wi, the lo-nibble and hi-nibble B
+// fragments side by side, so one 128-bit load feeds both MMAs of every matrix.
+template <int NV, int NMAT, bool SHARE_B = true>
+__device__ __forceinline__ void q4k_unit(const Q4KBlk (&A)[NMAT], const Q4KBlk (&B)[NMAT], const int (&kbs)[NMAT],
+                                         const LaneCtx<NV>& c, float (&pA)[NMAT][NV], float (&pB)[NMAT][NV]) {
+    const uint4* xbm[NMAT];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) xbm[m] = reinterpret_cast<const uint4*>(c.xb0 + kbs[SHARE_B ? 0 : m] * c.xstride);
+    float lo[NMAT][NV][4], hi[NMAT][NV][4];
 #pragma unroll
     for (int m = 0; m < NMAT; ++m)
 #pragma unroll
         for (int v = 0; v < NV; ++v)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) acc[m][v][0][i] = acc[m][v][1][i] = 0.f;
+            for (int i = 0; i < 4; ++i) lo[m][v][i] = hi[m][v][i] = 0.f;
 #pragma unroll
     for (int wi = 0; wi < 8; ++wi) {
-        uint2 blo[NV], bhi[NV];
+        uint4 f[NMAT][NV];
 #pragma unroll
-        for (int v = 0; v < NV; ++v) {
-            blo[v] = mine ? xb[((2 * wi) * 2 * NV + 2 * v) * 4] : make_uint2(0u, 0u);
-            bhi[v] = mine ? xb[((2 * wi + 1) * 2 * NV + 2 * v) * 4] : make_uint2(0u, 0u);
-        }
+        for (int m = 0; m < (SHARE_B ? 1 : NMAT); ++m)
+#pragma unroll
+            for (int v = 0; v < NV; ++v) f[m][v] = xbm[m][(wi * 2 * NV + 2 * v) * 4];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
-            const uint32_t qa[8] = {A[m].q0.x, A[m].q0.y, A[m].q0.z, A[m].q0.w, A[m].q1.x, A[m].q1.y, A[m].q1.z, A[m].q1.w};
-            const uint32_t qb[8] = {B[m].q0.x, B[m].q0.y, B[m].q0.z, B[m].q0.w, B[m].q1.x, B[m].q1.y, B[m].q1.z, B[m].q1.w};
-            const uint32_t a = qa[wi], b = qb[wi];
+            const int fm = SHARE_B ? 0 : m;
+            const uint32_t wA[8] = {A[m].q0.x, A[m].q0.y, A[m].q0.z, A[m].q0.w,
+                                    A[m].q1.x, A[m].q1.y, A[m].q1.z, A[m].q1.w};
+            const uint32_t wB[8] = {B[m].q0.x, B[m].q0.y, B[m].q0.z, B[m].q0.w,
+                                    B[m].q1.x, B[m].q1.y, B[m].q1.z, B[m].q1.w};
+            const uint32_t a = wA[wi], b = wB[wi];
             const uint32_t lo02a = lop3_and_or(a << 4, 0x00F000F0u, 0x3C003C00u);
             const uint32_t lo13a = lop3_and_or(a >> 4, 0x00F000F0u, 0x3C003C00u);
             const uint32_t hi02a = lop3_and_or(a, 0x00F000F0u, 0x3C003C00u);
@@ -291,29 +254,26 @@ __device__ __forceinline__ void q4k_unit_dist(const Q4KBlk (&A)[NMAT], const Q4K
             const uint32_t hi13b = lop3_and_or(b >> 8, 0x00F000F0u, 0x3C003C00u);
 #pragma unroll
             for (int v = 0; v < NV; ++v) {
-                mma16816(acc[m][v][0], lo02a, lo02b, lo13a, lo13b, blo[v].x, blo[v].y);
-                mma16816(acc[m][v][1], hi02a, hi02b, hi13a, hi13b, bhi[v].x, bhi[v].y);
+                mma16816(lo[m][v], lo02a, lo02b, lo13a, lo13b, f[fm][v].x, f[fm][v].y);
+                mma16816(hi[m][v], hi02a, hi02b, hi13a, hi13b, f[fm][v].z, f[fm][v].w);
             }
         }
     }
 #pragma unroll
     for (int m = 0; m < NMAT; ++m) {
-        int scA0, mA0, scA1, mA1, scB0, mB0, scB1, mB1;
-        q4k_scales(A[m].h, t, scA0, mA0, scA1, mA1);
-        q4k_scales(B[m].h, t, scB0, mB0, scB1, mB1);
-        const float2 ddA = __half22float2(u32_as_h2(A[m].h.x));  // (d, dmin)
-        const float2 ddB = __half22float2(u32_as_h2(B[m].h.x));
-        const float cA0 = 64.f * ddA.x * (float)scA0, cA1 = 64.f * ddA.x * (float)scA1;
-        const float cB0 = 64.f * ddB.x * (float)scB0, cB1 = 64.f * ddB.x * (float)scB1;
-        const float kA0 = cA0 + ddA.y * (float)mA0, kA1 = cA1 + ddA.y * (float)mA1;
-        const float kB0 = cB0 + ddB.y * (float)mB0, kB1 = cB1 + ddB.y * (float)mB1;
+        const int kb = kbs[SHARE_B ? 0 : m];
+        float2 s[NV];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) s[v] = *reinterpret_cast<const float2*>(c.sx + v * c.sxs + kb * 8 + 2 * c.t);
+        float cA0, kA0, cA1, kA1, cB0, kB0, cB1, kB1;
+        q4k_factors(A[m].h, c.t, cA0, kA0, cA1, kA1);
+        q4k_factors(B[m].h, c.t, cB0, kB0, cB1, kB1);
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
-            const float s0 = c.sx[v * c.sxs + kb * 8 + 2 * t], s1 = c.sx[v * c.sxs + kb * 8 + 2 * t + 1];
-            const float* a0 = acc[m][v][0];
-            const float* a1 = acc[m][v][1];
-            pA[m][v] += cA0 * (a0[0] + a0[1] * kLoScale) - s0 * kA0 + cA1 * (a1[0] + a1[1] * kLoScale) - s1 * kA1;
-            pB[m][v] += cB0 * (a0[2] + a0[3] * kLoScale) - s0 * kB0 + cB1 * (a1[2] + a1[3] * kLoScale) - s1 * kB1;
+            pA[m][v] += cA0 * (lo[m][v][0] + lo[m][v][1] * kLoScale) - s[v].x * kA0 +
+                        cA1 * (hi[m][v][0] + hi[m][v][1] * kLoScale) - s[v].y * kA1;
+            pB[m][v] += cB0 * (lo[m][v][2] + lo[m][v][3] * kLoScale) - s[v].x * kB0 +
+                        cB1 * (hi[m][v][2] + hi[m][v][3] * kLoScale) - s[v].y * kB1;
         }
     }
 }
@@ -337,7 +297,6 @@ struct Q6KBlk {
 template <int NV>
 __device__ __forceinline__ void q6k_block(const Q6KBlk& A, const Q6KBlk& B, int kb, const LaneCtx<NV>& c,
                                           float& dA, float& dB) {
-    constexpr int kEnt = 16 * 2 * NV * 4;
     const uint32_t kOff = 0x64206420u;  // (1056, 1056) in f16: 1024 magic + 32 code offset
     const float fdA = h2f(A.d), fdB = h2f(B.d);
     const uint32_t LA[8] = {A.l0.x, A.l0.y, A.l0.z, A.l0.w, A.l1.x, A.l1.y, A.l1.z, A.l1.w};
@@ -346,7 +305,7 @@ __device__ __forceinline__ void q6k_block(const Q6KBlk& A, const Q6KBlk& B, int 
     const uint32_t QHB[4] = {B.qh.x, B.qh.y, B.qh.z, B.qh.w};
     const uint32_t SA[4] = {A.sc.x, A.sc.y, A.sc.z, A.sc.w};
     const uint32_t SB[4] = {B.sc.x, B.sc.y, B.sc.z, B.sc.w};
-    const uint2* xb = c.xt + kb * kEnt;
+    const uint2* xb = c.xb0 + kb * c.xstride;
     float sumA = 0.f, sumB = 0.f;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -364,7 +323,7 @@ __device__ __forceinline__ void q6k_block(const Q6KBlk& A, const Q6KBlk& B, int 
                 const uint32_t ua = lop3_and_or(q < 2 ? la : (la >> 4), 0x0F0F0F0Fu, qa[q]);
                 const uint32_t ub = lop3_and_or(q < 2 ? lb : (lb >> 4), 0x0F0F0F0Fu, qb[q]);
                 const int m = 8 * h + 4 * lh + q;
-                const uint2 f = c.has_b ? xb[m * (2 * NV * 4)] : make_uint2(0u, 0u);
+                const uint2 f = xb[m * (2 * NV * 4)];
                 float acc[4] = {0.f, 0.f, 0.f, 0.f};
                 mma16816(acc, hsub2_u32(prmt(ua, 0x64646464u, 0x4240u), kOff),
                          hsub2_u32(prmt(ub, 0x64646464u, 0x4240u), kOff),
@@ -392,7 +351,6 @@ struct Q80Blk {
 template <int NV>
 __device__ __forceinline__ void q80_block(const Q80Blk& A, const Q80Blk& B, int kg, const LaneCtx<NV>& c, float& dA,
                                           float& dB) {
-    constexpr int kEnt = 8 * 2 * NV * 4;
     const uint32_t kOff = 0x64806480u;  // (1152, 1152): 1024 magic + 128 sign flip
     const uint32_t WA[8] = {A.q0.x, A.q0.y, A.q0.z, A.q0.w, A.q1.x, A.q1.y, A.q1.z, A.q1.w};
     const uint32_t WB[8] = {B.q0.x, B.q0.y, B.q0.z, B.q0.w, B.q1.x, B.q1.y, B.q1.z, B.q1.w};
@@ -400,7 +358,7 @@ __device__ __forceinline__ void q80_block(const Q80Blk& A, const Q80Blk& B, int 
     const float2 dB01 = __half22float2(u32_as_h2(B.d.x)), dB23 = __half22float2(u32_as_h2(B.d.y));
     const float fa[4] = {dA01.x, dA01.y, dA23.x, dA23.y};
     const float fb[4] = {dB01.x, dB01.y, dB23.x, dB23.y};
-    const uint2* xb = c.xt + kg * kEnt;
+    const uint2* xb = c.xb0 + kg * c.xstride;
     float sA = 0.f, sB = 0.f;
 #pragma unroll
     for (int blk = 0; blk < 4; ++blk) {
@@ -409,7 +367,7 @@ __device__ __forceinline__ void q80_block(const Q80Blk& A, const Q80Blk& B, int 
         for (int half = 0; half < 2; ++half) {
             const int w = 2 * blk + half;
             const uint32_t ua = WA[w] ^ 0x80808080u, ub = WB[w] ^ 0x80808080u;
-            const uint2 f = c.has_b ? xb[w * (2 * NV * 4)] : make_uint2(0u, 0u);
+            const uint2 f = xb[w * (2 * NV * 4)];
             mma16816(acc, hsub2_u32(prmt(ua, 0x64646464u, 0x4240u), kOff),
                      hsub2_u32(prmt(ub, 0x64646464u, 0x4240u), kOff),
                      hsub2_u32(prmt(ua, 0x64646464u, 0x4341u), kOff),
@@ -491,7 +449,27 @@ __device__ __forceinline__ void tile_load(typename BlkOf<F>::T& A, typename BlkO
 template <class F, int NV>
 __device__ __forceinline__ void blk_compute(const typename BlkOf<F>::T& A, const typename BlkOf<F>::T& B, int kb,
                                             const LaneCtx<NV>& c, float& dA, float& dB) {
-    if constexpr (F::kType == T_Q4_K) q4k_block<NV>(A, B, kb, c, dA, dB);
+    if constexpr (F::kType == T_Q4_K) {
+        float pa[1][NV], pb[1][NV];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) pa[0][v] = pb[0][v] = 0.f;
+        const Q4KBlk a1[1] = {A}, b1[1] = {B};
+        const int k1[1] = {kb};
+        q4k_unit<NV, 1>(a1, b1, k1, c, pa, pb);
+        dA = dB = 0.f;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            float sa = pa[0][v], sb = pb[0][v];
+            sa += __shfl_xor_sync(kFull, sa, 1);
+            sb += __shfl_xor_sync(kFull, sb, 1);
+            sa += __shfl_xor_sync(kFull, sa, 2);
+            sb += __shfl_xor_sync(kFull, sb, 2);
+            if (c.t == v) {
+                dA = sa;
+                dB = sb;
+            }
+        }
+    }
     else if constexpr (F::kType == T_Q6_K) q6k_block<NV>(A, B, kb, c, dA, dB);
     else q80_block<NV>(A, B, kb, c, dA, dB);
 }

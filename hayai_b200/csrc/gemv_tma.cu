@@ -28,11 +28,14 @@
 //
 // Compute.  Consumer warp w takes unit (matrix w / 8, block w % 8) of every stage of the
 // fused pair, or block w of every single-matrix stage; every warp waits for and releases
-// every stage in order (so no mbarrier phase can be mistaken for another).  Each warp
-// accumulates its share of the current tile in registers; at the tile's last stage the
-// consumer warps meet on a named barrier, warp 0 adds the per-warp partials in warp order
-// and finishes the tile (or, for a tile shared with the next CTA, stores its partial and
-// lets the last CTA to arrive finish it, adding CTA partials in CTA order).  All mbarrier
+// every stage in order (so no mbarrier phase can be mistaken for another).  Sixteen warps
+// (four per scheduler) keep enough independent MMA chains in flight.  Each warp
+// accumulates its share of the current tile in registers; at the tile's last stage it
+// drops the partial into the tile's shared-memory slot and counts itself in, without
+// waiting: the last warp to arrive adds the 16 partials in warp order and finishes the tile
+// (or, for a tile shared with the next CTA, stores its partial and lets the last CTA to
+// arrive finish it, adding CTA partials in CTA order).  A barrier at every tile end would
+// line all warps up behind the slowest unit and cost a third of the run time.  All mbarrier
 // waits are bounded: on expiry the kernel raises bit 1 of the error flag and skips the
 // remaining work.
 #include "gemv_launch.h"
@@ -41,46 +44,40 @@
 
 namespace hc {
 
-constexpr int kCW = 16;  // consumer warps = units per stage
+constexpr int kCW = 16;      // consumer warps
+constexpr int kUnits = 16;   // units per stage (one per consumer warp)
 constexpr int kTThreads = (kCW + 1) * 32;
 constexpr int kMaxStages = 8;
-constexpr int kBarTile = 1;  // named barrier: tile flush (consumers only)
 constexpr int kBarPro = 2;   // named barrier: prologue (consumers only)
+constexpr int kMaxTileSlots = kMaxStages + 2;
 
 // blocks per stage and matrix
-__host__ __device__ constexpr int stage_blocks(bool fused) { return fused ? kCW / 2 : kCW; }
+__host__ __device__ constexpr int stage_blocks(bool fused) { return fused ? kUnits / 2 : kUnits; }
 
 template <class F>
 __host__ __device__ constexpr int tma_stage_bytes(bool fused) {
-    return kCW * F::kTile;  // one tile-block image per consumer warp
+    return kUnits * F::kTile;
 }
 
-// Shared memory: [2S mbarriers, 128 B][table][Sx][Q4_K LUT][tile partials][ring]
+// Shared memory: [2S mbarriers, 128 B][table][zero block][Sx][tile partials: S+2 slots][ring]
 struct TmaSmem {
-    int table, sx, lut, red, ring;  // byte offsets
-    int fixed;                      // bytes before the ring
+    int table, zero, sx, red, ring;  // byte offsets
 };
 
+// bytes of one tile slot of per-warp partials
+__host__ __device__ constexpr int tile_slot_bytes(int nv) { return kCW * nv * 16 * 4; }
+
 template <class F>
-__host__ __device__ inline TmaSmem tma_smem_layout(int K, int nv) {
+__host__ __device__ inline TmaSmem tma_smem_layout(int K, int nv, int stages) {
     const GemvSmem g = gemv_smem_layout<F>(K, nv, false);
     TmaSmem s;
     s.table = 128;
-    s.sx = s.table + g.table_bytes;
-    s.lut = s.sx + g.sx_bytes;
-    s.red = s.lut + g.lut_bytes;
-    s.ring = s.red + 2 * kCW * nv * 16 * 4;
+    s.zero = s.table + g.table_bytes;
+    s.sx = s.zero + g.zero_bytes;
+    s.red = s.sx + g.sx_bytes;
+    s.ring = s.red + (stages + 2) * tile_slot_bytes(nv);
     s.ring = (s.ring + 127) & ~127;
-    s.fixed = s.ring;
     return s;
-}
-
-// The stage that starts at unit u of a range ending at u1: tile, first block, block count.
-__device__ __forceinline__ void stage_at(int u, int u1, int nbk, int sb, int& tile, int& kb, int& n) {
-    tile = u / nbk;
-    kb = u - tile * nbk;
-    const int cend = min((kb / sb + 1) * sb, nbk);
-    n = min(cend - kb, u1 - u);
 }
 
 // CTA that owns unit u when T units are split over C CTAs (C <= T).
@@ -94,8 +91,8 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tma_kernel(GemvArgs a, int 
     constexpr int kMats = FUSED ? 2 : 1;
     constexpr int SB = stage_blocks(FUSED);
     constexpr int kStage = tma_stage_bytes<F>(FUSED);
-    const TmaSmem L = tma_smem_layout<F>(a.K, NV);
     const int S = a.stages;
+    const TmaSmem L = tma_smem_layout<F>(a.K, NV, S);
     uint8_t* ring = smem + L.ring;
     const uint32_t full0 = smem_addr(smem), empty0 = full0 + 8 * kMaxStages;
 
@@ -106,6 +103,7 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tma_kernel(GemvArgs a, int 
     const int C = gridDim.x, cta = blockIdx.x;
     const int u0 = (int)((long long)cta * T / C), u1 = (int)((long long)(cta + 1) * T / C);
 
+    __shared__ int s_tcnt[kMaxTileSlots];  // arrivals per tile slot (see the tile flush)
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(full0 + 8 * s, 1);
@@ -113,16 +111,17 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tma_kernel(GemvArgs a, int 
         }
         mbar_fence_init();
     }
+    if (threadIdx.x < kMaxTileSlots) s_tcnt[threadIdx.x] = 0;
     __syncthreads();
 
     if (warp == kCW) {
         // ---------------------------------------------------------------- producer
         const uint32_t ring_s = smem_addr(ring);
         int s = 0, slot = 0, round = 0;
+        int tile = u0 / nbk, kb = u0 - tile * nbk;
         bool ok = true;
         for (int u = u0; u < u1 && ok;) {
-            int tile, kb, n;
-            stage_at(u, u1, nbk, SB, tile, kb, n);
+            const int n = min(min(SB - kb % SB, nbk - kb), u1 - u);
             if (round > 0 && !mbar_wait(empty0 + 8 * slot, (round - 1) & 1)) ok = false;
             if (ok) {
                 // blocks [kb, kb+n) of the tile are one contiguous run of tile-block images
@@ -137,6 +136,11 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tma_kernel(GemvArgs a, int 
                 }
             }
             u += n;
+            kb += n;
+            if (kb == nbk) {
+                kb = 0;
+                ++tile;
+            }
             ++s;
             if (++slot == S) {
                 slot = 0;
@@ -155,56 +159,45 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tma_kernel(GemvArgs a, int 
 
     // -------------------------------------------------------------------- consumers
     uint2* xt = reinterpret_cast<uint2*>(smem + L.table);
+    uint2* zero = reinterpret_cast<uint2*>(smem + L.zero);
     float* sx = reinterpret_cast<float*>(smem + L.sx);
-    uint2* lut = reinterpret_cast<uint2*>(smem + L.lut);
     float* red = reinterpret_cast<float*>(smem + L.red);
     __shared__ float s_red[32];
+    for (int i = threadIdx.x; i < table_entries_per_block<F>(NV); i += kCW * 32) zero[i] = make_uint2(0u, 0u);
     const NormArgs nrm{a.norm_w, a.norm_len, a.norm_eps};
     build_prologue<F, NV>(xt, sx, a.x, a.ldx, a.K, nvec, nrm, s_red, a.err, kCW * 32, kBarPro);
-    if constexpr (F::kType == T_Q4_K) {
-        for (int i = threadIdx.x; i < 64; i += kCW * 32) {
-            const float sc = (float)i;
-            lut[i] = make_uint2(pack_h2(sc, sc), pack_h2(-1024.f * sc, -1024.f * sc));
-            lut[64 + i] = make_uint2(pack_h2(sc * 0.0625f, sc * 0.0625f), pack_h2(-64.f * sc, -64.f * sc));
-        }
-    }
     named_bar_sync(kBarPro, kCW * 32);
 
     const int g = lane >> 2, t = lane & 3;
-    const int mt = FUSED ? warp / SB : 0;  // matrix of this warp
-    const int jj = warp % SB;              // block of the stage
-    LaneCtx<NV> ctx;
-    ctx.xt = xt + g * 4 + t;
-    ctx.sx = sx;
-    ctx.lut = lut;
-    ctx.sxs = a.K / 32;
-    ctx.nb = nbk;
-    ctx.g = g;
-    ctx.t = t;
-    ctx.has_b = g < 2 * NV;
+    const LaneCtx<NV> ctx = make_ctx<F, NV>(xt, zero, sx, a.K, lane);
 
+    // Warp w takes block w % SB of matrix w / SB of every stage.
+    const int mt = FUSED ? warp / SB : 0;
+    const int jj = warp % SB;
     using Blk = typename BlkOf<F>::T;
     float yA = 0.f, yB = 0.f;
-    float pA[1][NV], pB[1][NV];
+    float pA[1][NV], pB[1][NV];  // Q4_K: this lane's shares (see q4k_unit)
 #pragma unroll
     for (int v = 0; v < NV; ++v) pA[0][v] = pB[0][v] = 0.f;
     bool aborted = false;
-    int slot = 0, round = 0, tpar = 0;
+    int slot = 0, round = 0, tslot = 0;
+    const int NT = S + 2;  // tile slots: a warp runs at most S stages (so S tile ends) ahead
+    int tile = u0 / nbk, kb = u0 - tile * nbk;
     for (int u = u0; u < u1;) {
-        int tile, kb, n;
-        stage_at(u, u1, nbk, SB, tile, kb, n);
+        const int j0 = kb % SB;
+        const int n = min(min(SB - j0, nbk - kb), u1 - u);
         if (!aborted && !mbar_wait(full0 + 8 * slot, round & 1)) {
             aborted = true;
             if (lane == 0 && a.err) atomicOr(a.err, 2);
         }
-        const int j0 = kb % SB;
         if (!aborted && jj >= j0 && jj < j0 + n) {
             const int kbj = kb - j0 + jj;
             const uint8_t* tb = ring + slot * kStage + (mt * SB + jj) * F::kTile;
             if constexpr (F::kType == T_Q4_K) {
                 Q4KBlk A[1], B[1];
                 tile_load<F, true>(A[0], B[0], tb, g, t);
-                q4k_unit_dist<NV, 1>(A, B, kbj, ctx, pA, pB);
+                const int kbs[1] = {kbj};
+                q4k_unit<NV, 1>(A, B, kbs, ctx, pA, pB);
             } else {
                 Blk A, B;
                 tile_load<F, true>(A, B, tb, g, t);
@@ -216,12 +209,18 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tma_kernel(GemvArgs a, int 
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8 * slot);
-        u += n;
         if (++slot == S) {
             slot = 0;
             ++round;
         }
-        if (kb + n != nbk && u != u1) continue;
+        u += n;
+        kb += n;
+        const int ftile = tile;
+        if (kb == nbk) {
+            kb = 0;
+            ++tile;
+        }
+        if (kb != 0 && u != u1) continue;
 
         // ------------------------------------------------------------ tile flush
         if constexpr (F::kType == T_Q4_K) {
@@ -239,25 +238,36 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tma_kernel(GemvArgs a, int 
                 pA[0][v] = pB[0][v] = 0.f;
             }
         }
-        float* rw = red + (size_t)(tpar * kCW + warp) * NV * 16;
+        // Partials go to red[tslot][warp][v][16 rows] (warp w holds matrix w / SB).  No warp
+        // waits: the last warp to arrive (shared-memory counter) adds the 16 partials in warp
+        // order and finishes the tile, the others move on.
+        float* rw = red + (size_t)(tslot * kCW + warp) * NV * 16;
         if (t < NV) {
             rw[t * 16 + g] = yA;
             rw[t * 16 + g + 8] = yB;
         }
         yA = yB = 0.f;
-        named_bar_sync(kBarTile, kCW * 32);
-        if (warp == 0) {
-            const int tu0 = tile * nbk, tu1 = tu0 + nbk;
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            old = atomicAdd(&s_tcnt[tslot], 1);
+        }
+        old = __shfl_sync(kFull, old, 0);
+        if (old == kCW - 1) {
+            __syncwarp();
+            __threadfence_block();
+            const int tu0 = ftile * nbk, tu1 = tu0 + nbk;
             const bool whole = tu0 >= u0 && tu1 <= u1;
             const int row = lane & 15;
-            const int grow = tile * 16 + row;
-            const float* rr = red + (size_t)tpar * kCW * NV * 16;
+            const int grow = ftile * 16 + row;
+            const float* rr = red + (size_t)tslot * kCW * NV * 16;
             int cf = 0, ncon = 1;
             if (!whole) {
                 cf = cta_owner(tu0, C, T);
                 ncon = cta_owner(tu1 - 1, C, T) - cf + 1;
             }
-            float* ws = a.sk_ws + (size_t)tile * a.sk_slots * kMats * 4 * 16;
+            float* ws = a.sk_ws + (size_t)ftile * a.sk_slots * kMats * 4 * 16;
             float f[2][kMats];  // vectors lane>>4 and (lane>>4)+2
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
@@ -266,9 +276,8 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tma_kernel(GemvArgs a, int 
                 for (int m = 0; m < kMats; ++m) {
                     float acc = 0.f;
                     if (v < NV) {
-#pragma unroll 4
-                        for (int w = m * (kCW / kMats); w < (m + 1) * (kCW / kMats); ++w)
-                            acc += rr[(w * NV + v) * 16 + row];
+#pragma unroll
+                        for (int w = m * SB; w < (m + 1) * SB; ++w) acc += rr[(w * NV + v) * 16 + row];
                     }
                     f[q][m] = acc;
                     if (!whole && v < NV) ws[(((size_t)(cta - cf) * kMats + m) * 4 + v) * 16 + row] = acc;
@@ -279,7 +288,7 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tma_kernel(GemvArgs a, int 
                 __threadfence();
                 __syncwarp();
                 int old = 0;
-                if (lane == 0) old = atomicAdd(a.sk_cnt + tile, 1);
+                if (lane == 0) old = atomicAdd(a.sk_cnt + ftile, 1);
                 old = __shfl_sync(kFull, old, 0);
                 last = old == ncon - 1;
                 if (last) {
@@ -296,7 +305,7 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tma_kernel(GemvArgs a, int 
                             f[q][m] = acc;
                         }
                     }
-                    if (lane == 0) a.sk_cnt[tile] = 0;  // re-arm for the next launch
+                    if (lane == 0) a.sk_cnt[ftile] = 0;  // re-arm for the next launch
                 }
             }
             if (last && grow < a.M) {
@@ -311,16 +320,18 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tma_kernel(GemvArgs a, int 
                     }
                 }
             }
+            __syncwarp();
+            if (lane == 0) s_tcnt[tslot] = 0;  // slot free for tile + NT
         }
-        tpar ^= 1;
+        if (++tslot == NT) tslot = 0;
     }
 }
 
 // ------------------------------------------------------------------ host launch
 template <class F>
 static int tma_stages(int K, int nv, bool fused, int smem_limit) {
-    const int fixed = tma_smem_layout<F>(K, nv).fixed + 256;  // + static shared
-    int s = (smem_limit - fixed) / tma_stage_bytes<F>(fused);
+    const int fixed = tma_smem_layout<F>(K, nv, 0).ring + 512;  // + static shared
+    int s = (smem_limit - fixed) / (tma_stage_bytes<F>(fused) + tile_slot_bytes(nv));
     return s > kMaxStages ? kMaxStages : s;
 }
 
@@ -345,7 +356,7 @@ static cudaError_t tma_launch_one(GemvArgs a, int nvec, int num_sms, int smem_li
     const int S = tma_stages<F>(a.K, NV, FUSED, smem_limit);
     if (S < 2) return cudaErrorInvalidConfiguration;
     a.stages = S;
-    const int smem = tma_smem_layout<F>(a.K, NV).fixed + S * tma_stage_bytes<F>(FUSED);
+    const int smem = tma_smem_layout<F>(a.K, NV, S).ring + S * tma_stage_bytes<F>(FUSED);
     auto kern = gemv_tma_kernel<F, NV, FUSED>;
     static int configured_smem[64];  // per template instantiation and device
     int dev = 0;

@@ -195,17 +195,17 @@ __global__ void __launch_bounds__(256) moe_gemv_kernel(MoeStage s) {
     extern __shared__ __align__(16) uint8_t smem[];
     const GemvSmem L = gemv_smem_layout<F>(s.K, 1, FUSED);
     uint2* xt = reinterpret_cast<uint2*>(smem);
-    float* sx = reinterpret_cast<float*>(smem + L.table_bytes);
-    uint2* lut = reinterpret_cast<uint2*>(smem + L.table_bytes + L.sx_bytes);
-    float* red = reinterpret_cast<float*>(smem + L.table_bytes + L.sx_bytes + L.lut_bytes);
+    uint2* zero = reinterpret_cast<uint2*>(smem + L.table_bytes);
+    float* sx = reinterpret_cast<float*>(smem + L.table_bytes + L.zero_bytes);
+    float* red = reinterpret_cast<float*>(smem + L.table_bytes + L.zero_bytes + L.sx_bytes);
 
     const int p = blockIdx.x / s.items_per_pair, j = blockIdx.x % s.items_per_pair;
     const int e = s.ids[p];
     const float* x = s.x + (size_t)(p / s.x_div) * s.ldx;
     __shared__ float s_red[32];
     const NormArgs nrm{nullptr, 0, 0.f};
+    for (int i = threadIdx.x; i < table_entries_per_block<F>(1); i += blockDim.x) zero[i] = make_uint2(0u, 0u);
     build_prologue<F, 1>(xt, sx, x, s.ldx, s.K, 1, nrm, s_red, s.err);
-    if constexpr (F::kType == T_Q4_K) build_q4k_lut(lut);
     __syncthreads();
     if (e < 0) return;  // no expert (cannot happen for validated routing)
 
@@ -220,15 +220,7 @@ __global__ void __launch_bounds__(256) moe_gemv_kernel(MoeStage s) {
     const uint8_t* W2 = FUSED ? s.w2[e] : nullptr;
     float* y = s.y + (size_t)p * s.ldy;
     constexpr int kMats = FUSED ? 2 : 1;
-    LaneCtx<1> ctx;
-    ctx.xt = xt + g * 4 + t;
-    ctx.sx = sx;
-    ctx.lut = lut;
-    ctx.sxs = s.K / 32;
-    ctx.nb = nb;
-    ctx.g = g;
-    ctx.t = t;
-    ctx.has_b = g < 2;
+    const LaneCtx<1> ctx = make_ctx<F, 1>(xt, zero, sx, s.K, lane);
     for (int tb = 0; tb < ntiles; tb += groups) {
         const int tile = tb + grp;
         float yA[kMats], yB[kMats];

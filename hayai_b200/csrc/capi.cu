@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -193,6 +194,9 @@ extern "C" int hc_engine_init(int device, hc_engine** out) {
         return hc_cuda_error(ce, "cudaStreamCreate");
     }
     e->stream = e->own_stream;
+    // HAYAI_STACK_KERNEL=0 keeps batch-1 FFN stacks on the per-layer kernels
+    const char* sk = getenv("HAYAI_STACK_KERNEL");
+    if (sk && sk[0] == '0') e->use_stack_kernel = false;
     ce = cudaMalloc(&e->d_err, 16);
     if (ce == cudaSuccess) ce = cudaMemset(e->d_err, 0, 16);
     if (ce != cudaSuccess) {
@@ -211,6 +215,7 @@ extern "C" int hc_engine_free(hc_engine* e) {
     hc_drop_graphs(e);
     e->sk_ws.release();
     e->sk_cnt.release();
+    e->stack_bar.release();
     for (auto& kv : e->ptr_tables) cudaFree(kv.second);
     e->ptr_tables.clear();
     e->ws_raw.release();
@@ -755,6 +760,86 @@ static int stack_check(const StackArgs& s) {
     return HC_OK;
 }
 
+// Device table of per-layer {gate, up, down, norm} pointers, cached per stack.
+static int stack_table(hc_engine* e, const StackArgs& s, const void** out) {
+    uint64_t key = 0x5354434Bull;  // "STCK"
+    for (size_t l = 0; l < s.L; ++l) {
+        key = mix(key, (uint64_t)(uintptr_t)s.g[l]->dev);
+        key = mix(key, (uint64_t)(uintptr_t)s.u[l]->dev);
+        key = mix(key, (uint64_t)(uintptr_t)s.d[l]->dev);
+        key = mix(key, (uint64_t)(uintptr_t)(s.norm ? s.norm[l] : nullptr));
+    }
+    key = mix(key, s.L);
+    auto it = e->ptr_tables.find(key);
+    if (it == e->ptr_tables.end()) {
+        std::vector<const void*> host(4 * s.L);
+        for (size_t l = 0; l < s.L; ++l) {
+            host[4 * l + 0] = s.g[l]->dev;
+            host[4 * l + 1] = s.u[l]->dev;
+            host[4 * l + 2] = s.d[l]->dev;
+            host[4 * l + 3] = s.norm ? (const void*)s.norm[l] : nullptr;
+        }
+        void* d = nullptr;
+        HC_CUDA(cudaMalloc(&d, host.size() * sizeof(void*)));
+        cudaError_t ce = cudaMemcpy(d, host.data(), host.size() * sizeof(void*), cudaMemcpyHostToDevice);
+        if (ce != cudaSuccess) {
+            cudaFree(d);
+            return hc_cuda_error(ce, "stack table upload");
+        }
+        it = e->ptr_tables.emplace(key, d).first;
+    }
+    *out = it->second;
+    return HC_OK;
+}
+
+// Batch 1 with uniform layers: the whole stack as one persistent kernel (ffn_stack.cu).
+// *done = false leaves the stack to the per-layer kernels.
+static int stack_try_kernel(hc_engine* e, const StackArgs& s, float* x, size_t nvec, float* h, bool* done) {
+    *done = false;
+    if (!e->use_stack_kernel || nvec != 1) return HC_OK;
+    const hc_weights *g0 = s.g[0], *d0 = s.d[0];
+    const int ta = g0->type, td = d0->type;
+    if (!tiled_type(ta) || !tiled_type(td)) return HC_OK;
+    const size_t dm = d0->m, ff = g0->m;
+    if (g0->n != dm) return HC_OK;
+    for (size_t l = 0; l < s.L; ++l)
+        if (s.g[l]->type != ta || s.u[l]->type != ta || s.d[l]->type != td || s.g[l]->m != ff || s.d[l]->n != ff)
+            return HC_OK;
+    StackLaunch L{};
+    L.L = (int)s.L;
+    L.dm = (int)dm;
+    L.ff = (int)ff;
+    L.ts_a = (long long)g0->stride;
+    L.ts_b = (long long)d0->stride;
+    L.x = x;
+    L.h = h;
+    L.eps = s.eps;
+    L.err = e->d_err;
+    L.slots_a = gemv_sk_slots(ta, (int)ff, (int)dm, e->num_sms);
+    L.slots_b = gemv_sk_slots(td, (int)dm, (int)ff, e->num_sms);
+    cudaError_t ce = launch_ffn_stack(ta, td, L, e->num_sms, e->smem_optin, e->stream, true);
+    if (ce == cudaErrorInvalidConfiguration) {
+        cudaGetLastError();
+        return HC_OK;
+    }
+    if (ce != cudaSuccess) return hc_cuda_error(ce, "stack kernel setup");
+    // scratch: [barrier + chunk counters][x double buffer][down partials]
+    const size_t nbk_d = td == T_Q8_0 ? (ff / 32 + 3) / 4 : ff / 256;
+    const size_t cpt = (nbk_d + 15) / 16;  // chunks per down tile (16 kernel blocks each)
+    const size_t nbar = (1 + 2 * s.L) * 4, off_x = (nbar + 255) / 256 * 256, off_p = off_x + 2 * dm * 4;
+    const size_t total = off_p + ((dm + 15) / 16) * cpt * 16 * 4;
+    int rc = e->stack_bar.ensure(total);
+    if (!rc) rc = stack_table(e, s, &L.layers);
+    if (rc) return rc;
+    L.bar = (unsigned*)e->stack_bar.p;
+    L.xbuf = (float*)((uint8_t*)e->stack_bar.p + off_x);
+    L.parts = (float*)((uint8_t*)e->stack_bar.p + off_p);
+    ce = launch_ffn_stack(ta, td, L, e->num_sms, e->smem_optin, e->stream, false);
+    if (ce != cudaSuccess) return hc_cuda_error(ce, "stack kernel launch");
+    *done = true;
+    return HC_OK;
+}
+
 static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
     size_t ffmax = 0;
     for (size_t l = 0; l < s.L; ++l) ffmax = s.g[l]->m > ffmax ? s.g[l]->m : ffmax;
@@ -763,6 +848,9 @@ static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
     if (rc) return rc;
     if (old_h && old_h != e->ws_h.p) hc_drop_graphs(e);
     float* h = (float*)e->ws_h.p;
+    bool done = false;
+    rc = stack_try_kernel(e, s, x, nvec, h, &done);
+    if (rc || done) return rc;
     // size every workspace before a capture (no allocation may happen inside it)
     for (size_t l = 0; l < s.L; ++l) {
         float* ws;

@@ -34,6 +34,8 @@ struct hc_engine {
     DevBuf ws_raw, ws_gpu, ws_x, ws_y, ws_h, ws_g, ws_u, ws_misc;
     // stream-K partial sums and per-tile counters (counters zeroed once; kernels re-arm them)
     DevBuf sk_ws, sk_cnt;
+    DevBuf stack_bar;             // grid-barrier counter of the persistent FFN-stack kernel
+    bool use_stack_kernel = true; // batch-1 stacks run as one persistent kernel when they fit
     HostBuf hs_out;
     std::unordered_map<uint64_t, cudaGraphExec_t> graphs;  // captured FFN stacks
     std::unordered_map<uint64_t, void*> ptr_tables;        // device tables of expert pointers

@@ -1,0 +1,431 @@
+// ffn_stack.cu -- a whole residual SwiGLU FFN stack, batch 1, as ONE persistent kernel.
+//
+// Reference semantics: the per-layer FFN of a decode step (crates/hayai-core/src/
+// stream_infer.rs:2166, :3752-3864: rms_norm -> gate/up GEMV -> silu(g)*u -> down GEMV ->
+// residual add), layer after layer, on the GEMV pipeline of gemv_tma.cuh.
+//
+// Why one kernel: a launch of ~60 MB of weights streams at ~5 TB/s once it is running, but
+// the first stage of a launch only becomes usable ~4.5 us after the start (every SM's first
+// copies reach DRAM together), and the launch itself costs more.  In a stack the weights
+// never depend on the activations, so here the producer warp of every CTA streams the
+// weights of phase after phase (gate/up of layer 0, down of layer 0, gate/up of layer 1, ...)
+// through one ring without a pause, while the consumer warps cross a grid-wide barrier
+// between phases (the down GEMV needs all of h, the next gate/up all of x).  The first-data
+// latency is paid once per stack instead of twice per layer.
+//
+// Grid barrier: a counter in global memory (zeroed by the host before the launch); each CTA
+// adds one per phase and spins, bounded by a one-second timeout, until all CTAs have.  The
+// launch is cooperative, so all CTAs are resident.  On a timeout the kernel raises bit 1 of
+// the error flag and skips the remaining work; the producer's own waits are bounded too.
+// Activations written inside the kernel are read with coherent (L2) loads.
+#include <cuda_runtime.h>
+
+#include "gemv_launch.h"
+#include "gemv_tma.cuh"
+
+namespace hc {
+
+struct StackLayerPtrs {
+    const uint8_t* g;
+    const uint8_t* u;
+    const uint8_t* d;
+    const float* norm;  // RMSNorm weight [dm] or nullptr
+};
+
+struct StackKArgs {
+    const StackLayerPtrs* layers;  // device array [L]
+    int L;
+    int dm, ff;
+    long long ts_a, ts_b;  // tile strides of gate/up and of down
+    float* x;              // [dm] the caller's vector: read once (copied to xbuf[0] first), written at the end
+    float* xbuf;           // [2][dm] residual stream, layer l written to xbuf[l & 1]
+    float* parts;          // [dm / 16][chunks per tile][16] down partial sums
+    float* h;              // [ff]
+    float eps;
+    int* err;
+    float* sk_ws;
+    int* sk_cnt;
+    int slots_a, slots_b;  // stream-K slots per tile
+    unsigned* bar;         // [1 + 2L]: grid-barrier counter, then one chunk counter per phase (zero at launch)
+    int stages;
+    int slot_bytes;
+    int stage_off;  // byte offset of the x staging copy inside the table region
+};
+
+// Shared memory: [mbarriers, 128 B][table][zero block][Sx][tile slots][ring], each table-side
+// region sized for the larger of the two GEMVs (they are used one after the other).
+struct StackSmem {
+    int table, zero, sx, red, ring;
+};
+
+template <class FA, class FD>
+__host__ __device__ inline StackSmem stack_smem_layout(int dm, int ff, int stages) {
+    const GemvSmem a = gemv_smem_layout<FA>(dm, 1, false), b = gemv_smem_layout<FD>(ff, 1, false);
+    StackSmem s;
+    s.table = 128;
+    const int ta = ((a.table_bytes + 15) & ~15) + dm * 4;  // gate/up table + staging copy of x
+    s.zero = s.table + (ta > b.table_bytes ? ta : b.table_bytes);
+    s.sx = s.zero + (a.zero_bytes > b.zero_bytes ? a.zero_bytes : b.zero_bytes);
+    s.red = s.sx + (a.sx_bytes > b.sx_bytes ? a.sx_bytes : b.sx_bytes);
+    s.ring = s.red + (stages + 2) * tile_slot_bytes(1);
+    s.ring = (s.ring + 127) & ~127;
+    return s;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Consumer warps of every CTA meet here; `target` = CTAs x phases completed.  The arrival is a
+// release (it publishes every write the CTA's consumers made before the first bar.sync), the
+// poll an acquire; the second bar.sync passes the acquire on to the other consumer threads.
+__device__ void grid_sync(unsigned* bar, unsigned target, int* err, int* s_abort) {
+    named_bar_sync(kBarGrid, kCW * 32);  // this CTA's consumers are done with the phase
+    if (threadIdx.x == 0) {
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+        if (!*s_abort) {
+            const unsigned long long t0 = global_ns();
+            while (ld_acquire(bar) < target) {
+                if (global_ns() - t0 > 1000000000ull) {
+                    if (err) atomicOr(err, 2);
+                    *s_abort = 1;
+                    break;
+                }
+            }
+        }
+    }
+    named_bar_sync(kBarGrid, kCW * 32);
+}
+
+// ------------------------------------------------------------------ dynamic chunks
+// A phase (one GEMV) is cut into fixed chunks: gate/up into whole 16-row tiles, down into
+// runs of 16 kernel blocks of a tile.  CTAs take chunks from a per-phase counter as their
+// producer gets to them, so SMs that happen to stream faster take more (across a phase the
+// SMs' rates differ by up to ~25%, and which SMs are slow changes from phase to phase: an
+// equal static split would leave every phase waiting for the slowest SM).  Every value is
+// reduced in an order fixed by the chunk boundaries, never by which CTA ran a chunk, so the
+// result is deterministic.  Down chunks leave their 16-row partial sums in a buffer; the next
+// gate/up prologue adds them to the residual stream in chunk order.
+struct StageDesc {
+    int tile, kb, n;  // blocks [kb, kb + n) of the tile
+    int part;         // chunk of the tile (down)
+    int flags;
+};
+constexpr int kLastOfChunk = 1, kPhaseEnd = 2;
+
+struct PhaseGeo {
+    int nbk;      // kernel blocks per row
+    int cb;       // blocks per chunk
+    int cpt;      // chunks per tile
+    int nchunks;  // all chunks of the phase
+};
+
+template <class F>
+__device__ __forceinline__ PhaseGeo phase_geo(int M, int K, int cb) {
+    PhaseGeo g;
+    g.nbk = (K + F::kBlockElems - 1) / F::kBlockElems;
+    g.cb = cb < g.nbk ? cb : g.nbk;
+    g.cpt = (g.nbk + g.cb - 1) / g.cb;
+    g.nchunks = ((M + 15) / 16) * g.cpt;
+    return g;
+}
+
+// Producer warp: take chunks until the phase is exhausted, then post the phase-end marker.
+template <class F, bool FUSED>
+__device__ bool produce_chunks(Ring& r, StageDesc* desc, const uint8_t* w, const uint8_t* w2, long long tstride,
+                               const PhaseGeo& pg, unsigned* counter, int lane) {
+    constexpr int kMats = FUSED ? 2 : 1;
+    constexpr int SB = stage_blocks(FUSED);
+    while (true) {
+        // take a chunk only once a slot is free for it (late binding balances the SMs)
+        if (r.round > 0 && !mbar_wait(r.empty0 + 8 * r.slot, (r.round - 1) & 1)) return false;
+        int c = 0;
+        if (lane == 0) c = (int)atomicAdd(counter, 1u);
+        c = __shfl_sync(kFull, c, 0);
+        if (c >= pg.nchunks) {
+            if (lane == 0) {
+                desc[r.slot] = StageDesc{0, 0, 0, 0, kPhaseEnd};
+                mbar_arrive(r.full0 + 8 * r.slot);  // no bytes: completes at once
+            }
+            __syncwarp();
+            r.advance();
+            return true;
+        }
+        const int tile = c / pg.cpt, part = c - tile * pg.cpt;
+        const int kb1 = min((part + 1) * pg.cb, pg.nbk);
+        int kb = part * pg.cb;
+        while (true) {
+            const int n = min(SB - kb % SB, kb1 - kb);
+            const bool last = kb + n >= kb1;
+            const uint32_t full = r.full0 + 8 * r.slot;
+            if (lane == 0) {
+                desc[r.slot] = StageDesc{tile, kb, n, part, last ? kLastOfChunk : 0};
+                mbar_arrive_expect_tx(full, (uint32_t)(kMats * n * F::kTile));
+            }
+            __syncwarp();
+            if (lane < kMats) {
+                const uint8_t* src = (lane ? w2 : w) + (size_t)tile * tstride + (size_t)kb * F::kTile;
+                bulk_g2s(r.base_s + r.slot * r.slot_bytes + (lane * SB + kb % SB) * F::kTile, src,
+                         (uint32_t)(n * F::kTile), full);
+            }
+            r.advance();
+            kb += n;
+            if (last) break;
+            if (r.round > 0 && !mbar_wait(r.empty0 + 8 * r.slot, (r.round - 1) & 1)) return false;
+        }
+    }
+}
+
+// Consumer warps: every stage of the phase until the end marker.  Fused (gate/up): whole
+// tiles, h = silu(G xn) * (U xn).  Otherwise (down): chunk partials to part_out.
+template <class F, bool FUSED>
+__device__ void consume_chunks(Ring& r, const StageDesc* desc, const LaneCtx<1>& ctx, const PhaseGeo& pg, int M,
+                               float* y, float* part_out, float* red, int* tcnt, int& tslot, bool& aborted,
+                               int* err) {
+    constexpr int kMats = FUSED ? 2 : 1;
+    constexpr int SB = stage_blocks(FUSED);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int NT = r.S + 2;
+    const int mt = warp_matrix(warp, FUSED), jj = warp % SB;  // this warp's matrix and block
+    float yA = 0.f, yB = 0.f;
+    float pA[1][1] = {{0.f}}, pB[1][1] = {{0.f}};
+    while (!aborted) {
+        if (!mbar_wait(r.full0 + 8 * r.slot, r.round & 1)) {
+            aborted = true;
+            if (lane == 0 && err) atomicOr(err, 2);
+            break;
+        }
+        const StageDesc d = desc[r.slot];
+        if (d.flags & kPhaseEnd) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(r.empty0 + 8 * r.slot);
+            r.advance();
+            break;
+        }
+        const int j0 = d.kb % SB;
+        if (jj >= j0 && jj < j0 + d.n)
+            stage_unit<F, 1>(r.base + r.slot * r.slot_bytes + (mt * SB + jj) * F::kTile, d.kb - j0 + jj, ctx, yA, yB,
+                             pA, pB);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(r.empty0 + 8 * r.slot);
+        r.advance();
+        if (!(d.flags & kLastOfChunk)) continue;
+
+        // chunk flush: per-warp partials into a tile slot, the last warp to arrive reduces
+        warp_partials<F, 1>(red + (size_t)(tslot * kCW + warp) * 16, g, t, yA, yB, pA, pB);
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            old = atomicAdd(&tcnt[tslot], 1);
+        }
+        old = __shfl_sync(kFull, old, 0);
+        if (old == kCW - 1) {
+            __syncwarp();
+            __threadfence_block();
+            const float* rr = red + (size_t)tslot * kCW * 16;
+            const int row = lane & 15;
+            if (lane < 16) {
+                float f[kMats];
+#pragma unroll
+                for (int m = 0; m < kMats; ++m) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int w = m * SB; w < (m + 1) * SB; ++w) acc += rr[w * 16 + row];
+                    f[m] = acc;
+                }
+                if constexpr (FUSED) {
+                    const int grow = d.tile * 16 + row;
+                    if (grow < M) y[grow] = silu_mul(f[0], f[kMats - 1]);
+                } else {
+                    part_out[((size_t)d.tile * pg.cpt + d.part) * 16 + row] = f[0];
+                }
+            }
+            __syncwarp();
+            if (lane == 0) tcnt[tslot] = 0;
+        }
+        if (++tslot == NT) tslot = 0;
+    }
+}
+
+template <class FA, class FD>
+__global__ void __launch_bounds__(kTThreads, 1) ffn_stack_kernel(StackKArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_tcnt[kMaxTileSlots];
+    __shared__ float s_red[32];
+    __shared__ int s_abort;
+    __shared__ StageDesc s_desc[kMaxStages];
+    const int S = a.stages;
+    const StackSmem L = stack_smem_layout<FA, FD>(a.dm, a.ff, S);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    Ring r;
+    r.full0 = smem_addr(smem);
+    r.empty0 = r.full0 + 8 * kMaxStages;
+    r.base = smem + L.ring;
+    r.base_s = smem_addr(r.base);
+    r.S = S;
+    r.slot_bytes = a.slot_bytes;
+    r.slot = r.round = 0;
+    const PhaseGeo ga = phase_geo<FA>(a.ff, a.dm, 1 << 20);  // gate/up: whole tiles
+    const PhaseGeo gd = phase_geo<FD>(a.dm, a.ff, kUnits);   // down: 16-block runs
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(r.full0 + 8 * s, 1);
+            mbar_init(r.empty0 + 8 * s, kCW);
+        }
+        mbar_fence_init();
+        s_abort = 0;
+    }
+    if (threadIdx.x < kMaxTileSlots) s_tcnt[threadIdx.x] = 0;
+    __syncthreads();
+
+    if (warp == kCW) {  // producer: every phase's weights, back to back
+        bool ok = true;
+        for (int l = 0; l < a.L && ok; ++l) {
+            const StackLayerPtrs ly = a.layers[l];
+            ok = produce_chunks<FA, true>(r, s_desc, ly.g, ly.u, a.ts_a, ga, a.bar + 1 + 2 * l, lane);
+            if (ok) ok = produce_chunks<FD, false>(r, s_desc, ly.d, nullptr, a.ts_b, gd, a.bar + 2 + 2 * l, lane);
+        }
+        drain_ring(r, r.round * S + r.slot);
+        if (!ok && lane == 0 && a.err) atomicOr(a.err, 2);
+        return;
+    }
+
+    uint2* xt = reinterpret_cast<uint2*>(smem + L.table);
+    uint2* zero = reinterpret_cast<uint2*>(smem + L.zero);
+    float* sx = reinterpret_cast<float*>(smem + L.sx);
+    float* red = reinterpret_cast<float*>(smem + L.red);
+    for (int i = threadIdx.x; i < (L.sx - L.zero) / 8; i += kCW * 32) zero[i] = make_uint2(0u, 0u);
+    int tslot = 0;
+    bool aborted = false;
+    unsigned phases = 0;
+    const unsigned C = gridDim.x;
+    const int nc4 = a.dm / 4;  // float4 chunks of x; this CTA writes back [c0, c1)
+    const int c0 = (int)((long long)blockIdx.x * nc4 / C), c1 = (int)((long long)(blockIdx.x + 1) * nc4 / C);
+    for (int l = 0; l < a.L; ++l) {
+        const StackLayerPtrs ly = a.layers[l];
+        // gate/up: x_l = x_{l-1} + down partials of layer l-1; h = silu(G xn) * (U xn), xn = rms_norm(x_l)
+        {
+            const NormArgs nrm{ly.norm, a.dm, a.eps};
+            const float* xin = l == 0 ? a.xbuf : a.xbuf + (size_t)((l - 1) & 1) * a.dm;
+            // x_l, completed once (one pass over the partials), staged behind the gate/up table
+            float* xs = reinterpret_cast<float*>(smem + L.table + a.stage_off);
+            const XAccum acc = l == 0 ? XAccum{nullptr, 0, nullptr, 0, 0} : XAccum{a.parts, gd.cpt, nullptr, 0, 0};
+            float* xnext = a.xbuf + (size_t)(l & 1) * a.dm;
+            for (int c = threadIdx.x; c < nc4; c += kCW * 32) {
+                const float4 v = load_x4<kLdcg>(xin, c, acc);
+                reinterpret_cast<float4*>(xs)[c] = v;
+                if (l > 0 && c >= c0 && c < c1) reinterpret_cast<float4*>(xnext)[c] = v;
+            }
+            named_bar_sync(kBarPro, kCW * 32);
+            build_prologue<FA, 1, kPlain>(xt, sx, xs, a.dm, a.dm, 1, nrm, s_red, a.err, kCW * 32, kBarPro);
+            named_bar_sync(kBarPro, kCW * 32);
+            const LaneCtx<1> ctx = make_ctx<FA, 1>(xt, zero, sx, a.dm, lane);
+            consume_chunks<FA, true>(r, s_desc, ctx, ga, a.ff, a.h, nullptr, red, s_tcnt, tslot, aborted, a.err);
+            grid_sync(a.bar, ++phases * C, a.err, &s_abort);
+            if (s_abort) aborted = true;
+        }
+        // down: chunk partials of D h
+        {
+            const NormArgs nrm{nullptr, 0, 0.f};
+            build_prologue<FD, 1, kLdcg>(xt, sx, a.h, a.ff, a.ff, 1, nrm, s_red, a.err, kCW * 32, kBarPro);
+            named_bar_sync(kBarPro, kCW * 32);
+            const LaneCtx<1> ctx = make_ctx<FD, 1>(xt, zero, sx, a.ff, lane);
+            consume_chunks<FD, false>(r, s_desc, ctx, gd, a.dm, nullptr, a.parts, red, s_tcnt, tslot, aborted,
+                                      a.err);
+            grid_sync(a.bar, ++phases * C, a.err, &s_abort);
+            if (s_abort) aborted = true;
+        }
+    }
+    // x_L = x_{L-1} + the last down partials, into the caller's x
+    if (!aborted) {
+        const float* xin = a.xbuf + (size_t)((a.L - 1) & 1) * a.dm;
+        const XAccum acc{a.parts, gd.cpt, nullptr, 0, 0};
+        for (int c = c0 + (int)threadIdx.x; c < c1; c += kCW * 32)
+            reinterpret_cast<float4*>(a.x)[c] = load_x4<kLdcg>(xin, c, acc);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+template <class FA, class FD>
+static int stack_stages(int dm, int ff, int smem_limit, int* slot_bytes) {
+    const int sa = tma_stage_bytes<FA>(true), sb = tma_stage_bytes<FD>(false);
+    *slot_bytes = sa > sb ? sa : sb;
+    const int fixed = stack_smem_layout<FA, FD>(dm, ff, 0).ring + 512;  // + static shared
+    int s = (smem_limit - fixed) / (*slot_bytes + tile_slot_bytes(1));
+    return s > kMaxStages ? kMaxStages : s;
+}
+
+template <class FA, class FD>
+static cudaError_t launch_stack_t(StackKArgs a, int num_sms, int smem_limit, cudaStream_t stream, bool dry) {
+    int slot_bytes = 0;
+    const int S = stack_stages<FA, FD>(a.dm, a.ff, smem_limit, &slot_bytes);
+    if (S < 3) return cudaErrorInvalidConfiguration;  // too shallow to pay off: use the per-layer kernels
+    const int smem = stack_smem_layout<FA, FD>(a.dm, a.ff, S).ring + S * slot_bytes;
+    auto kern = ffn_stack_kernel<FA, FD>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    if (dry) return cudaSuccess;
+    a.stages = S;
+    a.slot_bytes = slot_bytes;
+    a.stage_off = (gemv_smem_layout<FA>(a.dm, 1, false).table_bytes + 15) & ~15;
+    e = cudaMemsetAsync(a.bar, 0, (size_t)(1 + 2 * a.L) * sizeof(unsigned), stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(a.xbuf, a.x, (size_t)a.dm * sizeof(float), cudaMemcpyDeviceToDevice, stream);
+    if (e != cudaSuccess) return e;
+    void* args[] = {&a};
+    return cudaLaunchCooperativeKernel((const void*)kern, dim3(num_sms), dim3(kTThreads), args, smem, stream);
+}
+
+// The CTA count the kernel runs with: one per SM, as the per-layer kernels (their partition
+// of each GEMV, and so the summation order, is the same).
+cudaError_t launch_ffn_stack(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
+                             cudaStream_t stream, bool dry) {
+    const int ntiles_a = (s.ff + 15) / 16, ntiles_b = (s.dm + 15) / 16;
+    const int nbk_a = (s.dm + (type_a == T_Q8_0 ? 127 : 255)) / (type_a == T_Q8_0 ? 128 : 256);
+    const int nbk_b = (s.ff + (type_d == T_Q8_0 ? 127 : 255)) / (type_d == T_Q8_0 ? 128 : 256);
+    if ((long long)ntiles_a * nbk_a < num_sms || (long long)ntiles_b * nbk_b < num_sms)
+        return cudaErrorInvalidConfiguration;  // fewer units than SMs: the per-layer kernels shrink their grid
+    if ((nbk_b + kUnits - 1) / kUnits > kMaxParts || s.dm % 4 || s.ff % 4)
+        return cudaErrorInvalidConfiguration;  // more down chunks per tile than the prologue adds up
+    StackKArgs a{};
+    a.layers = (const StackLayerPtrs*)s.layers;
+    a.L = s.L;
+    a.dm = s.dm;
+    a.ff = s.ff;
+    a.ts_a = s.ts_a;
+    a.ts_b = s.ts_b;
+    a.x = s.x;
+    a.xbuf = s.xbuf;
+    a.parts = s.parts;
+    a.h = s.h;
+    a.eps = s.eps;
+    a.err = s.err;
+    a.sk_ws = s.sk_ws;
+    a.sk_cnt = s.sk_cnt;
+    a.slots_a = s.slots_a;
+    a.slots_b = s.slots_b;
+    a.bar = s.bar;
+#define HC_STACK_CASE(TA, FAT, TD, FDT) \
+    if (type_a == TA && type_d == TD) return launch_stack_t<FAT, FDT>(a, num_sms, smem_limit, stream, dry);
+    HC_STACK_CASE(T_Q4_K, FmtQ4K, T_Q6_K, FmtQ6K)
+    HC_STACK_CASE(T_Q4_K, FmtQ4K, T_Q4_K, FmtQ4K)
+    HC_STACK_CASE(T_Q6_K, FmtQ6K, T_Q6_K, FmtQ6K)
+    HC_STACK_CASE(T_Q8_0, FmtQ80, T_Q8_0, FmtQ80)
+#undef HC_STACK_CASE
+    return cudaErrorInvalidConfiguration;
+}
+
+}  // namespace hc

@@ -15,6 +15,29 @@ cudaError_t launch_gemv_mma(int type, const GemvArgs& a, int nvec, bool fused, i
 bool gemv_mma_supported(int type);
 // Workspace of the stream-K split for an M x K launch: partial-sum floats and tile counters.
 void gemv_sk_workspace(int type, int M, int K, bool fused, int num_sms, size_t* ws_floats, size_t* counters);
+// Stream-K slots per tile (most CTAs sharing one tile) of an M x K GEMV on num_sms CTAs.
+int gemv_sk_slots(int type, int M, int K, int num_sms);
+
+// A batch-1 residual SwiGLU FFN stack in one persistent kernel (ffn_stack.cu).
+struct StackLaunch {
+    const void* layers;  // device array, per layer {gate, up, down, norm weight} pointers
+    int L, dm, ff;
+    long long ts_a, ts_b;  // tile strides of gate/up and of down
+    float* x;              // [dm], updated in place
+    float* xbuf;           // [2][dm] scratch
+    float* parts;          // [ceil(dm / 16) * ceil(ff / 4096)][16] scratch (down partials)
+    float* h;              // [ff]
+    float eps;
+    int* err;
+    float* sk_ws;
+    int* sk_cnt;
+    int slots_a, slots_b;
+    unsigned* bar;  // [1 + 2L] grid-barrier and chunk counters
+};
+// cudaErrorInvalidConfiguration: the shapes or formats are not covered (use the per-layer
+// kernels).  dry = only check that the launch is possible.
+cudaError_t launch_ffn_stack(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
+                             cudaStream_t stream, bool dry);
 
 // CUDA-core GEMV on the raw GGUF layout for F32 and the IQ2/IQ3 codebook formats.
 cudaError_t launch_gemv_simple(int type, const uint8_t* w, size_t row_bytes, int M, int K, const float* x,

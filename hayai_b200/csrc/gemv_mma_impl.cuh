@@ -67,11 +67,54 @@ __device__ __forceinline__ float block_sum(float s, float* scratch, int nthr, in
 // Builds the B-fragment table (entry e = ((block * kMmaPerBlock + mi) * 2NV + g) * 4 + t holds
 // {pack(x[e0], x[e2]), pack(x[e1], x[e3])} of vector g/2, part g&1 (hi / lo*2^11), with
 // e_j = block*kBlockElems + F::base(mi, t) + j) and, for Q4_K, the 32-element sub-block sums.
+// Optional second source of the activation (batch 1, persistent FFN stack): the vector is
+// x + the sum of `parts` partial vectors stored per 16-row tile as
+// part[(tile * parts + p) * 16 + row], added in p order; the float4 chunks [c0, c1) of the
+// completed vector are also stored to `out`.
+struct XAccum {
+    const float* part;  // nullptr: none
+    int parts;
+    float* out;
+    int c0, c1;
+};
+
+// How the prologue reads the activation: kLdg = read-only path (the vector is constant for the
+// kernel); kLdcg = coherent L2 loads (written earlier in the same kernel by other CTAs);
+// kPlain = generic loads (a staging copy in shared memory).
+enum XLoad { kLdg = 0, kLdcg = 1, kPlain = 2 };
+constexpr int kMaxParts = 8;
+
+// Activation chunk c (4 elements) of vector row xv, plus the partials of acc (all their loads
+// are issued before the first add, then added in part order).
+template <int LOAD>
+__device__ __forceinline__ float4 load_x4(const float* xv, int c, const XAccum& acc) {
+    const float4* p4 = reinterpret_cast<const float4*>(xv) + c;
+    float4 a = LOAD == kLdg ? __ldg(p4) : (LOAD == kLdcg ? __ldcg(p4) : *p4);
+    if (acc.part) {
+        const float* pp = acc.part + (size_t)(c >> 2) * acc.parts * 16 + (c & 3) * 4;
+        float4 d[kMaxParts];
+#pragma unroll
+        for (int p = 0; p < kMaxParts; ++p)
+            if (p < acc.parts) d[p] = __ldcg(reinterpret_cast<const float4*>(pp + p * 16));
+#pragma unroll
+        for (int p = 0; p < kMaxParts; ++p) {
+            if (p < acc.parts) {
+                a.x += d[p].x;
+                a.y += d[p].y;
+                a.z += d[p].z;
+                a.w += d[p].w;
+            }
+        }
+    }
+    return a;
+}
+
 // Run by threads [0, nthr) of the CTA (all of it by default); `bar` is the named barrier they
 // synchronise on.
-template <class F, int NV>
+template <class F, int NV, int LOAD = kLdg>
 __device__ void build_prologue(uint2* __restrict__ xt, float* __restrict__ sx, const float* __restrict__ x, int ldx,
-                               int K, int nvec, const NormArgs& nrm, float* scratch, int* err, int nthr, int bar) {
+                               int K, int nvec, const NormArgs& nrm, float* scratch, int* err, int nthr, int bar,
+                               const XAccum& acc = XAccum{nullptr, 0, nullptr, 0, 0}) {
     const int nb = (K + F::kBlockElems - 1) / F::kBlockElems;
     const int nchunk = K >> 2;                         // real float4 chunks
     const int ntab = (nb * F::kBlockElems) >> 2;       // chunks covered by the table (zero padded)
@@ -87,7 +130,7 @@ __device__ void build_prologue(uint2* __restrict__ xt, float* __restrict__ sx, c
                 const int nc = nrm.len >> 2;
 #pragma unroll 4
                 for (int c = threadIdx.x; c < nc; c += nthr) {
-                    const float4 a = __ldg(reinterpret_cast<const float4*>(xv) + c);
+                    const float4 a = load_x4<LOAD>(xv, c, acc);
                     s += (a.x * a.x + a.y * a.y) + (a.z * a.z + a.w * a.w);
                 }
             }
@@ -99,7 +142,8 @@ __device__ void build_prologue(uint2* __restrict__ xt, float* __restrict__ sx, c
             const int c = threadIdx.x + r * nthr;
             float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
             if (live && c < nchunk) {
-                a = __ldg(reinterpret_cast<const float4*>(xv) + c);
+                a = load_x4<LOAD>(xv, c, acc);
+                if (acc.out && v == 0 && c >= acc.c0 && c < acc.c1) reinterpret_cast<float4*>(acc.out)[c] = a;
                 if (nrm.w) {
                     if (4 * c < nrm.len) {
                         const float4 w = __ldg(reinterpret_cast<const float4*>(nrm.w) + c);

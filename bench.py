@@ -3,9 +3,11 @@
 and FFN tokens/s).
 
 Default workload: Llama-3-8B-shaped FFN stack, 32 layers resident
-in HBM, gate/up Q4_K, down Q6_K, batch-1 decode, x <- x + FFN_l(x).  One step = one token
-through all 32 layers.  Weights are seeded N(0, 0.02^2) quantized on the device with the
-reference's Q4_K quantizer (and this project's Q6_K quantizer); activations N(0, 1).
+in HBM, gate/up Q4_K, down Q6_K, batch-1 decode, x <- x + FFN_l(rms_norm(x)).  One step = one
+token through all 32 layers: at batch 1 the whole stack is ONE persistent kernel launch
+(ffn_stack.cu), otherwise two GEMV launches per layer.  Weights are seeded N(0, 0.02^2)
+quantized on the device with the reference's Q4_K quantizer (and this project's Q6_K
+quantizer); activations N(0, 1).  --layers N shrinks the stack (a small case for profilers).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
 
@@ -228,7 +230,9 @@ def run_reference(args):
     from hayai_b200 import _build
 
     _build.build_oracle()
-    c = CONFIGS[args.config]
+    c = dict(CONFIGS[args.config])
+    if args.layers:
+        c["layers"] = args.layers
     cores = oracle.get_threads()
     # a few distinct layers of the same shapes, generated on the host with the oracle
     S = 3
@@ -286,9 +290,13 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     import hayai_b200 as hb
 
-    c = CONFIGS[args.config]
+    c = dict(CONFIGS[args.config])
+    if args.layers:
+        c["layers"] = args.layers
     L, dm, kin, ff, tg, td = c["layers"], c["d_model"], c["k_in"], c["d_ff"], c["tg"], c["td"]
     B = args.batch
+    # the persistent stack kernel serves batch 1 when the FFN input width equals d_model
+    uses_stack = B == 1 and kin == dm and os.environ.get("HAYAI_STACK_KERNEL", "1") != "0"
     eng = hb.CudaEngine(local)
     stream = torch.cuda.Stream(dev)  # one stream for torch's copies, our kernels and the CUDA events
     torch.cuda.set_stream(stream)
@@ -369,30 +377,46 @@ def run_ours(args):
     value = world * args.steps * tok_bytes / t / 1e9
     tokens_per_s = world * args.steps * B / t
 
-    # ---- roofline: the dominant kernel (fused gate/up) timed alone, rotating over layers
-    h = torch.empty(B, ff, dtype=torch.float32, device=dev)
-    reps = 3 * L if L >= 8 else 96
-    for i in range(L):
-        eng.ffn_gateup_dev(G[i % L], U[i % L], x0, h, B, norm=NW[i % L], norm_len=dm, eps=EPS)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(dev)
-    e0.record(stream)
-    for i in range(reps):
-        eng.ffn_gateup_dev(G[i % L], U[i % L], x0, h, B, norm=NW[i % L], norm_len=dm, eps=EPS)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    gu_time = e0.elapsed_time(e1) / 1e3 / reps
-    gu_bytes = 2 * mat_bytes(tg, ff, kin)
+    # ---- roofline of the dominant kernel, timed with CUDA events on the stream it runs on.
+    # Batch 1 with uniform layers runs the whole stack as one persistent kernel per step
+    # (ffn_stack.cu); otherwise the fused gate/up GEMV is the largest kernel of a layer.
     peak, peak_kind = measured_peak()
-    achieved = gu_bytes / gu_time / 1e9
-    kkey = f"gateup_{args.config}_b{B}"
-    roofline = {"bound": "hbm", "kernel": "gemv_mma_kernel<FmtQ4K,1,true> (fused gate/up + SiLU*up)"
-                if tg == Q4_K else f"gemv_mma_kernel (fused gate/up, type {tg})",
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    names = {Q4_K: "FmtQ4K", Q6_K: "FmtQ6K", Q8_0: "FmtQ80"}
+    if uses_stack:
+        reps = max(3, min(args.steps, 20))
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for _ in range(reps):
+            eng.ffn_stack_dev(G, U, D, x, B, norms=NW, eps=EPS)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        k_time = e0.elapsed_time(e1) / 1e3 / reps
+        k_bytes = tok_bytes
+        kname = f"ffn_stack_kernel<{names[tg]},{names[td]}> (all {L} layers, one launch)"
+        kkey = f"stack_{args.config}_L{L}"
+    else:
+        h = torch.empty(B, ff, dtype=torch.float32, device=dev)
+        reps = 3 * L if L >= 8 else 96
+        for i in range(L):
+            eng.ffn_gateup_dev(G[i % L], U[i % L], x0, h, B, norm=NW[i % L], norm_len=dm, eps=EPS)
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for i in range(reps):
+            eng.ffn_gateup_dev(G[i % L], U[i % L], x0, h, B, norm=NW[i % L], norm_len=dm, eps=EPS)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        k_time = e0.elapsed_time(e1) / 1e3 / reps
+        k_bytes = 2 * mat_bytes(tg, ff, kin)
+        kname = f"gemv_tma_kernel<{names[tg]},{min(B, 4)},true> (fused gate/up + SiLU*up)"
+        kkey = f"gateup_{args.config}_b{B}"
+    achieved = k_bytes / k_time / 1e9
+    roofline = {"bound": "hbm", "kernel": kname,
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy burst)" if peak_kind == "measured"
                 else "fallback 6.65 TB/s",
-                "traffic": committed_traffic(kkey), "algorithmic_bytes_per_launch": gu_bytes,
-                "avg_launch_us": round(gu_time * 1e6, 2)}
+                "traffic": committed_traffic(kkey), "algorithmic_bytes_per_launch": k_bytes,
+                "avg_launch_us": round(k_time * 1e6, 2)}
 
     # ---- e2e through the host C-ABI call: pinned host x in, result out, every step
     n_e2e = min(args.steps, 200)
@@ -428,12 +452,13 @@ def run_ours(args):
             "scaling": "weak", "vs_baseline": None, "dtype": c_dtype(c),
             "data": "synthetic (seeded N(0,0.02^2) weights quantized on device, N(0,1) activations)",
             "config": {"workload": c["workload"], "batch": B, "layers": L, "d_model": dm, "d_ff": ff,
+                       "kernel_path": "persistent stack kernel" if uses_stack else "per-layer kernels",
                        "bytes_per_token": tok_bytes, "parallelism": f"replicas x{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2 (weights per step %.2f GB > 126 MB)" % (tok_bytes / 1e9)},
             "tokens_per_s": round(tokens_per_s, 2),
             "frac_of_8tbs": round(value / world / 8000.0, 4),
             "roofline": roofline, "e2e": e2e, "clocks": clocks,
-            "gpu_launches": args.steps * 2 * L,
+            "gpu_launches": args.steps * (1 if uses_stack else 2 * L),
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
@@ -456,6 +481,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="llama8b")
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=0, help="override the config's layer count (small profiling case)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -794,7 +794,7 @@ static int stack_table(hc_engine* e, const StackArgs& s, const void** out) {
 
 // Batch 1 with uniform layers: the whole stack as one persistent kernel (ffn_stack.cu).
 // *done = false leaves the stack to the per-layer kernels.
-static int stack_try_kernel(hc_engine* e, const StackArgs& s, float* x, size_t nvec, float* h, bool* done) {
+static int stack_try_kernel(hc_engine* e, const StackArgs& s, float* x, size_t nvec, bool* done) {
     *done = false;
     if (!e->use_stack_kernel || nvec != 1) return HC_OK;
     const hc_weights *g0 = s.g[0], *d0 = s.d[0];
@@ -812,29 +812,20 @@ static int stack_try_kernel(hc_engine* e, const StackArgs& s, float* x, size_t n
     L.ts_a = (long long)g0->stride;
     L.ts_b = (long long)d0->stride;
     L.x = x;
-    L.h = h;
     L.eps = s.eps;
     L.err = e->d_err;
-    L.slots_a = gemv_sk_slots(ta, (int)ff, (int)dm, e->num_sms);
-    L.slots_b = gemv_sk_slots(td, (int)dm, (int)ff, e->num_sms);
-    cudaError_t ce = launch_ffn_stack(ta, td, L, e->num_sms, e->smem_optin, e->stream, true);
+    size_t bytes = 0;
+    cudaError_t ce = launch_ffn_stack(ta, td, L, e->num_sms, e->smem_optin, e->stream, true, &bytes);
     if (ce == cudaErrorInvalidConfiguration) {
         cudaGetLastError();
         return HC_OK;
     }
     if (ce != cudaSuccess) return hc_cuda_error(ce, "stack kernel setup");
-    // scratch: [barrier + chunk counters][x double buffer][down partials]
-    const size_t nbk_d = td == T_Q8_0 ? (ff / 32 + 3) / 4 : ff / 256;
-    const size_t cpt = (nbk_d + 15) / 16;  // chunks per down tile (16 kernel blocks each)
-    const size_t nbar = (1 + 2 * s.L) * 4, off_x = (nbar + 255) / 256 * 256, off_p = off_x + 2 * dm * 4;
-    const size_t total = off_p + ((dm + 15) / 16) * cpt * 16 * 4;
-    int rc = e->stack_bar.ensure(total);
+    int rc = e->stack_bar.ensure(bytes);
     if (!rc) rc = stack_table(e, s, &L.layers);
     if (rc) return rc;
-    L.bar = (unsigned*)e->stack_bar.p;
-    L.xbuf = (float*)((uint8_t*)e->stack_bar.p + off_x);
-    L.parts = (float*)((uint8_t*)e->stack_bar.p + off_p);
-    ce = launch_ffn_stack(ta, td, L, e->num_sms, e->smem_optin, e->stream, false);
+    L.scratch = e->stack_bar.p;
+    ce = launch_ffn_stack(ta, td, L, e->num_sms, e->smem_optin, e->stream, false, nullptr);
     if (ce != cudaSuccess) return hc_cuda_error(ce, "stack kernel launch");
     *done = true;
     return HC_OK;
@@ -849,7 +840,7 @@ static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
     if (old_h && old_h != e->ws_h.p) hc_drop_graphs(e);
     float* h = (float*)e->ws_h.p;
     bool done = false;
-    rc = stack_try_kernel(e, s, x, nvec, h, &done);
+    rc = stack_try_kernel(e, s, x, nvec, &done);
     if (rc || done) return rc;
     // size every workspace before a capture (no allocation may happen inside it)
     for (size_t l = 0; l < s.L; ++l) {

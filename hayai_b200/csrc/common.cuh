@@ -93,6 +93,23 @@ __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
     return h2_as_u32(__hsub2(u32_as_h2(a), u32_as_h2(b)));
 }
 
+// Unsigned byte `byte` of `word` as f32 without the conversion pipe: the byte becomes the low
+// mantissa bits of 2^23 (one PRMT) and one FADD removes 2^23.  Exact.
+__device__ __forceinline__ float u8_to_f32(uint32_t word, int byte) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(word), "r"(0x4B000000u), "r"(0x7440u | (uint32_t)byte));
+    return __uint_as_float(d) - 8388608.0f;
+}
+
+// Signed byte `byte` of `word` as f32, without the conversion pipe: the byte, offset to
+// unsigned, becomes the low mantissa bits of 2^23 (one PRMT on 0x80-flipped bytes), and one
+// FADD removes 2^23 + 128.  Exact for every int8.  `flipped` = word ^ 0x80808080.
+__device__ __forceinline__ float s8_to_f32_flipped(uint32_t flipped, int byte) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(flipped), "r"(0x4B000000u), "r"(0x7440u | (uint32_t)byte));
+    return __uint_as_float(d) - 8388736.0f;
+}
+
 // ---------------------------------------------------------------- tensor core
 // D = A(16x16 f16, row) * B(16x8 f16, col) + C, f32 accumulate.
 // Fragment layout (PTX ISA, mma.m16n8k16): lane = 4*g + t;

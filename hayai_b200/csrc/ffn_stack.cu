@@ -18,6 +18,11 @@
 // launch is cooperative, so all CTAs are resident.  On a timeout the kernel raises bit 1 of
 // the error flag and skips the remaining work; the producer's own waits are bounded too.
 // Activations written inside the kernel are read with coherent (L2) loads.
+//
+// Phase boundaries are kept short: the warp that completes a 16-row tile of h writes it
+// straight into the down GEMV's fragment table in global memory (the down prologue is then a
+// copy), and the gate/up prologue completes x, sums its squares and normalises in two passes
+// over a staging copy.
 #include <cuda_runtime.h>
 
 #include "gemv_launch.h"
@@ -37,32 +42,34 @@ struct StackKArgs {
     int L;
     int dm, ff;
     long long ts_a, ts_b;  // tile strides of gate/up and of down
-    float* x;              // [dm] the caller's vector: read once (copied to xbuf[0] first), written at the end
-    float* xbuf;           // [2][dm] residual stream, layer l written to xbuf[l & 1]
+    float* x;              // [dm] the caller's vector: x_0 on entry, x_L on exit
+    float* xbuf;           // [2][dm] residual stream: x_l (0 < l < L) lives in xbuf[l & 1]
     float* parts;          // [dm / 16][chunks per tile][16] down partial sums
-    float* h;              // [ff]
+    uint2* htab;           // the down GEMV's fragment table of h, in global memory
+    float* hsx;            // [ff / 16] 16-element sums of h (Q4_K down)
     float eps;
     int* err;
-    float* sk_ws;
-    int* sk_cnt;
-    int slots_a, slots_b;  // stream-K slots per tile
-    unsigned* bar;         // [1 + 2L]: grid-barrier counter, then one chunk counter per phase (zero at launch)
+    unsigned* bar;  // [1 + 2L]: grid-barrier counter, then one chunk counter per phase (zero at launch)
     int stages;
     int slot_bytes;
-    int stage_off;  // byte offset of the x staging copy inside the table region
 };
 
-// Shared memory: [mbarriers, 128 B][table][zero block][Sx][tile slots][ring], each table-side
+// Shared memory: [mbarriers, 256 B][table][zero block][Sx][tile slots][ring], each table-side
 // region sized for the larger of the two GEMVs (they are used one after the other).
 struct StackSmem {
     int table, zero, sx, red, ring;
 };
 
+template <class F>
+__host__ __device__ inline int stack_stage_off(int dm) {
+    return (gemv_smem_layout<F>(dm, 1, false).table_bytes + 15) & ~15;  // staging copy of x, inside the table region
+}
+
 template <class FA, class FD>
 __host__ __device__ inline StackSmem stack_smem_layout(int dm, int ff, int stages) {
     const GemvSmem a = gemv_smem_layout<FA>(dm, 1, false), b = gemv_smem_layout<FD>(ff, 1, false);
     StackSmem s;
-    s.table = 128;
+    s.table = 256;
     const int ta = ((a.table_bytes + 15) & ~15) + dm * 4;  // gate/up table + staging copy of x
     s.zero = s.table + (ta > b.table_bytes ? ta : b.table_bytes);
     s.sx = s.zero + (a.zero_bytes > b.zero_bytes ? a.zero_bytes : b.zero_bytes);
@@ -112,11 +119,19 @@ __device__ void grid_sync(unsigned* bar, unsigned target, int* err, int* s_abort
 // SMs' rates differ by up to ~25%, and which SMs are slow changes from phase to phase: an
 // equal static split would leave every phase waiting for the slowest SM).  Every value is
 // reduced in an order fixed by the chunk boundaries, never by which CTA ran a chunk, so the
-// result is deterministic.  Down chunks leave their 16-row partial sums in a buffer; the next
-// gate/up prologue adds them to the residual stream in chunk order.
+// result is deterministic.
+//   gate/up: the warp that completes a tile writes h = silu(g) * u for its 16 rows straight
+//            into the down GEMV's fragment table in global memory (f16 hi/lo pairs at their
+//            table slots) plus the rows' sum (the Q4_K down needs 32-element sums of h), so
+//            the down prologue is a plain copy;
+//   down:    chunks leave their 16-row partial sums in a buffer; the next gate/up prologue
+//            adds them to the residual stream in chunk order.
+// (Completing the down tiles in the phase instead, the last chunk to arrive adding up the
+// others, costs a release/acquire round trip per chunk on the warp that is already the
+// furthest behind: it measured ~25% slower.)
 struct StageDesc {
     int tile, kb, n;  // blocks [kb, kb + n) of the tile
-    int part;         // chunk of the tile (down)
+    int part;         // chunk of the tile
     int flags;
 };
 constexpr int kLastOfChunk = 1, kPhaseEnd = 2;
@@ -129,7 +144,7 @@ struct PhaseGeo {
 };
 
 template <class F>
-__device__ __forceinline__ PhaseGeo phase_geo(int M, int K, int cb) {
+__host__ __device__ __forceinline__ PhaseGeo phase_geo(int M, int K, int cb) {
     PhaseGeo g;
     g.nbk = (K + F::kBlockElems - 1) / F::kBlockElems;
     g.cb = cb < g.nbk ? cb : g.nbk;
@@ -184,12 +199,42 @@ __device__ bool produce_chunks(Ring& r, StageDesc* desc, const uint8_t* w, const
     }
 }
 
-// Consumer warps: every stage of the phase until the end marker.  Fused (gate/up): whole
-// tiles, h = silu(G xn) * (U xn).  Otherwise (down): chunk partials to part_out.
-template <class F, bool FUSED>
-__device__ void consume_chunks(Ring& r, const StageDesc* desc, const LaneCtx<1>& ctx, const PhaseGeo& pg, int M,
-                               float* y, float* part_out, float* red, int* tcnt, int& tslot, bool& aborted,
-                               int* err) {
+// Where the chunks of a phase go.
+struct ChunkOut {
+    int M;         // rows of the GEMV
+    float* parts;  // down: chunk partials [tiles][chunks per tile][16]
+    uint2* htab;   // gate/up: the down GEMV's fragment table
+    float* hsx;    // gate/up: 16-row sums of h
+};
+
+// Gate/up tile: h for rows tile*16 + (lane & 15) (lanes 16-31 repeat lanes 0-15), written into
+// FT's fragment table; 4-row chunks are gathered on lanes 0, 4, 8, 12.
+template <class FT>
+__device__ __forceinline__ void finish_gateup(const ChunkOut& o, int tile, int lane, float g, float u, bool& bad) {
+    const int grow = tile * 16 + (lane & 15);
+    const float h = grow < o.M ? silu_mul(g, u) : 0.f;
+    const float h1 = __shfl_down_sync(kFull, h, 1), h2 = __shfl_down_sync(kFull, h, 2),
+                h3 = __shfl_down_sync(kFull, h, 3);
+    if (lane < 16 && (lane & 3) == 0) {
+        const float xs[4] = {h, h1, h2, h3};
+        const int slot = chunk_slot<FT>(tile * 4 + (lane >> 2));
+        pack_chunk(xs, o.htab[slot], o.htab[slot + FT::kLoOff], bad);
+    }
+    if constexpr (FT::kNeedSx) {
+        float s = h;
+        s += __shfl_xor_sync(kFull, s, 1);
+        s += __shfl_xor_sync(kFull, s, 2);
+        s += __shfl_xor_sync(kFull, s, 4);
+        s += __shfl_xor_sync(kFull, s, 8);
+        if (lane == 0) o.hsx[tile] = s;
+    }
+}
+
+// Consumer warps: every stage of the phase until the end marker.  F = weight format, FT = the
+// format whose fragment table the gate/up finishers write (the down GEMV's).
+template <class F, class FT, bool FUSED>
+__device__ void consume_chunks(Ring& r, const StageDesc* desc, const LaneCtx<1>& ctx, const PhaseGeo& pg,
+                               const ChunkOut& o, float* red, int* tcnt, int& tslot, bool& aborted, int* err) {
     constexpr int kMats = FUSED ? 2 : 1;
     constexpr int SB = stage_blocks(FUSED);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -197,6 +242,7 @@ __device__ void consume_chunks(Ring& r, const StageDesc* desc, const LaneCtx<1>&
     const int mt = warp_matrix(warp, FUSED), jj = warp % SB;  // this warp's matrix and block
     float yA = 0.f, yB = 0.f;
     float pA[1][1] = {{0.f}}, pB[1][1] = {{0.f}};
+    bool bad = false;
     while (!aborted) {
         if (!mbar_wait(r.full0 + 8 * r.slot, r.round & 1)) {
             aborted = true;
@@ -233,27 +279,96 @@ __device__ void consume_chunks(Ring& r, const StageDesc* desc, const LaneCtx<1>&
             __threadfence_block();
             const float* rr = red + (size_t)tslot * kCW * 16;
             const int row = lane & 15;
-            if (lane < 16) {
-                float f[kMats];
+            float f[kMats];
 #pragma unroll
-                for (int m = 0; m < kMats; ++m) {
-                    float acc = 0.f;
+            for (int m = 0; m < kMats; ++m) {
+                float acc = 0.f;
 #pragma unroll
-                    for (int w = m * SB; w < (m + 1) * SB; ++w) acc += rr[w * 16 + row];
-                    f[m] = acc;
-                }
-                if constexpr (FUSED) {
-                    const int grow = d.tile * 16 + row;
-                    if (grow < M) y[grow] = silu_mul(f[0], f[kMats - 1]);
-                } else {
-                    part_out[((size_t)d.tile * pg.cpt + d.part) * 16 + row] = f[0];
-                }
+                for (int w = m * SB; w < (m + 1) * SB; ++w) acc += rr[w * 16 + row];
+                f[m] = acc;
             }
             __syncwarp();
-            if (lane == 0) tcnt[tslot] = 0;
+            if (lane == 0) tcnt[tslot] = 0;  // slot free for chunk + NT
+            if constexpr (FUSED) {
+                finish_gateup<FT>(o, d.tile, lane, f[0], f[kMats - 1], bad);
+            } else {
+                if (lane < 16) o.parts[((size_t)d.tile * pg.cpt + d.part) * 16 + row] = f[0];
+            }
         }
         if (++tslot == NT) tslot = 0;
     }
+    if (bad && err) atomicOr(err, 1);
+}
+
+// Down prologue: the fragment table the gate/up finishers left in global memory is copied
+// into shared memory by one bulk copy (issued by consumer thread 0 after the phase barrier's
+// acquire, completing on tab_bar), while the threads build the Q4_K 32-element sums from
+// pairs of 16-row sums.  Returns false when the copy did not land in time.
+template <class F>
+__device__ __forceinline__ bool load_down_table(uint2* xt, float* sx, const StackKArgs& a, int tiles_a, uint32_t tab_bar,
+                                                uint32_t parity) {
+    const int bytes = gemv_smem_layout<F>(a.ff, 1, false).table_bytes;
+    if (threadIdx.x == 0) {
+        // the table was written through the generic proxy (by other SMs) and the shared
+        // region was last read through it; the copy goes through the async proxy
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive_expect_tx(tab_bar, (uint32_t)bytes);
+        bulk_g2s(smem_addr(xt), a.htab, (uint32_t)bytes, tab_bar);
+    }
+    if constexpr (F::kNeedSx) {
+        for (int j = threadIdx.x; j < bytes / 128; j += kCW * 32) {  // 32 elements = 8 chunks of 16 bytes
+            const float s0 = 2 * j < tiles_a ? __ldcg(a.hsx + 2 * j) : 0.f;
+            const float s1 = 2 * j + 1 < tiles_a ? __ldcg(a.hsx + 2 * j + 1) : 0.f;
+            sx[j] = s0 + s1;
+        }
+    }
+    return mbar_wait(tab_bar, parity);
+}
+
+// Gate/up prologue of a layer l > 0.  Pass 1: x_l = x_{l-1} + the down partials of layer l-1
+// (added in chunk order), this CTA's share [c0, c1) written back, sum of squares accumulated,
+// x_l * w staged in shared memory (the norm weight loads ride in the same round trip as the
+// activation's).  Pass 2: xn = (x_l * w) * inv (rms_norm, crates/hayai-cpu/src/attention.rs:
+// 142-147) into the fragment table, with F's 32-element sums for Q4_K.
+template <class F>
+__device__ void stack_prologue_a(uint2* xt, float* sx, float* xs, const float* xin, const XAccum& acc, float* xnext,
+                                 int c0, int c1, const float* nw, int dm, float eps, float* scratch, int* err) {
+    constexpr int kStep = kCW * 32;
+    const int nchunk = dm >> 2;
+    const int ntab = (((dm + F::kBlockElems - 1) / F::kBlockElems) * F::kBlockElems) >> 2;  // a multiple of 32
+    float4* xs4 = reinterpret_cast<float4*>(xs);
+    const float4* nw4 = reinterpret_cast<const float4*>(nw);
+    float ssq = 0.f;
+    for (int c = threadIdx.x; c < nchunk; c += kStep) {
+        const float4 w = nw ? __ldg(nw4 + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+        const float4 v = load_x4<kLdcg>(xin, c, acc);
+        if (c >= c0 && c < c1) reinterpret_cast<float4*>(xnext)[c] = v;
+        ssq += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+        xs4[c] = make_float4(v.x * w.x, v.y * w.y, v.z * w.z, v.w * w.w);
+    }
+    const float tot = block_sum(ssq, scratch, kStep, kBarPro);  // its barriers also publish xs
+    const float inv = nw ? 1.0f / sqrtf(tot / (float)dm + eps) : 1.0f;
+    bool bad = false;
+    for (int c = threadIdx.x; c < ntab; c += kStep) {  // whole warps: ntab is a multiple of 32
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c < nchunk) {
+            a = xs4[c];
+            a = make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+        }
+        const float v4[4] = {a.x, a.y, a.z, a.w};
+        const int slot = chunk_slot<F>(c);
+        pack_chunk(v4, xt[slot], xt[slot + F::kLoOff], bad);
+        if constexpr (F::kNeedSx) {
+            // 8 consecutive chunks (= consecutive lanes) form one 32-element sub-block
+            float s = (a.x + a.y) + (a.z + a.w);
+            s += __shfl_xor_sync(kFull, s, 1);
+            s += __shfl_xor_sync(kFull, s, 2);
+            s += __shfl_xor_sync(kFull, s, 4);
+            if ((threadIdx.x & 7) == 0) sx[c >> 3] = s;
+        }
+    }
+    if (bad && err) atomicOr(err, 1);
 }
 
 template <class FA, class FD>
@@ -269,6 +384,7 @@ __global__ void __launch_bounds__(kTThreads, 1) ffn_stack_kernel(StackKArgs a) {
     Ring r;
     r.full0 = smem_addr(smem);
     r.empty0 = r.full0 + 8 * kMaxStages;
+    const uint32_t tab_bar = r.empty0 + 8 * kMaxStages;  // the down table copy
     r.base = smem + L.ring;
     r.base_s = smem_addr(r.base);
     r.S = S;
@@ -276,12 +392,14 @@ __global__ void __launch_bounds__(kTThreads, 1) ffn_stack_kernel(StackKArgs a) {
     r.slot = r.round = 0;
     const PhaseGeo ga = phase_geo<FA>(a.ff, a.dm, 1 << 20);  // gate/up: whole tiles
     const PhaseGeo gd = phase_geo<FD>(a.dm, a.ff, kUnits);   // down: 16-block runs
+    const int tiles_a = (a.ff + 15) / 16;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(r.full0 + 8 * s, 1);
             mbar_init(r.empty0 + 8 * s, kCW);
         }
+        mbar_init(tab_bar, 1);
         mbar_fence_init();
         s_abort = 0;
     }
@@ -304,58 +422,91 @@ __global__ void __launch_bounds__(kTThreads, 1) ffn_stack_kernel(StackKArgs a) {
     uint2* zero = reinterpret_cast<uint2*>(smem + L.zero);
     float* sx = reinterpret_cast<float*>(smem + L.sx);
     float* red = reinterpret_cast<float*>(smem + L.red);
+    float* xs = reinterpret_cast<float*>(smem + L.table + stack_stage_off<FA>(a.dm));
     for (int i = threadIdx.x; i < (L.sx - L.zero) / 8; i += kCW * 32) zero[i] = make_uint2(0u, 0u);
+    // table chunks past the last tile of h are padding no finisher writes: zero them once
+    if (blockIdx.x == 0) {
+        const int nchunk = gemv_smem_layout<FD>(a.ff, 1, false).table_bytes / 16;
+        for (int c = tiles_a * 4 + (int)threadIdx.x; c < nchunk; c += kCW * 32) {
+            const int sl = chunk_slot<FD>(c);
+            a.htab[sl] = a.htab[sl + FD::kLoOff] = make_uint2(0u, 0u);
+        }
+    }
     int tslot = 0;
     bool aborted = false;
     unsigned phases = 0;
     const unsigned C = gridDim.x;
     const int nc4 = a.dm / 4;  // float4 chunks of x; this CTA writes back [c0, c1)
     const int c0 = (int)((long long)blockIdx.x * nc4 / C), c1 = (int)((long long)(blockIdx.x + 1) * nc4 / C);
+    const XAccum acc{a.parts, gd.cpt, nullptr, 0, 0};
+    // x_l: x_0 = the caller's x, then xbuf[l & 1]
+    auto xres = [&](int l) { return l == 0 ? a.x : a.xbuf + (size_t)(l & 1) * a.dm; };
     for (int l = 0; l < a.L; ++l) {
         const StackLayerPtrs ly = a.layers[l];
-        // gate/up: x_l = x_{l-1} + down partials of layer l-1; h = silu(G xn) * (U xn), xn = rms_norm(x_l)
+        // gate/up: h = silu(G xn) * (U xn), xn = rms_norm(x_l), x_l = x_{l-1} + D_{l-1} h_{l-1}
         {
-            const NormArgs nrm{ly.norm, a.dm, a.eps};
-            const float* xin = l == 0 ? a.xbuf : a.xbuf + (size_t)((l - 1) & 1) * a.dm;
-            // x_l, completed once (one pass over the partials), staged behind the gate/up table
-            float* xs = reinterpret_cast<float*>(smem + L.table + a.stage_off);
-            const XAccum acc = l == 0 ? XAccum{nullptr, 0, nullptr, 0, 0} : XAccum{a.parts, gd.cpt, nullptr, 0, 0};
-            float* xnext = a.xbuf + (size_t)(l & 1) * a.dm;
-            for (int c = threadIdx.x; c < nc4; c += kCW * 32) {
-                const float4 v = load_x4<kLdcg>(xin, c, acc);
-                reinterpret_cast<float4*>(xs)[c] = v;
-                if (l > 0 && c >= c0 && c < c1) reinterpret_cast<float4*>(xnext)[c] = v;
+            if (l == 0) {
+                const NormArgs nrm{ly.norm, a.dm, a.eps};
+                build_prologue<FA, 1, kLdcg>(xt, sx, a.x, a.dm, a.dm, 1, nrm, s_red, a.err, kCW * 32, kBarPro);
+            } else {
+                stack_prologue_a<FA>(xt, sx, xs, xres(l - 1), acc, xres(l), c0, c1, ly.norm, a.dm, a.eps, s_red, a.err);
             }
             named_bar_sync(kBarPro, kCW * 32);
-            build_prologue<FA, 1, kPlain>(xt, sx, xs, a.dm, a.dm, 1, nrm, s_red, a.err, kCW * 32, kBarPro);
-            named_bar_sync(kBarPro, kCW * 32);
             const LaneCtx<1> ctx = make_ctx<FA, 1>(xt, zero, sx, a.dm, lane);
-            consume_chunks<FA, true>(r, s_desc, ctx, ga, a.ff, a.h, nullptr, red, s_tcnt, tslot, aborted, a.err);
+            const ChunkOut o{a.ff, nullptr, a.htab, a.hsx};
+            consume_chunks<FA, FD, true>(r, s_desc, ctx, ga, o, red, s_tcnt, tslot, aborted, a.err);
             grid_sync(a.bar, ++phases * C, a.err, &s_abort);
             if (s_abort) aborted = true;
         }
         // down: chunk partials of D h
         {
-            const NormArgs nrm{nullptr, 0, 0.f};
-            build_prologue<FD, 1, kLdcg>(xt, sx, a.h, a.ff, a.ff, 1, nrm, s_red, a.err, kCW * 32, kBarPro);
+            if (!aborted && !load_down_table<FD>(xt, sx, a, tiles_a, tab_bar, l & 1)) {
+                aborted = true;
+                if (threadIdx.x == 0 && a.err) atomicOr(a.err, 2);
+            }
             named_bar_sync(kBarPro, kCW * 32);
             const LaneCtx<1> ctx = make_ctx<FD, 1>(xt, zero, sx, a.ff, lane);
-            consume_chunks<FD, false>(r, s_desc, ctx, gd, a.dm, nullptr, a.parts, red, s_tcnt, tslot, aborted,
-                                      a.err);
+            const ChunkOut o{a.dm, a.parts, nullptr, nullptr};
+            consume_chunks<FD, FD, false>(r, s_desc, ctx, gd, o, red, s_tcnt, tslot, aborted, a.err);
             grid_sync(a.bar, ++phases * C, a.err, &s_abort);
             if (s_abort) aborted = true;
         }
     }
-    // x_L = x_{L-1} + the last down partials, into the caller's x
+    // x_L = x_{L-1} + the last down partials, into the caller's x (for L = 1 each element is
+    // read and then written by the same thread)
     if (!aborted) {
-        const float* xin = a.xbuf + (size_t)((a.L - 1) & 1) * a.dm;
-        const XAccum acc{a.parts, gd.cpt, nullptr, 0, 0};
+        const float* xin = xres(a.L - 1);
         for (int c = c0 + (int)threadIdx.x; c < c1; c += kCW * 32)
             reinterpret_cast<float4*>(a.x)[c] = load_x4<kLdcg>(xin, c, acc);
     }
 }
 
 // ------------------------------------------------------------------ host side
+// Scratch layout (byte offsets, 256-aligned).
+struct StackScratch {
+    size_t bar, xbuf, parts, htab, hsx, total;
+};
+
+template <class FA, class FD>
+static StackScratch stack_scratch(int L, int dm, int ff) {
+    const PhaseGeo gd = phase_geo<FD>(dm, ff, kUnits);
+    const size_t ta = (size_t)(ff + 15) / 16, td = (size_t)(dm + 15) / 16;
+    StackScratch s;
+    size_t off = 0;
+    auto take = [&off](size_t bytes) {
+        const size_t o = off;
+        off = (off + bytes + 255) & ~(size_t)255;
+        return o;
+    };
+    s.bar = take((1 + 2 * (size_t)L) * 4);
+    s.xbuf = take(2 * (size_t)dm * 4);
+    s.parts = take(td * gd.cpt * 16 * 4);
+    s.htab = take((size_t)gemv_smem_layout<FD>(ff, 1, false).table_bytes);
+    s.hsx = take(ta * 4);
+    s.total = off;
+    return s;
+}
+
 template <class FA, class FD>
 static int stack_stages(int dm, int ff, int smem_limit, int* slot_bytes) {
     const int sa = tma_stage_bytes<FA>(true), sb = tma_stage_bytes<FD>(false);
@@ -366,11 +517,17 @@ static int stack_stages(int dm, int ff, int smem_limit, int* slot_bytes) {
 }
 
 template <class FA, class FD>
-static cudaError_t launch_stack_t(StackKArgs a, int num_sms, int smem_limit, cudaStream_t stream, bool dry) {
+static cudaError_t launch_stack_t(const StackLaunch& s, int num_sms, int smem_limit, cudaStream_t stream, bool dry,
+                                  size_t* scratch_bytes) {
+    const PhaseGeo ga = phase_geo<FA>(s.ff, s.dm, 1 << 20), gd = phase_geo<FD>(s.dm, s.ff, kUnits);
+    if ((long long)((s.ff + 15) / 16) * ga.nbk < num_sms || (long long)((s.dm + 15) / 16) * gd.nbk < num_sms)
+        return cudaErrorInvalidConfiguration;  // fewer units than SMs: the per-layer kernels shrink their grid
+    if (gd.cpt > kMaxParts || s.dm % 4 || s.ff % 4)
+        return cudaErrorInvalidConfiguration;  // more down chunks per tile than the prologue adds up
     int slot_bytes = 0;
-    const int S = stack_stages<FA, FD>(a.dm, a.ff, smem_limit, &slot_bytes);
+    const int S = stack_stages<FA, FD>(s.dm, s.ff, smem_limit, &slot_bytes);
     if (S < 3) return cudaErrorInvalidConfiguration;  // too shallow to pay off: use the per-layer kernels
-    const int smem = stack_smem_layout<FA, FD>(a.dm, a.ff, S).ring + S * slot_bytes;
+    const int smem = stack_smem_layout<FA, FD>(s.dm, s.ff, S).ring + S * slot_bytes;
     auto kern = ffn_stack_kernel<FA, FD>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -378,28 +535,12 @@ static cudaError_t launch_stack_t(StackKArgs a, int num_sms, int smem_limit, cud
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTThreads, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    if (dry) return cudaSuccess;
-    a.stages = S;
-    a.slot_bytes = slot_bytes;
-    a.stage_off = (gemv_smem_layout<FA>(a.dm, 1, false).table_bytes + 15) & ~15;
-    e = cudaMemsetAsync(a.bar, 0, (size_t)(1 + 2 * a.L) * sizeof(unsigned), stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(a.xbuf, a.x, (size_t)a.dm * sizeof(float), cudaMemcpyDeviceToDevice, stream);
-    if (e != cudaSuccess) return e;
-    void* args[] = {&a};
-    return cudaLaunchCooperativeKernel((const void*)kern, dim3(num_sms), dim3(kTThreads), args, smem, stream);
-}
-
-// The CTA count the kernel runs with: one per SM, as the per-layer kernels (their partition
-// of each GEMV, and so the summation order, is the same).
-cudaError_t launch_ffn_stack(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
-                             cudaStream_t stream, bool dry) {
-    const int ntiles_a = (s.ff + 15) / 16, ntiles_b = (s.dm + 15) / 16;
-    const int nbk_a = (s.dm + (type_a == T_Q8_0 ? 127 : 255)) / (type_a == T_Q8_0 ? 128 : 256);
-    const int nbk_b = (s.ff + (type_d == T_Q8_0 ? 127 : 255)) / (type_d == T_Q8_0 ? 128 : 256);
-    if ((long long)ntiles_a * nbk_a < num_sms || (long long)ntiles_b * nbk_b < num_sms)
-        return cudaErrorInvalidConfiguration;  // fewer units than SMs: the per-layer kernels shrink their grid
-    if ((nbk_b + kUnits - 1) / kUnits > kMaxParts || s.dm % 4 || s.ff % 4)
-        return cudaErrorInvalidConfiguration;  // more down chunks per tile than the prologue adds up
+    const StackScratch sc = stack_scratch<FA, FD>(s.L, s.dm, s.ff);
+    if (dry) {
+        if (scratch_bytes) *scratch_bytes = sc.total;
+        return cudaSuccess;
+    }
+    uint8_t* base = static_cast<uint8_t*>(s.scratch);
     StackKArgs a{};
     a.layers = (const StackLayerPtrs*)s.layers;
     a.L = s.L;
@@ -408,18 +549,27 @@ cudaError_t launch_ffn_stack(int type_a, int type_d, const StackLaunch& s, int n
     a.ts_a = s.ts_a;
     a.ts_b = s.ts_b;
     a.x = s.x;
-    a.xbuf = s.xbuf;
-    a.parts = s.parts;
-    a.h = s.h;
+    a.xbuf = reinterpret_cast<float*>(base + sc.xbuf);
+    a.parts = reinterpret_cast<float*>(base + sc.parts);
+    a.htab = reinterpret_cast<uint2*>(base + sc.htab);
+    a.hsx = reinterpret_cast<float*>(base + sc.hsx);
     a.eps = s.eps;
     a.err = s.err;
-    a.sk_ws = s.sk_ws;
-    a.sk_cnt = s.sk_cnt;
-    a.slots_a = s.slots_a;
-    a.slots_b = s.slots_b;
-    a.bar = s.bar;
+    a.bar = reinterpret_cast<unsigned*>(base + sc.bar);
+    a.stages = S;
+    a.slot_bytes = slot_bytes;
+    e = cudaMemsetAsync(a.bar, 0, sc.xbuf - sc.bar, stream);
+    if (e != cudaSuccess) return e;
+    void* args[] = {&a};
+    return cudaLaunchCooperativeKernel((const void*)kern, dim3(num_sms), dim3(kTThreads), args, smem, stream);
+}
+
+// The CTA count the kernel runs with: one per SM.
+cudaError_t launch_ffn_stack(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
+                             cudaStream_t stream, bool dry, size_t* scratch_bytes) {
 #define HC_STACK_CASE(TA, FAT, TD, FDT) \
-    if (type_a == TA && type_d == TD) return launch_stack_t<FAT, FDT>(a, num_sms, smem_limit, stream, dry);
+    if (type_a == TA && type_d == TD)   \
+        return launch_stack_t<FAT, FDT>(s, num_sms, smem_limit, stream, dry, scratch_bytes);
     HC_STACK_CASE(T_Q4_K, FmtQ4K, T_Q6_K, FmtQ6K)
     HC_STACK_CASE(T_Q4_K, FmtQ4K, T_Q4_K, FmtQ4K)
     HC_STACK_CASE(T_Q6_K, FmtQ6K, T_Q6_K, FmtQ6K)

@@ -24,20 +24,14 @@ struct StackLaunch {
     int L, dm, ff;
     long long ts_a, ts_b;  // tile strides of gate/up and of down
     float* x;              // [dm], updated in place
-    float* xbuf;           // [2][dm] scratch
-    float* parts;          // [ceil(dm / 16) * ceil(ff / 4096)][16] scratch (down partials)
-    float* h;              // [ff]
     float eps;
     int* err;
-    float* sk_ws;
-    int* sk_cnt;
-    int slots_a, slots_b;
-    unsigned* bar;  // [1 + 2L] grid-barrier and chunk counters
+    void* scratch;  // launch_ffn_stack(dry) reports its size
 };
 // cudaErrorInvalidConfiguration: the shapes or formats are not covered (use the per-layer
-// kernels).  dry = only check that the launch is possible.
+// kernels).  dry = only check that the launch is possible and report the scratch bytes.
 cudaError_t launch_ffn_stack(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
-                             cudaStream_t stream, bool dry);
+                             cudaStream_t stream, bool dry, size_t* scratch_bytes);
 
 // CUDA-core GEMV on the raw GGUF layout for F32 and the IQ2/IQ3 codebook formats.
 cudaError_t launch_gemv_simple(int type, const uint8_t* w, size_t row_bytes, int M, int K, const float* x,

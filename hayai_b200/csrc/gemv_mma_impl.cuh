@@ -42,6 +42,29 @@ __device__ __forceinline__ void inv_map(int e, int& mi, int& t) {
     else inv_q80(e, mi, t);
 }
 
+// Table slot (single vector) of the hi part of 4-element chunk c of the activation; the lo
+// part sits F::kLoOff entries further on.
+template <class F>
+__device__ __forceinline__ int chunk_slot(int c) {
+    const int e = 4 * c, kb = e / F::kBlockElems;
+    int mi, t;
+    inv_map<F>(e - kb * F::kBlockElems, mi, t);
+    return kb * table_entries_per_block<F>(1) + F::template tab<1>(mi, 0, t);
+}
+
+// One chunk as its two table entries: f16 hi parts and 2^11-scaled lo parts, elements paired
+// (0, 2) and (1, 3).  bad: an element outside the f16 range.
+__device__ __forceinline__ void pack_chunk(const float (&xs)[4], uint2& hi2, uint2& lo2, bool& bad) {
+    __half hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if (fabsf(xs[j]) >= 65504.0f && isfinite(xs[j])) bad = true;
+        split_f16(xs[j], hi[j], lo[j]);
+    }
+    hi2 = make_uint2(h2_as_u32(__halves2half2(hi[0], hi[2])), h2_as_u32(__halves2half2(hi[1], hi[3])));
+    lo2 = make_uint2(h2_as_u32(__halves2half2(lo[0], lo[2])), h2_as_u32(__halves2half2(lo[1], lo[3])));
+}
+
 // ------------------------------------------------------------------ prologue
 // Optional RMSNorm of the activation rows, applied while the fragment table is built:
 // xn[i] = (x[i] * inv[v]) * w[i] for i < len (rms_norm, crates/hayai-cpu/src/attention.rs:142-147).
@@ -158,19 +181,11 @@ __device__ void build_prologue(uint2* __restrict__ xt, float* __restrict__ sx, c
             }
             if (c < ntab) {
                 const float xs[4] = {a.x, a.y, a.z, a.w};
-                __half hi[4], lo[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    if (fabsf(xs[j]) >= 65504.0f && isfinite(xs[j])) bad = true;
-                    split_f16(xs[j], hi[j], lo[j]);
-                }
                 const int e = 4 * c, kb = e / F::kBlockElems;
                 int mi, t;
                 inv_map<F>(e - kb * F::kBlockElems, mi, t);
                 const int base = kb * table_entries_per_block<F>(NV) + F::template tab<NV>(mi, v, t);
-                xt[base] = make_uint2(h2_as_u32(__halves2half2(hi[0], hi[2])), h2_as_u32(__halves2half2(hi[1], hi[3])));
-                xt[base + F::kLoOff] =
-                    make_uint2(h2_as_u32(__halves2half2(lo[0], lo[2])), h2_as_u32(__halves2half2(lo[1], lo[3])));
+                pack_chunk(xs, xt[base], xt[base + F::kLoOff], bad);
             }
             if constexpr (F::kNeedSx) {
                 // 8 consecutive chunks (= consecutive lanes) form one 32-element sub-block
@@ -242,10 +257,26 @@ __device__ __forceinline__ void q4k_factors(const uint4& h, int t, float& c0, fl
     const uint32_t pm = t < 2 ? (Z & 0x3F3Fu) : (((W >> 4) & 0x0F0Fu) | ((Z >> 2) & 0x3030u));
     const float2 dd = __half22float2(u32_as_h2(h.x));
     const float d64 = 64.f * dd.x;
-    c0 = d64 * (float)(psc & 0xFFu);
-    c1 = d64 * (float)(psc >> 8);
-    k0 = fmaf(dd.y, (float)(pm & 0xFFu), c0);
-    k1 = fmaf(dd.y, (float)(pm >> 8), c1);
+    c0 = d64 * u8_to_f32(psc, 0);
+    c1 = d64 * u8_to_f32(psc, 1);
+    k0 = fmaf(dd.y, u8_to_f32(pm, 0), c0);
+    k1 = fmaf(dd.y, u8_to_f32(pm, 1), c1);
+}
+
+// The 8 codes of one Q4_K word as four f16x2 registers, every code as f16(1 + n/64): low
+// nibbles of bytes 0/2 (lo02) and 1/3 (lo13), high nibbles of bytes 0/2 (hi02) and 1/3 (hi13).
+// High nibbles sit at mantissa bits 4-7 under the 0x3C00 magic (one LOP3 per register; bytes
+// 1/3 after one shift by 8); low nibbles at mantissa bits 0-3 under the 0x6400 magic give
+// f16(1024 + n), turned into 1 + n/64 = (1024 + n) / 64 - 15 by one exact HFMA2, so two of
+// the four registers cost an FMA-pipe op instead of an ALU shift.
+__device__ __forceinline__ void q4k_codes(uint32_t w, uint32_t& lo02, uint32_t& lo13, uint32_t& hi02,
+                                          uint32_t& hi13) {
+    constexpr uint32_t kInv64 = 0x24002400u, kMinus15 = 0xCB80CB80u;  // f16x2 (1/64, 1/64), (-15, -15)
+    const uint32_t w8 = w >> 8;
+    hi02 = lop3_and_or(w, 0x00F000F0u, 0x3C003C00u);
+    hi13 = lop3_and_or(w8, 0x00F000F0u, 0x3C003C00u);
+    lo02 = hfma2_u32(lop3_and_or(w, 0x000F000Fu, 0x64006400u), kInv64, kMinus15);
+    lo13 = hfma2_u32(lop3_and_or(w8, 0x000F000Fu, 0x64006400u), kInv64, kMinus15);
 }
 
 // One Q4_K unit, lane-distributed sub-blocks.  Lane t's codes are chunk t of the super-block
@@ -287,15 +318,9 @@ __device__ __forceinline__ void q4k_unit(const Q4KBlk (&A)[NMAT], const Q4KBlk (
                                     A[m].q1.x, A[m].q1.y, A[m].q1.z, A[m].q1.w};
             const uint32_t wB[8] = {B[m].q0.x, B[m].q0.y, B[m].q0.z, B[m].q0.w,
                                     B[m].q1.x, B[m].q1.y, B[m].q1.z, B[m].q1.w};
-            const uint32_t a = wA[wi], b = wB[wi];
-            const uint32_t lo02a = lop3_and_or(a << 4, 0x00F000F0u, 0x3C003C00u);
-            const uint32_t lo13a = lop3_and_or(a >> 4, 0x00F000F0u, 0x3C003C00u);
-            const uint32_t hi02a = lop3_and_or(a, 0x00F000F0u, 0x3C003C00u);
-            const uint32_t hi13a = lop3_and_or(a >> 8, 0x00F000F0u, 0x3C003C00u);
-            const uint32_t lo02b = lop3_and_or(b << 4, 0x00F000F0u, 0x3C003C00u);
-            const uint32_t lo13b = lop3_and_or(b >> 4, 0x00F000F0u, 0x3C003C00u);
-            const uint32_t hi02b = lop3_and_or(b, 0x00F000F0u, 0x3C003C00u);
-            const uint32_t hi13b = lop3_and_or(b >> 8, 0x00F000F0u, 0x3C003C00u);
+            uint32_t lo02a, lo13a, hi02a, hi13a, lo02b, lo13b, hi02b, hi13b;
+            q4k_codes(wA[wi], lo02a, lo13a, hi02a, hi13a);
+            q4k_codes(wB[wi], lo02b, lo13b, hi02b, hi13b);
 #pragma unroll
             for (int v = 0; v < NV; ++v) {
                 mma16816(lo[m][v], lo02a, lo02b, lo13a, lo13b, f[fm][v].x, f[fm][v].y);
@@ -327,12 +352,6 @@ __device__ __forceinline__ void q4k_unit(const Q4KBlk (&A)[NMAT], const Q4KBlk (
 // then the f16 d plane (nb entries, padded to 16 B).  ql word wq = 4h + 2qq + lh of lane t
 // holds original ql bytes 64h + 32qq + 16lh + 4t..+3; qh word wh = 2h + lh holds
 // qh bytes 32h + 16lh + 4t..+3 (q6k.rs:26-57 layout).
-__device__ __forceinline__ float i8_to_f32(uint32_t word, int byte) {
-    const uint32_t b = (uint32_t)byte;
-    const uint32_t sel = b | ((0x8u | b) << 4) | ((0x8u | b) << 8) | ((0x8u | b) << 12);
-    return (float)(int)prmt(word, 0u, sel);
-}
-
 struct Q6KBlk {
     uint4 l0, l1, qh, sc;
     uint16_t d;
@@ -347,8 +366,9 @@ __device__ __forceinline__ void q6k_block(const Q6KBlk& A, const Q6KBlk& B, int 
     const uint32_t LB[8] = {B.l0.x, B.l0.y, B.l0.z, B.l0.w, B.l1.x, B.l1.y, B.l1.z, B.l1.w};
     const uint32_t QHA[4] = {A.qh.x, A.qh.y, A.qh.z, A.qh.w};
     const uint32_t QHB[4] = {B.qh.x, B.qh.y, B.qh.z, B.qh.w};
-    const uint32_t SA[4] = {A.sc.x, A.sc.y, A.sc.z, A.sc.w};
-    const uint32_t SB[4] = {B.sc.x, B.sc.y, B.sc.z, B.sc.w};
+    // int8 scales, 0x80-flipped for s8_to_f32_flipped
+    const uint32_t SA[4] = {A.sc.x ^ 0x80808080u, A.sc.y ^ 0x80808080u, A.sc.z ^ 0x80808080u, A.sc.w ^ 0x80808080u};
+    const uint32_t SB[4] = {B.sc.x ^ 0x80808080u, B.sc.y ^ 0x80808080u, B.sc.z ^ 0x80808080u, B.sc.w ^ 0x80808080u};
     const uint2* xb = c.xb0 + kb * c.xstride;
     float sumA = 0.f, sumB = 0.f;
 #pragma unroll
@@ -374,8 +394,8 @@ __device__ __forceinline__ void q6k_block(const Q6KBlk& A, const Q6KBlk& B, int 
                          hsub2_u32(prmt(ua, 0x64646464u, 0x4341u), kOff),
                          hsub2_u32(prmt(ub, 0x64646464u, 0x4341u), kOff), f.x, f.y);
                 const int si = 8 * h + 2 * q + lh;  // scale index = element / 16
-                sumA += i8_to_f32(SA[si >> 2], si & 3) * (acc[0] + acc[1] * kLoScale);
-                sumB += i8_to_f32(SB[si >> 2], si & 3) * (acc[2] + acc[3] * kLoScale);
+                sumA += s8_to_f32_flipped(SA[si >> 2], si & 3) * (acc[0] + acc[1] * kLoScale);
+                sumB += s8_to_f32_flipped(SB[si >> 2], si & 3) * (acc[2] + acc[3] * kLoScale);
             }
         }
     }

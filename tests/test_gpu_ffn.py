@@ -156,6 +156,24 @@ def test_stack_kernel_matches_per_layer_kernels(engine):
         engine.set_stream(None)
 
 
+@pytest.mark.parametrize("tg,td,dm,ff", [
+    (oracle.Q4_K, oracle.Q4_K, 1024, 5120),  # down needs 32-element sums of h; 2 chunks per down tile
+    (oracle.Q6_K, oracle.Q6_K, 1024, 5120),
+    (oracle.Q8_0, oracle.Q8_0, 1024, 2080),  # h table padded from 2080 to 17 x 128 elements
+    (oracle.Q4_K, oracle.Q6_K, 2048, 8192),  # 2 chunks per down tile, 64 x 32 tiles
+])
+def test_stack_kernel_formats(engine, tg, td, dm, ff):
+    L = 3
+    layers, res, norms = make_stack(engine, L, tg, td, dm, ff, 650)
+    x = oracle.normal(651, dm)
+    ref = oracle_stack(layers, norms, tg, td, dm, ff, x)
+    nd = [torch.from_numpy(n).cuda() for n in norms]
+    got = engine.ffn_stack(*split(res), x, norms=nd, eps=EPS)
+    assert_parity(ref, got, what=f"stack kernel {tg}/{td} {dm}x{ff}")
+    again = engine.ffn_stack(*split(res), x, norms=nd, eps=EPS)
+    assert np.array_equal(got, again)
+
+
 def test_stack_rejects_mismatched_layers(engine):
     import hayai_b200 as hb
 

@@ -55,7 +55,7 @@ CONFIGS = {
     "llama8b-q8": dict(layers=8, d_model=4096, k_in=4096, d_ff=14336, tg=Q8_0, td=Q8_0,
                        workload="Llama-3-8B FFN shape, Q8_0 x3, stack of 8 distinct layers"),
     "llama70b": dict(layers=80, d_model=8192, k_in=8192, d_ff=28672, tg=Q4_K, td=Q6_K,
-                     workload="Llama-3-70B FFN stack x80, gate/up Q4_K, down Q6_K, TP=1"),
+                     workload="Llama-3-70B FFN stack x80, gate/up Q4_K, down Q6_K, batch-1 decode"),
 }
 
 
@@ -295,21 +295,30 @@ def run_ours(args):
         c["layers"] = args.layers
     L, dm, kin, ff, tg, td = c["layers"], c["d_model"], c["k_in"], c["d_ff"], c["tg"], c["td"]
     B = args.batch
+    # tensor parallelism: every rank holds a d_ff shard of every layer (gate/up rows, down
+    # columns); the down partials are exchanged inside the stack kernel (or by NCCL with
+    # --tp-impl nccl, the library-collective baseline)
+    tp = args.tp and world > 1
+    if tp and (B != 1 or kin != dm):
+        raise SystemExit("--tp runs the batch-1 stack of an unpadded model")
+    ffl = ff // world if tp else ff  # this rank's d_ff
     # the persistent stack kernel serves batch 1 when the FFN input width equals d_model
-    uses_stack = B == 1 and kin == dm and os.environ.get("HAYAI_STACK_KERNEL", "1") != "0"
+    uses_stack = B == 1 and kin == dm and (tp or os.environ.get("HAYAI_STACK_KERNEL", "1") != "0")
+    if tp and args.tp_impl == "nccl":
+        uses_stack = False
     eng = hb.CudaEngine(local)
     stream = torch.cuda.Stream(dev)  # one stream for torch's copies, our kernels and the CUDA events
     torch.cuda.set_stream(stream)
     eng.set_stream(stream)
 
     # ---- resident weights, generated and quantized on the device
-    scratch = torch.empty(max(ff * kin, dm * ff), dtype=torch.float32, device=dev)
+    scratch = torch.empty(max(ffl * kin, dm * ffl), dtype=torch.float32, device=dev)
     want_cpu = (rank == 0 and world == 1 and not args.no_cpu_baseline)
     S_cpu = 3 if want_cpu else 0
     G, U, D, raw = [], [], [], []
     seed0 = 1_000_003 * (rank + 1)
 
-    padded = torch.zeros(ff, kin, dtype=torch.float32, device=dev) if kin != dm else None
+    padded = torch.zeros(ffl, kin, dtype=torch.float32, device=dev) if kin != dm else None
 
     def synth(t, m, n, seed, keep, n_real=None):
         """Seeded N(0, 0.02^2) m x n_real weights, zero-padded to n columns, quantized on device."""
@@ -330,11 +339,12 @@ def run_ours(args):
     NW = []  # per-layer RMSNorm weights (ffn_norm), N(1, 0.1^2)
     for l in range(L):
         keep = l < S_cpu
-        g, gh = synth(tg, ff, kin, seed0 + 4 * l, keep, dm)
-        u, uh = synth(tg, ff, kin, seed0 + 4 * l + 1, keep, dm)
-        d, dh = synth(td, dm, ff, seed0 + 4 * l + 2, keep)
+        g, gh = synth(tg, ffl, kin, seed0 + 4 * l, keep, dm)
+        u, uh = synth(tg, ffl, kin, seed0 + 4 * l + 1, keep, dm)
+        d, dh = synth(td, dm, ffl, seed0 + 4 * l + 2, keep)
         nw = torch.empty(dm, dtype=torch.float32, device=dev)
-        eng.synth_normal_dev(seed0 + 4 * l + 3, nw, 1.0, 0.1)
+        # the norm weights and x are replicated: the same seed on every rank under TP
+        eng.synth_normal_dev((1_000_003 if tp else seed0) + 4 * l + 3, nw, 1.0, 0.1)
         G.append(g)
         U.append(u)
         D.append(d)
@@ -344,14 +354,38 @@ def run_ours(args):
     del scratch, padded
     x0 = torch.zeros(B, kin, dtype=torch.float32, device=dev)
     xs = torch.empty(B * dm, dtype=torch.float32, device=dev)
-    eng.synth_normal_dev(7 + rank, xs, 0.0, 1.0)
+    eng.synth_normal_dev(7 + (0 if tp else rank), xs, 0.0, 1.0)
     x0[:, :dm] = xs.view(B, dm)
     x = x0.clone()
     torch.cuda.synchronize(dev)
+    peers = None
+    if tp:
+        from hayai_b200.tp import PeerGroup
+
+        peers = PeerGroup(eng)
+
+    def run_stack(xx):
+        if tp:
+            eng.ffn_stack_tp_dev(G, U, D, xx, norms=NW, eps=EPS)
+        else:
+            eng.ffn_stack_dev(G, U, D, xx, B, norms=NW, eps=EPS)
+
+    if tp and args.tp_impl == "nccl":
+        import torch.distributed as dist
+
+        h_ws = torch.empty(ffl, dtype=torch.float32, device=dev)
+        y_ws = torch.empty(dm, dtype=torch.float32, device=dev)
+
+        def run_stack(xx):  # noqa: F811 -- per-layer kernels + one NCCL all-reduce per layer
+            for l in range(L):
+                eng.ffn_gateup_dev(G[l], U[l], xx, h_ws, 1, norm=NW[l], norm_len=dm, eps=EPS)
+                eng.gemv_dev(D[l], h_ws, y_ws)
+                dist.all_reduce(y_ws)
+                xx.view(-1).add_(y_ws)
 
     def step():
         x.copy_(x0)
-        eng.ffn_stack_dev(G, U, D, x, B, norms=NW, eps=EPS)
+        run_stack(x)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -373,9 +407,10 @@ def run_ours(args):
     eng.sync()  # surfaces any device-side error flag
     t = max_over_ranks(t_local, world, dev)
     barrier(world)
-    tok_bytes = L * layer_bytes(c)
-    value = world * args.steps * tok_bytes / t / 1e9
-    tokens_per_s = world * args.steps * B / t
+    tok_bytes = L * layer_bytes(c)  # the whole model's weights per token (all shards under TP)
+    jobs = 1 if tp else world       # TP: one token stream over all ranks; else independent replicas
+    value = jobs * args.steps * tok_bytes / t / 1e9
+    tokens_per_s = jobs * args.steps * B / t
 
     # ---- roofline of the dominant kernel, timed with CUDA events on the stream it runs on.
     # Batch 1 with uniform layers runs the whole stack as one persistent kernel per step
@@ -388,15 +423,16 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
         e0.record(stream)
         for _ in range(reps):
-            eng.ffn_stack_dev(G, U, D, x, B, norms=NW, eps=EPS)
+            run_stack(x)
         e1.record(stream)
         torch.cuda.synchronize(dev)
         k_time = e0.elapsed_time(e1) / 1e3 / reps
-        k_bytes = tok_bytes
-        kname = f"ffn_stack_kernel<{names[tg]},{names[td]}> (all {L} layers, one launch)"
-        kkey = f"stack_{args.config}_L{L}"
+        k_bytes = tok_bytes // world if tp else tok_bytes  # this GPU's shard under TP
+        kname = f"ffn_stack_kernel<{names[tg]},{names[td]}> (all {L} layers, one launch" + \
+            (f", d_ff shard 1/{world} + in-kernel exchange)" if tp else ")")
+        kkey = f"stack_{args.config}_L{L}" + (f"_tp{world}" if tp else "")
     else:
-        h = torch.empty(B, ff, dtype=torch.float32, device=dev)
+        h = torch.empty(B, ffl, dtype=torch.float32, device=dev)
         reps = 3 * L if L >= 8 else 96
         for i in range(L):
             eng.ffn_gateup_dev(G[i % L], U[i % L], x0, h, B, norm=NW[i % L], norm_len=dm, eps=EPS)
@@ -407,7 +443,7 @@ def run_ours(args):
         e1.record(stream)
         torch.cuda.synchronize(dev)
         k_time = e0.elapsed_time(e1) / 1e3 / reps
-        k_bytes = 2 * mat_bytes(tg, ff, kin)
+        k_bytes = 2 * mat_bytes(tg, ffl, kin)
         kname = f"gemv_tma_kernel<{names[tg]},{min(B, 4)},true> (fused gate/up + SiLU*up)"
         kkey = f"gateup_{args.config}_b{B}"
     achieved = k_bytes / k_time / 1e9
@@ -424,20 +460,31 @@ def run_ours(args):
     x_in.copy_(x0.view(-1).cpu())
     x_out = torch.empty_like(x_in).pin_memory()
     xi, xo = x_in.numpy(), x_out.numpy()
+
+    def host_call():
+        if tp and args.tp_impl == "ours":
+            return eng.ffn_stack_tp(G, U, D, xi, norms=NW, eps=EPS)
+        if tp:  # NCCL baseline: the same per-layer loop on a device copy of the host vector
+            xd = torch.from_numpy(xi).to(dev, non_blocking=True)
+            run_stack(xd)
+            return xd.cpu().numpy()
+        return eng.ffn_stack(G, U, D, xi, B, norms=NW, eps=EPS)
+
     for _ in range(3):
-        eng.ffn_stack(G, U, D, xi, B, norms=NW, eps=EPS)
+        host_call()
     barrier(world)
     torch.cuda.synchronize(dev)
     e0.record(stream)
     for _ in range(n_e2e):
-        xo[:] = eng.ffn_stack(G, U, D, xi, B, norms=NW, eps=EPS)
+        xo[:] = host_call()
     e1.record(stream)
     torch.cuda.synchronize(dev)
     t_e2e = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
-    e2e = {"value": round(world * n_e2e * tok_bytes / t_e2e / 1e9, 2), "unit": "GB/s",
-           "tokens_per_s": round(world * n_e2e * B / t_e2e, 2), "steps": n_e2e,
+    e2e = {"value": round(jobs * n_e2e * tok_bytes / t_e2e / 1e9, 2), "unit": "GB/s",
+           "tokens_per_s": round(jobs * n_e2e * B / t_e2e, 2), "steps": n_e2e,
            "h2d_bytes_per_step": B * kin * 4, "d2h_bytes_per_step": B * kin * 4,
-           "api": "hc_ffn_stack (host buffers)"}
+           "api": ("hc_ffn_stack_tp" if tp and args.tp_impl == "ours" else
+                   "per-layer kernels + torch.distributed all_reduce" if tp else "hc_ffn_stack") + " (host buffers)"}
     assert np.isfinite(xo).all()
 
     cpu = None
@@ -449,20 +496,24 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": c_dtype(c),
+            "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": c_dtype(c),
             "data": "synthetic (seeded N(0,0.02^2) weights quantized on device, N(0,1) activations)",
             "config": {"workload": c["workload"], "batch": B, "layers": L, "d_model": dm, "d_ff": ff,
                        "kernel_path": "persistent stack kernel" if uses_stack else "per-layer kernels",
-                       "bytes_per_token": tok_bytes, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "bytes_per_token": tok_bytes,
+                       "parallelism": (f"tp{world} ({'in-kernel NVLink exchange' if args.tp_impl == 'ours' else 'NCCL all_reduce'})"
+                                       if tp else f"replicas x{world}" if world > 1 else "single"),
                        "l2": "inputs larger than L2 (weights per step %.2f GB > 126 MB)" % (tok_bytes / 1e9)},
             "tokens_per_s": round(tokens_per_s, 2),
-            "frac_of_8tbs": round(value / world / 8000.0, 4),
+            "frac_of_8tbs": round(value / world / 8000.0, 4),  # per GPU
             "roofline": roofline, "e2e": e2e, "clocks": clocks,
-            "gpu_launches": args.steps * (1 if uses_stack else 2 * L),
+            "gpu_launches": args.steps * (1 if uses_stack else 2 * L),  # per rank
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
+    if peers is not None:
+        peers.close()
     for w in G + U + D:
         w.free()
     eng.close()
@@ -482,6 +533,9 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="llama8b")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=0, help="override the config's layer count (small profiling case)")
+    ap.add_argument("--tp", action="store_true", help="tensor-parallel d_ff split over the ranks (batch 1)")
+    ap.add_argument("--tp-impl", choices=["ours", "nccl"], default="ours",
+                    help="exchange of the down partials: in-kernel NVLink stores, or NCCL all_reduce per layer")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -39,12 +39,6 @@ int hc_cuda_error(cudaError_t e, const char* what) {
     return hc_set_error(HC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
-#define HC_CUDA(call)                                              \
-    do {                                                           \
-        cudaError_t _e = (call);                                   \
-        if (_e != cudaSuccess) return hc_cuda_error(_e, #call);    \
-    } while (0)
-
 extern "C" const char* hc_last_error(void) { return g_last_error.c_str(); }
 
 // ------------------------------------------------------------------ labels / row bytes
@@ -216,6 +210,7 @@ extern "C" int hc_engine_free(hc_engine* e) {
     e->sk_ws.release();
     e->sk_cnt.release();
     e->stack_bar.release();
+    hc_peer_release(e);
     for (auto& kv : e->ptr_tables) cudaFree(kv.second);
     e->ptr_tables.clear();
     e->ws_raw.release();
@@ -794,9 +789,9 @@ static int stack_table(hc_engine* e, const StackArgs& s, const void** out) {
 
 // Batch 1 with uniform layers: the whole stack as one persistent kernel (ffn_stack.cu).
 // *done = false leaves the stack to the per-layer kernels.
-static int stack_try_kernel(hc_engine* e, const StackArgs& s, float* x, size_t nvec, bool* done) {
+static int stack_try_kernel(hc_engine* e, const StackArgs& s, float* x, size_t nvec, bool* done, bool tp = false) {
     *done = false;
-    if (!e->use_stack_kernel || nvec != 1) return HC_OK;
+    if ((!e->use_stack_kernel && !tp) || nvec != 1) return HC_OK;
     const hc_weights *g0 = s.g[0], *d0 = s.d[0];
     const int ta = g0->type, td = d0->type;
     if (!tiled_type(ta) || !tiled_type(td)) return HC_OK;
@@ -814,6 +809,12 @@ static int stack_try_kernel(hc_engine* e, const StackArgs& s, float* x, size_t n
     L.x = x;
     L.eps = s.eps;
     L.err = e->d_err;
+    if (tp) {
+        L.tp_rank = e->peer.rank;
+        L.tp_size = e->peer.world;
+        L.tp_regions = e->peer.d_peer;
+        L.tp_base = e->peer.tp_phases;
+    }
     size_t bytes = 0;
     cudaError_t ce = launch_ffn_stack(ta, td, L, e->num_sms, e->smem_optin, e->stream, true, &bytes);
     if (ce == cudaErrorInvalidConfiguration) {
@@ -919,6 +920,48 @@ extern "C" int hc_ffn_stack_dev(hc_engine* e, const hc_weights* const* g, const 
     if (!x) return hc_set_error(HC_ERR_INVALID, "null x");
     if (nvec == 0) return HC_OK;
     return stack_run(e, s, x, nvec);
+}
+
+// Tensor-parallel stack: the layers are this rank's d_ff shard (gate/up rows and down
+// columns of the same range); x is replicated and ends identical on every rank.
+extern "C" int hc_ffn_stack_tp_dev(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
+                                   const hc_weights* const* d, const float* const* norm_w, float eps, size_t L,
+                                   float* x) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    StackArgs s{g, u, d, norm_w, L, eps};
+    rc = stack_check(s);
+    if (rc) return rc;
+    if (!x) return hc_set_error(HC_ERR_INVALID, "null x");
+    if (!e->peer.connected) return hc_set_error(HC_ERR_INVALID, "tensor-parallel stack without a connected peer group");
+    if (g[0]->n != d[0]->m)
+        return hc_set_error(HC_ERR_UNSUPPORTED, "tensor-parallel stack: padded model width (%zu inputs, %zu outputs)",
+                            g[0]->n, d[0]->m);
+    bool done = false;
+    rc = stack_try_kernel(e, s, x, 1, &done, true);
+    if (rc) return rc;
+    if (!done)
+        return hc_set_error(HC_ERR_UNSUPPORTED,
+                            "tensor-parallel stack: formats or shard shape not covered by the persistent kernel");
+    e->peer.tp_phases += (uint32_t)L;
+    return HC_OK;
+}
+
+extern "C" int hc_ffn_stack_tp(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
+                               const hc_weights* const* d, const float* const* norm_w, float eps, size_t L,
+                               const float* x_in, float* x_out) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    if (!g || !g[0] || !x_in || !x_out) return hc_set_error(HC_ERR_INVALID, "null argument");
+    const size_t bytes = g[0]->n * 4;
+    rc = e->ws_x.ensure(bytes);
+    if (rc) return rc;
+    HC_CUDA(cudaMemcpyAsync(e->ws_x.p, x_in, bytes, cudaMemcpyHostToDevice, e->stream));
+    rc = hc_ffn_stack_tp_dev(e, g, u, d, norm_w, eps, L, (float*)e->ws_x.p);
+    if (rc) return rc;
+    HC_CUDA(cudaMemcpyAsync(x_out, e->ws_x.p, bytes, cudaMemcpyDeviceToHost, e->stream));
+    HC_CUDA(cudaStreamSynchronize(e->stream));
+    return hc_check_device_error(e);
 }
 
 extern "C" int hc_ffn_stack(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,

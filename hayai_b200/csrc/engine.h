@@ -21,6 +21,22 @@ struct HostBuf {
     void release();
 };
 
+// Exchange region shared with the other ranks of a tensor- or expert-parallel group (one
+// process per GPU; the regions are mapped into each other's address space with CUDA IPC, so
+// kernels store into a peer's region over NVLink).  Every rank's region has the same layout
+// (gemv_launch.h, kPeer*).
+constexpr int kMaxPeers = 8;
+struct PeerState {
+    int rank = 0, world = 1;
+    void* region = nullptr;      // this rank's region (exported)
+    size_t bytes = 0;
+    void* peer[kMaxPeers] = {};  // every rank's region as mapped here (peer[rank] = region)
+    void** d_peer = nullptr;     // device copy of peer[]
+    bool connected = false;
+    uint32_t tp_phases = 0;      // cross-GPU phases of the TP stack run so far (equal on every rank)
+    uint32_t ep_phases = 0;      // cross-GPU phases of the EP MoE run so far
+};
+
 // One GPU + stream: the counterpart of OpenClEngine (crates/hayai-opencl/src/context.rs:23).
 struct hc_engine {
     int device = 0;
@@ -39,6 +55,7 @@ struct hc_engine {
     HostBuf hs_out;
     std::unordered_map<uint64_t, cudaGraphExec_t> graphs;  // captured FFN stacks
     std::unordered_map<uint64_t, void*> ptr_tables;        // device tables of expert pointers
+    PeerState peer;                                        // tensor/expert-parallel group
 };
 
 // A resident weight matrix in the GPU layout of its format.
@@ -54,6 +71,14 @@ struct hc_weights {
 // internal helpers shared by the translation units of the C ABI
 int hc_set_error(int code, const char* fmt, ...);
 int hc_cuda_error(cudaError_t e, const char* what);
+
+#define HC_CUDA(call)                                           \
+    do {                                                        \
+        cudaError_t _e = (call);                                \
+        if (_e != cudaSuccess) return hc_cuda_error(_e, #call); \
+    } while (0)
+
+void hc_peer_release(hc_engine* e);  // unmap the peers' regions and free this rank's
 int hc_engine_activate(hc_engine* e);
 int hc_check_device_error(hc_engine* e);
 int hc_launch_gemv(hc_engine* e, const hc_weights* w, const float* x, size_t ldx, float* y, size_t ldy,

@@ -22,7 +22,7 @@
 // Phase boundaries are kept short: the warp that completes a 16-row tile of h writes it
 // straight into the down GEMV's fragment table in global memory (the down prologue is then a
 // copy), and the gate/up prologue completes x, sums its squares and normalises in two passes
-// over a staging copy.
+// over registers.
 #include <cuda_runtime.h>
 
 #include "gemv_launch.h"
@@ -52,6 +52,13 @@ struct StackKArgs {
     unsigned* bar;  // [1 + 2L]: grid-barrier counter, then one chunk counter per phase (zero at launch)
     int stages;
     int slot_bytes;
+    // tensor parallelism (tp_size > 1): the layers are this rank's d_ff shard; down chunk
+    // partials are stored into every rank's exchange region, [2][dm / 16][tp_size * cpt][16]
+    // (buffer = cross-GPU phase & 1, rank-major within a tile), and every rank adds them up in
+    // the same order, so the replicated residual stream stays identical on all ranks.
+    int tp_rank, tp_size;
+    char* const* tp_regions;  // [tp_size] the ranks' exchange regions as mapped on this GPU
+    unsigned tp_base;         // cross-GPU phases completed before this launch
 };
 
 // Shared memory: [mbarriers, 256 B][table][zero block][Sx][tile slots][ring], each table-side
@@ -60,18 +67,13 @@ struct StackSmem {
     int table, zero, sx, red, ring;
 };
 
-template <class F>
-__host__ __device__ inline int stack_stage_off(int dm) {
-    return (gemv_smem_layout<F>(dm, 1, false).table_bytes + 15) & ~15;  // staging copy of x, inside the table region
-}
 
 template <class FA, class FD>
 __host__ __device__ inline StackSmem stack_smem_layout(int dm, int ff, int stages) {
     const GemvSmem a = gemv_smem_layout<FA>(dm, 1, false), b = gemv_smem_layout<FD>(ff, 1, false);
     StackSmem s;
     s.table = 256;
-    const int ta = ((a.table_bytes + 15) & ~15) + dm * 4;  // gate/up table + staging copy of x
-    s.zero = s.table + (ta > b.table_bytes ? ta : b.table_bytes);
+    s.zero = s.table + (a.table_bytes > b.table_bytes ? a.table_bytes : b.table_bytes);
     s.sx = s.zero + (a.zero_bytes > b.zero_bytes ? a.zero_bytes : b.zero_bytes);
     s.red = s.sx + (a.sx_bytes > b.sx_bytes ? a.sx_bytes : b.sx_bytes);
     s.ring = s.red + (stages + 2) * tile_slot_bytes(1);
@@ -101,6 +103,51 @@ __device__ void grid_sync(unsigned* bar, unsigned target, int* err, int* s_abort
         if (!*s_abort) {
             const unsigned long long t0 = global_ns();
             while (ld_acquire(bar) < target) {
+                if (global_ns() - t0 > 1000000000ull) {
+                    if (err) atomicOr(err, 2);
+                    *s_abort = 1;
+                    break;
+                }
+            }
+        }
+    }
+    named_bar_sync(kBarGrid, kCW * 32);
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Cross-GPU phase end under tensor parallelism.  Every consumer thread has made its stores to
+// the peers' regions visible system-wide (fence) before the CTA's local arrival; CTA 0 waits
+// for all local CTAs, then adds one (release, system scope) to every rank's cross counter; all
+// CTAs wait (acquire, system scope) until their own rank's counter shows all ranks' signals
+// for this phase.  Both waits are bounded by one second (error bit 1, abort).
+__device__ void tp_sync(unsigned* bar, unsigned target, char* const* regions, int tp_rank, int tp_size,
+                        unsigned xtarget, int* err, int* s_abort) {
+    __threadfence_system();
+    named_bar_sync(kBarGrid, kCW * 32);
+    if (threadIdx.x == 0) {
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+        const unsigned* xbar = reinterpret_cast<const unsigned*>(regions[tp_rank] + kPeerTpBar);
+        const unsigned long long t0 = global_ns();
+        if (!*s_abort && blockIdx.x == 0) {
+            while (ld_acquire(bar) < target) {
+                if (global_ns() - t0 > 1000000000ull) {
+                    if (err) atomicOr(err, 2);
+                    *s_abort = 1;
+                    break;
+                }
+            }
+            if (!*s_abort)
+                for (int q = 0; q < tp_size; ++q)
+                    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(regions[q] + kPeerTpBar)
+                                 : "memory");
+        }
+        if (!*s_abort) {
+            while ((int)(ld_acquire_sys(xbar) - xtarget) < 0) {
                 if (global_ns() - t0 > 1000000000ull) {
                     if (err) atomicOr(err, 2);
                     *s_abort = 1;
@@ -205,6 +252,11 @@ struct ChunkOut {
     float* parts;  // down: chunk partials [tiles][chunks per tile][16]
     uint2* htab;   // gate/up: the down GEMV's fragment table
     float* hsx;    // gate/up: 16-row sums of h
+    // down under tensor parallelism: partials go to parts_off (floats) in every rank's region,
+    // tile stride tp_size * cpt, this rank's chunks at tp_rank * cpt
+    char* const* regions;
+    int tp_rank, tp_size;
+    size_t parts_off;
 };
 
 // Gate/up tile: h for rows tile*16 + (lane & 15) (lanes 16-31 repeat lanes 0-15), written into
@@ -291,8 +343,14 @@ __device__ void consume_chunks(Ring& r, const StageDesc* desc, const LaneCtx<1>&
             if (lane == 0) tcnt[tslot] = 0;  // slot free for chunk + NT
             if constexpr (FUSED) {
                 finish_gateup<FT>(o, d.tile, lane, f[0], f[kMats - 1], bad);
-            } else {
+            } else if (o.tp_size == 1) {
                 if (lane < 16) o.parts[((size_t)d.tile * pg.cpt + d.part) * 16 + row] = f[0];
+            } else if (lane < 16) {
+                // the fused all-reduce: this chunk's 16 sums into every rank's region (NVLink
+                // stores; made visible system-wide before the phase's cross-GPU signal)
+                const size_t off = ((size_t)d.tile * (o.tp_size * pg.cpt) + o.tp_rank * pg.cpt + d.part) * 16 + row;
+                for (int q = 0; q < o.tp_size; ++q)
+                    reinterpret_cast<float*>(o.regions[q])[o.parts_off + off] = f[0];
             }
         }
         if (++tslot == NT) tslot = 0;
@@ -328,44 +386,51 @@ __device__ __forceinline__ bool load_down_table(uint2* xt, float* sx, const Stac
 
 // Gate/up prologue of a layer l > 0.  Pass 1: x_l = x_{l-1} + the down partials of layer l-1
 // (added in chunk order), this CTA's share [c0, c1) written back, sum of squares accumulated,
-// x_l * w staged in shared memory (the norm weight loads ride in the same round trip as the
+// x_l * w kept in registers (the norm weight loads ride in the same round trip as the
 // activation's).  Pass 2: xn = (x_l * w) * inv (rms_norm, crates/hayai-cpu/src/attention.rs:
-// 142-147) into the fragment table, with F's 32-element sums for Q4_K.
+// 142-147) into the fragment table, with F's 32-element sums for Q4_K.  A thread owns chunks
+// tid + k * 512, k < kXRegs: d_model up to 4 * 4 * 512 = 8192 (checked at launch).
+constexpr int kXRegs = 4;
+
 template <class F>
-__device__ void stack_prologue_a(uint2* xt, float* sx, float* xs, const float* xin, const XAccum& acc, float* xnext,
-                                 int c0, int c1, const float* nw, int dm, float eps, float* scratch, int* err) {
+__device__ void stack_prologue_a(uint2* xt, float* sx, const float* xin, const XAccum& acc, float* xnext, int c0,
+                                 int c1, const float* nw, int dm, float eps, float* scratch, int* err) {
     constexpr int kStep = kCW * 32;
     const int nchunk = dm >> 2;
     const int ntab = (((dm + F::kBlockElems - 1) / F::kBlockElems) * F::kBlockElems) >> 2;  // a multiple of 32
-    float4* xs4 = reinterpret_cast<float4*>(xs);
     const float4* nw4 = reinterpret_cast<const float4*>(nw);
+    float4 xw[kXRegs];
     float ssq = 0.f;
-    for (int c = threadIdx.x; c < nchunk; c += kStep) {
-        const float4 w = nw ? __ldg(nw4 + c) : make_float4(1.f, 1.f, 1.f, 1.f);
-        const float4 v = load_x4<kLdcg>(xin, c, acc);
-        if (c >= c0 && c < c1) reinterpret_cast<float4*>(xnext)[c] = v;
-        ssq += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
-        xs4[c] = make_float4(v.x * w.x, v.y * w.y, v.z * w.z, v.w * w.w);
+#pragma unroll
+    for (int k = 0; k < kXRegs; ++k) {
+        const int c = threadIdx.x + k * kStep;
+        xw[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c < nchunk) {
+            const float4 w = nw ? __ldg(nw4 + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float4 v = load_x4<kLdcg>(xin, c, acc);
+            if (c >= c0 && c < c1) reinterpret_cast<float4*>(xnext)[c] = v;
+            ssq += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+            xw[k] = make_float4(v.x * w.x, v.y * w.y, v.z * w.z, v.w * w.w);
+        }
     }
-    const float tot = block_sum(ssq, scratch, kStep, kBarPro);  // its barriers also publish xs
+    const float tot = block_sum(ssq, scratch, kStep, kBarPro);
     const float inv = nw ? 1.0f / sqrtf(tot / (float)dm + eps) : 1.0f;
     bool bad = false;
-    for (int c = threadIdx.x; c < ntab; c += kStep) {  // whole warps: ntab is a multiple of 32
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (c < nchunk) {
-            a = xs4[c];
-            a = make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
-        }
-        const float v4[4] = {a.x, a.y, a.z, a.w};
-        const int slot = chunk_slot<F>(c);
-        pack_chunk(v4, xt[slot], xt[slot + F::kLoOff], bad);
-        if constexpr (F::kNeedSx) {
-            // 8 consecutive chunks (= consecutive lanes) form one 32-element sub-block
-            float s = (a.x + a.y) + (a.z + a.w);
-            s += __shfl_xor_sync(kFull, s, 1);
-            s += __shfl_xor_sync(kFull, s, 2);
-            s += __shfl_xor_sync(kFull, s, 4);
-            if ((threadIdx.x & 7) == 0) sx[c >> 3] = s;
+#pragma unroll
+    for (int k = 0; k < kXRegs; ++k) {
+        const int c = threadIdx.x + k * kStep;
+        if (c < ntab) {  // whole warps: ntab is a multiple of 32
+            const float v4[4] = {xw[k].x * inv, xw[k].y * inv, xw[k].z * inv, xw[k].w * inv};
+            const int slot = chunk_slot<F>(c);
+            pack_chunk(v4, xt[slot], xt[slot + F::kLoOff], bad);
+            if constexpr (F::kNeedSx) {
+                // 8 consecutive chunks (= consecutive lanes) form one 32-element sub-block
+                float s = (v4[0] + v4[1]) + (v4[2] + v4[3]);
+                s += __shfl_xor_sync(kFull, s, 1);
+                s += __shfl_xor_sync(kFull, s, 2);
+                s += __shfl_xor_sync(kFull, s, 4);
+                if ((threadIdx.x & 7) == 0) sx[c >> 3] = s;
+            }
         }
     }
     if (bad && err) atomicOr(err, 1);
@@ -422,7 +487,6 @@ __global__ void __launch_bounds__(kTThreads, 1) ffn_stack_kernel(StackKArgs a) {
     uint2* zero = reinterpret_cast<uint2*>(smem + L.zero);
     float* sx = reinterpret_cast<float*>(smem + L.sx);
     float* red = reinterpret_cast<float*>(smem + L.red);
-    float* xs = reinterpret_cast<float*>(smem + L.table + stack_stage_off<FA>(a.dm));
     for (int i = threadIdx.x; i < (L.sx - L.zero) / 8; i += kCW * 32) zero[i] = make_uint2(0u, 0u);
     // table chunks past the last tile of h are padding no finisher writes: zero them once
     if (blockIdx.x == 0) {
@@ -438,7 +502,14 @@ __global__ void __launch_bounds__(kTThreads, 1) ffn_stack_kernel(StackKArgs a) {
     const unsigned C = gridDim.x;
     const int nc4 = a.dm / 4;  // float4 chunks of x; this CTA writes back [c0, c1)
     const int c0 = (int)((long long)blockIdx.x * nc4 / C), c1 = (int)((long long)(blockIdx.x + 1) * nc4 / C);
-    const XAccum acc{a.parts, gd.cpt, nullptr, 0, 0};
+    const bool tp = a.tp_size > 1;
+    const size_t tp_buf = (size_t)((a.dm + 15) / 16) * a.tp_size * gd.cpt * 16;  // floats per buffer
+    // down partials of cross phase q (TP) or of the previous layer
+    auto parts_acc = [&](unsigned q) {
+        if (!tp) return XAccum{a.parts, gd.cpt, nullptr, 0, 0};
+        float* base = reinterpret_cast<float*>(a.tp_regions[a.tp_rank] + kPeerTpParts);
+        return XAccum{base + (q & 1) * tp_buf, a.tp_size * gd.cpt, nullptr, 0, 0};
+    };
     // x_l: x_0 = the caller's x, then xbuf[l & 1]
     auto xres = [&](int l) { return l == 0 ? a.x : a.xbuf + (size_t)(l & 1) * a.dm; };
     for (int l = 0; l < a.L; ++l) {
@@ -449,11 +520,12 @@ __global__ void __launch_bounds__(kTThreads, 1) ffn_stack_kernel(StackKArgs a) {
                 const NormArgs nrm{ly.norm, a.dm, a.eps};
                 build_prologue<FA, 1, kLdcg>(xt, sx, a.x, a.dm, a.dm, 1, nrm, s_red, a.err, kCW * 32, kBarPro);
             } else {
-                stack_prologue_a<FA>(xt, sx, xs, xres(l - 1), acc, xres(l), c0, c1, ly.norm, a.dm, a.eps, s_red, a.err);
+                stack_prologue_a<FA>(xt, sx, xres(l - 1), parts_acc(a.tp_base + l - 1), xres(l), c0, c1, ly.norm, a.dm,
+                                     a.eps, s_red, a.err);
             }
             named_bar_sync(kBarPro, kCW * 32);
             const LaneCtx<1> ctx = make_ctx<FA, 1>(xt, zero, sx, a.dm, lane);
-            const ChunkOut o{a.ff, nullptr, a.htab, a.hsx};
+            const ChunkOut o{a.ff, nullptr, a.htab, a.hsx, nullptr, 0, 1, 0};
             consume_chunks<FA, FD, true>(r, s_desc, ctx, ga, o, red, s_tcnt, tslot, aborted, a.err);
             grid_sync(a.bar, ++phases * C, a.err, &s_abort);
             if (s_abort) aborted = true;
@@ -466,9 +538,15 @@ __global__ void __launch_bounds__(kTThreads, 1) ffn_stack_kernel(StackKArgs a) {
             }
             named_bar_sync(kBarPro, kCW * 32);
             const LaneCtx<1> ctx = make_ctx<FD, 1>(xt, zero, sx, a.ff, lane);
-            const ChunkOut o{a.dm, a.parts, nullptr, nullptr};
+            const unsigned q = a.tp_base + l;  // cross-GPU phase
+            const ChunkOut o{a.dm,       a.parts,   nullptr,   nullptr,
+                             a.tp_regions, a.tp_rank, a.tp_size, (kPeerTpParts / 4) + (q & 1) * tp_buf};
             consume_chunks<FD, FD, false>(r, s_desc, ctx, gd, o, red, s_tcnt, tslot, aborted, a.err);
-            grid_sync(a.bar, ++phases * C, a.err, &s_abort);
+            if (tp)
+                tp_sync(a.bar, ++phases * C, a.tp_regions, a.tp_rank, a.tp_size, (q + 1) * (unsigned)a.tp_size, a.err,
+                        &s_abort);
+            else
+                grid_sync(a.bar, ++phases * C, a.err, &s_abort);
             if (s_abort) aborted = true;
         }
     }
@@ -476,6 +554,7 @@ __global__ void __launch_bounds__(kTThreads, 1) ffn_stack_kernel(StackKArgs a) {
     // read and then written by the same thread)
     if (!aborted) {
         const float* xin = xres(a.L - 1);
+        const XAccum acc = parts_acc(a.tp_base + a.L - 1);
         for (int c = c0 + (int)threadIdx.x; c < c1; c += kCW * 32)
             reinterpret_cast<float4*>(a.x)[c] = load_x4<kLdcg>(xin, c, acc);
     }
@@ -522,8 +601,13 @@ static cudaError_t launch_stack_t(const StackLaunch& s, int num_sms, int smem_li
     const PhaseGeo ga = phase_geo<FA>(s.ff, s.dm, 1 << 20), gd = phase_geo<FD>(s.dm, s.ff, kUnits);
     if ((long long)((s.ff + 15) / 16) * ga.nbk < num_sms || (long long)((s.dm + 15) / 16) * gd.nbk < num_sms)
         return cudaErrorInvalidConfiguration;  // fewer units than SMs: the per-layer kernels shrink their grid
-    if (gd.cpt > kMaxParts || s.dm % 4 || s.ff % 4)
-        return cudaErrorInvalidConfiguration;  // more down chunks per tile than the prologue adds up
+    if ((((s.dm + FA::kBlockElems - 1) / FA::kBlockElems) * FA::kBlockElems) / 4 > kXRegs * kCW * 32)
+        return cudaErrorInvalidConfiguration;  // the gate/up prologue holds at most kXRegs chunks per thread
+    const int tp = s.tp_size < 1 ? 1 : s.tp_size;
+    if (gd.cpt * tp > kMaxParts || s.dm % 4 || s.ff % 4)
+        return cudaErrorInvalidConfiguration;  // more down partials per tile than the prologue adds up
+    if (tp > 1 && (size_t)2 * ((s.dm + 15) / 16) * tp * gd.cpt * 16 * 4 > kPeerTpPartsBytes)
+        return cudaErrorInvalidConfiguration;
     int slot_bytes = 0;
     const int S = stack_stages<FA, FD>(s.dm, s.ff, smem_limit, &slot_bytes);
     if (S < 3) return cudaErrorInvalidConfiguration;  // too shallow to pay off: use the per-layer kernels
@@ -558,6 +642,10 @@ static cudaError_t launch_stack_t(const StackLaunch& s, int num_sms, int smem_li
     a.bar = reinterpret_cast<unsigned*>(base + sc.bar);
     a.stages = S;
     a.slot_bytes = slot_bytes;
+    a.tp_rank = tp > 1 ? s.tp_rank : 0;
+    a.tp_size = tp;
+    a.tp_regions = reinterpret_cast<char* const*>(s.tp_regions);
+    a.tp_base = s.tp_base;
     e = cudaMemsetAsync(a.bar, 0, sc.xbuf - sc.bar, stream);
     if (e != cudaSuccess) return e;
     void* args[] = {&a};

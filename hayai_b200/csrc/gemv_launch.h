@@ -19,6 +19,14 @@ void gemv_sk_workspace(int type, int M, int K, bool fused, int num_sms, size_t* 
 int gemv_sk_slots(int type, int M, int K, int num_sms);
 
 // A batch-1 residual SwiGLU FFN stack in one persistent kernel (ffn_stack.cu).
+// Layout of the peer exchange region (identical on every rank of a group).
+constexpr size_t kPeerTpBar = 0;                  // u32: cross-GPU counter of the TP stack
+constexpr size_t kPeerEpBar = 128;                // u32: cross-GPU counter of the EP MoE
+constexpr size_t kPeerTpParts = 4096;             // TP stack: down partials [2][d_model/16][parts][16] f32
+constexpr size_t kPeerTpPartsBytes = 4u << 20;    // d_model x parts (<= 8) x 2 buffers x 4 B up to 65536 x 8
+constexpr size_t kPeerEpData = kPeerTpParts + kPeerTpPartsBytes;  // EP MoE exchange data
+constexpr size_t kPeerRegionMin = kPeerEpData + (4u << 20);
+
 struct StackLaunch {
     const void* layers;  // device array, per layer {gate, up, down, norm weight} pointers
     int L, dm, ff;
@@ -27,6 +35,11 @@ struct StackLaunch {
     float eps;
     int* err;
     void* scratch;  // launch_ffn_stack(dry) reports its size
+    // tensor parallelism over tp_size ranks (1 = off): the layers are this rank's d_ff shard,
+    // the down partials go to every rank's exchange region
+    int tp_rank, tp_size;
+    void* const* tp_regions;  // device array [tp_size] of the ranks' regions as mapped here
+    unsigned tp_base;         // cross-GPU phases completed before this launch
 };
 // cudaErrorInvalidConfiguration: the shapes or formats are not covered (use the per-layer
 // kernels).  dry = only check that the launch is possible and report the scratch bytes.

@@ -313,6 +313,37 @@ class CudaEngine:
         _check(lib().hc_ffn_stack_dev(self.handle, _handles(gates), _handles(ups), _handles(downs), _norm_ptrs(norms),
                                       eps, len(gates), ctypes.c_void_p(_tptr(x)), nvec))
 
+    # ---------------------------------------------------------------- tensor parallelism
+    def peer_open(self, rank: int, world: int, nbytes: int = 16 << 20) -> bytes:
+        """Allocate this rank's exchange region; returns its IPC handle (to be gathered)."""
+        n = ctypes.c_size_t()
+        _check(lib().hc_peer_handle_bytes(ctypes.byref(n)))
+        buf = (ctypes.c_ubyte * n.value)()
+        _check(lib().hc_peer_open(self.handle, rank, world, nbytes, buf))
+        return bytes(buf)
+
+    def peer_connect(self, handles: Sequence[bytes]) -> None:
+        """Map every rank's region (handles in rank order, this rank's included)."""
+        blob = b"".join(handles)
+        buf = (ctypes.c_ubyte * len(blob)).from_buffer_copy(blob)
+        _check(lib().hc_peer_connect(self.handle, buf))
+
+    def peer_close(self) -> None:
+        _check(lib().hc_peer_close(self.handle))
+
+    def ffn_stack_tp_dev(self, gates, ups, downs, x, norms=None, eps: float = 1e-5) -> None:
+        """Tensor-parallel batch-1 stack over this rank's d_ff shard; x replicated, in place."""
+        _check(lib().hc_ffn_stack_tp_dev(self.handle, _handles(gates), _handles(ups), _handles(downs),
+                                         _norm_ptrs(norms), eps, len(gates), ctypes.c_void_p(_tptr(x))))
+
+    def ffn_stack_tp(self, gates, ups, downs, x, norms=None, eps: float = 1e-5) -> np.ndarray:
+        """Host-buffer version of ffn_stack_tp_dev (x copied in, the result copied out)."""
+        xv = _f32(x)
+        out = np.empty_like(xv)
+        _check(lib().hc_ffn_stack_tp(self.handle, _handles(gates), _handles(ups), _handles(downs), _norm_ptrs(norms),
+                                     eps, len(gates), xv.ctypes.data, out.ctypes.data))
+        return out
+
     def synth_normal_dev(self, seed: int, out, mean: float = 0.0, std: float = 1.0) -> None:
         """Fill a float32 CUDA tensor with seeded N(mean, std^2) values."""
         _check(lib().hc_synth_normal_dev(self.handle, seed & (2**64 - 1), out.numel(), mean, std,

@@ -173,6 +173,33 @@ int hc_ffn_stack(hc_engine* eng, const hc_weights* const* gate, const hc_weights
                  const hc_weights* const* down, const float* const* norm_w, float eps, size_t n_layers,
                  const float* x_in, float* x_out, size_t nvec);
 
+/* ---- tensor / expert parallelism (one process per GPU) -----------------------------
+ * No reference counterpart: the reference has no multi-GPU FFN.  A group of `world` ranks
+ * (<= 8, one GPU each) shares exchange regions: hc_peer_open allocates this rank's region
+ * (bytes >= 12 MiB; zeroed) and writes its CUDA IPC handle (hc_peer_handle_bytes bytes) to
+ * handle_out; the caller gathers every rank's handle over its own process group, in rank
+ * order, and passes them to hc_peer_connect; then all ranks must pass a host barrier before
+ * the first parallel call.  Kernels store partial results into the peers' regions over
+ * NVLink and signal each other with system-scope atomics (waits bounded by one second:
+ * HC_ERR_TIMEOUT).  Parallel calls are collective: every rank makes the same calls in the
+ * same order.  hc_peer_close (after a host barrier) unmaps and frees. */
+int hc_peer_handle_bytes(size_t* out);
+int hc_peer_open(hc_engine* eng, int rank, int world, size_t bytes, void* handle_out);
+int hc_peer_connect(hc_engine* eng, const void* handles);
+int hc_peer_close(hc_engine* eng);
+
+/* Tensor-parallel FFN stack (batch 1), SURVEY config 5 sharding: rank p holds gate/up rows
+ * and down columns [p*F/P, (p+1)*F/P) of every layer (F = d_ff, column shards whole
+ * super-blocks).  x [d_model] is replicated; each layer's down partials are pushed to every
+ * rank inside the persistent stack kernel (the all-reduce of stream_infer.rs's residual
+ * input, fused) and added in rank order, so x ends identical on every rank. */
+int hc_ffn_stack_tp_dev(hc_engine* eng, const hc_weights* const* gate, const hc_weights* const* up,
+                        const hc_weights* const* down, const float* const* norm_w, float eps, size_t n_layers,
+                        float* x);
+int hc_ffn_stack_tp(hc_engine* eng, const hc_weights* const* gate, const hc_weights* const* up,
+                    const hc_weights* const* down, const float* const* norm_w, float eps, size_t n_layers,
+                    const float* x_in, float* x_out);
+
 /* ---- MoE ---------------------------------------------------------------------------
  * Routing of route_experts (crates/hayai-core/src/moe_infer.rs:868-935, with
  * top_k_indices :852-862 and MoeMeta exec_plan.rs:244-272), on the device, for

@@ -56,7 +56,19 @@ CONFIGS = {
                        workload="Llama-3-8B FFN shape, Q8_0 x3, stack of 8 distinct layers"),
     "llama70b": dict(layers=80, d_model=8192, k_in=8192, d_ff=28672, tg=Q4_K, td=Q6_K,
                      workload="Llama-3-70B FFN stack x80, gate/up Q4_K, down Q6_K, batch-1 decode"),
+    # MoE: experts' gate/up d_ff x d_model and down d_model x d_ff
+    "qwen3moe": dict(layers=48, d_model=2048, k_in=2048, d_ff=768, tg=Q4_K, td=Q4_K, n_expert=128, top_k=8,
+                     tokens=16, workload="Qwen3-30B-A3B MoE FFN x48, 128 experts top-8, Q4_K experts, F32 router, "
+                                         "16 tokens, x <- x + MoE_l(x)"),
 }
+
+
+def expert_bytes(c):
+    return 2 * mat_bytes(c["tg"], c["d_ff"], c["d_model"]) + mat_bytes(c["td"], c["d_model"], c["d_ff"])
+
+
+def router_bytes(c):
+    return c["n_expert"] * c["d_model"] * 4
 
 
 def layer_bytes(c):
@@ -231,6 +243,8 @@ def run_reference(args):
 
     _build.build_oracle()
     c = dict(CONFIGS[args.config])
+    if "n_expert" in c:
+        return run_reference_moe(args, c, world)
     if args.layers:
         c["layers"] = args.layers
     cores = oracle.get_threads()
@@ -266,6 +280,232 @@ def run_reference(args):
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_reference_moe(args, c, world):
+    """The reference's CPU MoE path (router, top-k, per-pair expert FFN, combine: the C
+    restatement in oracle/) on one MoE layer per step, rank 0 only."""
+    import numpy as np
+
+    import oracle
+
+    E, k, T, dm, ff = c["n_expert"], c["top_k"], c["tokens"], c["d_model"], c["d_ff"]
+    t = c["tg"]
+    cores = oracle.get_threads()
+    wg = np.stack([oracle.quantize(t, oracle.normal(5000 + 3 * e, ff * dm, 0.0, 0.02)) for e in range(E)])
+    wu = np.stack([oracle.quantize(t, oracle.normal(5001 + 3 * e, ff * dm, 0.0, 0.02)) for e in range(E)])
+    wd = np.stack([oracle.quantize(t, oracle.normal(5002 + 3 * e, dm * ff, 0.0, 0.02)) for e in range(E)])
+    R = oracle.normal(4999, E * dm, 0.0, 0.02).reshape(E, dm)
+    x0 = oracle.normal(7, T * dm).reshape(T, dm)
+    x = x0.copy()
+    nbytes = []
+
+    def step():
+        nonlocal x
+        y, ids, _ = oracle.moe_ffn(R, E, k, t, wg, t, wu, t, wd, dm, ff, x)
+        nbytes.append(router_bytes(c) + len(np.unique(ids)) * expert_bytes(c))
+        x = (x + y).astype(np.float32)
+
+    for _ in range(args.warmup):
+        step()
+    nbytes.clear()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    gbs = sum(nbytes) / el / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": c_dtype(c),
+        "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) activations)",
+        "config": {"workload": c["workload"] + "; reference arm step = 1 MoE layer", "batch": T,
+                   "layers": c["layers"], "parallelism": "replicas"},
+        "tokens_per_s": round(args.steps * T / c["layers"] / el, 4),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"1 MoE layer ({E} experts, top-{k}, {T} tokens) per step, {cores} OpenMP "
+                                   "threads; algorithmic bytes = router + distinct experts selected; C restatement "
+                                   "of the reference Rust CPU path"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_moe(args):
+    """Config 4: the MoE FFN stack, 16 tokens per step through 48 MoE layers
+    (x <- x + MoE_l(x)); with --ep the experts are split over the ranks (expert parallelism,
+    in-kernel exchange of the routed outputs), otherwise every rank is a replica."""
+    import numpy as np
+    import torch
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    import hayai_b200 as hb
+    from hayai_b200.tp import PeerGroup, expert_range
+
+    c = dict(CONFIGS[args.config])
+    if args.layers:
+        c["layers"] = args.layers
+    L, E, k, T, dm, ff, tq = c["layers"], c["n_expert"], c["top_k"], c["tokens"], c["d_model"], c["d_ff"], c["tg"]
+    ep = args.ep and world > 1
+    lo, hi = expert_range(E, rank, world) if ep else (0, E)
+    eng = hb.CudaEngine(local)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    eng.set_stream(stream)
+
+    scratch = torch.empty(ff * dm, dtype=torch.float32, device=dev)
+
+    def synth(t, m, n, seed):
+        qk, bs = BLK[t]
+        src = scratch[:m * n]
+        eng.synth_normal_dev(seed, src, 0.0, 0.02)
+        q = torch.empty(m * n // qk * bs, dtype=torch.uint8, device=dev)
+        eng.quantize_dev(t, src, q)
+        return eng.upload_from_device(t, m, n, q)
+
+    # expert weights seeded by (layer, expert, role): identical wherever an expert lives
+    R, G, U, D = [], [], [], []
+    for l in range(L):
+        r = torch.empty(E, dm, dtype=torch.float32, device=dev)
+        eng.synth_normal_dev(9_000_011 * (l + 1), r, 0.0, 0.02)
+        R.append(r)
+        G.append([synth(tq, ff, dm, 3 * (l * E + e) + 1) for e in range(lo, hi)])
+        U.append([synth(tq, ff, dm, 3 * (l * E + e) + 2) for e in range(lo, hi)])
+        D.append([synth(c["td"], dm, ff, 3 * (l * E + e) + 3) for e in range(lo, hi)])
+    del scratch
+    x0 = torch.empty(T, dm, dtype=torch.float32, device=dev)
+    eng.synth_normal_dev(7, x0, 0.0, 1.0)
+    x = x0.clone()
+    y = torch.empty_like(x)
+    ids = [torch.empty(T, k, dtype=torch.int32, device=dev) for _ in range(L)]
+    peers = PeerGroup(eng) if ep else None
+    torch.cuda.synchronize(dev)
+
+    def layers(xx):  # all layers: one graph launch (hc_moe_stack_dev / _ep_dev)
+        eng.moe_stack_dev(R, k, G, U, D, xx, expert_lo=lo, ep=ep)
+
+    def step():
+        x.copy_(x0)
+        layers(x)
+
+    # the routing of every layer (untimed, per-layer calls): algorithmic bytes of a step =
+    # every layer's router + the distinct experts its 16 tokens selected (the same every step)
+    xr = x0.clone()
+    for l in range(L):
+        if ep:
+            eng.moe_ffn_ep_dev(R[l], k, G[l], U[l], D[l], lo, xr, y, ids[l])
+        else:
+            eng.moe_ffn_dev(R[l], k, G[l], U[l], D[l], xr, y, ids[l])
+        xr.add_(y)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    eng.sync()
+    assert torch.allclose(x, xr, rtol=1e-4, atol=1e-3), "graph stack and per-layer calls disagree"
+    distinct = [len(np.unique(i.cpu().numpy())) for i in ids]
+    step_bytes = L * router_bytes(c) + sum(distinct) * expert_bytes(c)
+    barrier(world)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    t_local = ev0.elapsed_time(ev1) / 1e3
+    eng.sync()
+    t = max_over_ranks(t_local, world, dev)
+    barrier(world)
+    jobs = 1 if ep else world
+    value = jobs * args.steps * step_bytes / t / 1e9
+
+    # roofline: the stack graph (per layer: router, top-k, grouping, two expert-grouped TMA
+    # GEMVs, combine) timed alone on its stream, against this rank's algorithmic bytes
+    peak, peak_kind = measured_peak()
+    reps = max(3, min(args.steps, 10))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(reps):
+        layers(xr)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    k_time = e0.elapsed_time(e1) / 1e3 / reps
+    local_experts = [len([e for e in np.unique(i.cpu().numpy()) if lo <= e < hi]) for i in ids]
+    k_bytes = L * router_bytes(c) + sum(local_experts) * expert_bytes(c)
+    achieved = k_bytes / k_time / 1e9
+    roofline = {"bound": "hbm", "kernel": f"MoE stack graph, {L} layers x (router_exact_kernel + "
+                "route_topk_warp_kernel + moe_group_kernel + moe_tma_kernel<FmtQ4K,true> + "
+                "moe_tma_kernel<FmtQ4K,false> + moe_combine_kernel)"
+                + (" with the expert shard and the in-kernel exchange" if ep else ""),
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy burst)" if peak_kind == "measured"
+                else "fallback 6.65 TB/s", "traffic": committed_traffic(f"moe_{args.config}"),
+                "algorithmic_bytes_per_launch": round(k_bytes), "avg_launch_us": round(k_time * 1e6, 2)}
+
+    # e2e: pinned host tokens in, the stack through the device API, the result out, every step
+    n_e2e = min(args.steps, 50)
+    x_in = x0.cpu().pin_memory()
+    x_out = torch.empty_like(x_in).pin_memory()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(n_e2e):
+        x.copy_(x_in, non_blocking=True)
+        layers(x)
+        x_out.copy_(x, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
+    assert torch.isfinite(x_out).all()
+    e2e = {"value": round(jobs * n_e2e * step_bytes / t_e2e / 1e9, 2), "unit": "GB/s",
+           "tokens_per_s": round(jobs * n_e2e * T / t_e2e, 2), "steps": n_e2e,
+           "h2d_bytes_per_step": T * dm * 4, "d2h_bytes_per_step": T * dm * 4,
+           "api": "hc_moe_ffn_ep_dev" if ep else "hc_moe_ffn_dev"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "strong" if ep else "weak", "vs_baseline": None, "dtype": c_dtype(c),
+            "data": "synthetic (seeded N(0,0.02^2) weights quantized on device, N(0,1) activations)",
+            "config": {"workload": c["workload"], "batch": T, "layers": L, "d_model": dm, "d_ff": ff,
+                       "n_expert": E, "top_k": k, "distinct_experts_per_layer": round(sum(distinct) / L, 2),
+                       "bytes_per_step": step_bytes,
+                       "parallelism": f"ep{world} (in-kernel NVLink exchange)" if ep else
+                       f"replicas x{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (weights per step %.2f GB > 126 MB)" % (step_bytes / 1e9)},
+            "tokens_per_s": round(jobs * args.steps * T / t, 2),
+            "frac_of_8tbs": round(value / world / 8000.0, 4),
+            "roofline": roofline, "e2e": e2e, "clocks": clocks,
+            "gpu_launches": args.steps * L * (7 if ep else 6),  # per rank: router, top-k, grouping, 2 GEMVs, combine (+EP signal)
+        }
+        print(json.dumps(line), flush=True)
+    if peers is not None:
+        peers.close()
+    for group in G + U + D:
+        for w in group:
+            w.free()
+    eng.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
     return 0
 
 
@@ -536,11 +776,14 @@ def main():
     ap.add_argument("--tp", action="store_true", help="tensor-parallel d_ff split over the ranks (batch 1)")
     ap.add_argument("--tp-impl", choices=["ours", "nccl"], default="ours",
                     help="exchange of the down partials: in-kernel NVLink stores, or NCCL all_reduce per layer")
+    ap.add_argument("--ep", action="store_true", help="expert-parallel MoE over the ranks (qwen3moe)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if "n_expert" in CONFIGS[args.config]:
+        return run_moe(args)
     return run_ours(args)
 
 

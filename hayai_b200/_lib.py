@@ -68,6 +68,9 @@ SIGNATURES: dict[str, list] = {
     "hc_route_experts_dev": [_P, _P, _P, _S, _S, _S, _S, _S, _I, _I, _F, _P, _P],
     "hc_router_scores_dev": [_P, _P, _S, _S, _P, _S, _P],
     "hc_moe_ffn_dev": [_P, _P, _S, _S, _I, _F, _P, _P, _P, _P, _S, _P, _P, _P],
+    "hc_moe_ffn_ep_dev": [_P, _P, _S, _S, _I, _F, _P, _P, _P, _S, _S, _P, _S, _P, _P, _P],
+    "hc_moe_stack_dev": [_P, _S, _P, _S, _S, _I, _F, _P, _P, _P, _P, _S],
+    "hc_moe_stack_ep_dev": [_P, _S, _P, _S, _S, _I, _F, _P, _P, _P, _S, _S, _P, _S],
     "hc_synth_normal_dev": [_P, ctypes.c_uint64, _S, _F, _F, _P],
     "hc_quantize_dev": [_P, _I, _P, _S, _P],
 }

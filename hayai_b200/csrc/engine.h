@@ -34,7 +34,6 @@ struct PeerState {
     void** d_peer = nullptr;     // device copy of peer[]
     bool connected = false;
     uint32_t tp_phases = 0;      // cross-GPU phases of the TP stack run so far (equal on every rank)
-    uint32_t ep_phases = 0;      // cross-GPU phases of the EP MoE run so far
 };
 
 // One GPU + stream: the counterpart of OpenClEngine (crates/hayai-opencl/src/context.rs:23).

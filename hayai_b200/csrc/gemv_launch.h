@@ -22,6 +22,7 @@ int gemv_sk_slots(int type, int M, int K, int num_sms);
 // Layout of the peer exchange region (identical on every rank of a group).
 constexpr size_t kPeerTpBar = 0;                  // u32: cross-GPU counter of the TP stack
 constexpr size_t kPeerEpBar = 128;                // u32: cross-GPU counter of the EP MoE
+constexpr size_t kPeerEpEpoch = 256;              // u32: EP MoE phases this rank has signalled (local)
 constexpr size_t kPeerTpParts = 4096;             // TP stack: down partials [2][d_model/16][parts][16] f32
 constexpr size_t kPeerTpPartsBytes = 4u << 20;    // d_model x parts (<= 8) x 2 buffers x 4 B up to 65536 x 8
 constexpr size_t kPeerEpData = kPeerTpParts + kPeerTpPartsBytes;  // EP MoE exchange data

@@ -134,18 +134,21 @@ __device__ __forceinline__ float4 load_x4(const float* xv, int c, const XAccum& 
 
 // Run by threads [0, nthr) of the CTA (all of it by default); `bar` is the named barrier they
 // synchronise on.
+// rows: optional per-vector row pointers (gathered rows; nullptr rows are zero) instead of
+// x + v * ldx.
 template <class F, int NV, int LOAD = kLdg>
 __device__ void build_prologue(uint2* __restrict__ xt, float* __restrict__ sx, const float* __restrict__ x, int ldx,
                                int K, int nvec, const NormArgs& nrm, float* scratch, int* err, int nthr, int bar,
-                               const XAccum& acc = XAccum{nullptr, 0, nullptr, 0, 0}) {
+                               const XAccum& acc = XAccum{nullptr, 0, nullptr, 0, 0},
+                               const float* const* rows = nullptr) {
     const int nb = (K + F::kBlockElems - 1) / F::kBlockElems;
     const int nchunk = K >> 2;                         // real float4 chunks
     const int ntab = (nb * F::kBlockElems) >> 2;       // chunks covered by the table (zero padded)
     const int rounds = (ntab + nthr - 1) / nthr;
     bool bad = false;
     for (int v = 0; v < NV; ++v) {
-        const float* xv = x + (size_t)v * ldx;
-        const bool live = v < nvec;
+        const float* xv = rows ? rows[v] : x + (size_t)v * ldx;
+        const bool live = v < nvec && xv != nullptr;
         float inv = 1.0f;
         if (nrm.w) {
             float s = 0.f;

@@ -393,6 +393,36 @@ class CudaEngine:
                                     ctypes.c_void_p(_tptr(x)), n_tok, ctypes.c_void_p(_tptr(y)),
                                     ctypes.c_void_p(_tptr(ids)), ctypes.c_void_p(_tptr(weights))))
 
+    def moe_ffn_ep_dev(self, router_w, top_k: int, gates, ups, downs, expert_lo: int, x, y, ids=None, weights=None,
+                       norm_topk_prob: bool = False, routed_scaling_factor: float = 1.0) -> None:
+        """Expert-parallel MoE: this rank holds experts [expert_lo, expert_lo + len(gates)); collective."""
+        E = router_w.shape[0]
+        n_tok = x.shape[0]
+        _check(lib().hc_moe_ffn_ep_dev(self.handle, ctypes.c_void_p(_tptr(router_w)), E, top_k, int(norm_topk_prob),
+                                       routed_scaling_factor, _handles(gates), _handles(ups), _handles(downs),
+                                       expert_lo, len(gates), ctypes.c_void_p(_tptr(x)), n_tok,
+                                       ctypes.c_void_p(_tptr(y)), ctypes.c_void_p(_tptr(ids)),
+                                       ctypes.c_void_p(_tptr(weights))))
+
+    def moe_stack_dev(self, routers, top_k: int, gates, ups, downs, x, expert_lo: int = 0, ep: bool = False,
+                      norm_topk_prob: bool = False, routed_scaling_factor: float = 1.0) -> None:
+        """x <- x + MoE_l(x) for every layer, in place (one graph launch).  routers: per-layer
+        [E][d_model] CUDA tensors; gates/ups/downs: per-layer lists of the experts held here
+        (all E, or [expert_lo, expert_lo + n) with ep=True, collective)."""
+        L = len(routers)
+        E = routers[0].shape[0]
+        n = len(gates[0])
+        flat = lambda ws: _handles([w for layer in ws for w in layer])  # noqa: E731
+        rp = (ctypes.c_void_p * L)(*[_tptr(r) for r in routers])
+        n_tok = x.shape[0]
+        if ep:
+            _check(lib().hc_moe_stack_ep_dev(self.handle, L, rp, E, top_k, int(norm_topk_prob), routed_scaling_factor,
+                                             flat(gates), flat(ups), flat(downs), expert_lo, n,
+                                             ctypes.c_void_p(_tptr(x)), n_tok))
+        else:
+            _check(lib().hc_moe_stack_dev(self.handle, L, rp, E, top_k, int(norm_topk_prob), routed_scaling_factor,
+                                          flat(gates), flat(ups), flat(downs), ctypes.c_void_p(_tptr(x)), n_tok))
+
 
 # ---------------------------------------------------------------------------- orchestrator mirror
 @dataclass

@@ -1,11 +1,14 @@
-"""Tensor parallelism of the FFN stack over the GPUs of one box (one process per GPU).
+"""Tensor and expert parallelism over the GPUs of one box (one process per GPU).
 
 Sharding (the d_ff split of the Llama-3-70B configuration): rank p of P holds gate/up rows
 [p*F/P, (p+1)*F/P) and the same range of down columns, cut at whole quantization blocks, so
 h never leaves its GPU.  The down projection then yields a partial sum on every rank; the
 persistent stack kernel pushes each layer's partials into every rank's exchange region over
 NVLink and adds them in rank order (hc_ffn_stack_tp_dev), so the replicated residual stream
-stays identical on all ranks.  ``PeerGroup`` sets up the exchange regions over a
+stays identical on all ranks.  Expert parallelism (the MoE layer) gives rank p the experts
+``expert_range(E, p, P)``; the router and top-k run replicated, each rank computes the pairs
+routed to its experts and stores their rows into every rank's region, and every rank
+combines them in top-k order (hc_moe_ffn_ep_dev).  ``PeerGroup`` sets up the exchange regions over a
 torch.distributed process group (gloo or nccl), which only carries the IPC handles.
 """
 from __future__ import annotations
@@ -43,6 +46,11 @@ def shard_cols(raw: np.ndarray, ggml_type: int, m: int, n: int, rank: int, world
     nb = n // qk
     blocks = np.frombuffer(memoryview(raw), dtype=np.uint8).reshape(m, nb, bs)
     return np.ascontiguousarray(blocks[:, lo // qk:hi // qk, :]).reshape(-1), hi - lo
+
+
+def expert_range(n_expert: int, rank: int, world: int) -> tuple[int, int]:
+    """Experts [lo, hi) held by rank under expert parallelism (n_expert / world each)."""
+    return shard_range(n_expert, rank, world, 1)
 
 
 def gather_handles(handle: bytes, group=None) -> list[bytes]:

@@ -224,6 +224,33 @@ int hc_moe_ffn_dev(hc_engine* eng, const float* router_w, size_t n_expert, size_
                    const hc_weights* const* down, const float* x, size_t n_tok, float* y, int32_t* ids_out,
                    float* w_out);
 
+/* Expert-parallel MoE FFN (SURVEY config 4 sharding): this rank holds experts
+ * [expert_lo, expert_lo + n_local) (gate/up/down arrays of n_local handles); router_w
+ * covers all n_expert experts and x [n_tok][d_model] is replicated, so every rank routes
+ * identically.  Each rank computes the (token, slot) pairs routed to its experts and stores
+ * their down rows into every rank's exchange region over NVLink (the all-to-all of routed
+ * outputs, fused into the expert GEMV's epilogue); after a cross-GPU signal every rank adds
+ * the rows in top-k order (moe_infer.rs:449-455), so y is identical on all ranks and does
+ * not depend on the rank count.  Needs a connected peer group; collective. */
+int hc_moe_ffn_ep_dev(hc_engine* eng, const float* router_w, size_t n_expert, size_t top_k, int norm_topk_prob,
+                      float routed_scaling_factor, const hc_weights* const* gate, const hc_weights* const* up,
+                      const hc_weights* const* down, size_t expert_lo, size_t n_local, const float* x, size_t n_tok,
+                      float* y, int32_t* ids_out, float* w_out);
+
+/* A stack of MoE layers for n_tok tokens, x <- x + MoE_l(x) for l = 0..n_layers-1 (the
+ * residual add of the callers of forward_moe, moe_infer.rs:222-223), in place on device
+ * memory, captured once into a CUDA graph and replayed.  router_w: n_layers device pointers
+ * ([n_expert][d_model] each); gate/up/down: n_layers x n_expert handles, layer-major.  The
+ * _ep variant holds experts [expert_lo, expert_lo + n_local) of every layer (n_layers x
+ * n_local handles) and exchanges the routed rows as hc_moe_ffn_ep_dev does; collective. */
+int hc_moe_stack_dev(hc_engine* eng, size_t n_layers, const float* const* router_w, size_t n_expert, size_t top_k,
+                     int norm_topk_prob, float routed_scaling_factor, const hc_weights* const* gate,
+                     const hc_weights* const* up, const hc_weights* const* down, float* x, size_t n_tok);
+int hc_moe_stack_ep_dev(hc_engine* eng, size_t n_layers, const float* const* router_w, size_t n_expert,
+                        size_t top_k, int norm_topk_prob, float routed_scaling_factor, const hc_weights* const* gate,
+                        const hc_weights* const* up, const hc_weights* const* down, size_t expert_lo, size_t n_local,
+                        float* x, size_t n_tok);
+
 /* ---- synthetic data ----------------------------------------------------------------
  * Seeded N(mean, std^2) floats on the device (splitmix64 at a position + Box-Muller in
  * double; the same stream as the test oracle's generator up to last-bit differences of

@@ -59,10 +59,15 @@ def test_route_experts_bit_exact(engine, variant):
         assert np.abs(rw - gw[t]).max() <= 1e-6 * max(1.0, float(np.abs(rw).max())) * 4
 
 
-@pytest.mark.parametrize("E,k,T", [(32, 4, 5), (128, 8, 16)])
-def test_moe_ffn_parity(engine, E, k, T):
-    dm, ff = 2048, 768
-    t = oracle.Q4_K
+@pytest.mark.parametrize("E,k,T,t,dm,ff", [
+    (32, 4, 5, oracle.Q4_K, 2048, 768),
+    (128, 8, 16, oracle.Q4_K, 2048, 768),   # Qwen3-30B-A3B shape
+    (8, 4, 16, oracle.Q4_K, 2048, 768),     # ~8 pairs per expert: experts split over several segments
+    (16, 2, 6, oracle.Q8_0, 1024, 512),
+    (16, 2, 6, oracle.Q6_K, 1024, 512),
+    (8, 2, 4, oracle.Q4_K, 4096, 512),      # gate/up K too long for one stage: per-pair kernel
+])
+def test_moe_ffn_parity(engine, E, k, T, t, dm, ff):
     wg = np.stack([quantized(t, ff, dm, 10 + 3 * e) for e in range(E)])
     wu = np.stack([quantized(t, ff, dm, 11 + 3 * e) for e in range(E)])
     wd = np.stack([quantized(t, dm, ff, 12 + 3 * e) for e in range(E)])
@@ -79,4 +84,33 @@ def test_moe_ffn_parity(engine, E, k, T):
     on_stream(engine, lambda: engine.moe_ffn_dev(Rd, k, G, U, Dn, Xd, Y, ids, wts))
     assert np.array_equal(ref_ids, ids.cpu().numpy())
     assert_parity(ref_w, wts.cpu().numpy(), what="routing weights")
-    assert_parity(ref_y, Y.cpu().numpy(), what=f"moe E={E} k={k}")
+    assert_parity(ref_y, Y.cpu().numpy(), what=f"moe E={E} k={k} type={t}")
+
+
+def test_moe_stack_parity(engine):
+    """x <- x + MoE_l(x) over 3 layers through one graph launch; replays are deterministic."""
+    E, k, T, dm, ff, L = 32, 4, 6, 2048, 768, 3
+    t = oracle.Q4_K
+    layers = []
+    for l in range(L):
+        wg = np.stack([quantized(t, ff, dm, 100 * l + 3 * e) for e in range(E)])
+        wu = np.stack([quantized(t, ff, dm, 100 * l + 1 + 3 * e) for e in range(E)])
+        wd = np.stack([quantized(t, dm, ff, 100 * l + 2 + 3 * e) for e in range(E)])
+        R = oracle.normal(900 + l, E * dm, 0, 0.02).reshape(E, dm)
+        layers.append((wg, wu, wd, R))
+    X = oracle.normal(950, T * dm).reshape(T, dm)
+    ref = X.copy()
+    for wg, wu, wd, R in layers:
+        y, _, _ = oracle.moe_ffn(R, E, k, t, wg, t, wu, t, wd, dm, ff, ref)
+        ref = (ref + y).astype(np.float32)
+    G = [[engine.upload(t, ff, dm, wg[e]) for e in range(E)] for wg, _, _, _ in layers]
+    U = [[engine.upload(t, ff, dm, wu[e]) for e in range(E)] for _, wu, _, _ in layers]
+    Dn = [[engine.upload(t, dm, ff, wd[e]) for e in range(E)] for _, _, wd, _ in layers]
+    Rd = [torch.from_numpy(R).cuda() for _, _, _, R in layers]
+    outs = []
+    for _ in range(2):
+        Xd = torch.from_numpy(X).cuda()
+        on_stream(engine, lambda: engine.moe_stack_dev(Rd, k, G, U, Dn, Xd))
+        outs.append(Xd.cpu().numpy())
+    assert_parity(ref, outs[0], what="moe stack x3")
+    assert np.array_equal(outs[0], outs[1])

@@ -10,6 +10,8 @@
 // reference's stable descending sort (ties -> lower expert id first).
 #include <string.h>
 
+#include <algorithm>
+
 #include <vector>
 
 #include "../../include/hayai_cuda.h"
@@ -457,20 +459,15 @@ __device__ int moe_cost_to_tile(long long q, const int* wcum, const int* w, int 
     return lo * tps + (int)((q - (long long)wcum[lo] * tps + w[lo] - 1) / w[lo]);
 }
 
-// One thread per expert of [e_lo, e_hi): count its pairs, scan the segment counts, emit the
-// segments in expert order, then cut both GEMVs' tile sequences into C ranges of equal cost:
-// ranges[0][0..C] over tps_a tiles per segment (gate/up), ranges[1][0..C] over tps_b (down).
-// nseg[0] = segments.  Shared memory: [P] ids | [P + 1] cost prefix | [P] tile costs.
-__global__ void moe_group_kernel(const int32_t* __restrict__ ids, int P, int e_lo, int e_hi, MoeSeg* __restrict__ segs,
-                                 int* __restrict__ nseg, int C, int tps_a, int tps_b, int* __restrict__ ranges) {
-    extern __shared__ int sh[];
-    int* sid = sh;
-    int* wcum = sh + P;
-    int* wseg = wcum + P + 1;
-    __shared__ int s_warp[32];
-    __shared__ int s_tot[2];
-    for (int p = threadIdx.x; p < P; p += blockDim.x) sid[p] = ids[p];
-    __syncthreads();
+// Group the routed pairs sid[0..P) (in shared memory): one thread per expert of [e_lo, e_hi)
+// counts its pairs, the block scans the segment counts and costs, the segments are emitted in
+// expert order, then both GEMVs' tile sequences are cut into C ranges of equal cost:
+// ranges[0..C] over tps_a tiles per segment (gate/up), ranges[C+1..2C+1] over tps_b (down).
+// nseg[0] = segments.  wcum [P + 1] and wseg [P] are shared-memory scratch.  Needs
+// blockDim.x >= e_hi - e_lo, a multiple of 32; every thread of the block calls it.
+__device__ void group_pairs(const int* sid, int P, int e_lo, int e_hi, MoeSeg* __restrict__ segs, int* __restrict__ nseg,
+                            int C, int tps_a, int tps_b, int* __restrict__ ranges, int* wcum, int* wseg, int* s_warp,
+                            int* s_tot) {
     const int e = e_lo + (int)threadIdx.x;
     const bool mine = e < e_hi;
     int n = 0;
@@ -517,6 +514,108 @@ __global__ void moe_group_kernel(const int32_t* __restrict__ ids, int P, int e_l
         ranges[c] = moe_cost_to_tile(ca * c / C, wcum, wseg, S, tps_a);
         ranges[C + 1 + c] = moe_cost_to_tile(cb * c / C, wcum, wseg, S, tps_b);
     }
+}
+
+__global__ void moe_group_kernel(const int32_t* __restrict__ ids, int P, int e_lo, int e_hi, MoeSeg* __restrict__ segs,
+                                 int* __restrict__ nseg, int C, int tps_a, int tps_b, int* __restrict__ ranges) {
+    extern __shared__ int sh[];  // [P] ids | [P + 1] cost prefix | [P] tile costs
+    __shared__ int s_warp[32];
+    __shared__ int s_tot[2];
+    for (int p = threadIdx.x; p < P; p += blockDim.x) sh[p] = ids[p];
+    __syncthreads();
+    group_pairs(sh, P, e_lo, e_hi, segs, nseg, C, tps_a, tps_b, ranges, sh + P, sh + 2 * P + 1, s_warp, s_tot);
+}
+
+// Routing and grouping in one block for up to 32 tokens and 256 experts (the decode-batch
+// case): warp t routes token t with its scores in registers (k rounds of a warp arg-max over
+// the experts not yet chosen, ties to the lower id: the reference's stable descending sort,
+// moe_infer.rs:852-862; softmax or sigmoid weights, renorm and scaling, :906-932, with
+// warp-tree max and sum), the ids go to shared memory, then the block groups the pairs.
+constexpr int kRouteRegs = 8;  // scores per lane: E <= 256
+
+__global__ void route_group_kernel(const float* __restrict__ scores, const float* __restrict__ bias, int T, RouteMeta m,
+                                   int32_t* __restrict__ ids, float* __restrict__ wout, int e_lo, int e_hi,
+                                   MoeSeg* __restrict__ segs, int* __restrict__ nseg, int C, int tps_a, int tps_b,
+                                   int* __restrict__ ranges) {
+    extern __shared__ int sh[];  // [P] ids | [P + 1] cost prefix | [P] tile costs
+    __shared__ int s_warp[32];
+    __shared__ int s_tot[2];
+    const int P = T * m.k;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < T) {
+        const float* sc = scores + (size_t)warp * m.E;
+        float v[kRouteRegs], b[kRouteRegs];
+#pragma unroll
+        for (int q = 0; q < kRouteRegs; ++q) {
+            const int j = lane + 32 * q;
+            v[q] = j < m.E ? sc[j] : -INFINITY;
+            b[q] = j < m.E ? (bias ? v[q] + bias[j] : v[q]) : -INFINITY;
+        }
+        unsigned taken = 0u;
+        int myid[16];  // chosen ids (k <= 16 here), replicated in every lane
+        for (int r = 0; r < m.k; ++r) {
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+#pragma unroll
+            for (int q = 0; q < kRouteRegs; ++q) {
+                const int j = lane + 32 * q;
+                if (j < m.E && !((taken >> q) & 1u) && (bi == 0x7fffffff || ranks_before(b[q], j, bv, bi))) {
+                    bv = b[q];
+                    bi = j;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(kFull, bv, o);
+                const int oi = __shfl_xor_sync(kFull, bi, o);
+                if (oi != 0x7fffffff && (bi == 0x7fffffff || ranks_before(ov, oi, bv, bi))) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+            myid[r] = bi;
+            if (lane == 0) {
+                ids[(size_t)warp * m.k + r] = bi;
+                sh[warp * m.k + r] = bi;
+            }
+        }
+        // weights of the chosen ids from the raw scores
+        float w[16];
+        float mx = -INFINITY, sum = 0.f;
+        if (m.gating != 1) {
+#pragma unroll
+            for (int q = 0; q < kRouteRegs; ++q) mx = fmaxf(mx, v[q]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+#pragma unroll
+            for (int q = 0; q < kRouteRegs; ++q)
+                if (lane + 32 * q < m.E) sum += expf(v[q] - mx);
+            sum = warp_sum(sum);
+        }
+        const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+        float wsum = 0.f;
+        for (int r = 0; r < m.k; ++r) {
+            const int id = myid[r];
+            float sv = 0.f;  // the chosen expert's raw score, from the lane that holds it
+#pragma unroll
+            for (int q = 0; q < kRouteRegs; ++q)
+                if (id == lane + 32 * q) sv = v[q];
+            sv = __shfl_sync(kFull, sv, id & 31);
+            w[r] = m.gating == 1 ? 1.0f / (1.0f + expf(-sv)) : expf(sv - mx) * inv;
+            wsum += w[r];
+        }
+        if (lane == 0) {
+            for (int r = 0; r < m.k; ++r) {
+                float x = w[r];
+                if (m.norm_topk_prob && wsum > 0.0f) x /= wsum;
+                if (fabsf(m.scale - 1.0f) > 1e-9f) x *= m.scale;
+                wout[(size_t)warp * m.k + r] = x;
+            }
+        }
+    }
+    __syncthreads();
+    group_pairs(sh, P, e_lo, e_hi, segs, nseg, C, tps_a, tps_b, ranges, sh + P, sh + 2 * P + 1, s_warp, s_tot);
 }
 
 struct MoeTmaArgs {
@@ -985,11 +1084,14 @@ static int moe_run(hc_engine* e, const float* router_w, size_t E, size_t k, int 
 
     // router and top-k: on every rank alike (x and the router are replicated)
     HC_CUDA(launch_router(router_w, x, (int)E, (int)dm, (int)T, scores, e->smem_optin, e->stream, e->d_err));
-    rc = route_dev(e, scores, nullptr, T, E, k, 0, 0, 0, norm, scale, ids, wts);
-    if (rc) return rc;
-
     const bool tma = moe_tma_fits(g0->type, true, (int)dm) && moe_tma_fits(d0->type, false, (int)ff) && n_held <= 1024 &&
                      (3 * P + 1) * 4 <= 48 * 1024 && ff % 4 == 0 && e->num_sms <= 1024;
+    // decode batches: routing and grouping in one block
+    const bool fused_route = tma && T <= 32 && E <= 32 * kRouteRegs && k <= 16;
+    if (!fused_route) {
+        rc = route_dev(e, scores, nullptr, T, E, k, 0, 0, 0, norm, scale, ids, wts);
+        if (rc) return rc;
+    }
     if (ep && !tma)
         return hc_set_error(HC_ERR_UNSUPPORTED, "expert-parallel MoE: expert shapes need the grouped pipeline "
                                                 "(gate/up K <= 8 and down K <= 16 kernel blocks)");
@@ -999,10 +1101,18 @@ static int moe_run(hc_engine* e, const float* router_w, size_t E, size_t k, int 
         int* nseg = (int*)(base + off_nseg);
         int* ranges = nseg + 64;
         const int C = e->num_sms;
-        const unsigned gthreads = (unsigned)((n_held + 31) / 32 * 32);
-        moe_group_kernel<<<1, gthreads, (3 * P + 1) * 4, e->stream>>>(ids, (int)P, (int)lo, (int)(lo + n_held), segs,
-                                                                     nseg, C, (int)((ff + 15) / 16),
-                                                                     (int)((dm + 15) / 16), ranges);
+        if (fused_route) {
+            const RouteMeta rm{(int)E, (int)k, 0, 0, 0, norm, scale};
+            const size_t nthr = std::max<size_t>(32 * T, (n_held + 31) / 32 * 32);
+            route_group_kernel<<<1, (unsigned)nthr, (3 * P + 1) * 4, e->stream>>>(
+                scores, nullptr, (int)T, rm, ids, wts, (int)lo, (int)(lo + n_held), segs, nseg, C, (int)((ff + 15) / 16),
+                (int)((dm + 15) / 16), ranges);
+        } else {
+            const unsigned gthreads = (unsigned)((n_held + 31) / 32 * 32);
+            moe_group_kernel<<<1, gthreads, (3 * P + 1) * 4, e->stream>>>(ids, (int)P, (int)lo, (int)(lo + n_held),
+                                                                         segs, nseg, C, (int)((ff + 15) / 16),
+                                                                         (int)((dm + 15) / 16), ranges);
+        }
         HC_CUDA(cudaGetLastError());
         MoeTmaArgs a1{};
         a1.segs = segs;

@@ -210,6 +210,7 @@ extern "C" int hc_engine_free(hc_engine* e) {
     e->sk_ws.release();
     e->sk_cnt.release();
     e->stack_bar.release();
+    e->ws_tc.release();
     hc_peer_release(e);
     for (auto& kv : e->ptr_tables) cudaFree(kv.second);
     e->ptr_tables.clear();
@@ -231,6 +232,19 @@ extern "C" int hc_engine_free(hc_engine* e) {
 void hc_drop_graphs(hc_engine* e) {
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
+}
+
+int hc_tc_prepare(hc_engine* e, size_t M, size_t K, size_t nvec, int mats, void** ws) {
+    const size_t need = tc_workspace_bytes((int)M, (int)K, (int)nvec, e->num_sms, mats);
+    if (need > e->ws_tc.cap) {
+        cudaStreamSynchronize(e->stream);
+        hc_drop_graphs(e);  // graphs captured earlier hold the old address
+        e->ws_tc.release();
+        int rc = e->ws_tc.ensure(need);
+        if (rc) return rc;
+    }
+    *ws = e->ws_tc.p;
+    return HC_OK;
 }
 
 int hc_sk_prepare(hc_engine* e, int type, size_t M, size_t K, bool fused, float** ws, int** cnt) {
@@ -389,7 +403,15 @@ int hc_launch_gemv(hc_engine* e, const hc_weights* w, const float* x, size_t ldx
     if (((uintptr_t)x & 15) || (ldx & 3))
         return hc_set_error(HC_ERR_INVALID, "x must be 16-byte aligned with ldx a multiple of 4");
     cudaError_t ce;
-    if (gemv_mma_supported(w->type)) {
+    if (tc_gemm_supported(w->type, (int)w->m, (int)w->n, (int)nvec)) {
+        // batches of 8+ rows: one pass over the weights on the tcgen05 tensor cores
+        void* ws;
+        int rc = hc_tc_prepare(e, w->m, w->n, nvec, 1, &ws);
+        if (rc) return rc;
+        ce = launch_tc_gemm((const uint8_t*)w->dev, nullptr, (long long)w->stride, (int)w->m, (int)w->n, x, (int)ldx,
+                            (int)nvec, y, (int)ldy, resid, (int)ldr, nullptr, 0, 0.f, ws, e->d_err, e->num_sms,
+                            e->smem_optin, e->stream);
+    } else if (gemv_mma_supported(w->type)) {
         GemvArgs a{};
         a.w = (const uint8_t*)w->dev;
         a.row_stride = (long long)w->stride;
@@ -615,6 +637,16 @@ int hc_launch_gateup(hc_engine* e, const hc_weights* g, const hc_weights* u, con
         return hc_set_error(HC_ERR_INVALID, "x must be 16-byte aligned with ldx a multiple of 4");
     if (norm_w && (norm_len == 0 || norm_len > g->n))
         return hc_set_error(HC_ERR_INVALID, "norm length %zu must be in [1, %zu]", norm_len, g->n);
+    if (g->type == u->type && g->stride == u->stride && tc_gemm_supported(g->type, (int)g->m, (int)g->n, (int)nvec)) {
+        void* ws;
+        int rc = hc_tc_prepare(e, g->m, g->n, nvec, 2, &ws);
+        if (rc) return rc;
+        cudaError_t ce = launch_tc_gemm((const uint8_t*)g->dev, (const uint8_t*)u->dev, (long long)g->stride,
+                                        (int)g->m, (int)g->n, x, (int)ldx, (int)nvec, h, (int)g->m, nullptr, 0, norm_w,
+                                        (int)norm_len, eps, ws, e->d_err, e->num_sms, e->smem_optin, e->stream);
+        if (ce != cudaSuccess) return hc_cuda_error(ce, "gate/up tensor-core launch");
+        return HC_OK;
+    }
     if (g->type == u->type && gemv_mma_supported(g->type)) {
         GemvArgs a{};
         a.w = (const uint8_t*)g->dev;
@@ -860,6 +892,11 @@ static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
         }
         if (!rc && gemv_mma_supported(s.d[l]->type))
             rc = hc_sk_prepare(e, s.d[l]->type, s.d[l]->m, s.d[l]->n, false, &ws, &cnt);
+        void* tws;
+        if (!rc && tc_gemm_supported(s.g[l]->type, (int)s.g[l]->m, (int)s.g[l]->n, (int)nvec))
+            rc = hc_tc_prepare(e, s.g[l]->m, s.g[l]->n, nvec, 2, &tws);
+        if (!rc && tc_gemm_supported(s.d[l]->type, (int)s.d[l]->m, (int)s.d[l]->n, (int)nvec))
+            rc = hc_tc_prepare(e, s.d[l]->m, s.d[l]->n, nvec, 1, &tws);
         if (rc) return rc;
     }
     if (!e->use_graphs) return stack_enqueue(e, s, x, nvec, h);

@@ -191,6 +191,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     return false;
 }
 
+// Bounded wait by polling (non-blocking probes, no suspension): for handoffs that are usually
+// not complete yet when the wait starts, where a suspended thread's wake-up would add latency.
+// ~2^25 probes: about a second.  False on timeout.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity) {
+    for (int i = 0; i < (1 << 25); ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+
 // Global -> shared bulk copy through the TMA engine, completing `bytes` on mbarrier `bar`.
 // dst, src and bytes must be multiples of 16.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {

@@ -50,6 +50,7 @@ struct hc_engine {
     // stream-K partial sums and per-tile counters (counters zeroed once; kernels re-arm them)
     DevBuf sk_ws, sk_cnt;
     DevBuf stack_bar;             // grid-barrier counter of the persistent FFN-stack kernel
+    DevBuf ws_tc;                 // batched Q8_0 tensor-core GEMM: canonical activations + partials
     bool use_stack_kernel = true; // batch-1 stacks run as one persistent kernel when they fit
     HostBuf hs_out;
     std::unordered_map<uint64_t, cudaGraphExec_t> graphs;  // captured FFN stacks
@@ -92,3 +93,6 @@ const char* hc_type_label(int t);
 // drops the captured CUDA graphs (they hold the old addresses).
 int hc_sk_prepare(hc_engine* e, int type, size_t M, size_t K, bool fused, float** ws, int** cnt);
 void hc_drop_graphs(hc_engine* e);
+// Scratch of the batched Q8_0 tensor-core GEMM (grows on demand; a reallocation drops the
+// captured CUDA graphs).
+int hc_tc_prepare(hc_engine* e, size_t M, size_t K, size_t nvec, int mats, void** ws);

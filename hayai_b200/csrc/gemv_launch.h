@@ -47,6 +47,16 @@ struct StackLaunch {
 cudaError_t launch_ffn_stack(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
                              cudaStream_t stream, bool dry, size_t* scratch_bytes);
 
+// Batched Q8_0 GEMV on the tcgen05 tensor cores (gemm_tc.cu), for 8..128 rows of x, M a
+// multiple of 128 and K of 128.  w2 != nullptr: fused gate/up, y = silu(G x') * (U x') with
+// x' = rms_norm(x) when norm_w is given.  ws: tc_workspace_bytes(...) bytes of scratch.
+bool tc_gemm_supported(int type, int M, int K, int nvec);
+size_t tc_workspace_bytes(int M, int K, int nvec, int num_sms, int mats);
+cudaError_t launch_tc_gemm(const uint8_t* w, const uint8_t* w2, long long tstride, int M, int K, const float* x,
+                           int ldx, int nvec, float* y, int ldy, const float* resid, int ldr, const float* norm_w,
+                           int norm_len, float eps, void* ws, int* err, int num_sms, int smem_limit,
+                           cudaStream_t stream);
+
 // CUDA-core GEMV on the raw GGUF layout for F32 and the IQ2/IQ3 codebook formats.
 cudaError_t launch_gemv_simple(int type, const uint8_t* w, size_t row_bytes, int M, int K, const float* x,
                                int ldx, float* y, int ldy, const float* resid, int ldr, int nvec,

@@ -50,7 +50,7 @@ def test_ffn_llama8b_layer(engine):
     assert_parity(ref, got, what="llama-8b ffn")
 
 
-@pytest.mark.parametrize("nvec", [1, 3, 8])
+@pytest.mark.parametrize("nvec", [1, 3, 8, 16, 40])
 def test_ffn_q8_0(engine, nvec):
     ref, got = run_ffn(engine, oracle.Q8_0, oracle.Q8_0, 1024, 2816, 300, nvec=nvec)
     assert_parity(ref, got, what=f"q8_0 ffn nvec={nvec}")
@@ -181,3 +181,16 @@ def test_stack_rejects_mismatched_layers(engine):
     _, b, _ = make_stack(engine, 1, oracle.Q4_K, oracle.Q4_K, 768, 1024, 710)
     with pytest.raises(hb.CudaError):
         engine.ffn_stack([a[0][0], b[0][0]], [a[0][1], b[0][1]], [a[0][2], b[0][2]], np.zeros(512, np.float32))
+
+
+@pytest.mark.parametrize("nvec", [8, 64])
+def test_stack_q8_0_tensor_core(engine, nvec):
+    """Config-3 shape family: Q8_0 stack with RMSNorm at batch 8 and 64 (tcgen05 path)."""
+    L, dm, ff = 2, 1024, 2816
+    layers, res, norms = make_stack(engine, L, oracle.Q8_0, oracle.Q8_0, dm, ff, 700)
+    X = oracle.normal(701, nvec * dm).reshape(nvec, dm)
+    nd = [torch.from_numpy(n).cuda() for n in norms]
+    got = engine.ffn_stack(*split(res), X.reshape(-1), nvec=nvec, norms=nd, eps=EPS).reshape(nvec, dm)
+    for b in range(0, nvec, max(1, nvec // 4)):
+        ref = oracle_stack(layers, norms, oracle.Q8_0, oracle.Q8_0, dm, ff, X[b])
+        assert_parity(ref, got[b], what=f"q8_0 stack batch {nvec} row {b}")

@@ -214,3 +214,42 @@ def test_deterministic(engine):
     a = engine.ggml_gemv_dispatch_bound(rw, x)
     b = engine.ggml_gemv_dispatch_bound(rw, x)
     assert np.array_equal(a, b)
+
+
+# ---------------------------------------------------------------- Q8_0 batches on tcgen05
+@pytest.mark.parametrize("batch,m,n", [
+    (8, 128, 1024),      # smallest tensor-core batch
+    (13, 256, 2048),     # ragged batch: rows padded to 16 in the MMA's N
+    (64, 512, 4096),     # config-3 batch, several K splits
+    (100, 128, 14336),   # long K (Llama-3-8B down), deep K split, N = 208
+])
+def test_q8_0_tensor_core_batches(engine, batch, m, n):
+    t = oracle.Q8_0
+    w = quantized(t, m, n, seed=71 + batch)
+    xs = oracle.normal(72 + batch, batch * n)
+    rw = engine.upload(t, m, n, w)
+    got = engine.ggml_gemv_batched(rw, xs, batch)
+    ref = np.concatenate([oracle.gemv(t, m, n, w, xs[b * n:(b + 1) * n]) for b in range(batch)])
+    assert_parity(ref, got, what=f"q8_0 tensor-core batch {batch} {m}x{n}")
+    again = engine.ggml_gemv_batched(rw, xs, batch)
+    assert np.array_equal(got, again)
+
+
+def test_q8_0_tensor_core_residual_dev(engine):
+    import torch
+
+    m, n, batch = 384, 1024, 24
+    w = quantized(oracle.Q8_0, m, n, seed=91)
+    xs = oracle.normal(92, batch * n).reshape(batch, n)
+    rs = oracle.normal(93, batch * m).reshape(batch, m)
+    rw = engine.upload(oracle.Q8_0, m, n, w)
+    X, R = torch.from_numpy(xs).cuda(), torch.from_numpy(rs).cuda()
+    Y = torch.empty(batch, m, device="cuda")
+    engine.set_stream(torch.cuda.current_stream())
+    try:
+        engine.gemv_dev(rw, X, Y, resid=R, nvec=batch)
+        torch.cuda.synchronize()
+    finally:
+        engine.set_stream(None)
+    ref = np.stack([oracle.gemv(oracle.Q8_0, m, n, w, xs[b]) + rs[b] for b in range(batch)])
+    assert_parity(ref, Y.cpu().numpy(), what="q8_0 tensor-core + residual")

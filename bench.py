@@ -546,6 +546,12 @@ def run_ours(args):
     uses_stack = B == 1 and kin == dm and (tp or os.environ.get("HAYAI_STACK_KERNEL", "1") != "0")
     if tp and args.tp_impl == "nccl":
         uses_stack = False
+
+    def tensor_core(t, m, k):  # Q8_0 at 8..128 rows runs on tcgen05: prep + GEMM + split-sum launches
+        return t == Q8_0 and 8 <= B <= 128 and m % 128 == 0 and k % 128 == 0
+
+    tc_gu, tc_dn = tensor_core(tg, ffl, kin), tensor_core(td, dm, ffl)
+    launches_per_layer = (3 if tc_gu else 1) + (3 if tc_dn else 1)
     eng = hb.CudaEngine(local)
     stream = torch.cuda.Stream(dev)  # one stream for torch's copies, our kernels and the CUDA events
     torch.cuda.set_stream(stream)
@@ -684,7 +690,9 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
         k_time = e0.elapsed_time(e1) / 1e3 / reps
         k_bytes = 2 * mat_bytes(tg, ffl, kin)
-        kname = f"gemv_tma_kernel<{names[tg]},{min(B, 4)},true> (fused gate/up + SiLU*up)"
+        kname = ("tc_prep_kernel (RMSNorm, f16 hi/lo) + tc_gemm_kernel (tcgen05, gate and up) + "
+                 "tc_finish_kernel (split sums, SiLU*up)" if tc_gu else
+                 f"gemv_tma_kernel<{names[tg]},{min(B, 4)},true> (fused gate/up + SiLU*up)")
         kkey = f"gateup_{args.config}_b{B}"
     achieved = k_bytes / k_time / 1e9
     roofline = {"bound": "hbm", "kernel": kname,
@@ -739,7 +747,8 @@ def run_ours(args):
             "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": c_dtype(c),
             "data": "synthetic (seeded N(0,0.02^2) weights quantized on device, N(0,1) activations)",
             "config": {"workload": c["workload"], "batch": B, "layers": L, "d_model": dm, "d_ff": ff,
-                       "kernel_path": "persistent stack kernel" if uses_stack else "per-layer kernels",
+                       "kernel_path": "persistent stack kernel" if uses_stack else
+                       "per-layer kernels" + (" (tcgen05 GEMM)" if tc_gu or tc_dn else ""),
                        "bytes_per_token": tok_bytes,
                        "parallelism": (f"tp{world} ({'in-kernel NVLink exchange' if args.tp_impl == 'ours' else 'NCCL all_reduce'})"
                                        if tp else f"replicas x{world}" if world > 1 else "single"),
@@ -747,7 +756,7 @@ def run_ours(args):
             "tokens_per_s": round(tokens_per_s, 2),
             "frac_of_8tbs": round(value / world / 8000.0, 4),  # per GPU
             "roofline": roofline, "e2e": e2e, "clocks": clocks,
-            "gpu_launches": args.steps * (1 if uses_stack else 2 * L),  # per rank
+            "gpu_launches": args.steps * (1 if uses_stack else launches_per_layer * L),  # per rank
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu

@@ -536,22 +536,25 @@ def run_ours(args):
     L, dm, kin, ff, tg, td = c["layers"], c["d_model"], c["k_in"], c["d_ff"], c["tg"], c["td"]
     B = args.batch
     # tensor parallelism: every rank holds a d_ff shard of every layer (gate/up rows, down
-    # columns); the down partials are exchanged inside the stack kernel (or by NCCL with
-    # --tp-impl nccl, the library-collective baseline)
+    # columns); the down partials are exchanged inside the stack kernel at batch 1, by one
+    # all-reduce kernel per layer at batch > 1 (or by NCCL with --tp-impl nccl, the
+    # library-collective baseline)
     tp = args.tp and world > 1
-    if tp and (B != 1 or kin != dm):
-        raise SystemExit("--tp runs the batch-1 stack of an unpadded model")
+    if tp and kin != dm:
+        raise SystemExit("--tp runs the stack of an unpadded model")
     ffl = ff // world if tp else ff  # this rank's d_ff
     # the persistent stack kernel serves batch 1 when the FFN input width equals d_model
     uses_stack = B == 1 and kin == dm and (tp or os.environ.get("HAYAI_STACK_KERNEL", "1") != "0")
     if tp and args.tp_impl == "nccl":
         uses_stack = False
 
-    def tensor_core(t, m, k):  # Q8_0 at 8..128 rows runs on tcgen05: prep + GEMM + split-sum launches
-        return t == Q8_0 and 8 <= B <= 128 and m % 128 == 0 and k % 128 == 0
+    def tensor_core(t, m, k):  # 8..128 rows run on tcgen05: prep + GEMM + slot-sum launches
+        if os.environ.get("HAYAI_TC_GEMM", "1") == "0" or not 8 <= B <= 128 or m % 128:
+            return False
+        return (t == Q8_0 and B >= 9 and k % 128 == 0) or (t in (Q4_K, Q6_K) and k % 256 == 0)
 
     tc_gu, tc_dn = tensor_core(tg, ffl, kin), tensor_core(td, dm, ffl)
-    launches_per_layer = (3 if tc_gu else 1) + (3 if tc_dn else 1)
+    launches_per_layer = (3 if tc_gu else 1) + (3 if tc_dn else 1) + (1 if tp and args.tp_impl == "ours" else 0)
     eng = hb.CudaEngine(local)
     stream = torch.cuda.Stream(dev)  # one stream for torch's copies, our kernels and the CUDA events
     torch.cuda.set_stream(stream)
@@ -612,22 +615,22 @@ def run_ours(args):
 
     def run_stack(xx):
         if tp:
-            eng.ffn_stack_tp_dev(G, U, D, xx, norms=NW, eps=EPS)
+            eng.ffn_stack_tp_dev(G, U, D, xx, B, norms=NW, eps=EPS)
         else:
             eng.ffn_stack_dev(G, U, D, xx, B, norms=NW, eps=EPS)
 
     if tp and args.tp_impl == "nccl":
         import torch.distributed as dist
 
-        h_ws = torch.empty(ffl, dtype=torch.float32, device=dev)
-        y_ws = torch.empty(dm, dtype=torch.float32, device=dev)
+        h_ws = torch.empty(B, ffl, dtype=torch.float32, device=dev)
+        y_ws = torch.empty(B, dm, dtype=torch.float32, device=dev)
 
         def run_stack(xx):  # noqa: F811 -- per-layer kernels + one NCCL all-reduce per layer
             for l in range(L):
-                eng.ffn_gateup_dev(G[l], U[l], xx, h_ws, 1, norm=NW[l], norm_len=dm, eps=EPS)
-                eng.gemv_dev(D[l], h_ws, y_ws)
+                eng.ffn_gateup_dev(G[l], U[l], xx, h_ws, B, norm=NW[l], norm_len=dm, eps=EPS)
+                eng.gemv_dev(D[l], h_ws, y_ws, nvec=B)
                 dist.all_reduce(y_ws)
-                xx.view(-1).add_(y_ws)
+                xx.view(-1).add_(y_ws.view(-1))
 
     def step():
         x.copy_(x0)
@@ -711,7 +714,7 @@ def run_ours(args):
 
     def host_call():
         if tp and args.tp_impl == "ours":
-            return eng.ffn_stack_tp(G, U, D, xi, norms=NW, eps=EPS)
+            return eng.ffn_stack_tp(G, U, D, xi, B, norms=NW, eps=EPS)
         if tp:  # NCCL baseline: the same per-layer loop on a device copy of the host vector
             xd = torch.from_numpy(xi).to(dev, non_blocking=True)
             run_stack(xd)
@@ -746,7 +749,8 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4), "higher_is_better": True,
             "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": c_dtype(c),
             "data": "synthetic (seeded N(0,0.02^2) weights quantized on device, N(0,1) activations)",
-            "config": {"workload": c["workload"], "batch": B, "layers": L, "d_model": dm, "d_ff": ff,
+            "config": {"workload": c["workload"].replace("batch-1 decode", f"batch {B}") if B > 1 else c["workload"],
+                       "batch": B, "layers": L, "d_model": dm, "d_ff": ff,
                        "kernel_path": "persistent stack kernel" if uses_stack else
                        "per-layer kernels" + (" (tcgen05 GEMM)" if tc_gu or tc_dn else ""),
                        "bytes_per_token": tok_bytes,

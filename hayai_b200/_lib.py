@@ -59,8 +59,8 @@ SIGNATURES: dict[str, list] = {
     "hc_ffn_gateup_dev": [_P, _P, _P, _P, _P, _S, _P, _S, _F],
     "hc_ffn_stack_dev": [_P, _P, _P, _P, _P, _F, _S, _P, _S],
     "hc_ffn_stack": [_P, _P, _P, _P, _P, _F, _S, _P, _P, _S],
-    "hc_ffn_stack_tp_dev": [_P, _P, _P, _P, _P, _F, _S, _P],
-    "hc_ffn_stack_tp": [_P, _P, _P, _P, _P, _F, _S, _P, _P],
+    "hc_ffn_stack_tp_dev": [_P, _P, _P, _P, _P, _F, _S, _P, _S],
+    "hc_ffn_stack_tp": [_P, _P, _P, _P, _P, _F, _S, _P, _P, _S],
     "hc_peer_handle_bytes": [_P],
     "hc_peer_open": [_P, _I, _I, _S, _P],
     "hc_peer_connect": [_P, _P],

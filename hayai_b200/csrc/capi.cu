@@ -191,6 +191,9 @@ extern "C" int hc_engine_init(int device, hc_engine** out) {
     // HAYAI_STACK_KERNEL=0 keeps batch-1 FFN stacks on the per-layer kernels
     const char* sk = getenv("HAYAI_STACK_KERNEL");
     if (sk && sk[0] == '0') e->use_stack_kernel = false;
+    // HAYAI_TC_GEMM=0 keeps batches on the mma.sync GEMV (one weight pass per 4 rows)
+    const char* tc = getenv("HAYAI_TC_GEMM");
+    if (tc && tc[0] == '0') e->use_tc = false;
     ce = cudaMalloc(&e->d_err, 16);
     if (ce == cudaSuccess) ce = cudaMemset(e->d_err, 0, 16);
     if (ce != cudaSuccess) {
@@ -234,8 +237,8 @@ void hc_drop_graphs(hc_engine* e) {
     e->graphs.clear();
 }
 
-int hc_tc_prepare(hc_engine* e, size_t M, size_t K, size_t nvec, int mats, void** ws) {
-    const size_t need = tc_workspace_bytes((int)M, (int)K, (int)nvec, e->num_sms, mats);
+int hc_tc_prepare(hc_engine* e, int type, size_t M, size_t K, size_t nvec, int mats, void** ws) {
+    const size_t need = tc_workspace_bytes(type, (int)M, (int)K, (int)nvec, e->num_sms, mats);
     if (need > e->ws_tc.cap) {
         cudaStreamSynchronize(e->stream);
         hc_drop_graphs(e);  // graphs captured earlier hold the old address
@@ -403,12 +406,12 @@ int hc_launch_gemv(hc_engine* e, const hc_weights* w, const float* x, size_t ldx
     if (((uintptr_t)x & 15) || (ldx & 3))
         return hc_set_error(HC_ERR_INVALID, "x must be 16-byte aligned with ldx a multiple of 4");
     cudaError_t ce;
-    if (tc_gemm_supported(w->type, (int)w->m, (int)w->n, (int)nvec)) {
+    if (e->use_tc && tc_gemm_supported(w->type, (int)w->m, (int)w->n, (int)nvec)) {
         // batches of 8+ rows: one pass over the weights on the tcgen05 tensor cores
         void* ws;
-        int rc = hc_tc_prepare(e, w->m, w->n, nvec, 1, &ws);
+        int rc = hc_tc_prepare(e, w->type, w->m, w->n, nvec, 1, &ws);
         if (rc) return rc;
-        ce = launch_tc_gemm((const uint8_t*)w->dev, nullptr, (long long)w->stride, (int)w->m, (int)w->n, x, (int)ldx,
+        ce = launch_tc_gemm(w->type, (const uint8_t*)w->dev, nullptr, (long long)w->stride, (int)w->m, (int)w->n, x, (int)ldx,
                             (int)nvec, y, (int)ldy, resid, (int)ldr, nullptr, 0, 0.f, ws, e->d_err, e->num_sms,
                             e->smem_optin, e->stream);
     } else if (gemv_mma_supported(w->type)) {
@@ -637,11 +640,12 @@ int hc_launch_gateup(hc_engine* e, const hc_weights* g, const hc_weights* u, con
         return hc_set_error(HC_ERR_INVALID, "x must be 16-byte aligned with ldx a multiple of 4");
     if (norm_w && (norm_len == 0 || norm_len > g->n))
         return hc_set_error(HC_ERR_INVALID, "norm length %zu must be in [1, %zu]", norm_len, g->n);
-    if (g->type == u->type && g->stride == u->stride && tc_gemm_supported(g->type, (int)g->m, (int)g->n, (int)nvec)) {
+    if (e->use_tc && g->type == u->type && g->stride == u->stride &&
+        tc_gemm_supported(g->type, (int)g->m, (int)g->n, (int)nvec)) {
         void* ws;
-        int rc = hc_tc_prepare(e, g->m, g->n, nvec, 2, &ws);
+        int rc = hc_tc_prepare(e, g->type, g->m, g->n, nvec, 2, &ws);
         if (rc) return rc;
-        cudaError_t ce = launch_tc_gemm((const uint8_t*)g->dev, (const uint8_t*)u->dev, (long long)g->stride,
+        cudaError_t ce = launch_tc_gemm(g->type, (const uint8_t*)g->dev, (const uint8_t*)u->dev, (long long)g->stride,
                                         (int)g->m, (int)g->n, x, (int)ldx, (int)nvec, h, (int)g->m, nullptr, 0, norm_w,
                                         (int)norm_len, eps, ws, e->d_err, e->num_sms, e->smem_optin, e->stream);
         if (ce != cudaSuccess) return hc_cuda_error(ce, "gate/up tensor-core launch");
@@ -864,21 +868,13 @@ static int stack_try_kernel(hc_engine* e, const StackArgs& s, float* x, size_t n
     return HC_OK;
 }
 
-static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
-    size_t ffmax = 0;
-    for (size_t l = 0; l < s.L; ++l) ffmax = s.g[l]->m > ffmax ? s.g[l]->m : ffmax;
-    void* old_h = e->ws_h.p;
-    int rc = e->ws_h.ensure(nvec * ffmax * 4);
-    if (rc) return rc;
-    if (old_h && old_h != e->ws_h.p) hc_drop_graphs(e);
-    float* h = (float*)e->ws_h.p;
-    bool done = false;
-    rc = stack_try_kernel(e, s, x, nvec, &done);
-    if (rc || done) return rc;
-    // size every workspace before a capture (no allocation may happen inside it)
+// Size every workspace the per-layer kernels of a stack use for nvec rows, before a capture
+// (no allocation may happen inside one).
+static int stack_prepare(hc_engine* e, const StackArgs& s, size_t nvec) {
     for (size_t l = 0; l < s.L; ++l) {
         float* ws;
         int* cnt;
+        int rc;
         if (s.g[l]->type == s.u[l]->type && gemv_mma_supported(s.g[l]->type)) {
             rc = hc_sk_prepare(e, s.g[l]->type, s.g[l]->m, s.g[l]->n, true, &ws, &cnt);
         } else {
@@ -893,14 +889,17 @@ static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
         if (!rc && gemv_mma_supported(s.d[l]->type))
             rc = hc_sk_prepare(e, s.d[l]->type, s.d[l]->m, s.d[l]->n, false, &ws, &cnt);
         void* tws;
-        if (!rc && tc_gemm_supported(s.g[l]->type, (int)s.g[l]->m, (int)s.g[l]->n, (int)nvec))
-            rc = hc_tc_prepare(e, s.g[l]->m, s.g[l]->n, nvec, 2, &tws);
-        if (!rc && tc_gemm_supported(s.d[l]->type, (int)s.d[l]->m, (int)s.d[l]->n, (int)nvec))
-            rc = hc_tc_prepare(e, s.d[l]->m, s.d[l]->n, nvec, 1, &tws);
+        if (!rc && e->use_tc && tc_gemm_supported(s.g[l]->type, (int)s.g[l]->m, (int)s.g[l]->n, (int)nvec))
+            rc = hc_tc_prepare(e, s.g[l]->type, s.g[l]->m, s.g[l]->n, nvec, 2, &tws);
+        if (!rc && e->use_tc && tc_gemm_supported(s.d[l]->type, (int)s.d[l]->m, (int)s.d[l]->n, (int)nvec))
+            rc = hc_tc_prepare(e, s.d[l]->type, s.d[l]->m, s.d[l]->n, nvec, 1, &tws);
         if (rc) return rc;
     }
-    if (!e->use_graphs) return stack_enqueue(e, s, x, nvec, h);
+    return HC_OK;
+}
 
+// Key of a captured stack: every address and shape the graph bakes in.
+static uint64_t stack_key(const hc_engine* e, const StackArgs& s, const float* x, size_t nvec, const float* h) {
     uint64_t key = mix(mix(mix(0, (uint64_t)(uintptr_t)x), nvec), s.L);
     key = mix(key, (uint64_t)(uintptr_t)h);
     key = mix(key, (uint64_t)(uintptr_t)e->ws_g.p);
@@ -916,6 +915,12 @@ static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
         key = mix(key, (uint64_t)(uintptr_t)(s.norm ? s.norm[l] : nullptr));
         key = mix(key, ((uint64_t)s.g[l]->type << 32) ^ s.g[l]->m ^ (s.g[l]->n << 20) ^ ((uint64_t)s.d[l]->type << 40));
     }
+    return key;
+}
+
+// Launch the graph cached under `key`, capturing enqueue() into it first if there is none.
+template <class F>
+static int graph_run(hc_engine* e, uint64_t key, F enqueue) {
     auto it = e->graphs.find(key);
     if (it == e->graphs.end()) {
         // capture on the engine's private stream (the caller's may be the legacy default
@@ -928,7 +933,7 @@ static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
             e->stream = caller;
             return hc_cuda_error(ce, "stack capture begin");
         }
-        rc = stack_enqueue(e, s, x, nvec, h);
+        int rc = enqueue();
         ce = cudaStreamEndCapture(e->stream, &graph);
         e->stream = caller;
         if (rc) {
@@ -946,6 +951,74 @@ static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
     return HC_OK;
 }
 
+// h workspace for nvec rows of the widest layer; moving it drops the captured graphs.
+static int stack_h(hc_engine* e, const StackArgs& s, size_t nvec, float** h) {
+    size_t ffmax = 0;
+    for (size_t l = 0; l < s.L; ++l) ffmax = s.g[l]->m > ffmax ? s.g[l]->m : ffmax;
+    void* old_h = e->ws_h.p;
+    int rc = e->ws_h.ensure(nvec * ffmax * 4);
+    if (rc) return rc;
+    if (old_h && old_h != e->ws_h.p) hc_drop_graphs(e);
+    *h = (float*)e->ws_h.p;
+    return HC_OK;
+}
+
+static int stack_run(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
+    float* h;
+    int rc = stack_h(e, s, nvec, &h);
+    if (rc) return rc;
+    bool done = false;
+    rc = stack_try_kernel(e, s, x, nvec, &done);
+    if (rc || done) return rc;
+    rc = stack_prepare(e, s, nvec);
+    if (rc) return rc;
+    if (!e->use_graphs) return stack_enqueue(e, s, x, nvec, h);
+    return graph_run(e, stack_key(e, s, x, nvec, h), [&] { return stack_enqueue(e, s, x, nvec, h); });
+}
+
+// Tensor-parallel stack at batch > 1, per layer: the fused gate/up of this rank's d_ff shard
+// (RMSNorm of the replicated x in its prologue), the down GEMV of the shard into a partial of
+// every output row, and the all-reduce of the partials into x over the exchange regions
+// (tp_reduce.cu).  x is replicated and stays bit-identical on every rank.
+static int stack_tp_enqueue(hc_engine* e, const StackArgs& s, float* x, size_t nvec, float* h, float* yp) {
+    const size_t dm = s.d[0]->m;
+    for (size_t l = 0; l < s.L; ++l) {
+        int rc = hc_launch_gateup(e, s.g[l], s.u[l], x, dm, h, nvec, s.norm ? s.norm[l] : nullptr, dm, s.eps);
+        if (!rc) rc = hc_launch_gemv(e, s.d[l], h, s.g[l]->m, yp, dm, nullptr, 0, nvec);
+        if (rc) return rc;
+        cudaError_t ce = launch_tp_allreduce(yp, x, nvec * dm, e->peer.d_peer, e->peer.rank, e->peer.world, e->d_err,
+                                             e->stream);
+        if (ce != cudaSuccess) return hc_cuda_error(ce, "tensor-parallel all-reduce");
+    }
+    return HC_OK;
+}
+
+static int stack_tp_batched(hc_engine* e, const StackArgs& s, float* x, size_t nvec) {
+    const size_t dm = s.d[0]->m;
+    const PeerState& pe = e->peer;
+    const size_t need = tp_exchange_bytes(pe.world, nvec * dm);
+    if (pe.bytes < need)
+        return hc_set_error(HC_ERR_INVALID,
+                            "tensor-parallel exchange of %zu rows x %zu needs a peer region of %zu bytes (have %zu)",
+                            nvec, dm, need, pe.bytes);
+    if (dm % 4 || ((uintptr_t)x) % 16)
+        return hc_set_error(HC_ERR_INVALID, "tensor-parallel exchange: x must be 16-byte aligned, d_model %% 4 == 0");
+    float* h;
+    int rc = stack_h(e, s, nvec, &h);
+    if (rc) return rc;
+    void* old_y = e->ws_tp.p;
+    rc = e->ws_tp.ensure(nvec * dm * 4);
+    if (rc) return rc;
+    if (old_y && old_y != e->ws_tp.p) hc_drop_graphs(e);
+    float* yp = (float*)e->ws_tp.p;
+    rc = stack_prepare(e, s, nvec);
+    if (rc) return rc;
+    if (!e->use_graphs) return stack_tp_enqueue(e, s, x, nvec, h, yp);
+    uint64_t key = mix(stack_key(e, s, x, nvec, h), 0x54504231ull);  // "TPB1"
+    key = mix(mix(key, (uint64_t)(uintptr_t)yp), (uint64_t)(uintptr_t)pe.d_peer);
+    return graph_run(e, key, [&] { return stack_tp_enqueue(e, s, x, nvec, h, yp); });
+}
+
 extern "C" int hc_ffn_stack_dev(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
                                 const hc_weights* const* d, const float* const* norm_w, float eps, size_t L, float* x,
                                 size_t nvec) {
@@ -960,10 +1033,12 @@ extern "C" int hc_ffn_stack_dev(hc_engine* e, const hc_weights* const* g, const 
 }
 
 // Tensor-parallel stack: the layers are this rank's d_ff shard (gate/up rows and down
-// columns of the same range); x is replicated and ends identical on every rank.
+// columns of the same range); x [nvec][d_model] is replicated and ends identical on every
+// rank.  Batch 1: the persistent stack kernel with the exchange inside; otherwise per-layer
+// kernels and the in-kernel all-reduce of tp_reduce.cu, captured as one graph.
 extern "C" int hc_ffn_stack_tp_dev(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
                                    const hc_weights* const* d, const float* const* norm_w, float eps, size_t L,
-                                   float* x) {
+                                   float* x, size_t nvec) {
     int rc = hc_engine_activate(e);
     if (rc) return rc;
     StackArgs s{g, u, d, norm_w, L, eps};
@@ -974,6 +1049,8 @@ extern "C" int hc_ffn_stack_tp_dev(hc_engine* e, const hc_weights* const* g, con
     if (g[0]->n != d[0]->m)
         return hc_set_error(HC_ERR_UNSUPPORTED, "tensor-parallel stack: padded model width (%zu inputs, %zu outputs)",
                             g[0]->n, d[0]->m);
+    if (nvec == 0) return HC_OK;
+    if (nvec > 1) return stack_tp_batched(e, s, x, nvec);
     bool done = false;
     rc = stack_try_kernel(e, s, x, 1, &done, true);
     if (rc) return rc;
@@ -986,15 +1063,16 @@ extern "C" int hc_ffn_stack_tp_dev(hc_engine* e, const hc_weights* const* g, con
 
 extern "C" int hc_ffn_stack_tp(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
                                const hc_weights* const* d, const float* const* norm_w, float eps, size_t L,
-                               const float* x_in, float* x_out) {
+                               const float* x_in, float* x_out, size_t nvec) {
     int rc = hc_engine_activate(e);
     if (rc) return rc;
     if (!g || !g[0] || !x_in || !x_out) return hc_set_error(HC_ERR_INVALID, "null argument");
-    const size_t bytes = g[0]->n * 4;
+    const size_t bytes = nvec * g[0]->n * 4;
+    if (bytes == 0) return HC_OK;
     rc = e->ws_x.ensure(bytes);
     if (rc) return rc;
     HC_CUDA(cudaMemcpyAsync(e->ws_x.p, x_in, bytes, cudaMemcpyHostToDevice, e->stream));
-    rc = hc_ffn_stack_tp_dev(e, g, u, d, norm_w, eps, L, (float*)e->ws_x.p);
+    rc = hc_ffn_stack_tp_dev(e, g, u, d, norm_w, eps, L, (float*)e->ws_x.p, nvec);
     if (rc) return rc;
     HC_CUDA(cudaMemcpyAsync(x_out, e->ws_x.p, bytes, cudaMemcpyDeviceToHost, e->stream));
     HC_CUDA(cudaStreamSynchronize(e->stream));

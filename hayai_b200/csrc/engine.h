@@ -51,7 +51,9 @@ struct hc_engine {
     DevBuf sk_ws, sk_cnt;
     DevBuf stack_bar;             // grid-barrier counter of the persistent FFN-stack kernel
     DevBuf ws_tc;                 // batched Q8_0 tensor-core GEMM: canonical activations + partials
+    DevBuf ws_tp;                 // tensor parallelism at batch > 1: this rank's down partial
     bool use_stack_kernel = true; // batch-1 stacks run as one persistent kernel when they fit
+    bool use_tc = true;           // batches of 8+ rows of Q8_0/Q4_K/Q6_K on the tcgen05 GEMM
     HostBuf hs_out;
     std::unordered_map<uint64_t, cudaGraphExec_t> graphs;  // captured FFN stacks
     std::unordered_map<uint64_t, void*> ptr_tables;        // device tables of expert pointers
@@ -95,4 +97,4 @@ int hc_sk_prepare(hc_engine* e, int type, size_t M, size_t K, bool fused, float*
 void hc_drop_graphs(hc_engine* e);
 // Scratch of the batched Q8_0 tensor-core GEMM (grows on demand; a reallocation drops the
 // captured CUDA graphs).
-int hc_tc_prepare(hc_engine* e, size_t M, size_t K, size_t nvec, int mats, void** ws);
+int hc_tc_prepare(hc_engine* e, int type, size_t M, size_t K, size_t nvec, int mats, void** ws);

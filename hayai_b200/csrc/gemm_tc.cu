@@ -1,30 +1,43 @@
-// gemm_tc.cu -- batched Q8_0 GEMV (B >= 8 activation rows) on the 5th-generation tensor cores.
+// gemm_tc.cu -- batched quantized GEMV (B >= 8 activation rows) on the 5th-generation tensor
+// cores, for Q8_0, Q4_K and Q6_K weights in the tile-major layout.
 //
-// Reference semantics: gemv_q8_0 (crates/hayai-model/src/quant.rs:598-615) applied to every row
-// of a batch, the multi-row case of execute_quant_gemv_batched (crates/hayai-opencl/src/
-// orchestrator.rs:240-267, which loops over rows on the CPU path).
+// Reference semantics: gemv_q8_0 (crates/hayai-model/src/quant.rs:598-615), gemv_q4_k
+// (q4k.rs:206-256 with gemv_q4k_sub32 :10-32 and get_scale_min_k4 :34-43) and gemv_q6_k
+// (q6k.rs:26-90) applied to every row of a batch, the multi-row case of
+// execute_quant_gemv_batched (crates/hayai-opencl/src/orchestrator.rs:240-267, which loops over
+// rows on the CPU path).
 //
-// Y[t][m] = sum_k W[m][k] x[t][k] with W in Q8_0 (per 32-element block: int8 codes q and an f16
-// scale d).  The block scale changes every 32 elements and every row, so it cannot ride on a
-// TMEM accumulator; instead the weights are dequantised in shared memory into two exact f16
-// operands: with w' = q * d * 2^8, A_hi = f16(w') (HMUL2) and A_lo = w' - A_hi (one HFMA2, exact:
-// q has 8 significant bits and d 11, so the remainder has at most 8), and A_hi + A_lo = w'
-// exactly.  The activations enter as two f16 columns per row, x = x_hi + x_lo * 2^-11 (rows
-// [0, Bp) and [Bp, 2 Bp) of the B operand), so one tcgen05.mma with N = 2 Bp multiplies both,
-// and D = A_hi X + A_lo X accumulates in f32 in TMEM; the epilogue forms
+// Y[t][m] = sum_k W[m][k] x[t][k].  The quantization scales change every 16-32 elements and
+// every row, so they cannot ride on a TMEM accumulator; instead every weight is dequantised in
+// shared memory to its f32 value exactly as the reference forms it, scaled by 2^8 (exact), and
+// split into two f16 operands w' = A_hi + A_lo:
+//   Q8_0  w' = q d 2^8: A_hi = f16(w') (HMUL2), A_lo = w' - A_hi (one HFMA2, exact: q has 8
+//         significant bits and d 11, so the remainder has at most 8);
+//   Q4_K  w' = (q d1 - m1) 2^8 (one FFMA, the reference's single rounding of f d1 - m1v with
+//         d1 = d sc, m1 = dmin m): A_hi = w' truncated to 11 significant bits, A_lo = f16(w' - A_hi);
+//   Q6_K  w' = q (d sc) 2^8 (one FMUL, the reference's rounding): split as for Q4_K.
+// The activations enter as two f16 columns per row, x = x_hi + x_lo * 2^-11 (rows [0, Bp) and
+// [Bp, 2 Bp) of the B operand), so one tcgen05.mma with N = 2 Bp multiplies both, and
+// D = A_hi X + A_lo X accumulates in f32 in TMEM (two accumulators: the A_hi and the A_lo
+// products are independent MMA chains); the epilogue forms
 // y = (D[:, t] + D[:, Bp + t] * 2^-11) * 2^-8.
 //
-// CTA = 128 output rows (the MMA's M) over a K range (split K: partial outputs per split, added
-// by the finishing kernel in split order, so results are deterministic), 10 warps:
-//   warp 0    TMA producers: lane 0 per 128-element group one bulk copy per 16-row tile of
-//             the tile-major weight layout (8 x 2176 B); lane 1 the activation chunks (64 K
-//             each, prepared in the MMA's operand layout by tc_prep_kernel, one copy each);
-//   warp 1    owns the TMEM columns; one elected lane issues the MMAs (4 K-steps x {hi, lo}
-//             per 64-K chunk) and tcgen05.commit frees the operand buffers;
-//   warps 2-9 dequantise each weight half-group into the A_hi / A_lo operand buffers (K-major,
-//             128-byte swizzle: rows of 128 B, 16-byte chunks XOR-permuted by row), then warps
-//             2-5 read the accumulator (tcgen05.ld, one TMEM lane quarter each) and write the
-//             partial outputs.
+// Persistent, stream-K: one CTA per SM walks a contiguous range of the work units (one weight
+// image = 128 or 256 K of one 128-row block of one matrix, in the order row block, matrix, K),
+// so the weight stream never pauses between row blocks.  A maximal run of units of one (row
+// block, matrix) in a CTA is a segment: it accumulates in one of two TMEM accumulator sets
+// and ends in a partial-output slot; the finishing kernel adds a row block's slots in CTA
+// order (deterministic), then SiLU(g) * u or the residual.  14 warps:
+//   warp 0     TMA producers: lane 0 per unit one bulk copy per 16-row tile of the tile-major
+//              layout (8 copies of one image); lane 1 the activation chunks (64 K each,
+//              prepared in the MMA's operand layout by tc_prep_kernel, one copy each);
+//   warp 1     owns the TMEM columns; one elected lane issues the MMAs (4 K-steps x {hi, lo}
+//              per 64-K chunk), tcgen05.commit frees the operand buffers and, at a segment's
+//              end, hands its accumulator set to the epilogue;
+//   warps 2-9  dequantise each 64-K chunk into the A_hi / A_lo operand buffers (K-major,
+//              128-byte swizzle: rows of 128 B, 16-byte chunks XOR-permuted by row);
+//   warps 10-13 the epilogue: one TMEM lane quarter each (tcgen05.ld), partial outputs out,
+//              then the accumulator set is free again.
 // Every wait is bounded (~1 s; error bit 1), and the TMEM columns are freed on every path.
 #include <cuda_fp16.h>
 
@@ -37,25 +50,46 @@ namespace hc {
 
 constexpr int kTcRows = 128;               // output rows per CTA (MMA M)
 constexpr int kTcChunk = 64;               // K per operand buffer
-constexpr int kTcImg = 2176;               // Q8_0 tile-block image: 16 rows x 128 K
-constexpr int kTcGps = 2;                  // 128-K groups per weight stage
-constexpr int kTcWStage = 8 * kTcGps * kTcImg;  // the CTA's 8 row tiles x kTcGps groups
 constexpr int kTcABytes = kTcRows * kTcChunk * 2;  // one f16 operand buffer (16 KB)
-constexpr int kTcThreads = 320;            // 10 warps
+constexpr int kTcThreads = 448;            // 14 warps
 constexpr int kTcMaxRing = 8;
-constexpr float kTcWScale = 256.f;         // w' = q * d * 2^8
+constexpr float kTcWScale = 256.f;         // w' = w * 2^8
+
+// Tile-block image of each format (repack.cu): bytes, K elements, images per weight stage
+// (one: a stage is one work unit).
+struct TcQ80 {
+    static constexpr int kType = T_Q8_0, kImg = 2176, kImgK = 128, kGps = 1;
+};
+struct TcQ4K {
+    static constexpr int kType = T_Q4_K, kImg = 2304, kImgK = 256, kGps = 1;
+};
+struct TcQ6K {
+    static constexpr int kType = T_Q6_K, kImg = 3360, kImgK = 256, kGps = 1;
+};
+template <class F>
+__host__ __device__ constexpr int tc_wstage() {  // the CTA's 8 row tiles x kGps images
+    return 8 * F::kGps * F::kImg;
+}
 
 struct TcArgs {
-    const uint8_t* w[2];  // tile-major Q8_0 matrices (blockIdx.z picks one)
+    const uint8_t* w[2];  // tile-major matrices (the unit's matrix index picks one)
     long long tstride;    // bytes per 16-row tile
     int M, K;
     const uint8_t* xc;    // activations, canonical: [K / 64 chunks][N rows][64] f16
     int N, B;             // MMA N = 2 Bp (hi rows, then lo rows); real rows
-    int cps;              // 64-K chunks per K split (even)
-    float* out;           // [z][split][B][M] partial outputs
+    int mats, nimg;       // matrices (1, or 2 for gate/up); images per row block and matrix
+    long long U;          // work units: (M / 128) * mats * nimg
+    int slots;            // partial-output slots per (row block, matrix)
+    int nsets;            // TMEM accumulator sets (2 when 4 N <= 512 columns)
+    float* out;           // partials [(row block, matrix)][slot][B][128]
     int* err;
-    int SW, NX, NA;       // ring depths: weight groups, activation chunks, operand buffers
+    int SW, NX, NA;       // ring depths: weight units, activation chunks, operand buffers
 };
+
+// The CTA (of G) whose unit range [c U / G, (c + 1) U / G) holds unit u.
+__host__ __device__ __forceinline__ int tc_owner(long long u, long long U, int G) {
+    return (int)(((u + 1) * G - 1) / U);
+}
 
 // Byte offset of (row r, k) in a 64-K operand buffer in the K-major 128-byte-swizzled layout:
 // every row is 128 B (64 f16 of K), 8 rows form a 1024-B atom, and the 16-byte chunk k / 8 of
@@ -110,27 +144,209 @@ __device__ __forceinline__ void tc_dequant4(uint32_t word, __half2 d, uint2& hi,
     lo = make_uint2(h2_as_u32(__hfma2(q01, d, __hneg2(h01))), h2_as_u32(__hfma2(q23, d, __hneg2(h23))));
 }
 
+// Two f32 weights (already x 2^8) as (hi, lo) f16x2 words: hi = the value truncated to 11
+// significant bits (exact in f16 for |w| in [2^-14, 65504)), lo = f16 of the exact remainder.
+__device__ __forceinline__ void tc_split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const float ha = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
+    const float hb = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
+    hi = pack_h2(ha, hb);
+    lo = pack_h2(a - ha, b - hb);
+}
+
+// Per-thread dequantisation of one 64-K chunk of the CTA's 128 rows (256 threads, dt = 0..255).
+// init() fixes the thread's offsets (words inside a weight stage, bytes inside an operand
+// buffer); chunk() reads the image at word offset `gw` of every tile run, chunk `sub` of it.
+template <class F>
+struct TcDq;
+
+// Q8_0 image (2176 B, 128 K): [q0: (r,t) at 16(4r+t)][q1: at 1024 + 16(4r+t)][d: row r at
+// 2048 + 8r]; word wi of piece (r,t) (q0: wi < 4, q1: wi - 4) = codes 16(wi & 1) + 4t..+3 of
+// block wi / 2.  Items (row r, piece t) x 2 per thread; chunk h = blocks 2h, 2h + 1.
+template <>
+struct TcDq<TcQ80> {
+    int cw[2], dwo[2], ao[2][4];
+    uint32_t dbits = 0;  // OR of the scales' f16 bits: bit 14 = a |d| >= 2 (127 d 2^8 past f16)
+    __device__ __forceinline__ void init(int dt) {
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+            const int item = dt + 256 * it, r = item >> 2, t = item & 3, rt = r >> 4, rr = r & 15;
+            cw[it] = rt * (TcQ80::kGps * TcQ80::kImg / 4) + (rr * 4 + t) * 4;
+            dwo[it] = rt * (TcQ80::kGps * TcQ80::kImg / 4) + 512 + 2 * rr;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) ao[it][q] = tc_canon(r, 32 * (q >> 1) + 16 * (q & 1) + 4 * t);
+        }
+    }
+    __device__ __forceinline__ void chunk(const uint32_t* ws, int h, uint8_t* ahi, uint8_t* alo) {
+        uint4 c[2];
+        uint32_t dw[2];
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+            c[it] = *reinterpret_cast<const uint4*>(ws + cw[it] + h * 256);
+            dw[it] = ws[dwo[it] + h];  // f16 d of blocks 2h (low) and 2h + 1 (high)
+        }
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+            dbits |= dw[it];
+            const __half2 dd = __hmul2(u32_as_h2(dw[it]), __float2half2_rn(kTcWScale));
+            const __half2 d0 = __low2half2(dd), d1 = __high2half2(dd);
+            const uint32_t words[4] = {c[it].x, c[it].y, c[it].z, c[it].w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {  // k = 32 (q >> 1) + 16 (q & 1) + 4 t
+                uint2 hi, lo;
+                tc_dequant4(words[q], q < 2 ? d0 : d1, hi, lo);
+                *reinterpret_cast<uint2*>(ahi + ao[it][q]) = hi;
+                *reinterpret_cast<uint2*>(alo + ao[it][q]) = lo;
+            }
+        }
+    }
+    __device__ __forceinline__ bool bad() const { return (dbits & 0x40004000u) != 0; }
+};
+
+// Q4_K image (2304 B, 256 K): [hdr: row r at 16r = d, dmin, 12 scale bytes][q0: (r,t) at
+// 256 + 16(4r+t) = qs bytes 32t..32t+15][q1: at 1280 + 16(4r+t) = qs bytes 32t+16..32t+31].
+// qs byte 32c + l holds element 64c + l (low nibble, sub-block 2c) and 64c + 32 + l (high
+// nibble, sub-block 2c + 1), so chunk c is piece t = c of every row.  Item = (row r, piece p):
+// chunk elements 16p + 0..15 (low nibbles) and 32 + 16p + 0..15 (high nibbles).
+template <>
+struct TcDq<TcQ4K> {
+    int hw, qw, ao[4];
+    float big = 0.f;  // max over sub-blocks of 2^8 (|d1| 15 + |m1|): w' must stay below 65504
+    __device__ __forceinline__ void init(int dt) {
+        const int r = dt >> 1, p = dt & 1, rt = r >> 4, rr = r & 15;
+        const int base = rt * (TcQ4K::kGps * TcQ4K::kImg / 4);
+        hw = base + 4 * rr;
+        qw = base + 64 + 16 * rr + 256 * p;
+        ao[0] = tc_canon(r, 16 * p);
+        ao[1] = tc_canon(r, 16 * p + 8);
+        ao[2] = tc_canon(r, 32 + 16 * p);
+        ao[3] = tc_canon(r, 40 + 16 * p);
+    }
+    __device__ __forceinline__ void chunk(const uint32_t* ws, int c, uint8_t* ahi, uint8_t* alo) {
+        const uint4 hd = *reinterpret_cast<const uint4*>(ws + hw);
+        const uint4 q = *reinterpret_cast<const uint4*>(ws + qw + 4 * c);
+        // get_scale_min_k4 of sub-blocks 2c (byte 0) and 2c + 1 (byte 1)
+        const int sh = 16 * (c & 1);
+        const uint32_t Y = hd.y >> sh, Z = hd.z >> sh, W = hd.w >> sh;
+        const uint32_t psc = c < 2 ? (Y & 0x3F3Fu) : ((W & 0x0F0Fu) | ((Y >> 2) & 0x3030u));
+        const uint32_t pm = c < 2 ? (Z & 0x3F3Fu) : (((W >> 4) & 0x0F0Fu) | ((Z >> 2) & 0x3030u));
+        const float2 dd = __half22float2(u32_as_h2(hd.x));
+        float d1[2], m1[2];
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+            d1[s] = (dd.x * u8_to_f32(psc, s)) * kTcWScale;  // d1 = d sc, m1v = dmin m (exact)
+            m1[s] = (dd.y * u8_to_f32(pm, s)) * kTcWScale;
+            big = fmaxf(big, fmaf(fabsf(d1[s]), 15.f, fabsf(m1[s])));
+        }
+        const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {  // s = 0: low nibbles (k 16p + 4wi + b), 1: high (+32)
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+                const uint32_t n = (s ? words[wi] >> 4 : words[wi]) & 0x0F0F0F0Fu;
+                float v[4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) v[b] = fmaf(u8_to_f32(n, b), d1[s], -m1[s]);
+                tc_split2(v[0], v[1], hi[wi & 1 ? 2 : 0], lo[wi & 1 ? 2 : 0]);
+                tc_split2(v[2], v[3], hi[wi & 1 ? 3 : 1], lo[wi & 1 ? 3 : 1]);
+                if (wi & 1) {
+                    const int o = ao[2 * s + (wi >> 1)];
+                    *reinterpret_cast<uint4*>(ahi + o) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    *reinterpret_cast<uint4*>(alo + o) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                }
+            }
+        }
+    }
+    __device__ __forceinline__ bool bad() const { return !(big < 65504.f); }
+};
+
+// Q6_K image (3360 B, 256 K): [l0: (r,t) at 16(4r+t)][l1: at 1024 + 16(4r+t)][qh: at
+// 2048 + 16(4r+t)][sc: row r at 3072 + 16r][d: row r at 3328 + 2r].  Word j = 2qq + lh of
+// piece (r,t) in l_h holds ql bytes 64h + 32qq + 16lh + 4t..+3; qh word 2h + lh holds qh bytes
+// 32h + 16lh + 4t..+3.  Chunk c = 2h + nib of the super-block: elements 32qq + l (l = 16lh +
+// 4t + i) with code nibble_nib(ql[l + 32qq]) | ((qh[l] >> (2qq + 4nib)) & 3) << 4, minus 32,
+// and scale sc[8h + 4nib + 2qq + lh] (q6k.rs:35-55).  Items (row r, piece t) x 2 per thread.
+template <>
+struct TcDq<TcQ6K> {
+    int lw[2], hw[2], sw[2], dw[2], dsh[2], ao[2][4];
+    float big = 0.f;  // max 2^8 |d sc| (|q| <= 32): w' must stay below 65504
+    __device__ __forceinline__ void init(int dt) {
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+            const int item = dt + 256 * it, r = item >> 2, t = item & 3, rt = r >> 4, rr = r & 15;
+            const int base = rt * (TcQ6K::kGps * TcQ6K::kImg / 4);
+            lw[it] = base + 4 * (4 * rr + t);
+            hw[it] = base + 512 + 4 * (4 * rr + t);
+            sw[it] = base + 768 + 4 * rr;
+            dw[it] = base + 832 + (rr >> 1);
+            dsh[it] = 16 * (rr & 1);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ao[it][j] = tc_canon(r, 32 * (j >> 1) + 16 * (j & 1) + 4 * t);
+        }
+    }
+    __device__ __forceinline__ void chunk(const uint32_t* ws, int c, uint8_t* ahi, uint8_t* alo) {
+        const int h = c >> 1, nib = c & 1;
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+            const uint4 l = *reinterpret_cast<const uint4*>(ws + lw[it] + 256 * h);
+            const uint2 qh = *reinterpret_cast<const uint2*>(ws + hw[it] + 2 * h);
+            const uint32_t scw = ws[sw[it] + c] ^ 0x80808080u;  // scales 8h + 4nib + 0..3
+            const float d = h2f((uint16_t)(ws[dw[it]] >> dsh[it]));
+            const uint32_t lws[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {  // j = 2qq + lh
+                const int qq = j >> 1, lh = j & 1;
+                const float ds = (d * s8_to_f32_flipped(scw, j)) * kTcWScale;  // (d sc) 2^8, exact
+                big = fmaxf(big, fabsf(ds) * 32.f);
+                const uint32_t lo4 = (nib ? lws[j] >> 4 : lws[j]) & 0x0F0F0F0Fu;
+                const uint32_t hb = lh ? qh.y : qh.x;
+                const int hs = 2 * qq + 4 * nib;  // the 2 qh bits move to bits 4-5 of each byte
+                const uint32_t up = (hs <= 4 ? hb << (4 - hs) : hb >> (hs - 4)) & 0x30303030u;
+                const uint32_t code = lo4 | up;
+                float v[4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    uint32_t u;  // code byte b as f32 (2^23 + code) by PRMT, minus 2^23 + 32
+                    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(u) : "r"(code), "r"(0x4B000000u), "r"(0x7440u | b));
+                    v[b] = (__uint_as_float(u) - 8388640.0f) * ds;
+                }
+                uint2 hi, lo;
+                tc_split2(v[0], v[1], hi.x, lo.x);
+                tc_split2(v[2], v[3], hi.y, lo.y);
+                *reinterpret_cast<uint2*>(ahi + ao[it][j]) = hi;
+                *reinterpret_cast<uint2*>(alo + ao[it][j]) = lo;
+            }
+        }
+    }
+    __device__ __forceinline__ bool bad() const { return !(big < 65504.f); }
+};
+
+template <class F>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
+    constexpr int CPI = F::kImgK / kTcChunk;  // chunks per image (= per unit)
+    constexpr int WST = tc_wstage<F>();
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ uint32_t s_tmem;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // barriers: w_full, w_empty [SW], x_full, x_empty [NX], a_full, a_empty [NA], done
-    // 1024-byte aligned base for the swizzled operand buffers (the launch adds 1 KB of slack)
+    const int G = gridDim.x, c = blockIdx.x;
+    const long long u0 = (long long)c * a.U / G, u1 = (long long)(c + 1) * a.U / G;
+    if (u0 >= u1) return;  // (no TMEM, no barriers used yet)
+    const int nu = (int)(u1 - u0), nj = nu * CPI;
+    // barriers: w_full, w_empty [SW], x_full, x_empty [NX], a_full, a_empty [NA],
+    // acc_full, acc_empty [2]; 1024-byte aligned base for the swizzled operand buffers (the
+    // launch adds 1 KB of slack)
     const uint32_t raw = smem_addr(smem), bars = (raw + 1023) & ~1023u;
     uint8_t* base = smem + (bars - raw);
     const uint32_t w_full = bars, w_empty = w_full + 8 * kTcMaxRing, x_full = w_empty + 8 * kTcMaxRing,
                    x_empty = x_full + 8 * kTcMaxRing, a_full = x_empty + 8 * kTcMaxRing,
-                   a_empty = a_full + 8 * kTcMaxRing, done = a_empty + 8 * kTcMaxRing;
+                   a_empty = a_full + 8 * kTcMaxRing, acc_full = a_empty + 8 * kTcMaxRing, acc_empty = acc_full + 16;
     uint8_t* wring = base + 1024;
-    uint8_t* xring = wring + a.SW * kTcWStage;
+    uint8_t* xring = wring + ((a.SW * WST + 1023) & ~1023);
     const int xbytes = a.N * kTcChunk * 2;
     uint8_t* aring = xring + ((a.NX * xbytes + 1023) & ~1023);
-    const uint8_t* W = a.w[blockIdx.z];
-    const int m0 = blockIdx.x * kTcRows, t0 = m0 / 16;
-    const int nchunk = a.K / kTcChunk;
-    const int c0 = blockIdx.y * a.cps, c1 = min(c0 + a.cps, nchunk), nj = c1 - c0;  // c0 even
-    // two accumulators (the A_hi and the A_lo products: independent MMA chains), N columns each
-    const uint32_t ncols = 2 * a.N <= 32 ? 32u : 2 * a.N <= 64 ? 64u : 2 * a.N <= 128 ? 128u : 2 * a.N <= 256 ? 256u : 512u;
+    // accumulator set s: A_hi products at columns s 2N + [0, N), A_lo products at + N
+    const uint32_t need = (uint32_t)(a.nsets * 2 * a.N);
+    const uint32_t ncols = need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : need <= 256 ? 256u : 512u;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < a.SW; ++i) {
@@ -145,10 +361,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
             mbar_init(a_full + 8 * i, 8);
             mbar_init(a_empty + 8 * i, 1);
         }
-        mbar_init(done, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(acc_full + 8 * i, 1);   // tcgen05.commit at a segment's end
+            mbar_init(acc_empty + 8 * i, 4);  // the 4 epilogue warps
+        }
         mbar_fence_init();
     }
-    if (warp == 1) {  // TMEM columns for the accumulator (warp-wide)
+    if (warp == 1) {  // TMEM columns for the accumulators (warp-wide)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
                      "r"(ncols)
                      : "memory");
@@ -161,37 +380,36 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
     bool bad = false, timeout = false;
 
     if (warp == 0) {
-        // ---- producers: lane 0 streams the weight groups, lane 1 the activation chunks, each
-        // as far ahead as its own ring allows (one thread for both let a full activation ring
-        // hold back the weight stream to two groups in flight)
+        // ---- producers: lane 0 streams the weight units, lane 1 the activation chunks, each
+        // as far ahead as its own ring allows
         if (lane == 0) {
-            // a stage: kTcGps consecutive groups of each of the 8 row tiles, one contiguous
-            // copy per tile (the groups of a tile are adjacent in the tile-major layout)
-            const int ng = nj / 2, ns = (ng + kTcGps - 1) / kTcGps;
-            for (int i = 0; i < ns; ++i) {
-                const int sw = i % a.SW, g = (c0 >> 1) + kTcGps * i, n = min(kTcGps, ng - kTcGps * i);
+            for (int i = 0; i < nu; ++i) {
+                const long long u = u0 + i;
+                const int run = (int)(u / a.nimg), img = (int)(u % a.nimg), rb = run / a.mats, z = run % a.mats;
+                const int sw = i % a.SW;
                 if (i >= a.SW && !mbar_wait(w_empty + 8 * sw, ((i / a.SW) - 1) & 1)) {
                     timeout = true;
                     break;
                 }
-                mbar_arrive_expect_tx(w_full + 8 * sw, (uint32_t)(8 * n * kTcImg));
+                mbar_arrive_expect_tx(w_full + 8 * sw, (uint32_t)(8 * F::kImg));
+                const uint8_t* W = a.w[z] + (size_t)rb * 8 * a.tstride + (size_t)img * F::kImg;
                 for (int rt = 0; rt < 8; ++rt)
-                    bulk_g2s(smem_addr(wring + sw * kTcWStage + rt * kTcGps * kTcImg),
-                             W + (size_t)(t0 + rt) * a.tstride + (size_t)g * kTcImg, (uint32_t)(n * kTcImg),
-                             w_full + 8 * sw);
+                    bulk_g2s(smem_addr(wring + sw * WST + rt * F::kImg), W + (size_t)rt * a.tstride,
+                             (uint32_t)F::kImg, w_full + 8 * sw);
             }
             // wait (bounded) until the last copies landed, so none writes after the CTA ends
-            for (int i = ns - a.SW < 0 ? 0 : ns - a.SW; i < ns && !timeout; ++i)
+            for (int i = nu - a.SW < 0 ? 0 : nu - a.SW; i < nu && !timeout; ++i)
                 if (!mbar_wait(w_full + 8 * (i % a.SW), (i / a.SW) & 1)) timeout = true;
         } else if (lane == 1) {
             for (int j = 0; j < nj; ++j) {
                 const int sx = j % a.NX;
+                const int kc = (int)((u0 + j / CPI) % a.nimg) * CPI + j % CPI;  // the chunk's K index
                 if (j >= a.NX && !mbar_wait(x_empty + 8 * sx, ((j / a.NX) - 1) & 1)) {
                     timeout = true;
                     break;
                 }
                 mbar_arrive_expect_tx(x_full + 8 * sx, (uint32_t)xbytes);
-                bulk_g2s(smem_addr(xring + sx * xbytes), a.xc + (size_t)(c0 + j) * xbytes, (uint32_t)xbytes,
+                bulk_g2s(smem_addr(xring + sx * xbytes), a.xc + (size_t)kc * xbytes, (uint32_t)xbytes,
                          x_full + 8 * sx);
             }
             for (int j = nj - a.NX < 0 ? 0 : nj - a.NX; j < nj && !timeout; ++j)
@@ -201,7 +419,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
         // ---- MMA issuer
         if (lane == 0) {
             const uint32_t idesc = (1u << 4) | ((uint32_t)(a.N >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+            int seg = -1;
+            uint32_t acc = 0;
             for (int j = 0; j < nj && !timeout; ++j) {
+                const long long u = u0 + j / CPI;
+                const int sub = j % CPI, img = (int)(u % a.nimg);
+                const bool first = sub == 0 && (img == 0 || u == u0);
+                const bool last = sub == CPI - 1 && (img == a.nimg - 1 || u == u1 - 1);
+                if (first) {
+                    ++seg;
+                    const int s = seg % a.nsets;
+                    acc = tmem + (uint32_t)(s * 2 * a.N);
+                    // the set's previous segment must have been read out
+                    if (seg >= a.nsets && !mbar_wait(acc_empty + 8 * s, ((seg / a.nsets) - 1) & 1)) {
+                        timeout = true;
+                        break;
+                    }
+                }
                 const int sa = j % a.NA, sx = j % a.NX;
                 if (!mbar_wait(a_full + 8 * sa, (j / a.NA) & 1) || !mbar_wait(x_full + 8 * sx, (j / a.NX) & 1)) {
                     timeout = true;
@@ -211,34 +445,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
                 const uint32_t ahi = smem_addr(aring + sa * 2 * kTcABytes), alo = ahi + kTcABytes;
                 const uint32_t xs = smem_addr(xring + sx * xbytes);
 #pragma unroll
-                for (int s = 0; s < kTcChunk / 16; ++s) {
-                    tc_mma(tmem, tc_desc(ahi + 32 * s), tc_desc(xs + 32 * s), idesc, (j | s) != 0);
-                    tc_mma(tmem + (uint32_t)a.N, tc_desc(alo + 32 * s), tc_desc(xs + 32 * s), idesc, (j | s) != 0);
+                for (int ks = 0; ks < kTcChunk / 16; ++ks) {
+                    const uint32_t on = (first && ks == 0) ? 0u : 1u;
+                    tc_mma(acc, tc_desc(ahi + 32 * ks), tc_desc(xs + 32 * ks), idesc, on);
+                    tc_mma(acc + (uint32_t)a.N, tc_desc(alo + 32 * ks), tc_desc(xs + 32 * ks), idesc, on);
                 }
                 tc_commit(a_empty + 8 * sa);
                 tc_commit(x_empty + 8 * sx);
+                if (last) tc_commit(acc_full + 8 * (seg % a.nsets));
             }
-            tc_commit(done);
         }
-    } else {
-        // ---- dequantisation: 256 threads, items (row r, piece t) x 2 per half-group; the
-        // shared-memory offsets of a thread's items are the same for every chunk
-        const int dt = threadIdx.x - 64;
-        int cw[2], dwo[2], ao[2][4];
-#pragma unroll
-        for (int it = 0; it < 2; ++it) {
-            const int item = dt + 256 * it, r = item >> 2, t = item & 3, rt = r >> 4, rr = r & 15;
-            cw[it] = rt * (kTcGps * kTcImg / 4) + (rr * 4 + t) * 4;  // code words (+ group image + 256 h)
-            dwo[it] = rt * (kTcGps * kTcImg / 4) + 512 + 2 * rr;      // d words (+ group image + h)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) ao[it][q] = tc_canon(r, 32 * (q >> 1) + 16 * (q & 1) + 4 * t);
-        }
-        uint32_t dbits = 0;  // OR of the scales' f16 bits: bit 14 = a |d| >= 2 (127 d 2^8 past f16)
+    } else if (warp < 10) {
+        // ---- dequantisation: 256 threads; a thread's shared-memory offsets are the same for
+        // every chunk
+        TcDq<F> dq;
+        dq.init(threadIdx.x - 64);
         for (int j = 0; j < nj && !timeout; ++j) {
-            const int gl = j >> 1, i = gl / kTcGps, h = j & 1, sw = i % a.SW, sa = j % a.NA;
-            const int gw = (gl % kTcGps) * (kTcImg / 4);  // the group's image inside each tile's run
-            const bool stage_first = (j % (2 * kTcGps)) == 0, stage_last = (j % (2 * kTcGps)) == 2 * kTcGps - 1;
-            if (stage_first && !mbar_wait(w_full + 8 * sw, (i / a.SW) & 1)) {
+            const int i = j / CPI, sub = j % CPI, sw = i % a.SW, sa = j % a.NA;
+            if (sub == 0 && !mbar_wait(w_full + 8 * sw, (i / a.SW) & 1)) {
                 timeout = true;
                 break;
             }
@@ -246,68 +470,51 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
                 timeout = true;
                 break;
             }
-            const uint32_t* ws = reinterpret_cast<const uint32_t*>(wring + sw * kTcWStage);
             uint8_t* ahi = aring + sa * 2 * kTcABytes;
-            uint8_t* alo = ahi + kTcABytes;
-            uint4 c[2];
-            uint32_t dw[2];
-#pragma unroll
-            for (int it = 0; it < 2; ++it) {
-                c[it] = *reinterpret_cast<const uint4*>(ws + cw[it] + gw + h * 256);
-                dw[it] = ws[dwo[it] + gw + h];  // f16 d of blocks 2h (low) and 2h + 1 (high)
-            }
-#pragma unroll
-            for (int it = 0; it < 2; ++it) {
-                dbits |= dw[it];
-                const __half2 dd = __hmul2(u32_as_h2(dw[it]), __float2half2_rn(kTcWScale));
-                const __half2 d0 = __low2half2(dd), d1 = __high2half2(dd);
-                const uint32_t words[4] = {c[it].x, c[it].y, c[it].z, c[it].w};
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {  // k = 32 (q >> 1) + 16 (q & 1) + 4 t
-                    uint2 hi, lo;
-                    tc_dequant4(words[q], q < 2 ? d0 : d1, hi, lo);
-                    *reinterpret_cast<uint2*>(ahi + ao[it][q]) = hi;
-                    *reinterpret_cast<uint2*>(alo + ao[it][q]) = lo;
-                }
-            }
+            dq.chunk(reinterpret_cast<const uint32_t*>(wring + sw * WST), sub, ahi, ahi + kTcABytes);
             // the MMA reads the operands through the async proxy
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(a_full + 8 * sa);
-                if (stage_last || j == nj - 1) mbar_arrive(w_empty + 8 * sw);
+                if (sub == CPI - 1) mbar_arrive(w_empty + 8 * sw);
             }
         }
-        if (dbits & 0x40004000u) bad = true;
-        // ---- epilogue: warps 2-5 read one TMEM lane quarter each
-        if (warp < 6 && !timeout) {
-            if (!mbar_wait(done, 0)) {
+        bad = dq.bad();
+    } else {
+        // ---- epilogue: warps 10-13 read TMEM lane quarters 2, 3, 0, 1 (warp % 4)
+        const int quarter = warp & 3, row = 32 * quarter + lane, Bp = a.N >> 1;
+        int seg = 0;
+        for (long long u = u0; u < u1 && !timeout; ++seg) {
+            const int run = (int)(u / a.nimg);
+            const long long ue = (long long)(run + 1) * a.nimg < u1 ? (long long)(run + 1) * a.nimg : u1;
+            const int s = seg % a.nsets;
+            if (!mbar_wait(acc_full + 8 * s, (seg / a.nsets) & 1)) {
                 timeout = true;
-            } else {
-                tc_fence_after();
-                const int quarter = warp & 3, row = m0 + 32 * quarter + lane;
-                const int Bp = a.N >> 1;
-                float* out = a.out + ((size_t)blockIdx.z * gridDim.y + blockIdx.y) * (size_t)a.B * a.M;
-                for (int cb = 0; cb < Bp; cb += 8) {
-                    float vh[8], vl[8], wh[8], wl[8];
-                    const uint32_t base = tmem + ((uint32_t)(32 * quarter) << 16);
-                    tc_ld8(base + cb, vh);
-                    tc_ld8(base + Bp + cb, vl);
-                    tc_ld8(base + a.N + cb, wh);  // the A_lo products
-                    tc_ld8(base + a.N + Bp + cb, wl);
+                break;
+            }
+            tc_fence_after();
+            const int slot = c - tc_owner((long long)run * a.nimg, a.U, G);
+            float* out = a.out + ((size_t)run * a.slots + slot) * (size_t)a.B * kTcRows;
+            const uint32_t tb = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(s * 2 * a.N);
+            for (int cb = 0; cb < Bp; cb += 8) {
+                float vh[8], vl[8], wh[8], wl[8];
+                tc_ld8(tb + cb, vh);
+                tc_ld8(tb + Bp + cb, vl);
+                tc_ld8(tb + a.N + cb, wh);  // the A_lo products
+                tc_ld8(tb + a.N + Bp + cb, wl);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        vh[e] += wh[e];
-                        vl[e] += wl[e];
-                    }
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int t = cb + e;
-                        if (t < a.B && row < a.M)
-                            out[(size_t)t * a.M + row] = (vh[e] + vl[e] * (1.0f / 2048.0f)) * (1.0f / kTcWScale);
-                    }
+                for (int e = 0; e < 8; ++e) {
+                    const int t = cb + e;
+                    if (t < a.B)
+                        out[(size_t)t * kTcRows + row] =
+                            ((vh[e] + wh[e]) + (vl[e] + wl[e]) * (1.0f / 2048.0f)) * (1.0f / kTcWScale);
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + 8 * s);
+            u = ue;
         }
     }
     if (bad && a.err) atomicOr(a.err, 1);
@@ -382,42 +589,43 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float* __restrict__ 
     if (bad && err) atomicOr(err, 1);
 }
 
-// Outputs, 4 per thread: y[t][m] = [resid[t][m] +] sum over splits (in order) of the partials
-// of matrix 0; with `gu`, h[t][m] = silu(sum g) * (sum u) over matrices 0 and 1.  M is a
-// multiple of 128.
-__global__ void tc_finish_kernel(const float* __restrict__ part, int splits, int B, int M, float* y, int ldy,
-                                 const float* resid, int ldr, bool gu) {
+// Outputs, 4 per thread: y[t][m] = [resid[t][m] +] the sum over a row block's partial slots
+// (CTA order) of matrix 0; with `gu`, h[t][m] = silu(sum g) * (sum u) over matrices 0 and 1.
+// M is a multiple of 128; the slots of (row block, matrix) run r are those of the CTAs that
+// own its first through last unit.
+__global__ void tc_finish_kernel(const float* __restrict__ part, long long U, int G, int nimg, int slots, int B, int M,
+                                 float* y, int ldy, const float* resid, int ldr, bool gu) {
     const int m4 = M >> 2;
     const int n4 = B * m4;
-    const size_t n = (size_t)B * M;
+    const int mats = gu ? 2 : 1;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
-        const int t = i / m4, m = (i - t * m4) * 4;
-        float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
-        for (int s = 0; s < splits; ++s) {
-            const float4 p = reinterpret_cast<const float4*>(part + (size_t)s * n)[i];
-            s0.x += p.x;
-            s0.y += p.y;
-            s0.z += p.z;
-            s0.w += p.w;
+        const int t = i / m4, m = (i - t * m4) * 4, rb = m / kTcRows, row = m % kTcRows;
+        float4 sum[2];
+        for (int z = 0; z < mats; ++z) {
+            const int run = rb * mats + z;
+            const int cf = tc_owner((long long)run * nimg, U, G), cl = tc_owner((long long)(run + 1) * nimg - 1, U, G);
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int j = 0; j <= cl - cf; ++j) {
+                const float4 p =
+                    *reinterpret_cast<const float4*>(part + (((size_t)run * slots + j) * B + t) * kTcRows + row);
+                acc.x += p.x;
+                acc.y += p.y;
+                acc.z += p.z;
+                acc.w += p.w;
+            }
+            sum[z] = acc;
         }
         float o[4];
         if (gu) {
-            for (int s = 0; s < splits; ++s) {
-                const float4 p = reinterpret_cast<const float4*>(part + ((size_t)splits + s) * n)[i];
-                s1.x += p.x;
-                s1.y += p.y;
-                s1.z += p.z;
-                s1.w += p.w;
-            }
-            o[0] = silu_mul(s0.x, s1.x);
-            o[1] = silu_mul(s0.y, s1.y);
-            o[2] = silu_mul(s0.z, s1.z);
-            o[3] = silu_mul(s0.w, s1.w);
+            o[0] = silu_mul(sum[0].x, sum[1].x);
+            o[1] = silu_mul(sum[0].y, sum[1].y);
+            o[2] = silu_mul(sum[0].z, sum[1].z);
+            o[3] = silu_mul(sum[0].w, sum[1].w);
         } else {
-            o[0] = s0.x;
-            o[1] = s0.y;
-            o[2] = s0.z;
-            o[3] = s0.w;
+            o[0] = sum[0].x;
+            o[1] = sum[0].y;
+            o[2] = sum[0].z;
+            o[3] = sum[0].w;
             if (resid) {  // may alias y: read, then written, here
 #pragma unroll
                 for (int j = 0; j < 4; ++j) o[j] = resid[(size_t)t * ldr + m + j] + o[j];
@@ -430,46 +638,85 @@ __global__ void tc_finish_kernel(const float* __restrict__ part, int splits, int
 
 // ------------------------------------------------------------------ host side
 static int tc_bp(int B) { return (B + 7) / 8 * 8; }
+static int tc_cpi(int type) { return type == T_Q8_0 ? TcQ80::kImgK / kTcChunk : TcQ4K::kImgK / kTcChunk; }
 
+// From 8 rows for Q4_K / Q6_K and 9 for Q8_0: below that the mma.sync GEMV (one weight pass per
+// 4 rows, cheaper per pass for Q8_0) is as fast or faster (measured on the Llama-3-8B FFN shapes).
 bool tc_gemm_supported(int type, int M, int K, int nvec) {
-    return type == T_Q8_0 && nvec >= 8 && nvec <= 128 && M % kTcRows == 0 && K % 128 == 0 && M > 0 && K > 0;
+    if (type != T_Q8_0 && type != T_Q4_K && type != T_Q6_K) return false;
+    const int min_rows = type == T_Q8_0 ? 9 : 8;
+    return nvec >= min_rows && nvec <= 128 && M > 0 && K > 0 && M % kTcRows == 0 &&
+           K % (kTcChunk * tc_cpi(type)) == 0;
 }
 
-// K splits: the count whose CTAs fill their last wave best (ties -> fewer splits), at least 4
-// groups of 128 K per split.
-static int tc_splits(int M, int K, int num_sms, int mats) {
-    const int blocks = M / kTcRows * mats, groups = K / 128;
-    int best = 1;
-    double best_eff = 0.0;
-    for (int s = 1; s <= 16 && groups / s >= 4; ++s) {
-        const int cps = ((2 * groups + s - 1) / s + 1) & ~1;  // chunks per split, even
-        const int real = (2 * groups + cps - 1) / cps;           // splits after rounding
-        if (real != s) continue;
-        const double waves = (double)blocks * s / num_sms;
-        const double eff = waves / std::ceil(waves);
-        if (eff > best_eff + 0.02) {
-            best_eff = eff;
-            best = s;
-        }
+// The stream-K partition of an M x K launch over min(num_sms, U) CTAs.
+struct TcPlan {
+    int nimg, mats, G, slots;
+    long long U;
+};
+
+static TcPlan tc_plan(int type, int M, int K, int num_sms, int mats) {
+    TcPlan p{};
+    p.nimg = K / (kTcChunk * tc_cpi(type));
+    p.mats = mats;
+    p.U = (long long)(M / kTcRows) * mats * p.nimg;
+    p.G = (int)(p.U < num_sms ? p.U : num_sms);
+    p.slots = 1;
+    for (long long r = 0; r < p.U / p.nimg; ++r) {
+        const int n = tc_owner((r + 1) * p.nimg - 1, p.U, p.G) - tc_owner(r * p.nimg, p.U, p.G) + 1;
+        p.slots = n > p.slots ? n : p.slots;
     }
-    return best;
+    return p;
 }
 
-size_t tc_workspace_bytes(int M, int K, int nvec, int num_sms, int mats) {
+size_t tc_workspace_bytes(int type, int M, int K, int nvec, int num_sms, int mats) {
+    const TcPlan p = tc_plan(type, M, K, num_sms, mats);
     const size_t N = 2 * (size_t)tc_bp(nvec);
-    const size_t xc = (size_t)K * N * 2, part = (size_t)mats * tc_splits(M, K, num_sms, mats) * nvec * M * 4;
+    const size_t xc = (size_t)K * N * 2;
+    const size_t part = (size_t)(M / kTcRows) * mats * p.slots * nvec * kTcRows * 4;
     return (xc + 255) / 256 * 256 + part;
 }
 
+// Ring depths that fit, operand buffers first, and the kernel's dynamic shared memory.
+template <class F>
+static cudaError_t tc_launch_kernel(TcArgs a, int G, int smem_limit, cudaStream_t stream) {
+    constexpr int WST = tc_wstage<F>();
+    const int xbytes = a.N * kTcChunk * 2;
+    // The operand buffers take the shared memory first (each makes a round trip dequant ->
+    // MMA -> commit -> dequant); the weight ring keeps about 64 KB in flight.
+    a.NA = 4;
+    a.SW = 70000 / WST > 2 ? (70000 / WST < kTcMaxRing ? 70000 / WST : kTcMaxRing) : 2;
+    a.NX = 4;
+    auto smem_of = [&](const TcArgs& t) {
+        return 1024 + ((t.SW * WST + 1023) & ~1023) + ((t.NX * xbytes + 1023) & ~1023) + t.NA * 2 * kTcABytes;
+    };
+    while (smem_of(a) > smem_limit - 2048 && a.NX > 2) --a.NX;
+    while (smem_of(a) > smem_limit - 2048 && a.NA > 2) --a.NA;
+    while (smem_of(a) > smem_limit - 2048 && a.SW > 2) --a.SW;
+    if (smem_of(a) > smem_limit - 2048) return cudaErrorInvalidConfiguration;
+    const int smem = smem_of(a) + 1024;  // slack for the 1024-byte alignment of the buffers
+    static int configured[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || configured[dev] < smem) {
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) configured[dev] = smem;
+    }
+    tc_gemm_kernel<F><<<G, kTcThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
 // y = W x (+ resid) for nvec rows of x (gate/up: w2 != nullptr, y = h = silu(G x) * (U x) with
-// x optionally RMS-normalised).  ws: tc_workspace_bytes(M, K, nvec, num_sms, 1 or 2) bytes.
-cudaError_t launch_tc_gemm(const uint8_t* w, const uint8_t* w2, long long tstride, int M, int K, const float* x,
-                           int ldx, int nvec, float* y, int ldy, const float* resid, int ldr, const float* norm_w,
-                           int norm_len, float eps, void* ws, int* err, int num_sms, int smem_limit,
-                           cudaStream_t stream) {
+// x optionally RMS-normalised).  ws: tc_workspace_bytes(type, M, K, nvec, num_sms, 1 or 2) bytes.
+cudaError_t launch_tc_gemm(int type, const uint8_t* w, const uint8_t* w2, long long tstride, int M, int K,
+                           const float* x, int ldx, int nvec, float* y, int ldy, const float* resid, int ldr,
+                           const float* norm_w, int norm_len, float eps, void* ws, int* err, int num_sms,
+                           int smem_limit, cudaStream_t stream) {
+    if (!tc_gemm_supported(type, M, K, nvec)) return cudaErrorInvalidValue;
     const int mats = w2 ? 2 : 1;
     const int Bp = tc_bp(nvec), N = 2 * Bp;
-    const int splits = tc_splits(M, K, num_sms, mats);
+    const TcPlan p = tc_plan(type, M, K, num_sms, mats);
     uint8_t* xc = static_cast<uint8_t*>(ws);
     float* part = reinterpret_cast<float*>(xc + ((size_t)K * N * 2 + 255) / 256 * 256);
     tc_prep_kernel<<<dim3(Bp, (K + 1023) / 1024), 256, 0, stream>>>(x, ldx, nvec, Bp, K, norm_w, norm_len, eps, xc,
@@ -485,40 +732,23 @@ cudaError_t launch_tc_gemm(const uint8_t* w, const uint8_t* w2, long long tstrid
     a.xc = xc;
     a.N = N;
     a.B = nvec;
-    const int nchunk = K / kTcChunk;
-    a.cps = ((nchunk + splits - 1) / splits + 1) & ~1;
+    a.mats = mats;
+    a.nimg = p.nimg;
+    a.U = p.U;
+    a.slots = p.slots;
+    a.nsets = 4 * N <= 512 ? 2 : 1;
     a.out = part;
     a.err = err;
-    // rings: what fits, operand buffers first
-    const int xbytes = N * kTcChunk * 2;
-    // The operand buffers bound the throughput: each makes a round trip dequant -> MMA ->
-    // commit -> dequant of about 2 us, so they get the shared memory first.
-    a.NA = 4;
-    a.SW = 2;
-    a.NX = 4;
-    auto smem_of = [&](const TcArgs& t) {
-        return 1024 + t.SW * kTcWStage + ((t.NX * xbytes + 1023) & ~1023) + t.NA * 2 * kTcABytes;
-    };
-    while (smem_of(a) > smem_limit - 2048 && a.NX > 2) --a.NX;
-    while (smem_of(a) > smem_limit - 2048 && a.NA > 2) --a.NA;
-    while (smem_of(a) > smem_limit - 2048 && a.SW > 1) --a.SW;
-    if (smem_of(a) > smem_limit - 2048) return cudaErrorInvalidConfiguration;
-    const int smem = smem_of(a) + 1024;  // slack for the 1024-byte alignment of the buffers
-    static int configured[64];
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 64 || configured[dev] < smem) {
-        e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        if (dev < 64) configured[dev] = smem;
+    switch (type) {
+        case T_Q8_0: e = tc_launch_kernel<TcQ80>(a, p.G, smem_limit, stream); break;
+        case T_Q4_K: e = tc_launch_kernel<TcQ4K>(a, p.G, smem_limit, stream); break;
+        default: e = tc_launch_kernel<TcQ6K>(a, p.G, smem_limit, stream); break;
     }
-    const dim3 grid(M / kTcRows, (nchunk + a.cps - 1) / a.cps, mats);
-    tc_gemm_kernel<<<grid, kTcThreads, smem, stream>>>(a);
-    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const size_t n = (size_t)nvec * M / 4;
     const unsigned blocks = (unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
-    tc_finish_kernel<<<blocks, 256, 0, stream>>>(part, (int)grid.y, nvec, M, y, ldy, resid, ldr, mats == 2);
+    tc_finish_kernel<<<blocks, 256, 0, stream>>>(part, p.U, p.G, p.nimg, p.slots, nvec, M, y, ldy, resid, ldr,
+                                                 mats == 2);
     return cudaGetLastError();
 }
 

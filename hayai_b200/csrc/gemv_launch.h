@@ -27,6 +27,17 @@ constexpr size_t kPeerTpParts = 4096;             // TP stack: down partials [2]
 constexpr size_t kPeerTpPartsBytes = 4u << 20;    // d_model x parts (<= 8) x 2 buffers x 4 B up to 65536 x 8
 constexpr size_t kPeerEpData = kPeerTpParts + kPeerTpPartsBytes;  // EP MoE exchange data
 constexpr size_t kPeerRegionMin = kPeerEpData + (4u << 20);
+constexpr size_t kPeerTpbBar = 384;             // u32: cross-GPU counter of the batched TP exchange
+constexpr size_t kPeerTpbEpoch = 512;           // u32: batched TP exchanges this rank has completed (local)
+constexpr size_t kPeerTpbDone = 640;            // u32: CTAs of the running exchange that finished (local)
+constexpr size_t kPeerTpbData = kPeerRegionMin; // batched TP: down partials [2][ranks][rows x d_model] f32
+
+// The all-reduce of a tensor-parallel FFN layer at any batch (tp_reduce.cu): x[n] += the sum
+// over ranks (in rank order) of every rank's yp[n], through the exchange regions.  Every rank
+// calls it with the same n; the region must hold tp_exchange_bytes(world, n).
+size_t tp_exchange_bytes(int world, size_t n);
+cudaError_t launch_tp_allreduce(const float* yp, float* x, size_t n, void* const* regions, int rank, int world,
+                                int* err, cudaStream_t stream);
 
 struct StackLaunch {
     const void* layers;  // device array, per layer {gate, up, down, norm weight} pointers
@@ -47,15 +58,16 @@ struct StackLaunch {
 cudaError_t launch_ffn_stack(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
                              cudaStream_t stream, bool dry, size_t* scratch_bytes);
 
-// Batched Q8_0 GEMV on the tcgen05 tensor cores (gemm_tc.cu), for 8..128 rows of x, M a
-// multiple of 128 and K of 128.  w2 != nullptr: fused gate/up, y = silu(G x') * (U x') with
-// x' = rms_norm(x) when norm_w is given.  ws: tc_workspace_bytes(...) bytes of scratch.
+// Batched GEMV on the tcgen05 tensor cores (gemm_tc.cu) for Q8_0, Q4_K and Q6_K, 8..128 rows of
+// x, M a multiple of 128 and K of the format's tile-block image (128 or 256).  w2 != nullptr:
+// fused gate/up, y = silu(G x') * (U x') with x' = rms_norm(x) when norm_w is given.
+// ws: tc_workspace_bytes(...) bytes of scratch.
 bool tc_gemm_supported(int type, int M, int K, int nvec);
-size_t tc_workspace_bytes(int M, int K, int nvec, int num_sms, int mats);
-cudaError_t launch_tc_gemm(const uint8_t* w, const uint8_t* w2, long long tstride, int M, int K, const float* x,
-                           int ldx, int nvec, float* y, int ldy, const float* resid, int ldr, const float* norm_w,
-                           int norm_len, float eps, void* ws, int* err, int num_sms, int smem_limit,
-                           cudaStream_t stream);
+size_t tc_workspace_bytes(int type, int M, int K, int nvec, int num_sms, int mats);
+cudaError_t launch_tc_gemm(int type, const uint8_t* w, const uint8_t* w2, long long tstride, int M, int K,
+                           const float* x, int ldx, int nvec, float* y, int ldy, const float* resid, int ldr,
+                           const float* norm_w, int norm_len, float eps, void* ws, int* err, int num_sms,
+                           int smem_limit, cudaStream_t stream);
 
 // CUDA-core GEMV on the raw GGUF layout for F32 and the IQ2/IQ3 codebook formats.
 cudaError_t launch_gemv_simple(int type, const uint8_t* w, size_t row_bytes, int M, int K, const float* x,

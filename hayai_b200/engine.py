@@ -314,7 +314,7 @@ class CudaEngine:
                                       eps, len(gates), ctypes.c_void_p(_tptr(x)), nvec))
 
     # ---------------------------------------------------------------- tensor parallelism
-    def peer_open(self, rank: int, world: int, nbytes: int = 16 << 20) -> bytes:
+    def peer_open(self, rank: int, world: int, nbytes: int = 64 << 20) -> bytes:
         """Allocate this rank's exchange region; returns its IPC handle (to be gathered)."""
         n = ctypes.c_size_t()
         _check(lib().hc_peer_handle_bytes(ctypes.byref(n)))
@@ -331,17 +331,17 @@ class CudaEngine:
     def peer_close(self) -> None:
         _check(lib().hc_peer_close(self.handle))
 
-    def ffn_stack_tp_dev(self, gates, ups, downs, x, norms=None, eps: float = 1e-5) -> None:
-        """Tensor-parallel batch-1 stack over this rank's d_ff shard; x replicated, in place."""
+    def ffn_stack_tp_dev(self, gates, ups, downs, x, nvec: int = 1, norms=None, eps: float = 1e-5) -> None:
+        """Tensor-parallel stack over this rank's d_ff shard; x [nvec][d_model] replicated, in place."""
         _check(lib().hc_ffn_stack_tp_dev(self.handle, _handles(gates), _handles(ups), _handles(downs),
-                                         _norm_ptrs(norms), eps, len(gates), ctypes.c_void_p(_tptr(x))))
+                                         _norm_ptrs(norms), eps, len(gates), ctypes.c_void_p(_tptr(x)), nvec))
 
-    def ffn_stack_tp(self, gates, ups, downs, x, norms=None, eps: float = 1e-5) -> np.ndarray:
+    def ffn_stack_tp(self, gates, ups, downs, x, nvec: int = 1, norms=None, eps: float = 1e-5) -> np.ndarray:
         """Host-buffer version of ffn_stack_tp_dev (x copied in, the result copied out)."""
         xv = _f32(x)
         out = np.empty_like(xv)
         _check(lib().hc_ffn_stack_tp(self.handle, _handles(gates), _handles(ups), _handles(downs), _norm_ptrs(norms),
-                                     eps, len(gates), xv.ctypes.data, out.ctypes.data))
+                                     eps, len(gates), xv.ctypes.data, out.ctypes.data, nvec))
         return out
 
     def synth_normal_dev(self, seed: int, out, mean: float = 0.0, std: float = 1.0) -> None:

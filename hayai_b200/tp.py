@@ -4,8 +4,9 @@ Sharding (the d_ff split of the Llama-3-70B configuration): rank p of P holds ga
 [p*F/P, (p+1)*F/P) and the same range of down columns, cut at whole quantization blocks, so
 h never leaves its GPU.  The down projection then yields a partial sum on every rank; the
 persistent stack kernel pushes each layer's partials into every rank's exchange region over
-NVLink and adds them in rank order (hc_ffn_stack_tp_dev), so the replicated residual stream
-stays identical on all ranks.  Expert parallelism (the MoE layer) gives rank p the experts
+NVLink and adds them in rank order (hc_ffn_stack_tp_dev, batch 1; at batch > 1 one all-reduce
+kernel after each layer's down GEMV does the same), so the replicated residual stream stays
+identical on all ranks.  Expert parallelism (the MoE layer) gives rank p the experts
 ``expert_range(E, p, P)``; the router and top-k run replicated, each rank computes the pairs
 routed to its experts and stores their rows into every rank's region, and every rank
 combines them in top-k order (hc_moe_ffn_ep_dev).  ``PeerGroup`` sets up the exchange regions over a
@@ -65,7 +66,7 @@ def gather_handles(handle: bytes, group=None) -> list[bytes]:
 class PeerGroup:
     """The exchange regions of one process group: open, gather handles, connect, barrier."""
 
-    def __init__(self, engine, group=None, nbytes: int = 16 << 20):
+    def __init__(self, engine, group=None, nbytes: int = 64 << 20):
         import torch.distributed as dist
 
         self.engine = engine

@@ -188,17 +188,20 @@ int hc_peer_open(hc_engine* eng, int rank, int world, size_t bytes, void* handle
 int hc_peer_connect(hc_engine* eng, const void* handles);
 int hc_peer_close(hc_engine* eng);
 
-/* Tensor-parallel FFN stack (batch 1), SURVEY config 5 sharding: rank p holds gate/up rows
+/* Tensor-parallel FFN stack, the config-5 sharding of Llama-3-70B: rank p holds gate/up rows
  * and down columns [p*F/P, (p+1)*F/P) of every layer (F = d_ff, column shards whole
- * super-blocks).  x [d_model] is replicated; each layer's down partials are pushed to every
- * rank inside the persistent stack kernel (the all-reduce of stream_infer.rs's residual
- * input, fused) and added in rank order, so x ends identical on every rank. */
+ * super-blocks).  x [nvec][d_model] is replicated; each layer's down output is all-reduced
+ * over the ranks' exchange regions (stream_infer.rs:2166's residual add after the down GEMV,
+ * with the sum over shards) and added in rank order, so x ends identical on every rank.
+ * nvec = 1: inside the persistent stack kernel.  nvec > 1: per-layer kernels plus one
+ * all-reduce kernel per layer, as one CUDA graph; the region must then hold
+ * 8 MiB + 4 KiB + 8 * P * nvec * d_model bytes (hc_peer_open's `bytes`). */
 int hc_ffn_stack_tp_dev(hc_engine* eng, const hc_weights* const* gate, const hc_weights* const* up,
                         const hc_weights* const* down, const float* const* norm_w, float eps, size_t n_layers,
-                        float* x);
+                        float* x, size_t nvec);
 int hc_ffn_stack_tp(hc_engine* eng, const hc_weights* const* gate, const hc_weights* const* up,
                     const hc_weights* const* down, const float* const* norm_w, float eps, size_t n_layers,
-                    const float* x_in, float* x_out);
+                    const float* x_in, float* x_out, size_t nvec);
 
 /* ---- MoE ---------------------------------------------------------------------------
  * Routing of route_experts (crates/hayai-core/src/moe_infer.rs:868-935, with

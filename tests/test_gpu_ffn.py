@@ -183,9 +183,10 @@ def test_stack_rejects_mismatched_layers(engine):
         engine.ffn_stack([a[0][0], b[0][0]], [a[0][1], b[0][1]], [a[0][2], b[0][2]], np.zeros(512, np.float32))
 
 
-@pytest.mark.parametrize("nvec", [8, 64])
+@pytest.mark.parametrize("nvec", [8, 16, 64])
 def test_stack_q8_0_tensor_core(engine, nvec):
-    """Config-3 shape family: Q8_0 stack with RMSNorm at batch 8 and 64 (tcgen05 path)."""
+    """Config-3 shape family: Q8_0 stack with RMSNorm at batch 8 (mma.sync GEMV), 16 and 64
+    (tcgen05 path)."""
     L, dm, ff = 2, 1024, 2816
     layers, res, norms = make_stack(engine, L, oracle.Q8_0, oracle.Q8_0, dm, ff, 700)
     X = oracle.normal(701, nvec * dm).reshape(nvec, dm)
@@ -194,3 +195,17 @@ def test_stack_q8_0_tensor_core(engine, nvec):
     for b in range(0, nvec, max(1, nvec // 4)):
         ref = oracle_stack(layers, norms, oracle.Q8_0, oracle.Q8_0, dm, ff, X[b])
         assert_parity(ref, got[b], what=f"q8_0 stack batch {nvec} row {b}")
+
+
+@pytest.mark.parametrize("nvec", [8, 16])
+def test_stack_kquant_tensor_core(engine, nvec):
+    """Config-5 batch shape family: Q4_K gate/up, Q6_K down with RMSNorm at batch 8 and 16
+    (tcgen05 path)."""
+    L, dm, ff = 2, 1024, 2816
+    layers, res, norms = make_stack(engine, L, oracle.Q4_K, oracle.Q6_K, dm, ff, 720)
+    X = oracle.normal(721, nvec * dm).reshape(nvec, dm)
+    nd = [torch.from_numpy(n).cuda() for n in norms]
+    got = engine.ffn_stack(*split(res), X.reshape(-1), nvec=nvec, norms=nd, eps=EPS).reshape(nvec, dm)
+    for b in range(0, nvec, max(1, nvec // 4)):
+        ref = oracle_stack(layers, norms, oracle.Q4_K, oracle.Q6_K, dm, ff, X[b])
+        assert_parity(ref, got[b], what=f"q4_k/q6_k stack batch {nvec} row {b}")

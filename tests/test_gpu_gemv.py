@@ -216,12 +216,13 @@ def test_deterministic(engine):
     assert np.array_equal(a, b)
 
 
-# ---------------------------------------------------------------- Q8_0 batches on tcgen05
+# ---------------------------------------------------------------- Q8_0 batches (9+) on tcgen05
 @pytest.mark.parametrize("batch,m,n", [
-    (8, 128, 1024),      # smallest tensor-core batch
-    (13, 256, 2048),     # ragged batch: rows padded to 16 in the MMA's N
-    (64, 512, 4096),     # config-3 batch, several K splits
-    (100, 128, 14336),   # long K (Llama-3-8B down), deep K split, N = 208
+    (9, 128, 1024),      # smallest Q8_0 tensor-core batch: rows padded to 16 in the MMA's N
+    (13, 256, 2048),     # ragged batch
+    (64, 512, 4096),     # config-3 batch, units split over several CTAs
+    (100, 128, 14336),   # long K (Llama-3-8B down), N = 208 (one accumulator set)
+    (128, 256, 1024),    # largest batch, N = 256
 ])
 def test_q8_0_tensor_core_batches(engine, batch, m, n):
     t = oracle.Q8_0
@@ -253,3 +254,44 @@ def test_q8_0_tensor_core_residual_dev(engine):
         engine.set_stream(None)
     ref = np.stack([oracle.gemv(oracle.Q8_0, m, n, w, xs[b]) + rs[b] for b in range(batch)])
     assert_parity(ref, Y.cpu().numpy(), what="q8_0 tensor-core + residual")
+
+
+# ---------------------------------------------------------------- Q4_K / Q6_K batches on tcgen05
+@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K])
+@pytest.mark.parametrize("batch,m,n", [
+    (8, 128, 1024),      # smallest tensor-core batch
+    (13, 256, 2048),     # ragged batch: rows padded to 16 in the MMA's N
+    (16, 384, 8192),     # config-5 batch (70B d_model), several K splits
+    (64, 128, 14336),    # Llama-3-8B down length, deep K split
+])
+def test_kquant_tensor_core_batches(engine, t, batch, m, n):
+    w = quantized(t, m, n, seed=171 + batch)
+    xs = oracle.normal(172 + batch, batch * n)
+    rw = engine.upload(t, m, n, w)
+    got = engine.ggml_gemv_batched(rw, xs, batch)
+    ref = np.concatenate([oracle.gemv(t, m, n, w, xs[b * n:(b + 1) * n]) for b in range(batch)])
+    assert_parity(ref, got, what=f"{hb.TYPE_LABELS[t]} tensor-core batch {batch} {m}x{n}")
+    again = engine.ggml_gemv_batched(rw, xs, batch)
+    assert np.array_equal(got, again)
+
+
+@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K])
+def test_kquant_tensor_core_reference_pattern(engine, t):
+    """The byte pattern of gemv_parity (compute.rs:1370-1396) at a tensor-core shape (128 rows,
+    batch 8).  Its Q6_K outputs reach |y| ~ 2300, where f32 summation order alone moves a
+    result by more than 1e-3 (the sequential f32 oracle is 3e-4 from the exact f64 value), so
+    besides rel-L2 <= 1e-4 against the oracle, each element is checked against the exact f64
+    product: |y - exact| <= 1e-3 + 2^-18 * sum_k |w_k x_k| (a few dozen f32 roundings of the
+    dot product's own scale)."""
+    m, n, batch = 128, 256, 8
+    w = ((np.arange(m * hb.row_bytes(t, n)) * 131 + 17) & 0x1F).astype(np.uint8)
+    xs = (np.arange(batch * n, dtype=np.float32) * np.float32(0.003) - np.float32(0.2)).astype(np.float32)
+    rw = engine.upload(t, m, n, w)
+    got = engine.ggml_gemv_batched(rw, xs, batch)
+    ref = np.concatenate([oracle.gemv(t, m, n, w, xs[b * n:(b + 1) * n]) for b in range(batch)])
+    assert_parity(ref, got, abs_tol=np.inf, what=f"{hb.TYPE_LABELS[t]} pattern batch {batch}")
+    W = oracle.dequant(t, w, m * n).reshape(m, n).astype(np.float64)
+    X = xs.reshape(batch, n).astype(np.float64)
+    exact = (X @ W.T).reshape(-1)
+    scale = (np.abs(X) @ np.abs(W).T).reshape(-1)
+    assert np.all(np.abs(got - exact) <= 1e-3 + scale * 2.0 ** -18)

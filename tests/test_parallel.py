@@ -5,8 +5,9 @@ unsharded FFN when the ranks' partial down outputs are added (oracle); the exper
 with replicated routing and a top-k-ordered combine of the exchanged rows reproduces the
 unpartitioned MoE (oracle); the IPC-handle exchange returns every rank's handle in rank
 order.  GPU (2 devices, marked gpu): the persistent stack kernel with the in-kernel NVLink
-exchange, and the expert-parallel MoE with its fused exchange, match the oracle and leave
-identical results on both ranks.
+exchange (batch 1), the per-layer kernels with the all-reduce kernel (batch > 1), and the
+expert-parallel MoE with its fused exchange match the oracle and leave identical results on
+both ranks.
 """
 import os
 import socket
@@ -104,11 +105,11 @@ def _gpu_rank(rank, world, port, case, result_path):
     eng = hb.CudaEngine(rank)
     peers = None
     try:
-        tg, td, dm, ff, L = case
+        tg, td, dm, ff, L, nvec = case
         layers = [(quantized(tg, ff, dm, 40 + 3 * l), quantized(tg, ff, dm, 41 + 3 * l),
                    quantized(td, dm, ff, 42 + 3 * l)) for l in range(L)]
         norms = [oracle.normal(70 + l, dm, 1.0, 0.1) for l in range(L)]
-        x = oracle.normal(80, dm)
+        X = oracle.normal(80, nvec * dm).reshape(nvec, dm)
         G, U, D = [], [], []
         for g, u, d in layers:
             gs, ffl = tpmod.shard_rows(g, tg, ff, dm, rank, world)
@@ -119,14 +120,20 @@ def _gpu_rank(rank, world, port, case, result_path):
             D.append(eng.upload(td, dm, ffl, ds))
         nd = [torch.from_numpy(n).cuda(rank) for n in norms]
         peers = tpmod.PeerGroup(eng)
-        got = eng.ffn_stack_tp(G, U, D, x, norms=nd, eps=EPS)
-        again = eng.ffn_stack_tp(G, U, D, x, norms=nd, eps=EPS)  # the cross-GPU counters carry over
+        got = eng.ffn_stack_tp(G, U, D, X.reshape(-1), nvec, norms=nd, eps=EPS).reshape(nvec, dm)
+        # the cross-GPU counters and device epochs carry over, also across the batch-1 and
+        # batched exchanges, which use separate counters and buffers
+        one = eng.ffn_stack_tp(G, U, D, X[0], norms=nd, eps=EPS) if nvec > 1 else None
+        again = eng.ffn_stack_tp(G, U, D, X.reshape(-1), nvec, norms=nd, eps=EPS).reshape(nvec, dm)
         outs = [None] * world
-        dist.all_gather_object(outs, (got, again))
+        dist.all_gather_object(outs, (got, again, one))
         if rank == 0:
-            ref = _oracle_stack(layers, norms, tg, td, dm, ff, x)
-            for r, (a, b) in enumerate(outs):
-                assert_parity(ref, a, what=f"tp{world} stack rank {r}")
+            for r, (a, b, o) in enumerate(outs):
+                for v in range(nvec):
+                    ref = _oracle_stack(layers, norms, tg, td, dm, ff, X[v])
+                    assert_parity(ref, a[v], what=f"tp{world} stack rank {r} row {v}")
+                    if v == 0 and o is not None:
+                        assert_parity(ref, o, what=f"tp{world} batch-1 stack between batched calls, rank {r}")
                 assert np.array_equal(a, outs[0][0]), "ranks disagree"
                 assert np.array_equal(a, b), "second call differs"
             with open(result_path, "w") as f:
@@ -140,8 +147,11 @@ def _gpu_rank(rank, world, port, case, result_path):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("case", [
-    (oracle.Q4_K, oracle.Q6_K, 1024, 4096, 3),   # one down chunk per tile and rank
-    (oracle.Q4_K, oracle.Q6_K, 1024, 16384, 2),  # two down chunks per tile and rank
+    (oracle.Q4_K, oracle.Q6_K, 1024, 4096, 3, 1),   # one down chunk per tile and rank
+    (oracle.Q4_K, oracle.Q6_K, 1024, 16384, 2, 1),  # two down chunks per tile and rank
+    (oracle.Q4_K, oracle.Q6_K, 1024, 4096, 3, 16),  # batch 16: per-layer kernels + all-reduce kernel
+    (oracle.Q8_0, oracle.Q8_0, 1024, 4096, 2, 12),  # batch 12 on the tcgen05 GEMM
+    (oracle.Q4_K, oracle.Q6_K, 1024, 4096, 2, 3),   # ragged batch
 ])
 def test_tp_stack_two_gpus(tmp_path, case):
     if torch.cuda.device_count() < 2:

@@ -27,17 +27,19 @@
 // so the weight stream never pauses between row blocks.  A maximal run of units of one (row
 // block, matrix) in a CTA is a segment: it accumulates in one of two TMEM accumulator sets
 // and ends in a partial-output slot; the finishing kernel adds a row block's slots in CTA
-// order (deterministic), then SiLU(g) * u or the residual.  14 warps:
-//   warp 0     TMA producers: lane 0 per unit one bulk copy per 16-row tile of the tile-major
-//              layout (8 copies of one image); lane 1 the activation chunks (64 K each,
-//              prepared in the MMA's operand layout by tc_prep_kernel, one copy each);
+// order (deterministic), then SiLU(g) * u or the residual.  15 warps:
+//   warp 0     weight producer: per unit one bulk copy per 16-row tile of the tile-major
+//              layout (8 copies of one image);
 //   warp 1     owns the TMEM columns; one elected lane issues the MMAs (4 K-steps x {hi, lo}
 //              per 64-K chunk), tcgen05.commit frees the operand buffers and, at a segment's
 //              end, hands its accumulator set to the epilogue;
 //   warps 2-9  dequantise each 64-K chunk into the A_hi / A_lo operand buffers (K-major,
 //              128-byte swizzle: rows of 128 B, 16-byte chunks XOR-permuted by row);
 //   warps 10-13 the epilogue: one TMEM lane quarter each (tcgen05.ld), partial outputs out,
-//              then the accumulator set is free again.
+//              then the accumulator set is free again;
+//   warp 14    activation producer: the 64-K chunks (prepared in the MMA's operand layout by
+//              tc_prep_kernel), one copy each.  Not a second lane of warp 0: the two producers'
+//              suspended mbarrier waits then held each other up (one third of the run time).
 // Every wait is bounded (~1 s; error bit 1), and the TMEM columns are freed on every path.
 #include <cuda_fp16.h>
 
@@ -51,7 +53,7 @@ namespace hc {
 constexpr int kTcRows = 128;               // output rows per CTA (MMA M)
 constexpr int kTcChunk = 64;               // K per operand buffer
 constexpr int kTcABytes = kTcRows * kTcChunk * 2;  // one f16 operand buffer (16 KB)
-constexpr int kTcThreads = 448;            // 14 warps
+constexpr int kTcThreads = 480;            // 15 warps
 constexpr int kTcMaxRing = 8;
 constexpr float kTcWScale = 256.f;         // w' = w * 2^8
 
@@ -379,10 +381,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
     const uint32_t tmem = s_tmem;
     bool bad = false, timeout = false;
 
-    if (warp == 0) {
-        // ---- producers: lane 0 streams the weight units, lane 1 the activation chunks, each
-        // as far ahead as its own ring allows
-        if (lane == 0) {
+    if (warp == 0 || warp == 14) {
+        // ---- producers, each as far ahead as its own ring allows: warp 0 the weight units,
+        // warp 14 the activation chunks
+        if (warp == 0 && lane == 0) {
             for (int i = 0; i < nu; ++i) {
                 const long long u = u0 + i;
                 const int run = (int)(u / a.nimg), img = (int)(u % a.nimg), rb = run / a.mats, z = run % a.mats;
@@ -392,7 +394,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
                     break;
                 }
                 mbar_arrive_expect_tx(w_full + 8 * sw, (uint32_t)(8 * F::kImg));
-                const uint8_t* W = a.w[z] + (size_t)rb * 8 * a.tstride + (size_t)img * F::kImg;
+                // (a select, not a.w[z]: a runtime index into the parameter struct makes the
+                // compiler copy the whole struct to local memory)
+                const uint8_t* W = (z ? a.w[1] : a.w[0]) + (size_t)rb * 8 * a.tstride + (size_t)img * F::kImg;
                 for (int rt = 0; rt < 8; ++rt)
                     bulk_g2s(smem_addr(wring + sw * WST + rt * F::kImg), W + (size_t)rt * a.tstride,
                              (uint32_t)F::kImg, w_full + 8 * sw);
@@ -400,7 +404,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
             // wait (bounded) until the last copies landed, so none writes after the CTA ends
             for (int i = nu - a.SW < 0 ? 0 : nu - a.SW; i < nu && !timeout; ++i)
                 if (!mbar_wait(w_full + 8 * (i % a.SW), (i / a.SW) & 1)) timeout = true;
-        } else if (lane == 1) {
+        } else if (warp == 14 && lane == 0) {
             for (int j = 0; j < nj; ++j) {
                 const int sx = j % a.NX;
                 const int kc = (int)((u0 + j / CPI) % a.nimg) * CPI + j % CPI;  // the chunk's K index

@@ -63,6 +63,43 @@ CONFIGS = {
 }
 
 
+# Single-GEMV workloads, one per GGML format: the Llama-3-8B gate shape (14336 x 4096), batch 1,
+# enough distinct resident copies to exceed L2.  (type id, elements, bytes per block)
+GEMV_FORMATS = {"q4_0": (2, 32, 18), "q4_1": (3, 32, 20), "q5_0": (6, 32, 22), "q5_1": (7, 32, 24),
+                "q8_0": (8, 32, 34), "q2_k": (10, 256, 84), "q3_k": (11, 256, 110), "q4_k": (12, 256, 144),
+                "q5_k": (13, 256, 176), "q6_k": (14, 256, 210), "iq2_xxs": (16, 256, 66), "iq2_xs": (17, 256, 74),
+                "iq3_xxs": (18, 256, 98), "iq4_nl": (20, 32, 18), "iq3_s": (21, 256, 110), "iq2_s": (22, 256, 82),
+                "iq4_xs": (23, 256, 136)}
+for _name, (_t, _qk, _bs) in GEMV_FORMATS.items():
+    BLK.setdefault(_t, (_qk, _bs))
+    CONFIGS["gemv-" + _name] = dict(gemv=True, t=_t, m=14336, k=4096,
+                                    workload=f"single {_name} GEMV, Llama-3-8B gate shape 14336 x 4096, batch 1")
+# f16 scale offsets and typical |value| / d of random codes (random valid blocks for the formats
+# without a quantizer here), and (offset, multiple of d) of a min field that centres the values
+_RAND_D_AT = {2: (0,), 3: (0,), 6: (0,), 7: (0,), 10: (80,), 11: (108,), 13: (0,), 16: (0,), 17: (0,), 18: (0,),
+              20: (0,), 21: (0,), 22: (0,), 23: (0,)}
+_RAND_SCALE = {2: 4.0, 3: 4.0, 6: 8.0, 7: 8.0, 10: 8.0, 11: 32.0, 13: 250.0, 16: 50.0, 17: 50.0, 18: 120.0, 20: 60.0,
+               21: 130.0, 22: 50.0, 23: 1000.0}
+_RAND_MIN_AT = {3: (2, -7.5), 7: (2, -15.5), 10: (82, 1.5), 13: (2, 15.5)}
+
+
+def random_blocks(t, m, n, seed, std=0.02):
+    """Random valid blocks of format t with the scales set for |w| ~ std (host numpy)."""
+    import numpy as np
+
+    qk, bs = BLK[t]
+    nblk = m * n // qk
+    rng = np.random.default_rng(seed)
+    b = rng.integers(0, 256, size=(nblk, bs), dtype=np.uint8)
+    d = (std / _RAND_SCALE[t] * rng.uniform(0.5, 1.5, nblk)).astype(np.float16)
+    for off in _RAND_D_AT[t]:
+        b[:, off:off + 2] = d.view(np.uint8).reshape(nblk, 2)
+    if t in _RAND_MIN_AT:
+        off, ratio = _RAND_MIN_AT[t]
+        b[:, off:off + 2] = (d.astype(np.float32) * np.float32(ratio)).astype(np.float16).view(np.uint8).reshape(nblk, 2)
+    return b.reshape(-1)
+
+
 def expert_bytes(c):
     return 2 * mat_bytes(c["tg"], c["d_ff"], c["d_model"]) + mat_bytes(c["td"], c["d_model"], c["d_ff"])
 
@@ -245,6 +282,10 @@ def run_reference(args):
     c = dict(CONFIGS[args.config])
     if "n_expert" in c:
         return run_reference_moe(args, c, world)
+    if c.get("gemv"):
+        print(json.dumps({"impl": "reference", "unavailable": "the reference arm is timed on the FFN configs; "
+                          "the GEMV configs carry the oracle's CPU baseline in their own line"}))
+        return 0
     if args.layers:
         c["layers"] = args.layers
     cores = oracle.get_threads()
@@ -777,6 +818,125 @@ def run_ours(args):
     return 0
 
 
+def run_gemv(args):
+    """One GEMV of the config's format per step (batch 1), rotating over resident copies."""
+    import numpy as np
+    import torch
+
+    import hayai_b200 as hb
+
+    c = CONFIGS[args.config]
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    t, M, K = c["t"], c["m"], c["k"]
+    mbytes = mat_bytes(t, M, K)
+    copies = max(2, -(-400_000_000 // mbytes))  # > L2 between reuses of one copy
+    eng = hb.CudaEngine(local)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    eng.set_stream(stream)
+    W, raw = [], None
+    for i in range(copies):
+        if t in (Q4_K, Q6_K, Q8_0):
+            src = torch.empty(M * K, dtype=torch.float32, device=dev)
+            eng.synth_normal_dev(1000 + i, src, 0.0, 0.02)
+            q = torch.empty(mbytes, dtype=torch.uint8, device=dev)
+            eng.quantize_dev(t, src, q)
+            W.append(eng.upload_from_device(t, M, K, q))
+            if i == 0:
+                raw = q.cpu().numpy()
+            del src, q
+        else:
+            hb_bytes = random_blocks(t, M, K, 1000 + i)
+            W.append(eng.upload(t, M, K, hb_bytes))
+            if i == 0:
+                raw = hb_bytes
+    x = torch.randn(K, device=dev)
+    y = torch.empty(M, device=dev)
+    torch.cuda.synchronize(dev)
+    for i in range(max(args.warmup, 3)):
+        eng.gemv_dev(W[i % copies], x, y)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        eng.gemv_dev(W[i % copies], x, y)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    eng.sync()
+    t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
+    value = world * args.steps * mbytes / t_dev / 1e9
+    peak, peak_kind = measured_peak()
+    # e2e: host x in, host y out through the reference-facing call, every step
+    xh = x.cpu().numpy()
+    n_e2e = min(args.steps, 100)
+    for i in range(3):
+        eng.ggml_gemv_dispatch_bound(W[i % copies], xh)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    for i in range(n_e2e):
+        yh = eng.ggml_gemv_dispatch_bound(W[i % copies], xh)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
+    assert np.isfinite(yh).all()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        rows = 2048
+        xr = xh.astype(np.float32)
+        done, t0 = 0, time.perf_counter()
+        while True:
+            oracle.gemv(t, rows, K, raw[:rows * mbytes // M], xr)
+            done += 1
+            el = time.perf_counter() - t0
+            if el >= min(args.cpu_seconds, 10.0) and done >= 2:
+                break
+        cpu = {"value": round(done * rows * mbytes / M / el / 1e9, 3), "unit": "GB/s", "cores": oracle.get_threads(),
+               "kind": "port", "sample": f"{done} GEMVs of the first {rows} rows on the C restatement, {el:.1f} s"}
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(t_dev / args.steps * 1e3, 5), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": args.config[len("gemv-"):] + "/f32",
+                "data": "synthetic (random valid blocks, or seeded N(0,0.02^2) weights quantized on device)",
+                "config": {"workload": c["workload"], "m": M, "k": K, "copies": copies,
+                           "l2": f"inputs larger than L2 ({copies} copies of {mbytes / 1e6:.1f} MB rotated)"},
+                "roofline": {"bound": "hbm", "kernel": "GEMV (one launch)", "achieved": round(value / world, 1),
+                             "peak": peak, "unit": "GB/s", "frac": round(value / world / peak, 4),
+                             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy burst)",
+                             "traffic": None, "algorithmic_bytes_per_launch": mbytes,
+                             "avg_launch_us": round(t_dev / args.steps * 1e6, 2)},
+                "e2e": {"value": round(world * n_e2e * mbytes / t_e2e / 1e9, 2), "unit": "GB/s", "steps": n_e2e,
+                        "h2d_bytes_per_step": K * 4, "d2h_bytes_per_step": M * 4,
+                        "api": "ggml_gemv_dispatch_bound (host buffers)"},
+                "clocks": clocks, "gpu_launches": args.steps}
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line))
+    for w in W:
+        w.free()
+    eng.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -797,6 +957,8 @@ def main():
         return run_reference(args)
     if "n_expert" in CONFIGS[args.config]:
         return run_moe(args)
+    if CONFIGS[args.config].get("gemv"):
+        return run_gemv(args)
     return run_ours(args)
 
 

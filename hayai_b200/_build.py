@@ -59,7 +59,8 @@ def gen_tables(force: bool = False) -> str:
     """Generate the IQ codebook header from the reference (needs the reference tree)."""
     script = os.path.join(CSRC, "gen_iq_tables.py")
     srcs = [os.path.join(REFERENCE, "crates/hayai-model/src/iq2.rs"),
-            os.path.join(REFERENCE, "crates/hayai-model/src/iq3.rs")]
+            os.path.join(REFERENCE, "crates/hayai-model/src/iq3.rs"),
+            os.path.join(REFERENCE, "crates/hayai-model/src/iq4.rs")]
     if all(os.path.exists(s) for s in srcs):
         if force or _newer(TABLES, srcs + [script]):
             _run([sys.executable, script, REFERENCE, TABLES])

@@ -53,6 +53,15 @@ const char* hc_type_label(int t) {
         case T_IQ2_S: return "iq2_s";
         case T_IQ3_XXS: return "iq3_xxs";
         case T_IQ3_S: return "iq3_s";
+        case T_Q4_0: return "q4_0";
+        case T_Q4_1: return "q4_1";
+        case T_Q5_0: return "q5_0";
+        case T_Q5_1: return "q5_1";
+        case T_Q2_K: return "q2_k";
+        case T_Q3_K: return "q3_k";
+        case T_Q5_K: return "q5_k";
+        case T_IQ4_NL: return "iq4_nl";
+        case T_IQ4_XS: return "iq4_xs";
         default: return "unknown";
     }
 }
@@ -60,8 +69,9 @@ const char* hc_type_label(int t) {
 static int block_elems(int t) {
     switch (t) {
         case T_F32: return 1;
-        case T_Q8_0: return 32;
+        case T_Q8_0: case T_Q4_0: case T_Q4_1: case T_Q5_0: case T_Q5_1: case T_IQ4_NL: return 32;
         case T_Q4_K: case T_Q6_K: case T_IQ2_XXS: case T_IQ2_XS: case T_IQ2_S: case T_IQ3_XXS: case T_IQ3_S:
+        case T_Q2_K: case T_Q3_K: case T_Q5_K: case T_IQ4_XS:
             return 256;
         default: return 0;
     }

@@ -1,10 +1,13 @@
-// gemv_simple.cu -- CUDA-core kernels on the raw GGUF layout: F32, the IQ2/IQ3 codebook
-// formats, the toy LUT-Q4 matmul, and the elementwise SwiGLU combine.
+// gemv_simple.cu -- CUDA-core kernels on the raw GGUF layout: F32, the IQ2/IQ3/IQ4 codebook
+// formats, the other GGML block formats (Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q5_K), the toy
+// LUT-Q4 matmul, and the elementwise SwiGLU combine.
 //
 // Reference semantics: gemv_f32 (crates/hayai-model/src/quant.rs:358-369), the IQ2 block
 // decoders (crates/hayai-model/src/iq2.rs:504-573, gemv macro :591-626), the IQ3 block
-// decoders (crates/hayai-model/src/iq3.rs:147-220, gemv :258-331), cpu_lut_matmul_q4
-// (crates/hayai-cpu/src/matmul.rs:48-82).
+// decoders (crates/hayai-model/src/iq3.rs:147-220, gemv :258-331), IQ4_NL / IQ4_XS
+// (iq4.rs:36-42, :121-138), Q4_0 / Q4_1 (quant.rs:538-596, :617-650), Q5_0 / Q5_1
+// (q5.rs:26-158), Q2_K (q2k.rs:26-58), Q3_K (q3k.rs:10-30, :52-84), Q5_K (q5k.rs:10-66),
+// cpu_lut_matmul_q4 (crates/hayai-cpu/src/matmul.rs:48-82).
 #include "common.cuh"
 #include "gemv_launch.h"
 
@@ -16,7 +19,9 @@ namespace hc {
 // Sign byte of a 7-bit index: the index with bit 7 = its parity (iq2.rs:18-27).
 __device__ __forceinline__ uint32_t ksigns(uint32_t i) { return (i & 127u) | ((__popc(i & 127u) & 1u) << 7); }
 
-__device__ __forceinline__ uint32_t ldb(const uint8_t* p) { return __ldg(p); }
+// Byte loads of a block; the group kernel stages blocks in shared memory, so these are
+// generic loads (no read-only-path form, which only addresses global memory).
+__device__ __forceinline__ uint32_t ldb(const uint8_t* p) { return *p; }
 __device__ __forceinline__ uint32_t ld_u16u(const uint8_t* p) { return ldb(p) | (ldb(p + 1) << 8); }
 __device__ __forceinline__ uint32_t ld_u32u(const uint8_t* p) { return ld_u16u(p) | (ld_u16u(p + 2) << 16); }
 __device__ __forceinline__ float ld_f16u(const uint8_t* p) { return h2f((uint16_t)ld_u16u(p)); }
@@ -44,11 +49,121 @@ __device__ __forceinline__ float dot4_grid(float db, uint32_t grid, uint32_t sig
     return s;
 }
 
-// One 32-element group (ib32) of an IQ block, dotted with x[0..32).
+// get_scale_min_k4 (q4k.rs:34-43, q5k.rs:10-18): 6-bit scale and min j of a K-quant header.
+__device__ __forceinline__ void scale_min_k4(const uint8_t* s, int j, float& sc, float& m) {
+    if (j < 4) {
+        sc = (float)(ldb(s + j) & 63u);
+        m = (float)(ldb(s + j + 4) & 63u);
+    } else {
+        sc = (float)((ldb(s + j + 4) & 0x0Fu) | ((ldb(s + j - 4) >> 6) << 4));
+        m = (float)((ldb(s + j + 4) >> 4) | ((ldb(s + j) >> 6) << 4));
+    }
+}
+
+// Q3_K scale i (0..15) of the 12 packed bytes, as unpack_q3_k_scales (q3k.rs:10-30) lays
+// them out: low 4 bits from byte i (i < 8) or the high nibble of byte i - 8, top 2 bits from
+// byte 8 + i % 4 at bit 2 (i / 4); minus 32.
+__device__ __forceinline__ float q3k_scale(const uint8_t* s12, int i) {
+    const uint32_t lo = i < 8 ? (ldb(s12 + i) & 0x0Fu) : (ldb(s12 + i - 8) >> 4);
+    const uint32_t hi = (ldb(s12 + 8 + (i & 3)) >> (2 * (i >> 2))) & 3u;
+    return (float)((int)(lo | (hi << 4)) - 32);
+}
+
+// One 32-element group (ib32) of a block, dotted with x[0..32).
 template <int TYPE>
-__device__ __forceinline__ float iq_group_dot(const uint8_t* blk, int ib32, const float* x) {
-    const float d = ld_f16u(blk);
+__device__ __forceinline__ float group_dot(const uint8_t* blk, int ib32, const float* x) {
     float s = 0.f;
+    if constexpr (TYPE == T_Q4_0 || TYPE == T_Q4_1 || TYPE == T_Q5_0 || TYPE == T_Q5_1 || TYPE == T_IQ4_NL) {
+        // 32-element blocks: element j from the low nibble of qs[j], j + 16 from the high one
+        const float d = ld_f16u(blk);
+        const float m = (TYPE == T_Q4_1 || TYPE == T_Q5_1) ? ld_f16u(blk + 2) : 0.f;
+        const int qoff = TYPE == T_Q4_0 || TYPE == T_IQ4_NL ? 2 : TYPE == T_Q4_1 ? 4 : TYPE == T_Q5_0 ? 6 : 8;
+        const uint32_t qh = TYPE == T_Q5_0 ? ld_u32u(blk + 2) : TYPE == T_Q5_1 ? ld_u32u(blk + 4) : 0u;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const uint32_t q = ldb(blk + qoff + j);
+            uint32_t c0 = q & 0x0Fu, c1 = q >> 4;
+            float w0, w1;
+            if constexpr (TYPE == T_Q5_0 || TYPE == T_Q5_1) {
+                c0 |= ((qh >> j) << 4) & 0x10u;
+                c1 |= (qh >> (j + 12)) & 0x10u;
+            }
+            if constexpr (TYPE == T_Q4_0) {
+                w0 = (float)((int)c0 - 8) * d;
+                w1 = (float)((int)c1 - 8) * d;
+            } else if constexpr (TYPE == T_Q5_0) {
+                w0 = (float)((int)c0 - 16) * d;
+                w1 = (float)((int)c1 - 16) * d;
+            } else if constexpr (TYPE == T_IQ4_NL) {
+                w0 = d * (float)hc_iq4nl_values[c0];
+                w1 = d * (float)hc_iq4nl_values[c1];
+            } else {  // Q4_1, Q5_1
+                w0 = (float)c0 * d + m;
+                w1 = (float)c1 * d + m;
+            }
+            s += w0 * x[j];
+            s += w1 * x[j + 16];
+        }
+        return s;
+    } else if constexpr (TYPE == T_Q2_K) {
+        // half n = ib32 / 4, shift 2 (ib32 % 4); elements 0-15 from q[l], 16-31 from q[16 + l]
+        const int n = ib32 >> 2, j = ib32 & 3;
+        const float d = ld_f16u(blk + 80), dmin = ld_f16u(blk + 82);
+        const uint8_t* q = blk + 16 + 32 * n;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t sc = ldb(blk + 8 * n + 2 * j + h);
+            const float dl = d * (float)(sc & 0xFu), ml = dmin * (float)(sc >> 4);
+#pragma unroll
+            for (int l = 0; l < 16; ++l) s += (dl * (float)((ldb(q + 16 * h + l) >> (2 * j)) & 3u) - ml) * x[16 * h + l];
+        }
+        return s;
+    } else if constexpr (TYPE == T_Q3_K) {
+        const int n = ib32 >> 2, j = ib32 & 3;
+        const float dall = ld_f16u(blk + 108);
+        const uint8_t* q = blk + 32 + 32 * n;
+        const uint32_t mbit = 1u << (4 * n + j);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float dl = dall * q3k_scale(blk + 96, 8 * n + 2 * j + h);
+#pragma unroll
+            for (int l = 0; l < 16; ++l) {
+                const int qv = (int)((ldb(q + 16 * h + l) >> (2 * j)) & 3u);
+                const int hm = (ldb(blk + 16 * h + l) & mbit) ? 0 : 4;
+                s += dl * (float)(qv - hm) * x[16 * h + l];
+            }
+        }
+        return s;
+    } else if constexpr (TYPE == T_Q5_K) {
+        // chunk c = ib32 / 2: low nibbles of ql[32c + l] (ib32 even) or high ones, fifth bit
+        // qh[l] & (1 or 2) << 2c, scale and min ib32
+        const int c = ib32 >> 1, hi = ib32 & 1;
+        float sc, mn;
+        scale_min_k4(blk + 4, ib32, sc, mn);
+        const float d1 = ld_f16u(blk) * sc, m1 = ld_f16u(blk + 2) * mn;
+        const uint32_t u = (hi ? 2u : 1u) << (2 * c);
+#pragma unroll
+        for (int l = 0; l < 32; ++l) {
+            const uint32_t ql = ldb(blk + 48 + 32 * c + l);
+            const uint32_t v = (hi ? ql >> 4 : ql & 0x0Fu) + ((ldb(blk + 16 + l) & u) ? 16u : 0u);
+            s += (d1 * (float)v - m1) * x[l];
+        }
+        return s;
+    } else if constexpr (TYPE == T_IQ4_XS) {
+        const float d = ld_f16u(blk);
+        const uint32_t sh = ld_u16u(blk + 2);
+        const int ls = (int)(((ldb(blk + 4 + ib32 / 2) >> (4 * (ib32 & 1))) & 0x0Fu) | (((sh >> (2 * ib32)) & 3u) << 4));
+        const float dl = d * (float)(ls - 32);
+        const uint8_t* qs = blk + 8 + 16 * ib32;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const uint32_t q = ldb(qs + j);
+            s += dl * (float)hc_iq4nl_values[q & 0x0Fu] * x[j];
+            s += dl * (float)hc_iq4nl_values[q >> 4] * x[j + 16];
+        }
+        return s;
+    }
+    const float d = ld_f16u(blk);
     if constexpr (TYPE == T_IQ2_XXS) {
         const uint32_t aux0 = ld_u32u(blk + 2 + 8 * ib32), aux1 = ld_u32u(blk + 2 + 8 * ib32 + 4);
         const float db = d * (0.5f + (float)(aux1 >> 28)) * 0.25f;
@@ -95,32 +210,160 @@ __device__ __forceinline__ float iq_group_dot(const uint8_t* blk, int ib32, cons
     return s;
 }
 
-template <int TYPE, int BLK>
-__global__ void __launch_bounds__(256) gemv_iq_kernel(const uint8_t* __restrict__ w, size_t row_bytes, int M,
-                                                       int K, const float* __restrict__ x, int ldx,
-                                                       float* __restrict__ y, int ldy, const float* resid, int ldr,
-                                                       int nvec) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    const int nwarps = (gridDim.x * blockDim.x) >> 5;
-    const int nb = K / 256;
+// Elements e..e+3 (e a multiple of 4) of the 32-element group ib32 of a block, dotted with x4:
+// the same values as group_dot, one quarter-octet at a time, so that 8 lanes share a group and
+// a warp's activation loads are 512 contiguous bytes.
+__device__ __forceinline__ float dot4_signed(float db, uint32_t grid4, uint32_t signs, const float4& x) {
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float g = (float)((grid4 >> (8 * j)) & 0xffu);
+        v[j] = (signs >> j) & 1u ? -db * g : db * g;
+    }
+    return v[0] * x.x + v[1] * x.y + v[2] * x.z + v[3] * x.w;
+}
+
+template <int TYPE>
+__device__ __forceinline__ float group_dot4(const uint8_t* blk, int ib32, int e, const float4& x) {
+    float w[4];
+    if constexpr (TYPE == T_Q4_0 || TYPE == T_Q4_1 || TYPE == T_Q5_0 || TYPE == T_Q5_1 || TYPE == T_IQ4_NL) {
+        // element j < 16: low nibble of qs[j]; j >= 16: high nibble of qs[j - 16]
+        const float d = ld_f16u(blk);
+        const float m = (TYPE == T_Q4_1 || TYPE == T_Q5_1) ? ld_f16u(blk + 2) : 0.f;
+        const int qoff = TYPE == T_Q4_0 || TYPE == T_IQ4_NL ? 2 : TYPE == T_Q4_1 ? 4 : TYPE == T_Q5_0 ? 6 : 8;
+        const uint32_t qh = TYPE == T_Q5_0 ? ld_u32u(blk + 2) : TYPE == T_Q5_1 ? ld_u32u(blk + 4) : 0u;
+        const bool hi = e >= 16;
+        const int j0 = hi ? e - 16 : e;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = j0 + i;
+            const uint32_t q = ldb(blk + qoff + j);
+            uint32_t c = hi ? q >> 4 : q & 0x0Fu;
+            if constexpr (TYPE == T_Q5_0 || TYPE == T_Q5_1) c |= hi ? (qh >> (j + 12)) & 0x10u : ((qh >> j) << 4) & 0x10u;
+            if constexpr (TYPE == T_Q4_0) w[i] = (float)((int)c - 8) * d;
+            else if constexpr (TYPE == T_Q5_0) w[i] = (float)((int)c - 16) * d;
+            else if constexpr (TYPE == T_IQ4_NL) w[i] = d * (float)hc_iq4nl_values[c];
+            else w[i] = (float)c * d + m;
+        }
+    } else if constexpr (TYPE == T_Q2_K || TYPE == T_Q3_K) {
+        // half n = ib32 / 4, shift 2 (ib32 % 4); elements 0-15 from q[l], 16-31 from q[16 + l]
+        const int n = ib32 >> 2, jj = ib32 & 3, h = e >> 4, l0 = e & 15;
+        const uint8_t* q = blk + (TYPE == T_Q2_K ? 16 : 32) + 32 * n + 16 * h;
+        if constexpr (TYPE == T_Q2_K) {
+            const uint32_t sc = ldb(blk + 8 * n + 2 * jj + h);
+            const float dl = ld_f16u(blk + 80) * (float)(sc & 0xFu), ml = ld_f16u(blk + 82) * (float)(sc >> 4);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w[i] = dl * (float)((ldb(q + l0 + i) >> (2 * jj)) & 3u) - ml;
+        } else {
+            const float dl = ld_f16u(blk + 108) * q3k_scale(blk + 96, 8 * n + 2 * jj + h);
+            const uint32_t mbit = 1u << (4 * n + jj);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int qv = (int)((ldb(q + l0 + i) >> (2 * jj)) & 3u);
+                const int hm = (ldb(blk + 16 * h + l0 + i) & mbit) ? 0 : 4;
+                w[i] = dl * (float)(qv - hm);
+            }
+        }
+    } else if constexpr (TYPE == T_Q5_K) {
+        const int c = ib32 >> 1, hi = ib32 & 1;
+        float sc, mn;
+        scale_min_k4(blk + 4, ib32, sc, mn);
+        const float d1 = ld_f16u(blk) * sc, m1 = ld_f16u(blk + 2) * mn;
+        const uint32_t u = (hi ? 2u : 1u) << (2 * c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t ql = ldb(blk + 48 + 32 * c + e + i);
+            const uint32_t v = (hi ? ql >> 4 : ql & 0x0Fu) + ((ldb(blk + 16 + e + i) & u) ? 16u : 0u);
+            w[i] = d1 * (float)v - m1;
+        }
+    } else if constexpr (TYPE == T_IQ4_XS) {
+        const uint32_t sh = ld_u16u(blk + 2);
+        const int ls = (int)(((ldb(blk + 4 + ib32 / 2) >> (4 * (ib32 & 1))) & 0x0Fu) | (((sh >> (2 * ib32)) & 3u) << 4));
+        const float dl = ld_f16u(blk) * (float)(ls - 32);
+        const bool hi = e >= 16;
+        const uint8_t* qs = blk + 8 + 16 * ib32 + (hi ? e - 16 : e);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t q = ldb(qs + i);
+            w[i] = dl * (float)hc_iq4nl_values[hi ? q >> 4 : q & 0x0Fu];
+        }
+    } else {
+        // IQ2 (8-element grid points: half (e / 4) % 2 of point e / 8) and IQ3 (4-element points)
+        const float d = ld_f16u(blk);
+        const int l = e >> 3, half = (e >> 2) & 1;
+        if constexpr (TYPE == T_IQ2_XXS) {
+            const uint32_t aux0 = ld_u32u(blk + 2 + 8 * ib32), aux1 = ld_u32u(blk + 2 + 8 * ib32 + 4);
+            const float db = d * (0.5f + (float)(aux1 >> 28)) * 0.25f;
+            const uint64_t g = hc_iq2xxs_grid[(aux0 >> (8 * l)) & 0xff];
+            return dot4_signed(db, (uint32_t)(g >> (32 * half)), ksigns(aux1 >> (7 * l)) >> (4 * half), x);
+        } else if constexpr (TYPE == T_IQ2_XS) {
+            const uint32_t sc = ldb(blk + 66 + ib32);
+            const float db = d * (0.5f + (float)(l < 2 ? sc & 0xf : sc >> 4)) * 0.25f;
+            const uint32_t q = ld_u16u(blk + 2 + 2 * (4 * ib32 + l));
+            const uint64_t g = hc_iq2xs_grid[q & 511];
+            return dot4_signed(db, (uint32_t)(g >> (32 * half)), ksigns(q >> 9) >> (4 * half), x);
+        } else if constexpr (TYPE == T_IQ2_S) {
+            const uint32_t sc = ldb(blk + 74 + ib32), qh = ldb(blk + 66 + ib32);
+            const float db = d * (0.5f + (float)(l < 2 ? sc & 0xf : sc >> 4)) * 0.25f;
+            const uint32_t idx = ldb(blk + 2 + 4 * ib32 + l) | ((qh << (8 - 2 * l)) & 0x300u);
+            const uint64_t g = hc_iq2s_grid[idx];
+            return dot4_signed(db, (uint32_t)(g >> (32 * half)), ldb(blk + 34 + 4 * ib32 + l) >> (4 * half), x);
+        } else if constexpr (TYPE == T_IQ3_XXS) {
+            const uint32_t aux = ld_u32u(blk + 66 + 4 * ib32);
+            const float db = d * (0.5f + (float)(aux >> 28)) * 0.5f;
+            const uint32_t g = hc_iq3xxs_grid[ldb(blk + 2 + 8 * ib32 + 2 * l + half)];
+            return dot4_signed(db, g, ksigns(aux >> (7 * l)) >> (4 * half), x);
+        } else {  // IQ3_S
+            const uint32_t sc = ldb(blk + 106 + ib32 / 2), qh = ldb(blk + 66 + ib32);
+            const float db = d * (1.0f + 2.0f * (float)((sc >> (4 * (ib32 & 1))) & 0xf));
+            const uint32_t idx = ldb(blk + 2 + 8 * ib32 + 2 * l + half) | ((qh << (8 - 2 * l - half)) & 256u);
+            return dot4_signed(db, hc_iq3s_grid[idx], ldb(blk + 74 + 4 * ib32 + l) >> (4 * half), x);
+        }
+    }
+    return w[0] * x.x + w[1] * x.y + w[2] * x.z + w[3] * x.w;
+}
+
+// One warp per (row, vector).  The warp first stages a segment of whole blocks of the row
+// (<= kGroupSeg bytes) in its shared-memory buffer with coalesced 16-byte loads (the raw GGUF
+// rows are byte-aligned only; the copy starts at the 16-byte boundary below the segment and
+// may read up to 15 bytes past the row, inside the 16 bytes of padding every weight allocation
+// carries), then decodes it with 8 lanes per 32-element group, 4 elements per lane (QK
+// elements and BLK bytes per block, QK / 32 groups per block).  One lane per group made every
+// activation load instruction touch 32 cache lines and ran at 0.04-0.09 of the HBM peak.
+constexpr int kGroupSeg = 4096;
+
+template <int TYPE, int QK, int BLK>
+__global__ void __launch_bounds__(256, 4) gemv_group_kernel(const uint8_t* __restrict__ w, size_t row_bytes, int M,
+                                                          int K, const float* __restrict__ x, int ldx,
+                                                          float* __restrict__ y, int ldy, const float* resid, int ldr,
+                                                          int nvec) {
+    constexpr int G = QK / 32;
+    constexpr int SEGB = kGroupSeg / BLK;  // blocks per segment
+    __shared__ __align__(16) uint8_t sbuf[8][kGroupSeg + 32];
+    const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = blockIdx.x * 8 + wib, nwarps = gridDim.x * 8;
+    uint8_t* buf = sbuf[wib];
+    const int nb = K / QK;
     for (int rv = warp; rv < M * nvec; rv += nwarps) {
         const int row = rv % M, v = rv / M;
         const uint8_t* wr = w + (size_t)row * row_bytes;
         const float* xv = x + (size_t)v * ldx;
         float s = 0.f;
-        for (int gi = lane; gi < nb * 8; gi += 32) {
-            const int b = gi >> 3, ib32 = gi & 7;
-            float xs[32];
-            const float4* xp = reinterpret_cast<const float4*>(xv + b * 256 + 32 * ib32);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                float4 a = __ldg(xp + q);
-                xs[4 * q] = a.x;
-                xs[4 * q + 1] = a.y;
-                xs[4 * q + 2] = a.z;
-                xs[4 * q + 3] = a.w;
+        for (int b0 = 0; b0 < nb; b0 += SEGB) {
+            const int nbs = nb - b0 < SEGB ? nb - b0 : SEGB;
+            const uintptr_t g0 = reinterpret_cast<uintptr_t>(wr + (size_t)b0 * BLK), a0 = g0 & ~(uintptr_t)15;
+            const int lead = (int)(g0 - a0), nchunks = (lead + nbs * BLK + 15) >> 4;
+            __syncwarp();  // the previous segment has been decoded
+            for (int c = lane; c < nchunks; c += 32)
+                *reinterpret_cast<uint4*>(buf + 16 * c) = ldg_stream128(reinterpret_cast<const void*>(a0 + 16 * c));
+            __syncwarp();
+            const uint8_t* sb = buf + lead;
+            // 8 lanes per group, 4 elements each: lanes 8g..8g+7 read 128 contiguous bytes of x
+            for (int gi = lane >> 3; gi < nbs * G; gi += 4) {
+                const int b = gi / G, ib32 = gi % G, e = 4 * (lane & 7);
+                const float4 x4 = __ldg(reinterpret_cast<const float4*>(xv + (size_t)(b0 + b) * QK + 32 * ib32 + e));
+                s += group_dot4<TYPE>(sb + b * BLK, ib32, e, x4);
             }
-            s += iq_group_dot<TYPE>(wr + (size_t)b * BLK, ib32, xs);
         }
         s = warp_sum(s);
         if (lane == 0) y[(size_t)v * ldy + row] = (resid ? resid[(size_t)v * ldr + row] : 0.f) + s;
@@ -149,8 +392,13 @@ static int grid_for(int work_warps) {
 }
 
 bool gemv_simple_supported(int type) {
-    return type == T_F32 || type == T_IQ2_XXS || type == T_IQ2_XS || type == T_IQ2_S || type == T_IQ3_XXS ||
-           type == T_IQ3_S;
+    switch (type) {
+        case T_F32: case T_IQ2_XXS: case T_IQ2_XS: case T_IQ2_S: case T_IQ3_XXS: case T_IQ3_S: case T_Q4_0:
+        case T_Q4_1: case T_Q5_0: case T_Q5_1: case T_Q2_K: case T_Q3_K: case T_Q5_K: case T_IQ4_NL: case T_IQ4_XS:
+            return true;
+        default:
+            return false;
+    }
 }
 
 cudaError_t launch_gemv_simple(int type, const uint8_t* w, size_t row_bytes, int M, int K, const float* x, int ldx,
@@ -162,20 +410,35 @@ cudaError_t launch_gemv_simple(int type, const uint8_t* w, size_t row_bytes, int
                                                       y, ldy, resid, ldr, nvec);
             break;
         case T_IQ2_XXS:
-            gemv_iq_kernel<T_IQ2_XXS, 66><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
+            gemv_group_kernel<T_IQ2_XXS, 256, 66><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
             break;
         case T_IQ2_XS:
-            gemv_iq_kernel<T_IQ2_XS, 74><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
+            gemv_group_kernel<T_IQ2_XS, 256, 74><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
             break;
         case T_IQ2_S:
-            gemv_iq_kernel<T_IQ2_S, 82><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
+            gemv_group_kernel<T_IQ2_S, 256, 82><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
             break;
         case T_IQ3_XXS:
-            gemv_iq_kernel<T_IQ3_XXS, 98><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
+            gemv_group_kernel<T_IQ3_XXS, 256, 98><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
             break;
         case T_IQ3_S:
-            gemv_iq_kernel<T_IQ3_S, 110><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
+            gemv_group_kernel<T_IQ3_S, 256, 110><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
             break;
+#define HC_GROUP_CASE(T, QK, BLK)                                                                       \
+    case T:                                                                                             \
+        gemv_group_kernel<T, QK, BLK><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, \
+                                                                nvec);                                  \
+        break;
+        HC_GROUP_CASE(T_Q4_0, 32, 18)
+        HC_GROUP_CASE(T_Q4_1, 32, 20)
+        HC_GROUP_CASE(T_Q5_0, 32, 22)
+        HC_GROUP_CASE(T_Q5_1, 32, 24)
+        HC_GROUP_CASE(T_IQ4_NL, 32, 18)
+        HC_GROUP_CASE(T_Q2_K, 256, 84)
+        HC_GROUP_CASE(T_Q3_K, 256, 110)
+        HC_GROUP_CASE(T_Q5_K, 256, 176)
+        HC_GROUP_CASE(T_IQ4_XS, 256, 136)
+#undef HC_GROUP_CASE
         default:
             return cudaErrorInvalidValue;
     }

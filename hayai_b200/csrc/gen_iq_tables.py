@@ -8,6 +8,7 @@ script reads them at build time from the reference's own Rust tables
 
     crates/hayai-model/src/iq2.rs  IQ2XXS_GRID (:30), IQ2XS_GRID (:98), IQ2S_GRID (:230)
     crates/hayai-model/src/iq3.rs  IQ3XXS_GRID (:29), IQ3S_GRID (:65)
+    crates/hayai-model/src/iq4.rs  KVALUES_IQ4NL (:15), the 16 signed levels of IQ4_NL / IQ4_XS
 
 and writes them as a C header (``_gen/iq_tables.h``) that both the CUDA
 library and the CPU oracle include.  The generated header is a build product
@@ -47,6 +48,22 @@ def extract(src: str, name: str, n: int) -> list[int]:
     return vals
 
 
+SIGNED = [
+    # (rust file, rust name, C name, expected length): decimal i8 tables
+    ("crates/hayai-model/src/iq4.rs", "KVALUES_IQ4NL", "hc_iq4nl_values", 16),
+]
+
+
+def extract_i8(src: str, name: str, n: int) -> list[int]:
+    m = re.search(r"const\s+" + name + r"\s*:\s*\[i8;\s*(\d+)\]\s*=\s*\[(.*?)\];", src, re.S)
+    if not m:
+        raise SystemExit(f"gen_iq_tables: table {name} not found")
+    vals = [int(tok) for tok in re.findall(r"-?\d+", m.group(2))]
+    if int(m.group(1)) != n or len(vals) != n or any(v < -128 or v > 127 for v in vals):
+        raise SystemExit(f"gen_iq_tables: {name} is not {n} int8 values")
+    return vals
+
+
 def main(argv: list[str]) -> int:
     if len(argv) != 3:
         print(__doc__)
@@ -79,6 +96,14 @@ def main(argv: list[str]) -> int:
             chunk = ", ".join(f"0x{v:0{width}x}{suffix}" for v in vals[i:i + per])
             lines.append(f"    {chunk},")
         lines.append("};")
+        lines.append("")
+    for path, rname, cname, n in SIGNED:
+        full = os.path.join(ref, path)
+        if full not in cache:
+            with open(full, encoding="utf-8") as f:
+                cache[full] = f.read()
+        vals = extract_i8(cache[full], rname, n)
+        lines.append(f"HC_IQ_QUAL int8_t {cname}[{n}] = {{{', '.join(str(v) for v in vals)}}};")
         lines.append("")
     os.makedirs(os.path.dirname(os.path.abspath(out)), exist_ok=True)
     tmp = out + ".tmp"

@@ -41,6 +41,15 @@ size_t raw_row_bytes(int type, int K) {
         case T_IQ2_S: return (size_t)K / 256 * 82;
         case T_IQ3_XXS: return (size_t)K / 256 * 98;
         case T_IQ3_S: return (size_t)K / 256 * 110;
+        case T_Q4_0: return (size_t)K / 32 * 18;
+        case T_Q4_1: return (size_t)K / 32 * 20;
+        case T_Q5_0: return (size_t)K / 32 * 22;
+        case T_Q5_1: return (size_t)K / 32 * 24;
+        case T_IQ4_NL: return (size_t)K / 32 * 18;
+        case T_Q2_K: return (size_t)K / 256 * 84;
+        case T_Q3_K: return (size_t)K / 256 * 110;
+        case T_Q5_K: return (size_t)K / 256 * 176;
+        case T_IQ4_XS: return (size_t)K / 256 * 136;
         default: return 0;
     }
 }

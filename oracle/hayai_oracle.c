@@ -58,10 +58,21 @@ int or_get_threads(void) {
 #define IQ3_XXS_BLOCK 98
 #define IQ3_S_BLOCK 110
 
-/* GgmlType ids, crates/hayai-model/src/gguf_types.rs:43-77 */
+#define Q4_0_BLOCK 18
+#define Q4_1_BLOCK 20
+#define Q5_0_BLOCK 22
+#define Q5_1_BLOCK 24
+#define Q2_K_BLOCK 84
+#define Q3_K_BLOCK 110
+#define Q5_K_BLOCK 176
+#define IQ4_NL_BLOCK 18
+#define IQ4_XS_BLOCK 136
+
+/* GgmlType ids, crates/hayai-model/src/gguf_types.rs:6-40 */
 enum {
-    T_F32 = 0, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ2_XS = 17,
-    T_IQ3_XXS = 18, T_IQ3_S = 21, T_IQ2_S = 22
+    T_F32 = 0, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q2_K = 10, T_Q3_K = 11,
+    T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ2_XS = 17, T_IQ3_XXS = 18, T_IQ4_NL = 20,
+    T_IQ3_S = 21, T_IQ2_S = 22, T_IQ4_XS = 23
 };
 
 /* ------------------------------------------------------------------------ */
@@ -661,10 +672,334 @@ int or_gemv_iq2_s(size_t m, size_t n, const uint8_t* w, const float* x, float* y
 int or_gemv_iq3_xxs(size_t m, size_t n, const uint8_t* w, const float* x, float* y) { return gemv_blockwise(m, n, w, x, y, dequant_iq3_xxs_block, IQ3_XXS_BLOCK); }
 int or_gemv_iq3_s(size_t m, size_t n, const uint8_t* w, const float* x, float* y) { return gemv_blockwise(m, n, w, x, y, dequant_iq3_s_block, IQ3_S_BLOCK); }
 
+/* ------------------------------------------------------------------------ */
+/* Q4_0, Q4_1, Q5_0, Q5_1 (32-element blocks)                                */
+/* ------------------------------------------------------------------------ */
+
+/* crates/hayai-model/src/quant.rs:617-632 (extract_q4_0_row) */
+static void dequant_q4_0_block(const uint8_t* b, float* y) {
+    float d = rd_f16(b);
+    const uint8_t* qs = b + 2;
+    for (int j = 0; j < 16; j++) {
+        y[j] = (float)((int)(qs[j] & 0x0F) - 8) * d;
+        y[j + 16] = (float)((int)(qs[j] >> 4) - 8) * d;
+    }
+}
+
+/* crates/hayai-model/src/quant.rs:538-574: per block, two 8-lane chunks accumulate
+ * (ql*d)*xl + (qh*d)*xh lane by lane; the lanes' reduce_sum (taken in lane order here)
+ * joins the row sum. */
+int or_gemv_q4_0(size_t nrows, size_t ncols, const uint8_t* data, const float* input, float* output) {
+    if (ncols % 32) return -1;
+    size_t bpr = ncols / 32, rb = bpr * Q4_0_BLOCK;
+    #pragma omp parallel for schedule(static)
+    for (size_t row = 0; row < nrows; row++) {
+        float sum = 0.0f;
+        for (size_t b = 0; b < bpr; b++) {
+            const uint8_t* base = data + row * rb + b * Q4_0_BLOCK;
+            float d = rd_f16(base);
+            const uint8_t* qs = base + 2;
+            const float* x = input + b * 32;
+            float ql[16], qh[16], acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int j = 0; j < 16; j++) {
+                ql[j] = (float)((int)(qs[j] & 0x0F) - 8);
+                qh[j] = (float)((int)(qs[j] >> 4) - 8);
+            }
+            for (int c = 0; c < 2; c++) {
+                int o = c * 8;
+                for (int i = 0; i < 8; i++) acc[i] += ql[o + i] * d * x[o + i] + qh[o + i] * d * x[16 + o + i];
+            }
+            float r = 0.0f;
+            for (int i = 0; i < 8; i++) r += acc[i];
+            sum += r;
+        }
+        output[row] = sum;
+    }
+    return 0;
+}
+
+/* crates/hayai-model/src/quant.rs:634-650 (extract_q4_1_row) */
+static void dequant_q4_1_block(const uint8_t* b, float* y) {
+    float d = rd_f16(b), m = rd_f16(b + 2);
+    const uint8_t* qs = b + 4;
+    for (int j = 0; j < 16; j++) {
+        y[j] = (float)(qs[j] & 0x0F) * d + m;
+        y[j + 16] = (float)(qs[j] >> 4) * d + m;
+    }
+}
+
+/* crates/hayai-model/src/quant.rs:576-596 */
+int or_gemv_q4_1(size_t nrows, size_t ncols, const uint8_t* data, const float* input, float* output) {
+    if (ncols % 32) return -1;
+    size_t bpr = ncols / 32, rb = bpr * Q4_1_BLOCK;
+    #pragma omp parallel for schedule(static)
+    for (size_t row = 0; row < nrows; row++) {
+        float sum = 0.0f;
+        for (size_t b = 0; b < bpr; b++) {
+            const uint8_t* base = data + row * rb + b * Q4_1_BLOCK;
+            float d = rd_f16(base), m = rd_f16(base + 2);
+            const uint8_t* qs = base + 4;
+            const float* x = input + b * 32;
+            for (int j = 0; j < 16; j++) {
+                sum += ((float)(qs[j] & 0x0F) * d + m) * x[j];
+                sum += ((float)(qs[j] >> 4) * d + m) * x[j + 16];
+            }
+        }
+        output[row] = sum;
+    }
+    return 0;
+}
+
+/* The fifth bits of Q5_0 / Q5_1 element j and j + 16 (crates/hayai-model/src/q5.rs:30-33). */
+static inline int q5_hi0(uint32_t qh, int j) { return (int)(((qh >> j) << 4) & 0x10); }
+static inline int q5_hi1(uint32_t qh, int j) { return (int)((qh >> (j + 12)) & 0x10); }
+
+/* crates/hayai-model/src/q5.rs:26-38 */
+static void dequant_q5_0_block(const uint8_t* b, float* y) {
+    float d = rd_f16(b);
+    uint32_t qh = rd_u32(b + 2);
+    const uint8_t* qs = b + 6;
+    for (int j = 0; j < 16; j++) {
+        int x0 = ((qs[j] & 0x0F) | q5_hi0(qh, j)) - 16;
+        int x1 = ((qs[j] >> 4) | q5_hi1(qh, j)) - 16;
+        y[j] = (float)x0 * d;
+        y[j + 16] = (float)x1 * d;
+    }
+}
+
+/* crates/hayai-model/src/q5.rs:40-76 */
+int or_gemv_q5_0(size_t nrows, size_t ncols, const uint8_t* data, const float* input, float* output) {
+    if (ncols % 32) return -1;
+    size_t bpr = ncols / 32, rb = bpr * Q5_0_BLOCK;
+    #pragma omp parallel for schedule(static)
+    for (size_t row = 0; row < nrows; row++) {
+        float sum = 0.0f;
+        for (size_t b = 0; b < bpr; b++) {
+            const uint8_t* base = data + row * rb + b * Q5_0_BLOCK;
+            float d = rd_f16(base);
+            uint32_t qh = rd_u32(base + 2);
+            const uint8_t* qs = base + 6;
+            const float* x = input + b * 32;
+            for (int j = 0; j < 16; j++) {
+                int x0 = ((qs[j] & 0x0F) | q5_hi0(qh, j)) - 16;
+                int x1 = ((qs[j] >> 4) | q5_hi1(qh, j)) - 16;
+                sum += (float)x0 * d * x[j];
+                sum += (float)x1 * d * x[j + 16];
+            }
+        }
+        output[row] = sum;
+    }
+    return 0;
+}
+
+/* crates/hayai-model/src/q5.rs:96-122 */
+static void dequant_q5_1_block(const uint8_t* b, float* y) {
+    float d = rd_f16(b), m = rd_f16(b + 2);
+    uint32_t qh = rd_u32(b + 4);
+    const uint8_t* qs = b + 8;
+    for (int j = 0; j < 16; j++) {
+        int x0 = (qs[j] & 0x0F) | q5_hi0(qh, j);
+        int x1 = (qs[j] >> 4) | q5_hi1(qh, j);
+        y[j] = (float)x0 * d + m;
+        y[j + 16] = (float)x1 * d + m;
+    }
+}
+
+/* crates/hayai-model/src/q5.rs:124-158 */
+int or_gemv_q5_1(size_t nrows, size_t ncols, const uint8_t* data, const float* input, float* output) {
+    if (ncols % 32) return -1;
+    size_t bpr = ncols / 32, rb = bpr * Q5_1_BLOCK;
+    #pragma omp parallel for schedule(static)
+    for (size_t row = 0; row < nrows; row++) {
+        float sum = 0.0f;
+        for (size_t b = 0; b < bpr; b++) {
+            const uint8_t* base = data + row * rb + b * Q5_1_BLOCK;
+            float d = rd_f16(base), m = rd_f16(base + 2);
+            uint32_t qh = rd_u32(base + 4);
+            const uint8_t* qs = base + 8;
+            const float* x = input + b * 32;
+            for (int j = 0; j < 16; j++) {
+                int x0 = (qs[j] & 0x0F) | q5_hi0(qh, j);
+                int x1 = (qs[j] >> 4) | q5_hi1(qh, j);
+                sum += ((float)x0 * d + m) * x[j];
+                sum += ((float)x1 * d + m) * x[j + 16];
+            }
+        }
+        output[row] = sum;
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Q2_K, Q3_K, Q5_K (256-element super-blocks)                               */
+/* ------------------------------------------------------------------------ */
+
+/* The elements of a K-quant super-block in the reference's order, each computed by
+ * `elem` exactly as the reference's GEMV forms it, then summed into one running sum:
+ * crates/hayai-model/src/q2k.rs:60-118, q3k.rs:93-146, q5k.rs:69-127 (their dequant
+ * blocks :26-58, :52-84, :36-66 produce the same values). */
+static void dequant_q2_k_block(const uint8_t* b, float* y) {
+    const uint8_t* scales = b;
+    const uint8_t* q = b + 16;
+    float d = rd_f16(b + 80), mn = rd_f16(b + 82);
+    int yo = 0, is = 0;
+    for (int n = 0; n < QK_K / 128; n++) {
+        for (int j = 0; j < 4; j++) {
+            int shift = 2 * j;
+            for (int h = 0; h < 2; h++) {
+                uint8_t sc = scales[is++];
+                float dl = d * (float)(sc & 0xF), ml = mn * (float)(sc >> 4);
+                for (int l = 0; l < 16; l++) y[yo + l] = dl * (float)((q[l + 16 * h] >> shift) & 3) - ml;
+                yo += 16;
+            }
+        }
+        q += 32;
+    }
+}
+
+/* crates/hayai-model/src/q3k.rs:10-30 (unpack_q3_k_scales) */
+static void unpack_q3_k_scales(const uint8_t* s12, int8_t* out) {
+    const uint32_t kmask1 = 0x03030303u, kmask2 = 0x0f0f0f0fu;
+    uint32_t aux[4];
+    aux[0] = rd_u32(s12);
+    aux[1] = rd_u32(s12 + 4);
+    aux[2] = rd_u32(s12 + 8);
+    uint32_t tmp = aux[2];
+    aux[2] = ((aux[0] >> 4) & kmask2) | (((tmp >> 4) & kmask1) << 4);
+    aux[3] = ((aux[1] >> 4) & kmask2) | (((tmp >> 6) & kmask1) << 4);
+    aux[0] = (aux[0] & kmask2) | (((tmp >> 0) & kmask1) << 4);
+    aux[1] = (aux[1] & kmask2) | (((tmp >> 2) & kmask1) << 4);
+    for (int i = 0; i < 4; i++)
+        for (int j = 0; j < 4; j++) out[4 * i + j] = (int8_t)(uint8_t)(aux[i] >> (8 * j));
+}
+
+static void dequant_q3_k_block(const uint8_t* b, float* y) {
+    const uint8_t* hmask = b;
+    const uint8_t* q = b + 32;
+    int8_t scales[16];
+    unpack_q3_k_scales(b + 96, scales);
+    float d_all = rd_f16(b + 108);
+    int yo = 0, is = 0;
+    uint8_t m = 1;
+    for (int n = 0; n < QK_K / 128; n++) {
+        for (int j = 0; j < 4; j++) {
+            int shift = 2 * j;
+            for (int h = 0; h < 2; h++) {
+                float dl = d_all * (float)((int)scales[is++] - 32);
+                for (int l = 0; l < 16; l++) {
+                    int qv = (q[l + 16 * h] >> shift) & 3;
+                    int hm = (hmask[l + 16 * h] & m) ? 0 : 4;
+                    y[yo + l] = dl * (float)(qv - hm);
+                }
+                yo += 16;
+            }
+            m <<= 1;
+        }
+        q += 32;
+    }
+}
+
+/* crates/hayai-model/src/q5k.rs:10-18 (scale_min) is get_scale_min_k4 above. */
+static void dequant_q5_k_block(const uint8_t* b, float* y) {
+    float d = rd_f16(b), mn = rd_f16(b + 2);
+    const uint8_t* scales = b + 4;
+    const uint8_t* qh = b + 16;
+    const uint8_t* ql = b + 48;
+    int yo = 0, is = 0;
+    uint8_t u1 = 1, u2 = 2;
+    for (int c = 0; c < QK_K / 64; c++) {
+        uint8_t sc0, m0, sc1, m1;
+        get_scale_min_k4(is, scales, &sc0, &m0);
+        get_scale_min_k4(is + 1, scales, &sc1, &m1);
+        float d1 = d * (float)sc0, m1v = mn * (float)m0, d2 = d * (float)sc1, m2v = mn * (float)m1;
+        for (int l = 0; l < 32; l++) y[yo + l] = d1 * (float)((ql[l] & 0x0F) + ((qh[l] & u1) ? 16 : 0)) - m1v;
+        yo += 32;
+        for (int l = 0; l < 32; l++) y[yo + l] = d2 * (float)((ql[l] >> 4) + ((qh[l] & u2) ? 16 : 0)) - m2v;
+        yo += 32;
+        ql += 32;
+        is += 2;
+        u1 <<= 2;
+        u2 <<= 2;
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* IQ4_NL (32-element blocks), IQ4_XS (256)                                  */
+/* ------------------------------------------------------------------------ */
+
+/* crates/hayai-model/src/iq4.rs:36-42 */
+static void dequant_iq4_nl_block(const uint8_t* b, float* y) {
+    float d = rd_f16(b);
+    const uint8_t* qs = b + 2;
+    for (int j = 0; j < 16; j++) {
+        y[j] = d * (float)hc_iq4nl_values[qs[j] & 0x0F];
+        y[j + 16] = d * (float)hc_iq4nl_values[qs[j] >> 4];
+    }
+}
+
+/* crates/hayai-model/src/iq4.rs:121-138 */
+static void dequant_iq4_xs_block(const uint8_t* b, float* y) {
+    float d = rd_f16(b);
+    uint32_t scales_h = (uint32_t)(b[2] | (b[3] << 8));
+    const uint8_t* scales_l = b + 4;
+    const uint8_t* qs = b + 8;
+    for (int ib = 0; ib < 8; ib++) {
+        int ls = ((scales_l[ib / 2] >> (4 * (ib % 2))) & 0x0F) | (int)(((scales_h >> (2 * ib)) & 3) << 4);
+        float dl = d * (float)(ls - 32);
+        for (int j = 0; j < 16; j++) {
+            y[32 * ib + j] = dl * (float)hc_iq4nl_values[qs[j] & 0x0F];
+            y[32 * ib + 16 + j] = dl * (float)hc_iq4nl_values[qs[j] >> 4];
+        }
+        qs += 16;
+    }
+}
+
+/* One running sum over each block's values in element order, the block decoded exactly as the
+ * reference's GEMV forms each product's weight: crates/hayai-model/src/q2k.rs:60-118,
+ * q3k.rs:93-146, q5k.rs:69-127, iq4.rs:44-78 (IQ4_NL, 32-element blocks; the reference sums
+ * element j, then j + 16, per j), iq4.rs:140-186 (IQ4_XS). */
+static int gemv_blocks_seq(size_t nrows, size_t ncols, const uint8_t* data, const float* input, float* output,
+                           block_fn fn, size_t qk, size_t blk) {
+    if (ncols % qk) return -1;
+    size_t bpr = ncols / qk, rb = bpr * blk;
+    #pragma omp parallel for schedule(static)
+    for (size_t row = 0; row < nrows; row++) {
+        float tmp[QK_K];
+        float sum = 0.0f;
+        for (size_t b = 0; b < bpr; b++) {
+            fn(data + row * rb + b * blk, tmp);
+            const float* x = input + b * qk;
+            if (qk == 32) {  /* IQ4_NL: j then j + 16 */
+                for (int j = 0; j < 16; j++) {
+                    sum += tmp[j] * x[j];
+                    sum += tmp[j + 16] * x[j + 16];
+                }
+            } else if (fn == dequant_iq4_xs_block) {  /* IQ4_XS: per 32-group, j then j + 16 */
+                for (int ib = 0; ib < 8; ib++)
+                    for (int j = 0; j < 16; j++) {
+                        sum += tmp[32 * ib + j] * x[32 * ib + j];
+                        sum += tmp[32 * ib + 16 + j] * x[32 * ib + 16 + j];
+                    }
+            } else {
+                for (int j = 0; j < (int)qk; j++) sum += tmp[j] * x[j];
+            }
+        }
+        output[row] = sum;
+    }
+    return 0;
+}
+
+int or_gemv_q2_k(size_t m, size_t n, const uint8_t* w, const float* x, float* y) { return gemv_blocks_seq(m, n, w, x, y, dequant_q2_k_block, QK_K, Q2_K_BLOCK); }
+int or_gemv_q3_k(size_t m, size_t n, const uint8_t* w, const float* x, float* y) { return gemv_blocks_seq(m, n, w, x, y, dequant_q3_k_block, QK_K, Q3_K_BLOCK); }
+int or_gemv_q5_k(size_t m, size_t n, const uint8_t* w, const float* x, float* y) { return gemv_blocks_seq(m, n, w, x, y, dequant_q5_k_block, QK_K, Q5_K_BLOCK); }
+int or_gemv_iq4_nl(size_t m, size_t n, const uint8_t* w, const float* x, float* y) { return gemv_blocks_seq(m, n, w, x, y, dequant_iq4_nl_block, 32, IQ4_NL_BLOCK); }
+int or_gemv_iq4_xs(size_t m, size_t n, const uint8_t* w, const float* x, float* y) { return gemv_blocks_seq(m, n, w, x, y, dequant_iq4_xs_block, QK_K, IQ4_XS_BLOCK); }
+
 /* Block dequantizers exported for layout cross-checks against an independent decoder. */
 int or_dequant(int type, const uint8_t* bytes, size_t n, float* out) {
     block_fn fn = NULL;
     size_t blk = 0;
+    size_t qk = QK_K;
     switch (type) {
         case T_Q4_K: return or_dequant_q4_k(bytes, n, out);
         case T_Q6_K: return or_dequant_q6_k(bytes, n, out);
@@ -674,10 +1009,19 @@ int or_dequant(int type, const uint8_t* bytes, size_t n, float* out) {
         case T_IQ2_S: fn = dequant_iq2_s_block; blk = IQ2_S_BLOCK; break;
         case T_IQ3_XXS: fn = dequant_iq3_xxs_block; blk = IQ3_XXS_BLOCK; break;
         case T_IQ3_S: fn = dequant_iq3_s_block; blk = IQ3_S_BLOCK; break;
+        case T_Q4_0: fn = dequant_q4_0_block; blk = Q4_0_BLOCK; qk = 32; break;
+        case T_Q4_1: fn = dequant_q4_1_block; blk = Q4_1_BLOCK; qk = 32; break;
+        case T_Q5_0: fn = dequant_q5_0_block; blk = Q5_0_BLOCK; qk = 32; break;
+        case T_Q5_1: fn = dequant_q5_1_block; blk = Q5_1_BLOCK; qk = 32; break;
+        case T_IQ4_NL: fn = dequant_iq4_nl_block; blk = IQ4_NL_BLOCK; qk = 32; break;
+        case T_Q2_K: fn = dequant_q2_k_block; blk = Q2_K_BLOCK; break;
+        case T_Q3_K: fn = dequant_q3_k_block; blk = Q3_K_BLOCK; break;
+        case T_Q5_K: fn = dequant_q5_k_block; blk = Q5_K_BLOCK; break;
+        case T_IQ4_XS: fn = dequant_iq4_xs_block; blk = IQ4_XS_BLOCK; break;
         default: return -2;
     }
-    if (n % QK_K) return -1;
-    for (size_t i = 0; i < n / QK_K; i++) fn(bytes + i * blk, out + i * QK_K);
+    if (n % qk) return -1;
+    for (size_t i = 0; i < n / qk; i++) fn(bytes + i * blk, out + i * qk);
     return 0;
 }
 
@@ -693,6 +1037,15 @@ int or_gemv(int type, size_t nrows, size_t ncols, const uint8_t* w, const float*
         case T_IQ2_S: return or_gemv_iq2_s(nrows, ncols, w, x, y);
         case T_IQ3_XXS: return or_gemv_iq3_xxs(nrows, ncols, w, x, y);
         case T_IQ3_S: return or_gemv_iq3_s(nrows, ncols, w, x, y);
+        case T_Q4_0: return or_gemv_q4_0(nrows, ncols, w, x, y);
+        case T_Q4_1: return or_gemv_q4_1(nrows, ncols, w, x, y);
+        case T_Q5_0: return or_gemv_q5_0(nrows, ncols, w, x, y);
+        case T_Q5_1: return or_gemv_q5_1(nrows, ncols, w, x, y);
+        case T_Q2_K: return or_gemv_q2_k(nrows, ncols, w, x, y);
+        case T_Q3_K: return or_gemv_q3_k(nrows, ncols, w, x, y);
+        case T_Q5_K: return or_gemv_q5_k(nrows, ncols, w, x, y);
+        case T_IQ4_NL: return or_gemv_iq4_nl(nrows, ncols, w, x, y);
+        case T_IQ4_XS: return or_gemv_iq4_xs(nrows, ncols, w, x, y);
         default: return -2;
     }
 }

@@ -5,20 +5,28 @@ import numpy as np
 
 import oracle
 
-QK = {oracle.F32: 1, oracle.Q8_0: 32, oracle.Q4_K: 256, oracle.Q6_K: 256, oracle.IQ2_XXS: 256,
-      oracle.IQ2_XS: 256, oracle.IQ2_S: 256, oracle.IQ3_XXS: 256, oracle.IQ3_S: 256}
+QK = {t: qk for t, (qk, _) in oracle.BLOCK.items()}
 IQ_TYPES = [oracle.IQ2_XXS, oracle.IQ2_XS, oracle.IQ2_S, oracle.IQ3_XXS, oracle.IQ3_S]
-# typical |decoded value| / d for random codes: block scale factor x mean grid value
+# The other GGML block formats (raw GGUF rows, CUDA-core GEMV)
+BLOCK_TYPES = [oracle.Q4_0, oracle.Q4_1, oracle.Q5_0, oracle.Q5_1, oracle.Q2_K, oracle.Q3_K, oracle.Q5_K,
+               oracle.IQ4_NL, oracle.IQ4_XS]
+# typical |decoded value| / d for random codes: block scale factor x mean code or grid value
 IQ_SCALE = {oracle.IQ2_XXS: 50.0, oracle.IQ2_XS: 50.0, oracle.IQ2_S: 50.0, oracle.IQ3_XXS: 120.0,
-            oracle.IQ3_S: 130.0}
-# byte offsets of the f16 scales inside a block, per IQ type (d at 0)
+            oracle.IQ3_S: 130.0, oracle.Q4_0: 4.0, oracle.Q4_1: 4.0, oracle.Q5_0: 8.0, oracle.Q5_1: 8.0,
+            oracle.Q2_K: 8.0, oracle.Q3_K: 32.0, oracle.Q5_K: 250.0, oracle.IQ4_NL: 60.0, oracle.IQ4_XS: 1000.0}
+# byte offsets of the f16 scale d inside a block
 F16_AT = {oracle.Q4_K: (0, 2), oracle.Q6_K: (208,), oracle.Q8_0: (0,), oracle.IQ2_XXS: (0,), oracle.IQ2_XS: (0,),
-          oracle.IQ2_S: (0,), oracle.IQ3_XXS: (0,), oracle.IQ3_S: (0,)}
+          oracle.IQ2_S: (0,), oracle.IQ3_XXS: (0,), oracle.IQ3_S: (0,), oracle.Q4_0: (0,), oracle.Q4_1: (0,),
+          oracle.Q5_0: (0,), oracle.Q5_1: (0,), oracle.Q2_K: (80,), oracle.Q3_K: (108,), oracle.Q5_K: (0,),
+          oracle.IQ4_NL: (0,), oracle.IQ4_XS: (0,)}
+# the f16 min / dmin: (byte offset, multiple of d) chosen to centre the decoded values near zero
+MIN_AT = {oracle.Q4_1: (2, -7.5), oracle.Q5_1: (2, -15.5), oracle.Q2_K: (82, 1.5), oracle.Q5_K: (2, 15.5)}
 
 
 def quantized(ggml_type: int, m: int, n: int, seed: int, std: float = 0.02) -> np.ndarray:
-    """Seeded weights: N(0, std^2) quantized (Q4_K with the reference quantizer), or
-    random valid blocks with d in [0.002, 0.02] for the IQ formats."""
+    """Seeded weights: N(0, std^2) quantized (Q4_K with the reference quantizer), or random
+    valid blocks with their scales set for a realistic magnitude (~std) for the IQ formats and
+    the other GGML block formats."""
     if ggml_type == oracle.F32:
         return oracle.normal(seed, m * n, 0.0, std).view(np.uint8).copy()
     if ggml_type in (oracle.Q4_K, oracle.Q6_K, oracle.Q8_0):
@@ -33,6 +41,10 @@ def quantized(ggml_type: int, m: int, n: int, seed: int, std: float = 0.02) -> n
     d = (std / IQ_SCALE[ggml_type] * (0.5 + 0.5 * (1.0 + np.tanh(u)))).astype(np.float16)
     for off in F16_AT[ggml_type]:
         b[:, off:off + 2] = d.view(np.uint8).reshape(nblk, 2)
+    if ggml_type in MIN_AT:
+        off, ratio = MIN_AT[ggml_type]
+        mn = (d.astype(np.float32) * np.float32(ratio)).astype(np.float16)
+        b[:, off:off + 2] = mn.view(np.uint8).reshape(nblk, 2)
     return b.reshape(-1).copy()
 
 

@@ -54,7 +54,7 @@ def test_row_bytes_rejects_partial_block():
 
 def test_unsupported_type_is_a_hard_error():
     with pytest.raises(hayai_b200.CudaError) as e:
-        hayai_b200.row_bytes(2, 256)  # Q4_0: no kernel in this backend
+        hayai_b200.row_bytes(19, 256)  # IQ1_S: no kernel (the reference hard-fails IQ1 too)
     assert e.value.code == _lib.HC_ERR_UNSUPPORTED
 
 

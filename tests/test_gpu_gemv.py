@@ -10,11 +10,11 @@ import torch
 
 import hayai_b200 as hb
 import oracle
-from tests.helpers import IQ_TYPES, MAX_ABS, REL_L2, assert_parity, quantized
+from tests.helpers import BLOCK_TYPES, IQ_TYPES, MAX_ABS, REL_L2, assert_parity, quantized
 
 pytestmark = pytest.mark.gpu
 
-ALL = [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, oracle.F32, *IQ_TYPES]
+ALL = [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, oracle.F32, *IQ_TYPES, *BLOCK_TYPES]
 LUT = np.array([-0.5, -0.4, -0.3, -0.2, -0.1, 0.0, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 1.0], np.float32)
 
 
@@ -72,7 +72,7 @@ def test_reference_q8_0_fixture(engine):
     assert np.abs(ref - engine.ggml_gemv_q8_0(m, n, w, x)).max() < 1e-3
 
 
-@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, *IQ_TYPES])
+@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, *IQ_TYPES, *BLOCK_TYPES])
 def test_reference_gemv_parity_pattern(engine, t):
     # gemv_parity (compute.rs:1370-1396): bytes (i*131+17)&0x1F, input i*0.003-0.2, m32 n256
     m, n = 32, 256
@@ -95,7 +95,8 @@ def test_reference_batched_q4_k(engine):
     assert np.abs(expected - outputs).max() < 1e-3
 
 
-@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, oracle.IQ2_S, oracle.F32])
+@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, oracle.IQ2_S, oracle.F32, oracle.Q5_0,
+                               oracle.Q3_K, oracle.IQ4_XS])
 @pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 8])
 def test_batched_all_types(engine, t, batch):
     m, n = 80, 1024
@@ -180,7 +181,7 @@ def test_invalid_shapes_rejected(engine):
         engine.ggml_gemv_dispatch(oracle.Q4_K, 4, 256, np.zeros(3 * 144, np.uint8), np.zeros(256, np.float32))
     assert "weight buffer" in str(e.value)
     with pytest.raises(hb.CudaError) as e:
-        engine.ggml_gemv_dispatch(2, 4, 256, np.zeros(4 * 144, np.uint8), np.zeros(256, np.float32))
+        engine.ggml_gemv_dispatch(19, 4, 256, np.zeros(4 * 144, np.uint8), np.zeros(256, np.float32))  # IQ1_S
     assert e.value.code == 2
 
 

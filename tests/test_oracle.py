@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 import oracle
-from tests.helpers import IQ_TYPES, quantized
+from tests.helpers import BLOCK_TYPES, IQ_TYPES, quantized
 
 LUT = np.array([-0.5, -0.4, -0.3, -0.2, -0.1, 0.0, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 1.0],
                dtype=np.float32)
@@ -151,15 +151,12 @@ def test_route_ties_keep_lower_expert_id():
 
 
 # ----------------------------------------------------------------------------- independent decoder
-@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, *IQ_TYPES])
+@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, *IQ_TYPES, *BLOCK_TYPES])
 def test_dequant_matches_gguf_py(t):
     gguf = pytest.importorskip("gguf")
     from gguf.quants import dequantize
 
-    qtype = {oracle.Q4_K: gguf.GGMLQuantizationType.Q4_K, oracle.Q6_K: gguf.GGMLQuantizationType.Q6_K,
-             oracle.Q8_0: gguf.GGMLQuantizationType.Q8_0, oracle.IQ2_XXS: gguf.GGMLQuantizationType.IQ2_XXS,
-             oracle.IQ2_XS: gguf.GGMLQuantizationType.IQ2_XS, oracle.IQ2_S: gguf.GGMLQuantizationType.IQ2_S,
-             oracle.IQ3_XXS: gguf.GGMLQuantizationType.IQ3_XXS, oracle.IQ3_S: gguf.GGMLQuantizationType.IQ3_S}[t]
+    qtype = gguf.GGMLQuantizationType(t)  # the GGML type ids are the same numbers
     qk, bs = oracle.BLOCK[t]
     m, n = 8, 1024
     w = quantized(t, m, n, seed=100 + t)
@@ -168,7 +165,7 @@ def test_dequant_matches_gguf_py(t):
     assert np.array_equal(ref, got)
 
 
-@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, *IQ_TYPES])
+@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, *IQ_TYPES, *BLOCK_TYPES])
 def test_gemv_matches_dequant_dot(t):
     m, n = 48, 1024
     w = quantized(t, m, n, seed=200 + t)

@@ -1,7 +1,8 @@
 """Generate tests/golden/golden.npz: small seeded GEMV fixtures for every format.
 
 For each format: seeded packed weights (Q4_K from the reference quantizer restated in the
-oracle; Q6_K/Q8_0 from the project quantizers; IQ formats as random valid blocks), a seeded
+oracle; Q6_K/Q8_0 from the project quantizers; the IQ and the other block formats as random
+valid blocks), a seeded
 N(0,1) input, and two outputs:
   * ``_y``     -- the oracle's f32 output (regression pin of the restatement), and
   * ``_y64``   -- an independent float64 product of the weights decoded by gguf-py 0.19.0
@@ -28,7 +29,10 @@ def main() -> None:
     fmts = {"q4_k": (oracle.Q4_K, Q.Q4_K), "q6_k": (oracle.Q6_K, Q.Q6_K), "q8_0": (oracle.Q8_0, Q.Q8_0),
             "iq2_xxs": (oracle.IQ2_XXS, Q.IQ2_XXS), "iq2_xs": (oracle.IQ2_XS, Q.IQ2_XS),
             "iq2_s": (oracle.IQ2_S, Q.IQ2_S), "iq3_xxs": (oracle.IQ3_XXS, Q.IQ3_XXS),
-            "iq3_s": (oracle.IQ3_S, Q.IQ3_S)}
+            "iq3_s": (oracle.IQ3_S, Q.IQ3_S), "q4_0": (oracle.Q4_0, Q.Q4_0), "q4_1": (oracle.Q4_1, Q.Q4_1),
+            "q5_0": (oracle.Q5_0, Q.Q5_0), "q5_1": (oracle.Q5_1, Q.Q5_1), "q2_k": (oracle.Q2_K, Q.Q2_K),
+            "q3_k": (oracle.Q3_K, Q.Q3_K), "q5_k": (oracle.Q5_K, Q.Q5_K), "iq4_nl": (oracle.IQ4_NL, Q.IQ4_NL),
+            "iq4_xs": (oracle.IQ4_XS, Q.IQ4_XS)}
     out = {}
     m, n = 16, 512
     for i, (name, (t, qt)) in enumerate(fmts.items()):

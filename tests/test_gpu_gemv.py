@@ -296,3 +296,18 @@ def test_kquant_tensor_core_reference_pattern(engine, t):
     exact = (X @ W.T).reshape(-1)
     scale = (np.abs(X) @ np.abs(W).T).reshape(-1)
     assert np.all(np.abs(got - exact) <= 1e-3 + scale * 2.0 ** -18)
+
+
+def test_golden_fixtures_on_gpu(engine):
+    """The committed golden vectors (tests/golden/make_golden.py): every format's CUDA GEMV
+    against the oracle's pinned output and the gguf-py float64 product."""
+    import os
+
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden.npz"))
+    names = sorted(k[:-2] for k in g.files if k.endswith("_w"))
+    assert len(names) == 17
+    for name in names:
+        t, m, n = (int(v) for v in g[name + "_meta"])
+        got = engine.ggml_gemv_dispatch(t, m, n, g[name + "_w"], g[name + "_x"])
+        assert_parity(g[name + "_y"], got, what=f"golden {name}")
+        assert_parity(g[name + "_y64"], got, what=f"golden {name} vs f64")

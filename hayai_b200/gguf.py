@@ -131,7 +131,12 @@ class GgufFile:
             if size < 24:
                 raise GgufError("truncated GGUF header")
             mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
-        g = cls._parse(str(path), memoryview(mm))
+        try:
+            with memoryview(mm) as view:
+                g = cls._parse(str(path), view)
+        except BaseException:
+            mm.close()
+            raise
         g._map = mm
         return g
 
@@ -221,6 +226,11 @@ class GgufFile:
         return g, u, d, norm
 
     def close(self) -> None:
+        """Unmap the file.  While arrays returned by ``tensor_bytes`` are alive the mapping
+        stays open (it is released when the last of them goes)."""
         if self._map is not None:
-            self._map.close()
+            try:
+                self._map.close()
+            except BufferError:
+                pass
             self._map = None

@@ -23,7 +23,8 @@ LIBDIR = os.path.join(PKG, "lib")
 CUDA_LIB = os.path.join(LIBDIR, "libhayai_cuda.so")
 ORACLE_DIR = os.path.join(ROOT, "oracle")
 ORACLE_LIB = os.path.join(ORACLE_DIR, "_build", "liboracle.so")
-REFERENCE = os.environ.get("HAYAI_REFERENCE", "/root/reference")
+# the reference checkout (read for its format tables at build time): beside the repository
+REFERENCE = os.environ.get("HAYAI_REFERENCE", os.path.join(os.path.dirname(ROOT), "reference"))
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -227,7 +227,7 @@ int hc_moe_ffn_dev(hc_engine* eng, const float* router_w, size_t n_expert, size_
                    const hc_weights* const* down, const float* x, size_t n_tok, float* y, int32_t* ids_out,
                    float* w_out);
 
-/* Expert-parallel MoE FFN (SURVEY config 4 sharding): this rank holds experts
+/* Expert-parallel MoE FFN (the Qwen3-30B-A3B sharding): this rank holds experts
  * [expert_lo, expert_lo + n_local) (gate/up/down arrays of n_local handles); router_w
  * covers all n_expert experts and x [n_tok][d_model] is replicated, so every rank routes
  * identically.  Each rank computes the (token, slot) pairs routed to its experts and stores

@@ -584,8 +584,10 @@ def run_ours(args):
     if tp and kin != dm:
         raise SystemExit("--tp runs the stack of an unpadded model")
     ffl = ff // world if tp else ff  # this rank's d_ff
-    # the persistent stack kernel serves batch 1 when the FFN input width equals d_model
-    uses_stack = B == 1 and kin == dm and (tp or os.environ.get("HAYAI_STACK_KERNEL", "1") != "0")
+    # the persistent stack kernel serves batch 1 when the FFN input width is d_model (or d_model
+    # zero-padded to whole super-blocks)
+    padded_ok = kin == dm or (c["tg"] != Q8_0 and kin == -(-dm // 256) * 256)
+    uses_stack = B == 1 and padded_ok and (tp or os.environ.get("HAYAI_STACK_KERNEL", "1") != "0")
     if tp and args.tp_impl == "nccl":
         uses_stack = False
 

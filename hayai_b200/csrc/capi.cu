@@ -842,7 +842,10 @@ static int stack_try_kernel(hc_engine* e, const StackArgs& s, float* x, size_t n
     const int ta = g0->type, td = d0->type;
     if (!tiled_type(ta) || !tiled_type(td)) return HC_OK;
     const size_t dm = d0->m, ff = g0->m;
-    if (g0->n != dm) return HC_OK;
+    // gate/up inputs: d_model, or d_model zero-padded to whole super-blocks (SmolLM's 576 ->
+    // 768 for Q4_K); the kernel's prologue pads the fragment table to whole blocks with zeros
+    // and touches only the first d_model entries of x
+    if (g0->n != dm && !(ta != T_Q8_0 && g0->n == (dm + 255) / 256 * 256)) return HC_OK;
     for (size_t l = 0; l < s.L; ++l)
         if (s.g[l]->type != ta || s.u[l]->type != ta || s.d[l]->type != td || s.g[l]->m != ff || s.d[l]->n != ff)
             return HC_OK;

@@ -74,6 +74,11 @@ for _name, (_t, _qk, _bs) in GEMV_FORMATS.items():
     BLK.setdefault(_t, (_qk, _bs))
     CONFIGS["gemv-" + _name] = dict(gemv=True, t=_t, m=14336, k=4096,
                                     workload=f"single {_name} GEMV, Llama-3-8B gate shape 14336 x 4096, batch 1")
+# The toy LUT-Q4 matmul of the reference's `hayai bench` (crates/hayai-cli/src/main.rs:601-646):
+# SmolLM-135M FFN shape 1536 x 576, weights 0xAB, x = 1, a fixed 16-entry LUT.
+CONFIGS["lut-q4"] = dict(lut=True, m=1536, n=576,
+                         workload="toy LUT-Q4 matmul of `hayai bench`: 1536 x 576, weights 0xAB, x = 1")
+LUT16 = [-0.5, -0.4, -0.3, -0.2, -0.1, 0.0, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 1.0]
 # f16 scale offsets and typical |value| / d of random codes (random valid blocks for the formats
 # without a quantizer here), and (offset, multiple of d) of a min field that centres the values
 _RAND_D_AT = {2: (0,), 3: (0,), 6: (0,), 7: (0,), 10: (80,), 11: (108,), 13: (0,), 16: (0,), 17: (0,), 18: (0,),
@@ -282,9 +287,9 @@ def run_reference(args):
     c = dict(CONFIGS[args.config])
     if "n_expert" in c:
         return run_reference_moe(args, c, world)
-    if c.get("gemv"):
+    if c.get("gemv") or c.get("lut"):
         print(json.dumps({"impl": "reference", "unavailable": "the reference arm is timed on the FFN configs; "
-                          "the GEMV configs carry the oracle's CPU baseline in their own line"}))
+                          "the GEMV and LUT configs carry the oracle's CPU baseline in their own line"}))
         return 0
     if args.layers:
         c["layers"] = args.layers
@@ -939,6 +944,122 @@ def run_gemv(args):
     return 0
 
 
+def run_lut(args):
+    """The `hayai bench` LUT-Q4 matmul.  value: device-timed, rotating copies past L2 (the HBM
+    figure); e2e: the reference's own bench loop, one host-buffer call per step on the same
+    442 KB of weights (cache-resident, as in the reference), also reported as GFLOP/s."""
+    import numpy as np
+    import torch
+
+    import hayai_b200 as hb
+
+    c = CONFIGS[args.config]
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    M, N = c["m"], c["n"]
+    wbytes = M * N // 2
+    copies = -(-400_000_000 // wbytes)
+    eng = hb.CudaEngine(local)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    eng.set_stream(stream)
+    W = torch.full((copies, wbytes), 0xAB, dtype=torch.uint8, device=dev)
+    lut = torch.tensor(LUT16, dtype=torch.float32, device=dev)
+    x = torch.ones(N, dtype=torch.float32, device=dev)
+    y = torch.empty(M, dtype=torch.float32, device=dev)
+    for i in range(max(args.warmup, 3)):
+        eng.lut_matmul_q4_dev(M, N, W[i % copies], lut, x, y)
+    torch.cuda.synchronize(dev)
+    # a launch from Python takes longer than the kernel: the device figure replays the
+    # launches from a CUDA graph (per_graph launches over rotating copies)
+    per_graph = min(args.steps, 100)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(per_graph):
+            eng.lut_matmul_q4_dev(M, N, W[i % copies], lut, x, y)
+    reps = max(1, args.steps // per_graph)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    eng.sync()
+    launches = reps * per_graph
+    t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
+    value = world * launches * wbytes / t_dev / 1e9
+    wh = np.full(wbytes, 0xAB, np.uint8)
+    lh, xh = np.asarray(LUT16, np.float32), np.ones(N, np.float32)
+    for _ in range(5):
+        yh = eng.lut_matmul_q4(M, N, wh, lh, xh)
+    n_e2e = 500
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(n_e2e):
+        yh = eng.lut_matmul_q4(M, N, wh, lh, xh)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
+    assert np.isfinite(yh).all()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        done, t0 = 0, time.perf_counter()
+        while True:
+            oracle.lut_matmul_q4(M, N, wh, lh, xh)
+            done += 1
+            el = time.perf_counter() - t0
+            if el >= min(args.cpu_seconds, 5.0) and done >= 2:
+                break
+        cpu = {"value": round(done * wbytes / el / 1e9, 3), "unit": "GB/s", "cores": oracle.get_threads(),
+               "kind": "port", "gflops": round(done * 2 * M * N / el / 1e9, 3),
+               "sample": f"{done} calls of the C restatement of cpu_lut_matmul_q4, {el:.1f} s"}
+    peak, peak_kind = measured_peak()
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": launches,
+                "warmup": args.warmup, "ms_per_step": round(t_dev / launches * 1e3, 5), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "lut-q4/f32",
+                "data": "synthetic (the reference bench's constant weights, LUT and input)",
+                "config": {"workload": c["workload"], "m": M, "n": N, "copies": copies,
+                           "l2": f"inputs larger than L2 ({copies} copies of {wbytes / 1e3:.0f} KB rotated)"},
+                "roofline": {"bound": "hbm", "kernel": "lut_q4_kernel (one launch)", "achieved": round(value / world, 1),
+                             "peak": peak, "unit": "GB/s", "frac": round(value / world / peak, 4),
+                             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy burst)",
+                             "traffic": None, "algorithmic_bytes_per_launch": wbytes,
+                             "avg_launch_us": round(t_dev / launches * 1e6, 2), "gflops": round(
+                                 world * launches * 2 * M * N / t_dev / 1e9, 2)},
+                "e2e": {"value": round(world * n_e2e * wbytes / t_e2e / 1e9, 2), "unit": "GB/s", "steps": n_e2e,
+                        "gflops": round(world * n_e2e * 2 * M * N / t_e2e / 1e9, 2),
+                        "h2d_bytes_per_step": wbytes + 16 * 4 + N * 4, "d2h_bytes_per_step": M * 4,
+                        "api": "hc_lut_matmul_q4 (host buffers, as the reference bench calls execute_lut_matmul)"},
+                "clocks": clocks, "gpu_launches": launches, "timing": "CUDA graph replay of the launches"}
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line))
+    del graph, W
+    eng.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -961,6 +1082,8 @@ def main():
         return run_moe(args)
     if CONFIGS[args.config].get("gemv"):
         return run_gemv(args)
+    if CONFIGS[args.config].get("lut"):
+        return run_lut(args)
     return run_ours(args)
 
 

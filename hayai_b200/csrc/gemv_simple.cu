@@ -450,19 +450,37 @@ cudaError_t launch_gemv_simple(int type, const uint8_t* w, size_t row_bytes, int
 // the 16-entry LUT lives in shared memory.
 __global__ void __launch_bounds__(256) lut_q4_kernel(const uint8_t* __restrict__ w, int M, int N,
                                                       const float* __restrict__ lut16, const float* __restrict__ x,
-                                                      float* __restrict__ y) {
+                                                      float* __restrict__ y, bool stage_x, bool words) {
     __shared__ float lut[16];
+    extern __shared__ __align__(16) float xs[];  // x, when staged (N floats)
     if (threadIdx.x < 16) lut[threadIdx.x] = lut16[threadIdx.x];
+    if (stage_x)
+        for (int i = threadIdx.x; i < N; i += blockDim.x) xs[i] = __ldg(x + i);
     __syncthreads();
+    const float* xv = stage_x ? xs : x;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
     const int pc = N / 2;
     for (int row = warp; row < M; row += nwarps) {
         const uint8_t* wr = w + (size_t)row * pc;
         float s = 0.f;
-        for (int c = lane; c < pc; c += 32) {
-            const uint32_t b = __ldg(wr + c);
-            s += __ldg(x + 2 * c) * lut[b & 15] + __ldg(x + 2 * c + 1) * lut[b >> 4];
+        if (words) {
+            // 4 bytes (8 codes) per lane and step: byte k of word c holds elements 8c + 2k (low
+            // nibble) and 8c + 2k + 1 (high nibble); x comes from shared memory
+            const uint32_t* w4 = reinterpret_cast<const uint32_t*>(wr);
+            for (int c = lane; c < pc / 4; c += 32) {
+                const uint32_t b = __ldg(w4 + c);
+                const float4 xa = *reinterpret_cast<const float4*>(xv + 8 * c);
+                const float4 xb = *reinterpret_cast<const float4*>(xv + 8 * c + 4);
+                s += xa.x * lut[b & 15] + xa.y * lut[(b >> 4) & 15] + xa.z * lut[(b >> 8) & 15] +
+                     xa.w * lut[(b >> 12) & 15] + xb.x * lut[(b >> 16) & 15] + xb.y * lut[(b >> 20) & 15] +
+                     xb.z * lut[(b >> 24) & 15] + xb.w * lut[b >> 28];
+            }
+        } else {
+            for (int c = lane; c < pc; c += 32) {
+                const uint32_t b = __ldg(wr + c);
+                s += xv[2 * c] * lut[b & 15] + xv[2 * c + 1] * lut[b >> 4];
+            }
         }
         s = warp_sum(s);
         if (lane == 0) y[row] = s;
@@ -471,7 +489,11 @@ __global__ void __launch_bounds__(256) lut_q4_kernel(const uint8_t* __restrict__
 
 cudaError_t launch_lut_matmul_q4(const uint8_t* w, int M, int N, const float* lut16, const float* x, float* y,
                                  cudaStream_t stream) {
-    lut_q4_kernel<<<grid_for(M), 256, 0, stream>>>(w, M, N, lut16, x, y);
+    // x is staged in shared memory when it fits the default 48 KB; the word path needs whole
+    // 4-byte words per row (N a multiple of 8) on 4-byte aligned weights
+    const bool stage_x = (size_t)N * 4 <= 48 * 1024;
+    const bool words = stage_x && N % 8 == 0 && (reinterpret_cast<uintptr_t>(w) & 3) == 0;
+    lut_q4_kernel<<<grid_for(M), 256, stage_x ? (size_t)N * 4 : 0, stream>>>(w, M, N, lut16, x, y, stage_x, words);
     return cudaGetLastError();
 }
 

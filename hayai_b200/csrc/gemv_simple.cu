@@ -327,9 +327,8 @@ __device__ __forceinline__ float group_dot4(const uint8_t* blk, int ib32, int e,
 // (<= kGroupSeg bytes) in its shared-memory buffer with coalesced 16-byte loads (the raw GGUF
 // rows are byte-aligned only; the copy starts at the 16-byte boundary below the segment and
 // may read up to 15 bytes past the row, inside the 16 bytes of padding every weight allocation
-// carries), then decodes it: 8 lanes per 32-element block, 4 elements each, or 4 lanes per
-// 32-element group of a super-block, 8 elements each (QK elements and BLK bytes per block,
-// QK / 32 groups per block).  One lane per group made every
+// carries), then decodes it with 4 lanes per 32-element group, 8 elements each (QK elements
+// and BLK bytes per block, QK / 32 groups per block).  One lane per group made every
 // activation load instruction touch 32 cache lines and ran at 0.04-0.09 of the HBM peak.
 constexpr int kGroupSeg = 4096;
 
@@ -369,12 +368,14 @@ __global__ void __launch_bounds__(256, 4) gemv_group_kernel(const uint8_t* __res
                     s += group_dot4<TYPE>(sb + b * BLK, ib32, e, xa) + group_dot4<TYPE>(sb + b * BLK, ib32, e + 4, xb);
                 }
             } else {
-                // 32-element blocks: 8 lanes per block, 4 elements each (measured faster here);
-                // lanes 8g..8g+7 read the block's 128 contiguous bytes of x
-                for (int gi = lane >> 3; gi < nbs * G; gi += 4) {
-                    const int b = gi / G, ib32 = gi % G, e = 4 * (lane & 7);
-                    const float4 x4 = __ldg(reinterpret_cast<const float4*>(xv + (size_t)(b0 + b) * QK + 32 * ib32 + e));
-                    s += group_dot4<TYPE>(sb + b * BLK, ib32, e, x4);
+                // 32-element blocks: 4 lanes per block, 8 elements each, elements e..e+3 and
+                // e+16..e+19 (the low and high nibbles of the same 4 bytes, read once)
+                for (int gi = lane >> 2; gi < nbs * G; gi += 8) {
+                    const int b = gi / G, ib32 = gi % G, e = 4 * (lane & 3);
+                    const float* xp = xv + (size_t)(b0 + b) * QK + 32 * ib32 + e;
+                    const float4 xa = __ldg(reinterpret_cast<const float4*>(xp));
+                    const float4 xb = __ldg(reinterpret_cast<const float4*>(xp + 16));
+                    s += group_dot4<TYPE>(sb + b * BLK, ib32, e, xa) + group_dot4<TYPE>(sb + b * BLK, ib32, e + 16, xb);
                 }
             }
         }

@@ -65,6 +65,7 @@ SIGNATURES: dict[str, list] = {
     "hc_peer_open": [_P, _I, _I, _S, _P],
     "hc_peer_connect": [_P, _P],
     "hc_peer_close": [_P],
+    "hc_peer_region": [_P, _P, _P],
     "hc_route_experts_dev": [_P, _P, _P, _S, _S, _S, _S, _S, _I, _I, _F, _P, _P],
     "hc_router_scores_dev": [_P, _P, _S, _S, _P, _S, _P],
     "hc_moe_ffn_dev": [_P, _P, _S, _S, _I, _F, _P, _P, _P, _P, _S, _P, _P, _P],

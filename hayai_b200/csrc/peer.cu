@@ -93,6 +93,16 @@ extern "C" int hc_peer_close(hc_engine* e) {
     return HC_OK;
 }
 
+extern "C" int hc_peer_region(hc_engine* e, void** region, size_t* bytes) {
+    int rc = hc_engine_activate(e);
+    if (rc) return rc;
+    if (!region || !bytes) return hc_set_error(HC_ERR_INVALID, "null argument");
+    if (!e->peer.region) return hc_set_error(HC_ERR_INVALID, "peer group not opened");
+    *region = e->peer.region;
+    *bytes = e->peer.bytes;
+    return HC_OK;
+}
+
 extern "C" int hc_peer_handle_bytes(size_t* out) {
     if (!out) return hc_set_error(HC_ERR_INVALID, "null argument");
     *out = sizeof(cudaIpcMemHandle_t);

@@ -334,6 +334,12 @@ class CudaEngine:
     def peer_close(self) -> None:
         _check(lib().hc_peer_close(self.handle))
 
+    def peer_region(self) -> tuple[int, int]:
+        """(device address, bytes) of this rank's exchange region."""
+        p, n = ctypes.c_void_p(), ctypes.c_size_t()
+        _check(lib().hc_peer_region(self.handle, ctypes.byref(p), ctypes.byref(n)))
+        return p.value, n.value
+
     def ffn_stack_tp_dev(self, gates, ups, downs, x, nvec: int = 1, norms=None, eps: float = 1e-5) -> None:
         """Tensor-parallel stack over this rank's d_ff shard; x [nvec][d_model] replicated, in place."""
         _check(lib().hc_ffn_stack_tp_dev(self.handle, _handles(gates), _handles(ups), _handles(downs),

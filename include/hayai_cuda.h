@@ -190,6 +190,9 @@ int hc_peer_handle_bytes(size_t* out);
 int hc_peer_open(hc_engine* eng, int rank, int world, size_t bytes, void* handle_out);
 int hc_peer_connect(hc_engine* eng, const void* handles);
 int hc_peer_close(hc_engine* eng);
+/* This rank's exchange region (device address and size) for diagnostics: its layout holds
+ * the exchange counters and epochs.  No reference counterpart. */
+int hc_peer_region(hc_engine* eng, void** region, size_t* bytes);
 
 /* Tensor-parallel FFN stack, the config-5 sharding of Llama-3-70B: rank p holds gate/up rows
  * and down columns [p*F/P, (p+1)*F/P) of every layer (F = d_ff, column shards whole

@@ -281,3 +281,49 @@ def test_ep_moe_two_gpus(tmp_path):
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     mp.spawn(_gpu_ep_rank, args=(2, port, (16, 4, 8, 2048, 768), str(res)), nprocs=2, join=True)
     assert res.read_text() == "ok"
+
+
+# ---------------------------------------------------------------- failure detection
+@pytest.mark.gpu
+def test_exchange_wait_expires_and_engine_recovers(engine):
+    """A rank whose peers never signal: the exchange's wait is bounded (about a second), the
+    call reports HC_ERR_TIMEOUT, and the engine keeps working.  A one-rank group whose device
+    epoch is moved ahead of its counter stands in for a peer that never arrives (a counter
+    that nothing will raise); no GPU fault is involved."""
+    import time
+
+    from cuda.bindings import runtime as rt
+
+    import hayai_b200 as hb
+    from hayai_b200 import _lib
+
+    tg, td, dm, ff, nvec = oracle.Q4_K, oracle.Q6_K, 1024, 2048, 16
+    g, u, d = quantized(tg, ff, dm, 301), quantized(tg, ff, dm, 302), quantized(td, dm, ff, 303)
+    nw = oracle.normal(304, dm, 1.0, 0.1)
+    G, U, D = [engine.upload(tg, ff, dm, g)], [engine.upload(tg, ff, dm, u)], [engine.upload(td, dm, ff, d)]
+    N = [torch.from_numpy(nw).cuda()]
+    X = oracle.normal(305, nvec * dm).reshape(nvec, dm)
+    engine.peer_connect([engine.peer_open(0, 1)])
+    try:
+        got = engine.ffn_stack_tp(G, U, D, X.reshape(-1), nvec, norms=N, eps=EPS).reshape(nvec, dm)
+        for v in (0, nvec - 1):
+            assert_parity(_oracle_stack([(g, u, d)], [nw], tg, td, dm, ff, X[v]), got[v], what=f"one-rank tp row {v}")
+        region, _ = engine.peer_region()
+        epoch = np.zeros(1, np.uint32)
+        kind = rt.cudaMemcpyKind
+        assert rt.cudaMemcpy(epoch.ctypes.data, region + 512, 4, kind.cudaMemcpyDeviceToHost)[0] == \
+            rt.cudaError_t.cudaSuccess
+        assert epoch[0] == 1  # one exchange so far
+        epoch[0] += 5  # the next exchange now waits for signals that never come
+        assert rt.cudaMemcpy(region + 512, epoch.ctypes.data, 4, kind.cudaMemcpyHostToDevice)[0] == \
+            rt.cudaError_t.cudaSuccess
+        t0 = time.time()
+        with pytest.raises(hb.CudaError) as e:
+            engine.ffn_stack_tp(G, U, D, X.reshape(-1), nvec, norms=N, eps=EPS)
+        assert e.value.code == _lib.HC_ERR_TIMEOUT
+        assert time.time() - t0 < 30
+    finally:
+        engine.peer_close()
+    # the context is intact: the same weights still give the oracle's answer
+    x = X[0].copy()
+    assert_parity(oracle.gemv(tg, ff, dm, g, x), engine.ggml_gemv_dispatch_bound(G[0], x), what="after timeout")

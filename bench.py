@@ -5,7 +5,8 @@ and FFN tokens/s).
 Default workload: Llama-3-8B-shaped FFN stack, 32 layers resident
 in HBM, gate/up Q4_K, down Q6_K, batch-1 decode, x <- x + FFN_l(rms_norm(x)).  One step = one
 token through all 32 layers: at batch 1 the whole stack is ONE persistent kernel launch
-(ffn_stack.cu), otherwise two GEMV launches per layer.  Weights are seeded N(0, 0.02^2)
+(ffn_stack.cu), otherwise the per-layer kernels as one CUDA graph (two GEMV launches per layer,
+six on the tcgen05 batch path).  Weights are seeded N(0, 0.02^2)
 quantized on the device with the reference's Q4_K quantizer (and this project's Q6_K
 quantizer); activations N(0, 1).  --layers N shrinks the stack (a small case for profilers).
 
@@ -13,7 +14,9 @@ quantizer); activations N(0, 1).  --layers N shrinks the stack (a small case for
 
 Multi-GPU (torchrun, one rank per GPU): configs 1-3 do not shard, so every rank runs an
 independent replica ("weak" scaling, no collective on the data path); value = all ranks'
-bytes / max-over-ranks time.
+bytes / max-over-ranks time.  --tp (llama70b) and --ep (qwen3moe) shard the model instead.
+
+Other workloads: --config smollm | llama8b-q8 | llama70b | qwen3moe | lut-q4 | gemv-<format>.
 
 --impl reference times the reference's CPU implementation of the path (the C restatement
 in oracle/, the Rust reference cannot be built here) on this host's cores, on a bounded

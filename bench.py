@@ -1072,7 +1072,7 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="llama8b")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=0, help="override the config's layer count (small profiling case)")
-    ap.add_argument("--tp", action="store_true", help="tensor-parallel d_ff split over the ranks (batch 1)")
+    ap.add_argument("--tp", action="store_true", help="tensor-parallel d_ff split over the ranks (any --batch)")
     ap.add_argument("--tp-impl", choices=["ours", "nccl"], default="ours",
                     help="exchange of the down partials: in-kernel NVLink stores, or NCCL all_reduce per layer")
     ap.add_argument("--ep", action="store_true", help="expert-parallel MoE over the ranks (qwen3moe)")

@@ -136,3 +136,33 @@ def test_ffn_stack_from_gguf_file(tmp_path, engine):
         xn = oracle.rms_norm(ref, nw, EPS)
         ref = (ref + oracle.ffn_swiglu(oracle.Q4_K, g, oracle.Q4_K, u, oracle.Q6_K, d, dm, ff, dm, xn)).astype(np.float32)
     assert_parity(ref, got, what="stack loaded from GGUF")
+
+
+def test_metadata_value_types(tmp_path):
+    """Every metadata value type the reference reads (gguf.rs:633-672): scalars, bool, string,
+    and (nested) arrays, as gguf-py writes them."""
+    gguf = pytest.importorskip("gguf")
+    p = tmp_path / "meta.gguf"
+    w = gguf.GGUFWriter(str(p), "llama")
+    w.add_uint32("t.u32", 7)
+    w.add_int32("t.i32", -3)
+    w.add_float32("t.f32", 0.25)
+    w.add_uint64("t.u64", 1 << 40)
+    w.add_bool("t.bool", True)
+    w.add_string("t.str", "héllo")
+    w.add_array("t.arr", [1, 2, 3])
+    w.add_array("t.strs", ["a", "bc"])
+    w.add_tensor("x", np.arange(8, dtype=np.float32))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    g = hg.GgufFile.open(p)
+    try:
+        m = g.metadata
+        assert (m["t.u32"], m["t.i32"], m["t.f32"], m["t.u64"], m["t.bool"]) == (7, -3, 0.25, 1 << 40, True)
+        assert m["t.str"] == "héllo"
+        assert m["t.arr"] == [1, 2, 3] and m["t.strs"] == ["a", "bc"]
+        assert np.array_equal(g.f32("x"), np.arange(8, dtype=np.float32))
+    finally:
+        g.close()

@@ -83,6 +83,38 @@ def _cpu_rank(rank, world, port, case):
         dist.destroy_process_group()
 
 
+def _cpu_rank_batch(rank, world, port, nvec):
+    """The batched exchange's semantics: every row's partial down outputs, summed over the ranks
+    in rank order and added to the replicated residual, reproduce the unsharded stack layer."""
+    dist = _init(rank, world, port)
+    try:
+        tg, td, dm, ff = oracle.Q4_K, oracle.Q6_K, 512, 2048
+        wg, wu, wd = quantized(tg, ff, dm, 41), quantized(tg, ff, dm, 42), quantized(td, dm, ff, 43)
+        nw = oracle.normal(44, dm, 1.0, 0.1)
+        X = oracle.normal(45, nvec * dm).reshape(nvec, dm)
+        g, ffl = tpmod.shard_rows(wg, tg, ff, dm, rank, world)
+        u, _ = tpmod.shard_rows(wu, tg, ff, dm, rank, world)
+        d, _ = tpmod.shard_cols(wd, td, dm, ff, rank, world)
+        parts = []
+        for v in range(nvec):
+            xn = oracle.rms_norm(X[v], nw, EPS)
+            h = oracle.swiglu(oracle.gemv(tg, ffl, dm, g, xn), oracle.gemv(tg, ffl, dm, u, xn))
+            parts.append(oracle.gemv(td, dm, ffl, d, h))
+        gathered = [None] * world
+        dist.all_gather_object(gathered, np.stack(parts))
+        got = (X + tpmod.tp_partial_sum(gathered)).astype(np.float32)
+        for v in range(nvec):
+            ref = _oracle_stack([(wg, wu, wd)], [nw], tg, td, dm, ff, X[v])
+            assert_parity(ref, got[v], what=f"tp{world} batch row {v} rank {rank}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_batched_exchange_two_ranks_gloo():
+    port = _free_port()
+    mp.spawn(_cpu_rank_batch, args=(2, port, 3), nprocs=2, join=True)
+
+
 def test_tp_sharding_two_ranks_gloo():
     port = _free_port()
     mp.spawn(_cpu_rank, args=(2, port, (oracle.Q4_K, oracle.Q6_K, 512, 2048)), nprocs=2, join=True)

@@ -166,3 +166,42 @@ def test_metadata_value_types(tmp_path):
         assert np.array_equal(g.f32("x"), np.arange(8, dtype=np.float32))
     finally:
         g.close()
+
+
+def test_parser_rejects_arbitrary_bytes_cleanly(tmp_path):
+    """Truncations and byte flips of a valid file: the parser either succeeds or raises
+    GgufError, never another exception (the reference's hostile-input guards, gguf.rs:39-48)."""
+    hyp = pytest.importorskip("hypothesis")
+    from hypothesis import HealthCheck, given, settings
+    from hypothesis import strategies as st
+
+    src = tmp_path / "ok.gguf"
+    write_gguf(src, {"blk.0.ffn_gate.weight": (oracle.Q4_K, 256, 16, quantized(oracle.Q4_K, 16, 256, 9)),
+                     "blk.0.ffn_norm.weight": (oracle.F32, 256, 1, oracle.normal(10, 256))}, {"llama.block_count": 1})
+    good = src.read_bytes()
+    bad = tmp_path / "fuzz.gguf"
+
+    @settings(max_examples=300, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+    @given(cut=st.integers(0, len(good)), flips=st.lists(st.tuples(st.integers(0, len(good) - 1),
+                                                                   st.integers(0, 255)), max_size=6))
+    def check(cut, flips):
+        b = bytearray(good[:max(cut, 0)])
+        for pos, val in flips:
+            if pos < len(b):
+                b[pos] = val
+        bad.write_bytes(bytes(b))
+        try:
+            g = hg.GgufFile.open(bad)
+        except hg.GgufError:
+            return
+        try:
+            for t in g.tensors:
+                try:
+                    g.tensor_bytes(t)
+                except hg.GgufError:
+                    pass
+        finally:
+            g.close()
+
+    assert hyp is not None
+    check()

@@ -217,3 +217,32 @@ def test_golden_vectors_match_independent_decoder():
         name = key[:-4]
         y, y64 = g[name + "_y"].astype(np.float64), g[key]
         assert np.linalg.norm(y - y64) / np.linalg.norm(y64) < 1e-5, name
+
+
+def test_dequant_matches_gguf_py_on_arbitrary_blocks():
+    """Any bytes are a valid block of these formats (scales and codes are bit fields): the
+    oracle's decoders agree with gguf-py bit for bit on arbitrary blocks, not only on the seeded
+    ones.  Blocks whose f16 scales are inf/NaN are skipped (both sides give non-finite values)."""
+    gguf = pytest.importorskip("gguf")
+    hyp = pytest.importorskip("hypothesis")
+    from gguf.quants import dequantize
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    types = [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, *IQ_TYPES, *BLOCK_TYPES]
+
+    @settings(max_examples=200, deadline=None)
+    @given(t=st.sampled_from(types), data=st.data())
+    def check(t, data):
+        qk, bs = oracle.BLOCK[t]
+        nblk = data.draw(st.integers(1, 4))
+        raw = np.frombuffer(data.draw(st.binary(min_size=nblk * bs, max_size=nblk * bs)), np.uint8).copy()
+        with np.errstate(all="ignore"):
+            ref = dequantize(raw.reshape(-1, bs), gguf.GGMLQuantizationType(t)).reshape(-1).astype(np.float32)
+        if not np.isfinite(ref).all():
+            return
+        got = oracle.dequant(t, raw, nblk * qk)
+        assert np.array_equal(ref, got), t
+
+    assert hyp is not None
+    check()

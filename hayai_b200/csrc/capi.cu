@@ -390,8 +390,10 @@ extern "C" int hc_weights_free(hc_weights* w) {
     if (!w) return HC_OK;
     int cur = -1;
     cudaGetDevice(&cur);
-    if (cur != w->device) cudaSetDevice(w->device);
+    const bool other = cur != w->device;
+    if (other) cudaSetDevice(w->device);
     cudaFree(w->dev);
+    if (other && cur >= 0) cudaSetDevice(cur);  // leave the caller's device current
     delete w;
     return HC_OK;
 }

@@ -25,8 +25,9 @@ constexpr size_t kPeerEpBar = 128;                // u32: cross-GPU counter of t
 constexpr size_t kPeerEpEpoch = 256;              // u32: EP MoE phases this rank has signalled (local)
 constexpr size_t kPeerTpParts = 4096;             // TP stack: down partials [2][d_model/16][parts][16] f32
 constexpr size_t kPeerTpPartsBytes = 4u << 20;    // d_model x parts (<= 8) x 2 buffers x 4 B up to 65536 x 8
-constexpr size_t kPeerEpData = kPeerTpParts + kPeerTpPartsBytes;  // EP MoE exchange data
-constexpr size_t kPeerRegionMin = kPeerEpData + (4u << 20);
+constexpr size_t kPeerEpData = kPeerTpParts + kPeerTpPartsBytes;  // EP MoE exchange data [2][T*k][d_model] f32
+constexpr size_t kPeerEpDataBytes = 24u << 20;    // e.g. 2 x 384 routed rows x 8192 x 4 B
+constexpr size_t kPeerRegionMin = kPeerEpData + kPeerEpDataBytes;
 constexpr size_t kPeerTpbBar = 384;             // u32: cross-GPU counter of the batched TP exchange
 constexpr size_t kPeerTpbEpoch = 512;           // u32: batched TP exchanges this rank has completed (local)
 constexpr size_t kPeerTpbDone = 640;            // u32: CTAs of the running exchange that finished (local)

@@ -1058,9 +1058,13 @@ static int moe_run(hc_engine* e, const float* router_w, size_t E, size_t k, int 
     PeerState& pe = e->peer;
     if (ep) {
         if (!pe.connected) return hc_set_error(HC_ERR_INVALID, "expert-parallel MoE without a connected peer group");
-        if (pe.bytes < kPeerEpData + 2 * P * dm * 4)
-            return hc_set_error(HC_ERR_INVALID, "expert-parallel MoE: %zu tokens x top-%zu x %zu exceed the exchange region",
-                                T, k, dm);
+        // the EP rows must stay inside their own area: the batched tensor-parallel exchange
+        // owns the bytes after it
+        if (2 * P * dm * 4 > kPeerEpDataBytes || pe.bytes < kPeerEpData + 2 * P * dm * 4)
+            return hc_set_error(HC_ERR_INVALID,
+                                "expert-parallel MoE: %zu tokens x top-%zu x %zu need %zu exchange bytes; the EP area "
+                                "holds %zu",
+                                T, k, dm, 2 * P * dm * 4, (size_t)kPeerEpDataBytes);
     }
     if (T == 0) return HC_OK;
     // workspace: scores [T][E] | ids [P] | w [P] | h [P][ff] | D [P][dm] | segments [P] | count

@@ -9,7 +9,8 @@ dimensions.  The file is memory-mapped; a tensor's bytes are a zero-copy view un
 uploaded (``upload`` / ``load_ffn_layer``).
 
 Validation follows the reference: bad magic, a version outside 1..4, counts larger than the
-file, more than 4 dimensions or a zero dimension, duplicate names, a non-power-of-two
+file, more than 4 dimensions or a zero dimension, an unknown type id, an element count, byte
+size, absolute offset or byte range that overflows u64, duplicate names, a non-power-of-two
 ``general.alignment``, and tensor ranges past the end of the file are errors (``GgufError``).
 """
 from __future__ import annotations
@@ -63,12 +64,23 @@ class TensorInfo:
         return n
 
 
+U64_MAX = (1 << 64) - 1
+
+
 def tensor_nbytes(info: TensorInfo) -> int:
-    """Bytes of a tensor: whole blocks of its type (gguf.rs:240-284)."""
+    """Bytes of a tensor: whole blocks of its type (gguf.rs:240-284).  An element count or a
+    byte size that does not fit in u64 is an error, as the reference's checked arithmetic
+    makes it."""
+    n = info.n_elements
+    if n > U64_MAX:
+        raise GgufError(f"tensor {info.name} element count overflow")
     if info.type_id not in _BLOCKS:
         raise GgufError(f"unsupported ggml type {info.type_id} for tensor {info.name}")
     qk, bs = _BLOCKS[info.type_id]
-    return -(-info.n_elements // qk) * bs
+    nbytes = -(-n // qk) * bs
+    if nbytes > U64_MAX:
+        raise GgufError(f"tensor {info.name} byte size overflow")
+    return nbytes
 
 
 class _Reader:
@@ -168,6 +180,8 @@ class GgufFile:
             if any(d == 0 for d in dims):
                 raise GgufError(f"tensor {name} has a zero dimension")
             info = TensorInfo(name, dims, r.unpack("I"), r.unpack("Q"))
+            # sizes are validated while parsing, so no later computation can overflow (gguf.rs:85-87)
+            tensor_nbytes(info)
             if name in index:
                 raise GgufError(f"duplicate tensor name {name}")
             index[name] = i
@@ -176,6 +190,13 @@ class GgufFile:
         if not isinstance(alignment, int) or alignment <= 0 or alignment & (alignment - 1):
             raise GgufError(f"invalid general.alignment {alignment} (must be a non-zero power of two)")
         data_offset = -(-r.pos // alignment) * alignment
+        # no absolute offset or byte range may wrap u64 (gguf.rs:105-115)
+        for t in tensors:
+            start = data_offset + t.offset
+            if start > U64_MAX:
+                raise GgufError(f"tensor {t.name} absolute offset overflow")
+            if start + tensor_nbytes(t) > U64_MAX:
+                raise GgufError(f"tensor {t.name} byte range overflow")
         g = cls(path, version, alignment, metadata, tensors, data_offset)
         g._index = index
         return g

@@ -89,6 +89,12 @@ def _tensor_entry(name, dims, t=0, offset=0):
     (_header(n_kv=1, kv=struct.pack("<Q", 17) + b"general.alignment" + struct.pack("<II", 4, 24),
              tensors=_tensor_entry("a", [4])) + b"\0" * 64, "alignment"),
     (_header(tensors=_tensor_entry("a", [1 << 20])) + b"\0" * 64, "out of bounds"),
+    # sizes and ranges are validated while the directory is parsed (gguf.rs:85-115)
+    (_header(tensors=_tensor_entry("a", [4], t=99)) + b"\0" * 64, "unsupported ggml type"),
+    (_header(tensors=_tensor_entry("a", [1 << 40, 1 << 40])) + b"\0" * 64, "element count overflow"),
+    (_header(tensors=_tensor_entry("a", [(1 << 62) + 1], t=0)) + b"\0" * 64, "byte size overflow"),
+    (_header(tensors=_tensor_entry("a", [4], offset=(1 << 64) - 1)) + b"\0" * 64, "absolute offset overflow"),
+    (_header(tensors=_tensor_entry("a", [4], offset=(1 << 64) - 70)) + b"\0" * 64, "byte range overflow"),
     (_header()[:20], "truncated"),
 ])
 def test_rejects_malformed_files(tmp_path, blob, what):

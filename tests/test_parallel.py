@@ -359,3 +359,46 @@ def test_exchange_wait_expires_and_engine_recovers(engine):
     # the context is intact: the same weights still give the oracle's answer
     x = X[0].copy()
     assert_parity(oracle.gemv(tg, ff, dm, g, x), engine.ggml_gemv_dispatch_bound(G[0], x), what="after timeout")
+
+
+@pytest.mark.gpu
+def test_ep_rows_beyond_their_exchange_area_are_rejected(engine):
+    """The expert-parallel MoE exchanges its routed rows through a fixed area of the peer
+    region; the batched tensor-parallel exchange owns the bytes after it.  A call whose rows
+    would not fit (2 x tokens x top-k x d_model x 4 B above the area) is rejected before any
+    launch, and the same one-rank group still runs a call that fits, matching the oracle."""
+    import hayai_b200 as hb
+    from hayai_b200 import _lib
+
+    t, E, k, dm, ff = oracle.Q4_K, 4, 4, 2048, 256
+    g = [quantized(t, ff, dm, 400 + e) for e in range(E)]
+    u = [quantized(t, ff, dm, 410 + e) for e in range(E)]
+    d = [quantized(t, dm, ff, 420 + e) for e in range(E)]
+    G = [engine.upload(t, ff, dm, w) for w in g]
+    U = [engine.upload(t, ff, dm, w) for w in u]
+    D = [engine.upload(t, dm, ff, w) for w in d]
+    r = oracle.normal(430, E * dm, 0.0, 0.02).reshape(E, dm)
+    R = torch.from_numpy(r).cuda()
+    engine.peer_connect([engine.peer_open(0, 1)])
+    try:
+        T = 400  # 1600 routed rows: 2 x 1600 x 2048 x 4 B = 26.2 MB, above the 24 MiB area
+        X = torch.zeros(T, dm, device="cuda")
+        Y = torch.zeros(T, dm, device="cuda")
+        with pytest.raises(hb.CudaError) as e:
+            engine.moe_ffn_ep_dev(R, k, G, U, D, 0, X, Y)
+        assert e.value.code == _lib.HC_ERR_INVALID
+        assert "EP area" in str(e.value)
+        T = 8
+        xh = oracle.normal(431, T * dm).reshape(T, dm)
+        X = torch.from_numpy(xh).cuda()
+        Y = torch.zeros(T, dm, device="cuda")
+        ids = torch.zeros(T, k, dtype=torch.int32, device="cuda")
+        engine.moe_ffn_ep_dev(R, k, G, U, D, 0, X, Y, ids)
+        torch.cuda.synchronize()
+        want, want_ids, _ = oracle.moe_ffn(r, E, k, t, np.stack(g), t, np.stack(u), t, np.stack(d), dm, ff, xh)
+        assert np.array_equal(ids.cpu().numpy(), want_ids)
+        assert_parity(want, Y.cpu().numpy(), what="one-rank EP after the rejection")
+    finally:
+        engine.peer_close()
+        for w in G + U + D:
+            w.free()

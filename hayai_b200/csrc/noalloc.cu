@@ -16,8 +16,6 @@
 // HC_ERR_INVALID before anything is enqueued.  Every call on a device shares the one array
 // and leaves its contents behind, so calls whose kernels overlap on the GPU (two streams,
 // two engines on one device) race on it: serialise them.
-#include <mutex>
-
 #include "engine.h"
 #include "gemv_launch.h"
 #include "gemv_mma.cuh"
@@ -31,23 +29,20 @@ constexpr size_t kScratchCounters = 16384;            // one counter per 16-row 
 // One array: the partial sums, then the tile counters (stored as int).
 static __device__ __align__(256) float g_gemv_scratch[kScratchWsFloats + kScratchCounters];
 
-constexpr int kMaxDevices = 64;
-static std::mutex g_scratch_mu;
-static float* g_scratch_dev[kMaxDevices];  // device address of g_gemv_scratch, per device
-
 // Device address of the scratch array on `dev`, which must be the current device.  Host code
 // only sees a host-side stand-in under the name g_gemv_scratch; the address a kernel may use
-// comes from cudaGetSymbolAddress, looked up once per device and cached.
+// comes from cudaGetSymbolAddress.  It is looked up on every call (a lookup allocates
+// nothing): a cached address would go stale if the device's context were reset and the module
+// loaded again.  The first lookup on a device loads this library's device code there.
 static int scratch_address(int dev, float** out) {
-    if (dev < 0 || dev >= kMaxDevices) return hc_set_error(HC_ERR_INVALID, "device %d out of range", dev);
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_dev[dev]) {
-        void* p = nullptr;
-        cudaError_t ce = cudaGetSymbolAddress(&p, g_gemv_scratch);
-        if (ce != cudaSuccess) return hc_cuda_error(ce, "cudaGetSymbolAddress(static GEMV scratch)");
-        g_scratch_dev[dev] = static_cast<float*>(p);
-    }
-    *out = g_scratch_dev[dev];
+    int cur = -1;
+    cudaError_t ce = cudaGetDevice(&cur);
+    if (ce != cudaSuccess) return hc_cuda_error(ce, "cudaGetDevice");
+    if (cur != dev) return hc_set_error(HC_ERR_INVALID, "device %d is not current (%d is)", dev, cur);
+    void* p = nullptr;
+    ce = cudaGetSymbolAddress(&p, g_gemv_scratch);
+    if (ce != cudaSuccess) return hc_cuda_error(ce, "cudaGetSymbolAddress(static GEMV scratch)");
+    *out = static_cast<float*>(p);
     return HC_OK;
 }
 

@@ -126,9 +126,10 @@ int hc_gemv_dev(hc_engine* eng, const hc_weights* w, const float* x, size_t ldx,
  * stream-K split needs comes from a static device array of the library (4 MiB of partial
  * sums + 16384 tile counters per GPU, held until exit); a matrix that needs more is
  * rejected with HC_ERR_INVALID (every Llama-3 8B/70B FFN matrix and a 128256 x 4096 output
- * projection fit; M above 262144 never does).  The first call on
- * a device looks the array's address up (cudaGetSymbolAddress): make that first call
- * before any stream capture.  All calls on a device share the array, so calls that overlap
+ * projection fit; M above 262144 never does).  Every call looks the array's address up
+ * on the current device (cudaGetSymbolAddress, which allocates nothing); on the first call
+ * on a device that lookup also loads the library's device code there, so make that first
+ * call before any stream capture.  All calls on a device share the array, so calls that overlap
  * on the GPU race: serialise them.  Other formats return HC_ERR_UNSUPPORTED. */
 int hc_gemv_dev_noalloc(hc_engine* eng, const hc_weights* w, const float* x, size_t ldx, float* y, size_t ldy,
                         const float* resid, size_t ldr, size_t nvec);

@@ -3,21 +3,23 @@
 Callers whose device memory belongs to their own pool allocator, or whose decode loop cannot
 absorb a cudaMalloc, use this entry point instead of hc_gemv_dev: its stream-K scratch is a
 static array inside the library.  These tests call both entry points through the C ABI on
-the same resident weights and inputs and require the same results, twice in a row (the
-second call runs on the scratch the first one left behind).
+the same resident weights and inputs and require bit-identical results (the same kernel with
+the same split runs behind both) and parity with the CPU oracle, twice in a row (the second
+call runs on the scratch the first one left behind).
 
 The file name sorts last so that a run stopping at the first failure has run every other
 test before this one; the tests pass alone in a fresh process and after the others.
 """
 import ctypes
 
+import numpy as np
 import pytest
 import torch
 
 import oracle
 from hayai_b200 import _lib
 from hayai_b200._lib import lib
-from tests.helpers import assert_parity
+from tests.helpers import assert_parity, quantized
 
 pytestmark = pytest.mark.gpu
 
@@ -37,24 +39,35 @@ def _call(name, engine, w, x, y, resid, nvec):
     (oracle.Q6_K, 1024, 14336, 1, False),   # FFN-down shape: long rows
     (oracle.Q8_0, 2048, 4096, 3, True),     # several vectors + residual
     (oracle.Q4_K, 14336, 4096, 2, True),    # Llama-3-8B gate/up shape
+    # 9 vectors: three launches of the kernel (4 + 4 + 1 vectors); 1000 rows (not a multiple
+    # of 128) keep hc_gemv_dev off the tcgen05 batch path, so both calls run the same kernel
+    (oracle.Q6_K, 1000, 2048, 9, True),
 ])
-def test_noalloc_matches_gemv_dev_twice(engine, t, m, n, nvec, with_resid):
-    w = engine.synth_weights(t, m, n, seed=101 + t)
-    g = torch.Generator().manual_seed(7 + t)
-    x = torch.randn(nvec, n, generator=g).cuda()
-    resid = torch.randn(nvec, m, generator=g).cuda() if with_resid else None
+def test_noalloc_matches_gemv_dev_and_oracle_twice(engine, t, m, n, nvec, with_resid):
+    raw = quantized(t, m, n, seed=101 + t)
+    w = engine.upload(t, m, n, raw)
+    xh = oracle.normal(7 + t, nvec * n).reshape(nvec, n)
+    rh = oracle.normal(9 + t, nvec * m).reshape(nvec, m) if with_resid else None
+    want = np.stack([oracle.gemv(t, m, n, raw, xh[v]) for v in range(nvec)])
+    if rh is not None:
+        want = want + rh
+    x = torch.from_numpy(xh).cuda()
+    resid = torch.from_numpy(rh).cuda() if rh is not None else None
     stream = torch.cuda.current_stream()
     engine.set_stream(stream)
     try:
         ref = torch.full((nvec, m), float("nan"), device="cuda")
         assert _call("hc_gemv_dev", engine, w, x, ref, resid, nvec) == _lib.HC_OK, lib().hc_last_error()
         torch.cuda.synchronize()
+        assert_parity(want, ref.cpu().numpy(), what="hc_gemv_dev vs oracle")
         for call in range(2):
             y = torch.full((nvec, m), float("nan"), device="cuda")
             rc = _call("hc_gemv_dev_noalloc", engine, w, x, y, resid, nvec)
             assert rc == _lib.HC_OK, lib().hc_last_error()
             torch.cuda.synchronize()
-            assert_parity(ref.cpu().numpy(), y.cpu().numpy(), what=f"call {call + 1}")
+            # the same kernel with the same split as hc_gemv_dev: bit-identical results
+            assert torch.equal(ref, y), f"call {call + 1}: differs from hc_gemv_dev"
+            assert_parity(want, y.cpu().numpy(), what=f"call {call + 1} vs oracle")
         engine.sync()  # device error flag clear
     finally:
         engine.set_stream(None)
@@ -92,7 +105,7 @@ def test_noalloc_rejects_oversized_and_unsupported(engine):
         assert _call("hc_gemv_dev", engine, w, xs, ref, None, 1) == _lib.HC_OK
         assert _call("hc_gemv_dev_noalloc", engine, w, xs, got, None, 1) == _lib.HC_OK, lib().hc_last_error()
         torch.cuda.synchronize()
-        assert_parity(ref.cpu().numpy(), got.cpu().numpy(), what="after rejection")
+        assert torch.equal(ref, got), "after the rejections: differs from hc_gemv_dev"
     finally:
         engine.set_stream(None)
         w.free()

@@ -6,7 +6,8 @@ matmul / FFN op API on top of it.
 """
 from .engine import (BLOCK, F32, IQ2_S, IQ2_XS, IQ2_XXS, IQ3_S, IQ3_XXS, IQ4_NL, IQ4_XS, Q2_K, Q3_K,  # noqa: F401
                      Q4_0, Q4_1, Q4_K, Q5_0, Q5_1, Q5_K, Q6_K, Q8_0, TYPE_LABELS, CudaEngine, CudaError,
-                     EngineOrchestrator, PendingGemv, QuantMatrix, ResidentWeights, device_count, row_bytes)
+                     PendingGemv, QuantMatrix, ResidentWeights, device_count, row_bytes)
+from .orchestrator import EngineOrchestrator
 
 __all__ = ["CudaEngine", "CudaError", "EngineOrchestrator", "PendingGemv", "QuantMatrix", "ResidentWeights",
            "device_count", "row_bytes", "F32", "Q8_0", "Q4_K", "Q6_K", "IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS",

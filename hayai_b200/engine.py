@@ -4,9 +4,9 @@
 (crates/hayai-opencl/src/compute.rs:45-461, async_gemv.rs:60-130): the same method
 names, argument meaning (m = output rows, n = input columns, GGUF-layout weight bytes)
 and error behaviour (validation failures and unsupported types raise, there is no
-silent CPU fallback, orchestrator.rs:403-409).  ``QuantMatrix`` and
-``EngineOrchestrator.execute_quant_gemv`` mirror the hayai-core call sites
-(crates/hayai-model/src/quant.rs:31-117, crates/hayai-core/src/orchestrator.rs:222-269).
+silent CPU fallback, orchestrator.rs:403-409).  ``QuantMatrix`` mirrors
+crates/hayai-model/src/quant.rs:31-117; the orchestrator's dispatch is in
+``hayai_b200.orchestrator``.
 
 Device-memory entry points (``*_dev``) take torch CUDA tensors: torch is used for device
 memory and streams only; all compute runs in the native library.
@@ -433,37 +433,43 @@ class CudaEngine:
                                           flat(gates), flat(ups), flat(downs), ctypes.c_void_p(_tptr(x)), n_tok))
 
 
-# ---------------------------------------------------------------------------- orchestrator mirror
+# ---------------------------------------------------------------------------- QuantMatrix
 @dataclass
 class QuantMatrix:
-    """GGUF-layout matrix (quant.rs:31-37): ``ncols`` contiguous, y[nrows] = W x[ncols]."""
+    """GGUF-layout matrix (quant.rs:31-37): ``ncols`` contiguous, y[nrows] = W x[ncols].
+
+    ``data`` holds the GGUF bytes: an owned copy (``owned``), or a view of the caller's buffer
+    (``view``, quant.rs:97-117: the caller keeps the buffer alive, no copy is made).  The GEMV
+    runs on the GPU through ``hayai_b200.orchestrator.EngineOrchestrator``; there is no host
+    GEMV in this backend."""
     name: str
     ncols: int
     nrows: int
     ggml_type: int
     data: np.ndarray
-    _resident: dict = field(default_factory=dict, repr=False)
+
+    def __post_init__(self):
+        if self.ggml_type not in BLOCK:  # no kernel for it: the GEMV raises, not the constructor
+            return
+        qk, bs = BLOCK[self.ggml_type]
+        if self.ncols % qk:
+            raise CudaError(_lib.HC_ERR_INVALID, f"'{self.name}': ncols {self.ncols} is not a multiple of {qk}")
+        need = self.nrows * (self.ncols // qk) * bs
+        if self.data.nbytes < need:
+            raise CudaError(_lib.HC_ERR_INVALID, f"'{self.name}': {self.data.nbytes} bytes, {need} needed")
+
+    @classmethod
+    def owned(cls, name: str, ncols: int, nrows: int, ggml_type: int, data) -> "QuantMatrix":
+        return cls(name, ncols, nrows, ggml_type, np.array(_u8(data), copy=True))
+
+    @classmethod
+    def view(cls, name: str, ncols: int, nrows: int, ggml_type: int, data) -> "QuantMatrix":
+        return cls(name, ncols, nrows, ggml_type, _u8(data))
 
 
-class EngineOrchestrator:
-    """GPU-only dispatch of quantized GEMVs (orchestrator.rs:222-269, 394-422): matrices are
-    uploaded once per engine and reused; a type without a kernel is a hard error."""
+def __getattr__(name):  # the orchestrator mirror moved to hayai_b200.orchestrator
+    if name == "EngineOrchestrator":
+        from .orchestrator import EngineOrchestrator
 
-    def __init__(self, device: int = 0):
-        self.engine = CudaEngine(device)
-
-    def _resident(self, m: QuantMatrix) -> ResidentWeights:
-        rw = m._resident.get(id(self.engine))
-        if rw is None:
-            rw = self.engine.upload(m.ggml_type, m.nrows, m.ncols, m.data)
-            m._resident[id(self.engine)] = rw
-        return rw
-
-    def execute_quant_gemv(self, matrix: QuantMatrix, input, output=None) -> np.ndarray:
-        return self.engine.ggml_gemv_dispatch_bound(self._resident(matrix), input, output)
-
-    def execute_quant_gemv_batched(self, matrix: QuantMatrix, inputs, batch: int, outputs=None) -> np.ndarray:
-        return self.engine.ggml_gemv_batched(self._resident(matrix), inputs, batch, outputs)
-
-    def execute_lut_matmul(self, m, n, weights_q4, lut, input, output=None) -> np.ndarray:
-        return self.engine.lut_matmul_q4(m, n, weights_q4, lut, input, output)
+        return EngineOrchestrator
+    raise AttributeError(name)

@@ -36,6 +36,24 @@ def test_python_binding_covers_header():
     assert declared_symbols() == set(_lib.exported_symbols())
 
 
+def test_rust_binding_covers_header():
+    """The hayai-cuda crate (integration/hayai-cuda, not compiled here: no Rust toolchain on
+    this image) declares exactly the header's entry points, with as many parameters each."""
+    root = os.path.dirname(HEADER)
+    ffi = open(os.path.join(root, "..", "integration", "hayai-cuda", "src", "ffi.rs")).read()
+    rust = dict(re.findall(r"pub fn (hc_[a-z0-9_]+)\(([^)]*)\)", ffi, flags=re.S))
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    c = dict(re.findall(r"\b(hc_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text, flags=re.S))
+    assert set(rust) == set(c) == declared_symbols()
+
+    def nparams(args):
+        args = args.strip()
+        return 0 if args in ("", "void") else args.count(",") + 1
+
+    for name in c:
+        assert nparams(rust[name]) == nparams(c[name]), name
+
+
 # gemv_row_bytes (crates/hayai-opencl/src/compute.rs:877-907) for the formats with a kernel here
 @pytest.mark.parametrize("t,n,expect", [
     (hayai_b200.Q4_K, 4096, 16 * 144), (hayai_b200.Q6_K, 14336, 56 * 210), (hayai_b200.Q8_0, 4096, 128 * 34),

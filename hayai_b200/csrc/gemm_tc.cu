@@ -262,48 +262,48 @@ struct TcDq<TcQ4K> {
     __device__ __forceinline__ bool bad() const { return !(big < 65504.f); }
 };
 
-// Q6_K image (3360 B, 256 K): [l0: (r,t) at 16(4r+t)][l1: at 1024 + 16(4r+t)][qh: at
-// 2048 + 16(4r+t)][sc: row r at 3072 + 16r][d: row r at 3328 + 2r].  Word j = 2qq + lh of
-// piece (r,t) in l_h holds ql bytes 64h + 32qq + 16lh + 4t..+3; qh word 2h + lh holds qh bytes
-// 32h + 16lh + 4t..+3.  Chunk c = 2h + nib of the super-block: elements 32qq + l (l = 16lh +
-// 4t + i) with code nibble_nib(ql[l + 32qq]) | ((qh[l] >> (2qq + 4nib)) & 3) << 4, minus 32,
-// and scale sc[8h + 4nib + 2qq + lh] (q6k.rs:35-55).  Items (row r, piece t) x 2 per thread.
+// Q6_K image (3360 B, 256 K), lane-distributed (repack.cu): piece (r, t) of l0 / l1 / qh at
+// 16(4r + t) in its 1024-B region holds ql bytes 64h + 16s + i / ql bytes 64h + 32 + 16s + i /
+// qh bytes 32h + 16s + i (h = t >> 1, s = t & 1, i < 16); word t of row r's scales (3072 +
+// 16r) holds sc[8h + s + 2q] in byte q; d of row r at 3328 + 2r.  Chunk c = 2h + nib of the
+// super-block: elements 32qq + l of half h (q = 2 nib + qq, l = 16s + i), code
+// nibble_nib(ql) | ((qh >> 2q) & 3) << 4, minus 32, scale byte q of word 2h + s
+// (q6k.rs:35-55).  One item (row r, s) per thread: its 32 elements of every chunk.
 template <>
 struct TcDq<TcQ6K> {
-    int lw[2], hw[2], sw[2], dw[2], dsh[2], ao[2][4];
+    int lw, sw, dw, dsh, ao[2][4];
     float big = 0.f;  // max 2^8 |d sc| (|q| <= 32): w' must stay below 65504
     __device__ __forceinline__ void init(int dt) {
+        const int r = dt >> 1, s = dt & 1, rt = r >> 4, rr = r & 15;
+        const int base = rt * (TcQ6K::kGps * TcQ6K::kImg / 4);
+        lw = base + 4 * (4 * rr + s);  // piece t = 2h + s: + 8h words
+        sw = base + 768 + 4 * rr + s;  // word t: + 2h
+        dw = base + 832 + (rr >> 1);
+        dsh = 16 * (rr & 1);
 #pragma unroll
-        for (int it = 0; it < 2; ++it) {
-            const int item = dt + 256 * it, r = item >> 2, t = item & 3, rt = r >> 4, rr = r & 15;
-            const int base = rt * (TcQ6K::kGps * TcQ6K::kImg / 4);
-            lw[it] = base + 4 * (4 * rr + t);
-            hw[it] = base + 512 + 4 * (4 * rr + t);
-            sw[it] = base + 768 + 4 * rr;
-            dw[it] = base + 832 + (rr >> 1);
-            dsh[it] = 16 * (rr & 1);
+        for (int qq = 0; qq < 2; ++qq)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) ao[it][j] = tc_canon(r, 32 * (j >> 1) + 16 * (j & 1) + 4 * t);
-        }
+            for (int k = 0; k < 4; ++k) ao[qq][k] = tc_canon(r, 32 * qq + 16 * s + 4 * k);
     }
     __device__ __forceinline__ void chunk(const uint32_t* ws, int c, uint8_t* ahi, uint8_t* alo) {
         const int h = c >> 1, nib = c & 1;
+        const uint4 l0 = *reinterpret_cast<const uint4*>(ws + lw + 8 * h);
+        const uint4 l1 = *reinterpret_cast<const uint4*>(ws + lw + 8 * h + 256);
+        const uint4 qh = *reinterpret_cast<const uint4*>(ws + lw + 8 * h + 512);
+        const uint32_t scw = ws[sw + 2 * h] ^ 0x80808080u;
+        const float d = h2f((uint16_t)(ws[dw] >> dsh));
+        const uint32_t Q[4] = {qh.x, qh.y, qh.z, qh.w};
 #pragma unroll
-        for (int it = 0; it < 2; ++it) {
-            const uint4 l = *reinterpret_cast<const uint4*>(ws + lw[it] + 256 * h);
-            const uint2 qh = *reinterpret_cast<const uint2*>(ws + hw[it] + 2 * h);
-            const uint32_t scw = ws[sw[it] + c] ^ 0x80808080u;  // scales 8h + 4nib + 0..3
-            const float d = h2f((uint16_t)(ws[dw[it]] >> dsh[it]));
-            const uint32_t lws[4] = {l.x, l.y, l.z, l.w};
+        for (int qq = 0; qq < 2; ++qq) {
+            const int q = 2 * nib + qq;
+            const float ds = (d * s8_to_f32_flipped(scw, q)) * kTcWScale;  // (d sc) 2^8, exact
+            big = fmaxf(big, fabsf(ds) * 32.f);
+            const uint32_t L[4] = {qq ? l1.x : l0.x, qq ? l1.y : l0.y, qq ? l1.z : l0.z, qq ? l1.w : l0.w};
+            const int hs = 2 * q;  // the 2 qh bits move to bits 4-5 of each byte
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {  // j = 2qq + lh
-                const int qq = j >> 1, lh = j & 1;
-                const float ds = (d * s8_to_f32_flipped(scw, j)) * kTcWScale;  // (d sc) 2^8, exact
-                big = fmaxf(big, fabsf(ds) * 32.f);
-                const uint32_t lo4 = (nib ? lws[j] >> 4 : lws[j]) & 0x0F0F0F0Fu;
-                const uint32_t hb = lh ? qh.y : qh.x;
-                const int hs = 2 * qq + 4 * nib;  // the 2 qh bits move to bits 4-5 of each byte
-                const uint32_t up = (hs <= 4 ? hb << (4 - hs) : hb >> (hs - 4)) & 0x30303030u;
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t lo4 = (nib ? L[k] >> 4 : L[k]) & 0x0F0F0F0Fu;
+                const uint32_t up = (hs <= 4 ? Q[k] << (4 - hs) : Q[k] >> (hs - 4)) & 0x30303030u;
                 const uint32_t code = lo4 | up;
                 float v[4];
 #pragma unroll
@@ -315,8 +315,8 @@ struct TcDq<TcQ6K> {
                 uint2 hi, lo;
                 tc_split2(v[0], v[1], hi.x, lo.x);
                 tc_split2(v[2], v[3], hi.y, lo.y);
-                *reinterpret_cast<uint2*>(ahi + ao[it][j]) = hi;
-                *reinterpret_cast<uint2*>(alo + ao[it][j]) = lo;
+                *reinterpret_cast<uint2*>(ahi + ao[qq][k]) = hi;
+                *reinterpret_cast<uint2*>(alo + ao[qq][k]) = lo;
             }
         }
     }

@@ -5,9 +5,9 @@
 // Design (one warp = one 16-row tile over a range of super-blocks):
 //  * Weights are dequantized in registers straight into the A fragment of
 //    mma.m16n8k16 (f16 in, f32 accumulate).  Integer codes are exact in f16.
-//    Q4_K folds its 6-bit sub-block scale into the same HFMA2 that removes the
-//    f16 magic offset (q*sc <= 945 is exact in f16), so one MMA may span
-//    several sub-blocks; Q6_K and Q8_0 apply their scale per MMA in f32.
+//    Q4_K and Q6_K are lane-distributed (each lane's k-slots belong to its own
+//    sub-blocks / scale groups, so an accumulator column holds one group) and
+//    apply their scales once per group in f32; Q8_0 applies its scale per MMA.
 //  * Activations are split as x = hi + lo * 2^-11 (both f16), occupying two
 //    columns of the B operand, so the tensor-core product carries ~22 bits of
 //    x -- enough for the reference's f32 contract (rel-L2 <= 1e-4).  Columns
@@ -68,6 +68,8 @@ struct FmtQ4K {
     // byte p = 32t + 4wi + j of qs; low nibble -> 64t + 4wi + j, high -> +32
     __device__ static int base(int mi, int t) { return 64 * t + 4 * (mi >> 1) + 32 * (mi & 1); }
     static constexpr bool kNeedSx = true;
+    // accumulators come back per lane (lane-distributed columns): lane shares summed over t
+    static constexpr bool kLaneShares = true;
     // table slot (within a block) of the hi part of MMA mi = 2 wi + nib, vector v, lane t:
     // the lo- and hi-nibble fragments of one word sit side by side (one 128-bit load)
     template <int NV>
@@ -82,17 +84,19 @@ struct FmtQ6K {
     static constexpr int kTile = 3360, kL0 = 0, kL1 = 1024, kQh = 2048, kSc = 3072, kD = 3328;
     static constexpr int kBlockElems = 256;
     static constexpr int kMmaPerBlock = 16;
-    // mi = 8h + 4lh + q covers scale group (h, q, lh): elements 128h + 32q + 16lh + [0,16)
+    // lane-distributed: lane t owns half h = t >> 1, l in [16s, 16s + 16), s = t & 1; MMA
+    // mi = 4q + j takes elements 4j..4j+3 of its scale group q (128h + 32q + 16s + 4j)
     __device__ static int base(int mi, int t) {
-        int h = mi >> 3, lh = (mi >> 2) & 1, q = mi & 3;
-        return 128 * h + 32 * q + 16 * lh + 4 * t;
+        return 128 * (t >> 1) + 32 * (mi >> 2) + 16 * (t & 1) + 4 * (mi & 3);
     }
     static constexpr bool kNeedSx = false;
+    static constexpr bool kLaneShares = true;
+    // the B table of Q4_K: MMA pairs side by side, hi and lo parts 8 entries apart
     template <int NV>
     __device__ static int tab(int mi, int v, int t) {
-        return (mi * 2 * NV + 2 * v) * 4 + t;
+        return (((mi >> 1) * 2 * NV + 2 * v) * 4 + t) * 2 + (mi & 1);
     }
-    static constexpr int kLoOff = 4;
+    static constexpr int kLoOff = 8;
 };
 
 // Q8_0 kernels work on groups of 4 Q8_0 blocks (128 elements, 8 MMAs); mi = 2*blk + half.
@@ -103,6 +107,7 @@ struct FmtQ80 {
     static constexpr int kMmaPerBlock = 8;
     __device__ static int base(int mi, int t) { return 16 * mi + 4 * t; }
     static constexpr bool kNeedSx = false;
+    static constexpr bool kLaneShares = false;
     template <int NV>
     __device__ static int tab(int mi, int v, int t) {
         return (mi * 2 * NV + 2 * v) * 4 + t;

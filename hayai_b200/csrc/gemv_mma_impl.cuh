@@ -26,9 +26,9 @@ __device__ __forceinline__ void inv_q4k(int e, int& mi, int& t) {
     mi = 2 * ((r & 31) >> 2) + (r >> 5);
 }
 __device__ __forceinline__ void inv_q6k(int e, int& mi, int& t) {
-    const int h = e >> 7, r = e & 127, q = r >> 5, r2 = r & 31, lh = r2 >> 4;
-    t = (r2 & 15) >> 2;  // 128h + 32q + 16lh + 4t
-    mi = 8 * h + 4 * lh + q;
+    const int h = e >> 7, r = e & 127, q = r >> 5, s = (r >> 4) & 1, j = (r >> 2) & 3;
+    t = 2 * h + s;  // 128h + 32q + 16s + 4j
+    mi = 4 * q + j;
 }
 __device__ __forceinline__ void inv_q80(int e, int& mi, int& t) {
     mi = e >> 4;  // 16mi + 4t
@@ -232,7 +232,7 @@ __device__ __forceinline__ LaneCtx<NV> make_ctx(const uint2* xt, const uint2* ze
     c.sxs = K / 32;
     int off;
     bool live;
-    if constexpr (F::kType == T_Q4_K) {
+    if constexpr (F::kLaneShares) {
         off = ((c.g & 1) * 4 + c.t) * 2;  // part g&1 of owner lane g>>1, lane t
         live = (c.g >> 1) == c.t;
     } else {
@@ -351,59 +351,77 @@ __device__ __forceinline__ void q4k_unit(const Q4KBlk (&A)[NMAT], const Q4KBlk (
 }
 
 // ------------------------------------------------------------------ Q6_K (GPU layout)
-// Row: nb blocks of 208 B {ql_perm[4 lanes][8 words] | qh_perm[4 lanes][4 words] | sc[16]},
-// then the f16 d plane (nb entries, padded to 16 B).  ql word wq = 4h + 2qq + lh of lane t
-// holds original ql bytes 64h + 32qq + 16lh + 4t..+3; qh word wh = 2h + lh holds
-// qh bytes 32h + 16lh + 4t..+3 (q6k.rs:26-57 layout).
+// Lane-distributed (repack.cu): lane t of a row owns half h = t >> 1 and l in [16s, 16s + 16),
+// s = t & 1, i.e. the four scale groups 8h + 2q + s (q < 4) whole: elements 128h + 32q + 16s + i.
+// Its pieces: l0 = ql bytes 64h + 16s + i (low nibble: q = 0, high: q = 2), l1 = ql bytes
+// 64h + 32 + 16s + i (q = 1, 3), qh = qh bytes 32h + 16s + i (bits 2q..2q+1), sc = the int8
+// scales of its groups (byte q), and d (q6k.rs:26-57).  MMA mi = 4q + j takes codes
+// i = 4j..4j+3 of group q, bytes 0/2 in k-slots 2t, 2t+1 and bytes 1/3 in 2t+8, 2t+9 (the
+// pairing of Q4_K); B holds lane t's x only in columns 2t (hi) and 2t+1 (lo), so each group's
+// accumulator stays on its own lane and the scale is applied once per group (4 MMAs) in f32.
+// pA/pB receive the lane's share of rows g / g+8 (summed over t by the caller).  The codes
+// enter as f16(1024 + c) by one PRMT of the merged 6-bit bytes and one exact HSUB2 of 1056.
 struct Q6KBlk {
-    uint4 l0, l1, qh, sc;
+    uint4 l0, l1, qh;
+    uint32_t sc;
     uint16_t d;
 };
 
 template <int NV>
-__device__ __forceinline__ void q6k_block(const Q6KBlk& A, const Q6KBlk& B, int kb, const LaneCtx<NV>& c,
-                                          float& dA, float& dB) {
+__device__ __forceinline__ void q6k_unit(const Q6KBlk& A, const Q6KBlk& B, int kb, const LaneCtx<NV>& c,
+                                         float (&pA)[1][NV], float (&pB)[1][NV]) {
     const uint32_t kOff = 0x64206420u;  // (1056, 1056) in f16: 1024 magic + 32 code offset
-    const float fdA = h2f(A.d), fdB = h2f(B.d);
-    const uint32_t LA[8] = {A.l0.x, A.l0.y, A.l0.z, A.l0.w, A.l1.x, A.l1.y, A.l1.z, A.l1.w};
-    const uint32_t LB[8] = {B.l0.x, B.l0.y, B.l0.z, B.l0.w, B.l1.x, B.l1.y, B.l1.z, B.l1.w};
-    const uint32_t QHA[4] = {A.qh.x, A.qh.y, A.qh.z, A.qh.w};
-    const uint32_t QHB[4] = {B.qh.x, B.qh.y, B.qh.z, B.qh.w};
-    // int8 scales, 0x80-flipped for s8_to_f32_flipped
-    const uint32_t SA[4] = {A.sc.x ^ 0x80808080u, A.sc.y ^ 0x80808080u, A.sc.z ^ 0x80808080u, A.sc.w ^ 0x80808080u};
-    const uint32_t SB[4] = {B.sc.x ^ 0x80808080u, B.sc.y ^ 0x80808080u, B.sc.z ^ 0x80808080u, B.sc.w ^ 0x80808080u};
-    const uint2* xb = c.xb0 + kb * c.xstride;
-    float sumA = 0.f, sumB = 0.f;
+    const uint32_t LA[2][4] = {{A.l0.x, A.l0.y, A.l0.z, A.l0.w}, {A.l1.x, A.l1.y, A.l1.z, A.l1.w}};
+    const uint32_t LB[2][4] = {{B.l0.x, B.l0.y, B.l0.z, B.l0.w}, {B.l1.x, B.l1.y, B.l1.z, B.l1.w}};
+    const uint32_t QA[4] = {A.qh.x, A.qh.y, A.qh.z, A.qh.w};
+    const uint32_t QB[4] = {B.qh.x, B.qh.y, B.qh.z, B.qh.w};
+    const uint4* xb = reinterpret_cast<const uint4*>(c.xb0 + kb * c.xstride);
+    float acc[4][NV][4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int q = 0; q < 4; ++q)
 #pragma unroll
-        for (int lh = 0; lh < 2; ++lh) {
-            const uint32_t QA = QHA[2 * h + lh], QB = QHB[2 * h + lh];
-            const uint32_t qa[4] = {(QA << 4) & 0x30303030u, (QA << 2) & 0x30303030u, QA & 0x30303030u,
-                                    (QA >> 2) & 0x30303030u};
-            const uint32_t qb[4] = {(QB << 4) & 0x30303030u, (QB << 2) & 0x30303030u, QB & 0x30303030u,
-                                    (QB >> 2) & 0x30303030u};
+        for (int v = 0; v < NV; ++v)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int qq = q & 1;
-                const uint32_t la = LA[4 * h + 2 * qq + lh], lb = LB[4 * h + 2 * qq + lh];
-                const uint32_t ua = lop3_and_or(q < 2 ? la : (la >> 4), 0x0F0F0F0Fu, qa[q]);
-                const uint32_t ub = lop3_and_or(q < 2 ? lb : (lb >> 4), 0x0F0F0F0Fu, qb[q]);
-                const int m = 8 * h + 4 * lh + q;
-                const uint2 f = xb[m * (2 * NV * 4)];
-                float acc[4] = {0.f, 0.f, 0.f, 0.f};
-                mma16816(acc, hsub2_u32(prmt(ua, 0x64646464u, 0x4240u), kOff),
-                         hsub2_u32(prmt(ub, 0x64646464u, 0x4240u), kOff),
-                         hsub2_u32(prmt(ua, 0x64646464u, 0x4341u), kOff),
-                         hsub2_u32(prmt(ub, 0x64646464u, 0x4341u), kOff), f.x, f.y);
-                const int si = 8 * h + 2 * q + lh;  // scale index = element / 16
-                sumA += s8_to_f32_flipped(SA[si >> 2], si & 3) * (acc[0] + acc[1] * kLoScale);
-                sumB += s8_to_f32_flipped(SB[si >> 2], si & 3) * (acc[2] + acc[3] * kLoScale);
+            for (int i = 0; i < 4; ++i) acc[q][v][i] = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+            uint4 f[NV];
+#pragma unroll
+            for (int v = 0; v < NV; ++v) f[v] = xb[((2 * q + jp) * 2 * NV + 2 * v) * 4];
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+                const int j = 2 * jp + jj;
+                const uint32_t la = LA[q & 1][j], lb = LB[q & 1][j];
+                const int qs = 4 - 2 * q;  // qh bits 2q..2q+1 -> bits 4..5 of each byte
+                const uint32_t ha = (qs >= 0 ? QA[j] << qs : QA[j] >> -qs) & 0x30303030u;
+                const uint32_t hb = (qs >= 0 ? QB[j] << qs : QB[j] >> -qs) & 0x30303030u;
+                const uint32_t ua = lop3_and_or(q < 2 ? la : (la >> 4), 0x0F0F0F0Fu, ha);
+                const uint32_t ub = lop3_and_or(q < 2 ? lb : (lb >> 4), 0x0F0F0F0Fu, hb);
+                const uint32_t a0 = hsub2_u32(prmt(ua, 0x64646464u, 0x4240u), kOff);
+                const uint32_t a1 = hsub2_u32(prmt(ub, 0x64646464u, 0x4240u), kOff);
+                const uint32_t a2 = hsub2_u32(prmt(ua, 0x64646464u, 0x4341u), kOff);
+                const uint32_t a3 = hsub2_u32(prmt(ub, 0x64646464u, 0x4341u), kOff);
+#pragma unroll
+                for (int v = 0; v < NV; ++v)
+                    mma16816(acc[q][v], a0, a1, a2, a3, jj ? f[v].z : f[v].x, jj ? f[v].w : f[v].y);
             }
         }
     }
-    dA = fdA * sumA;
-    dB = fdB * sumB;
+    const uint32_t SA = A.sc ^ 0x80808080u, SB = B.sc ^ 0x80808080u;  // flipped for s8_to_f32_flipped
+    const float dA = h2f(A.d), dB = h2f(B.d);
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+        float sa = 0.f, sb = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            sa += s8_to_f32_flipped(SA, q) * (acc[q][v][0] + acc[q][v][1] * kLoScale);
+            sb += s8_to_f32_flipped(SB, q) * (acc[q][v][2] + acc[q][v][3] * kLoScale);
+        }
+        pA[0][v] += dA * sa;
+        pB[0][v] += dB * sb;
+    }
 }
 
 // ------------------------------------------------------------------ Q8_0 (GPU layout)
@@ -489,12 +507,14 @@ __device__ __forceinline__ void tile_load(typename BlkOf<F>::T& A, typename BlkO
         B.l1 = ld_piece<kShared>(tb + F::kL1 + pb);
         A.qh = ld_piece<kShared>(tb + F::kQh + pa);
         B.qh = ld_piece<kShared>(tb + F::kQh + pb);
-        A.sc = ld_piece<kShared>(tb + F::kSc + 16 * g);
-        B.sc = ld_piece<kShared>(tb + F::kSc + 16 * (g + 8));
         if constexpr (kShared) {
+            A.sc = *reinterpret_cast<const uint32_t*>(tb + F::kSc + 16 * g + 4 * t);
+            B.sc = *reinterpret_cast<const uint32_t*>(tb + F::kSc + 16 * (g + 8) + 4 * t);
             A.d = *reinterpret_cast<const uint16_t*>(tb + F::kD + 2 * g);
             B.d = *reinterpret_cast<const uint16_t*>(tb + F::kD + 2 * (g + 8));
         } else {
+            A.sc = ldg_stream32(tb + F::kSc + 16 * g + 4 * t);
+            B.sc = ldg_stream32(tb + F::kSc + 16 * (g + 8) + 4 * t);
             A.d = ldg_u16(tb + F::kD + 2 * g);
             B.d = ldg_u16(tb + F::kD + 2 * (g + 8));
         }
@@ -516,13 +536,17 @@ __device__ __forceinline__ void tile_load(typename BlkOf<F>::T& A, typename BlkO
 template <class F, int NV>
 __device__ __forceinline__ void blk_compute(const typename BlkOf<F>::T& A, const typename BlkOf<F>::T& B, int kb,
                                             const LaneCtx<NV>& c, float& dA, float& dB) {
-    if constexpr (F::kType == T_Q4_K) {
+    if constexpr (F::kLaneShares) {
         float pa[1][NV], pb[1][NV];
 #pragma unroll
         for (int v = 0; v < NV; ++v) pa[0][v] = pb[0][v] = 0.f;
-        const Q4KBlk a1[1] = {A}, b1[1] = {B};
-        const int k1[1] = {kb};
-        q4k_unit<NV, 1>(a1, b1, k1, c, pa, pb);
+        if constexpr (F::kType == T_Q4_K) {
+            const Q4KBlk a1[1] = {A}, b1[1] = {B};
+            const int k1[1] = {kb};
+            q4k_unit<NV, 1>(a1, b1, k1, c, pa, pb);
+        } else {
+            q6k_unit<NV>(A, B, kb, c, pa, pb);
+        }
         dA = dB = 0.f;
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
@@ -537,7 +561,6 @@ __device__ __forceinline__ void blk_compute(const typename BlkOf<F>::T& A, const
             }
         }
     }
-    else if constexpr (F::kType == T_Q6_K) q6k_block<NV>(A, B, kb, c, dA, dB);
     else q80_block<NV>(A, B, kb, c, dA, dB);
 }
 

@@ -60,8 +60,8 @@ __host__ __device__ constexpr int tile_slot_bytes(int nv) { return kCW * nv * 16
 // matrix of consumer warp w
 __host__ __device__ constexpr int warp_matrix(int w, bool fused) { return fused ? w / (kUnits / 2) : 0; }
 
-// One consumer warp's unit of a stage: rows g, g+8 of the tile-block image at tb.  Q4_K
-// accumulates lane shares in pA/pB, the other formats row sums in yA/yB.
+// One consumer warp's unit of a stage: rows g, g+8 of the tile-block image at tb.  Q4_K and
+// Q6_K accumulate lane shares in pA/pB, Q8_0 row sums in yA/yB.
 template <class F, int NV>
 __device__ __forceinline__ void stage_unit(const uint8_t* tb, int kbj, const LaneCtx<NV>& ctx, float& yA, float& yB,
                                            float (&pA)[1][NV], float (&pB)[1][NV]) {
@@ -70,6 +70,10 @@ __device__ __forceinline__ void stage_unit(const uint8_t* tb, int kbj, const Lan
         tile_load<F, true>(A[0], B[0], tb, ctx.g, ctx.t);
         const int kbs[1] = {kbj};
         q4k_unit<NV, 1>(A, B, kbs, ctx, pA, pB);
+    } else if constexpr (F::kType == T_Q6_K) {
+        Q6KBlk A, B;
+        tile_load<F, true>(A, B, tb, ctx.g, ctx.t);
+        q6k_unit<NV>(A, B, kbj, ctx, pA, pB);
     } else {
         typename BlkOf<F>::T A, B;
         tile_load<F, true>(A, B, tb, ctx.g, ctx.t);
@@ -80,12 +84,12 @@ __device__ __forceinline__ void stage_unit(const uint8_t* tb, int kbj, const Lan
     }
 }
 
-// End of a tile (or chunk) for one warp: its partials (Q4_K lane shares reduced over t
-// first) go to red_w[v][16 rows]; the accumulators restart at zero.
+// End of a tile (or chunk) for one warp: its partials (lane shares reduced over t first)
+// go to red_w[v][16 rows]; the accumulators restart at zero.
 template <class F, int NV>
 __device__ __forceinline__ void warp_partials(float* red_w, int g, int t, float& yA, float& yB, float (&pA)[1][NV],
                                               float (&pB)[1][NV]) {
-    if constexpr (F::kType == T_Q4_K) {
+    if constexpr (F::kLaneShares) {
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
             float sa = pA[0][v], sb = pB[0][v];

@@ -12,11 +12,13 @@
 //  Q4_K image (2304 B):  [hdr: row r at 16r, the block's first 16 bytes (d, dmin, scales)]
 //                        [q0: (r,t) at 256 + 16(4r+t) = qs bytes 32t..32t+15]
 //                        [q1: (r,t) at 1280 + 16(4r+t) = qs bytes 32t+16..32t+31]
-//  Q6_K image (3360 B):  [l0: (r,t) at 16(4r+t)][l1: at 1024 + 16(4r+t)][qh: at 2048 + 16(4r+t)]
-//                        [sc: row r at 3072 + 16r][d: row r at 3328 + 2r]
-//                        l0 word j (j < 4) of lane t / l1 word j: ql word wq = j / 4 + j of the
-//                        lane-t view, which holds ql bytes 64h + 32qq + 16lh + 4t..+3 for
-//                        wq = 4h + 2qq + lh; qh word wh = 2h + lh holds qh bytes 32h + 16lh + 4t..+3
+//  Q6_K image (3360 B), lane-distributed: lane t of a row owns half h = t >> 1, l in
+//                        [16s, 16s + 16), s = t & 1 (the 4 scale groups 8h + 2q + s, q < 4):
+//                        [l0: (r,t) at 16(4r+t) = ql bytes 64h + 16s .. +15]
+//                        [l1: at 1024 + 16(4r+t) = ql bytes 64h + 32 + 16s .. +15]
+//                        [qh: at 2048 + 16(4r+t) = qh bytes 32h + 16s .. +15]
+//                        [sc: row r at 3072 + 16r, word t = scales 8h + s + 2q in byte q]
+//                        [d: row r at 3328 + 2r]
 //  Q8_0 image (2176 B), one group = 4 GGUF blocks = 128 elements:
 //                        [q0: (r,t) at 16(4r+t)][q1: at 1024 + 16(4r+t)][d: row r at 2048 + 8r]
 //                        word wi of lane t (q0: wi < 4, q1: wi - 4) = codes 16(wi & 1) + 4t..+3 of
@@ -112,23 +114,18 @@ __device__ __forceinline__ uint32_t tiled_word(const uint8_t* __restrict__ raw, 
             }
             return v;
         }
-        int r, off;
-        if (w < 768) {
-            const int reg = w >> 8, p = (w & 255) >> 2, j = w & 3, t = p & 3;
-            r = p >> 2;
-            if (reg < 2) {
-                const int wq = 4 * reg + j, h = wq >> 2, qq = (wq >> 1) & 1, lh = wq & 1;
-                off = 64 * h + 32 * qq + 16 * lh + 4 * t;
-            } else {
-                const int h = j >> 1, lh = j & 1;
-                off = 128 + 32 * h + 16 * lh + 4 * t;
-            }
-        } else {
-            r = (w - 768) >> 2;
-            off = 192 + 4 * (w & 3);
-        }
+        const int seg = w >> 8, p = (w & 255) >> 2, j = w & 3;
+        const int r = seg < 3 ? p >> 2 : (w - 768) >> 2;
+        const int t = seg < 3 ? p & 3 : w & 3, h = t >> 1, s = t & 1;
         const int row = tile * 16 + r;
-        return row < M ? rd4(raw + (size_t)row * raw_rb + (size_t)kb * 210 + off) : 0u;
+        if (row >= M) return 0u;
+        const uint8_t* blk = raw + (size_t)row * raw_rb + (size_t)kb * 210;
+        if (seg == 0) return rd4(blk + 64 * h + 16 * s + 4 * j);
+        if (seg == 1) return rd4(blk + 64 * h + 32 + 16 * s + 4 * j);
+        if (seg == 2) return rd4(blk + 128 + 32 * h + 16 * s + 4 * j);
+        uint32_t v = 0;  // the lane's 4 int8 scales, group q in byte q
+        for (int q = 0; q < 4; ++q) v |= (uint32_t)blk[192 + 8 * h + s + 2 * q] << (8 * q);
+        return v;
     } else {  // Q8_0, kb = group of 4 blocks
         if (w >= 512) {  // d: row r = k / 2, blocks 4G + 2(k & 1) + {0, 1}
             const int k = w - 512, row = tile * 16 + (k >> 1);

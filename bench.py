@@ -399,6 +399,7 @@ def run_moe(args):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     import hayai_b200 as hb
+    import oracle
     from hayai_b200.tp import PeerGroup, expert_range
 
     c = dict(CONFIGS[args.config])
@@ -450,17 +451,47 @@ def run_moe(args):
     # the routing of every layer (untimed, per-layer calls): algorithmic bytes of a step =
     # every layer's router + the distinct experts its 16 tokens selected (the same every step)
     xr = x0.clone()
+    y0 = None
     for l in range(L):
         if ep:
             eng.moe_ffn_ep_dev(R[l], k, G[l], U[l], D[l], lo, xr, y, ids[l])
         else:
             eng.moe_ffn_dev(R[l], k, G[l], U[l], D[l], xr, y, ids[l])
+        if l == 0:
+            y0 = y.clone()
         xr.add_(y)
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(dev)
     eng.sync()
     assert torch.allclose(x, xr, rtol=1e-4, atol=1e-3), "graph stack and per-layer calls disagree"
+    parity = None
+    if rank == 0 and not args.no_parity:
+        # layer 0 of the timed model (every expert, wherever it lives: the seeds are per expert)
+        # against the C oracle: router + top-k + expert FFNs + combine on the same bytes
+        def synth_bytes(t, m, n, seed):
+            qk, bs = BLK[t]
+            src = torch.empty(m * n, dtype=torch.float32, device=dev)
+            eng.synth_normal_dev(seed, src, 0.0, 0.02)
+            q = torch.empty(m * n // qk * bs, dtype=torch.uint8, device=dev)
+            eng.quantize_dev(t, src, q)
+            return q.cpu().numpy()
+        wg = np.stack([synth_bytes(tq, ff, dm, 3 * e + 1) for e in range(E)])
+        wu = np.stack([synth_bytes(tq, ff, dm, 3 * e + 2) for e in range(E)])
+        wd = np.stack([synth_bytes(c["td"], dm, ff, 3 * e + 3) for e in range(E)])
+        t0 = time.perf_counter()
+        y_ref, ids_ref, _ = oracle.moe_ffn(R[0].cpu().numpy(), E, k, tq, wg, tq, wu, c["td"], wd, dm, ff,
+                                          x0.cpu().numpy())
+        got = y0.cpu().numpy().astype(np.float64)
+        err = got - y_ref.astype(np.float64)
+        rel = float(np.linalg.norm(err) / max(np.linalg.norm(y_ref), 1e-30))
+        mx = float(np.abs(err).max())
+        same_ids = bool(np.array_equal(ids[0].cpu().numpy(), ids_ref))
+        parity = {"rel_l2": rel, "max_abs": mx, "ids_bit_exact": same_ids, "layers": 1, "tokens": T,
+                  "pass": rel <= 1e-4 and mx <= 1e-3 and same_ids, "tolerance": {"rel_l2": 1e-4, "max_abs": 1e-3},
+                  "vs": "oracle/ moe_ffn (C restatement of the reference CPU path) on layer 0's bytes, all experts",
+                  "oracle_s": round(time.perf_counter() - t0, 2)}
+        del wg, wu, wd
     distinct = [len(np.unique(i.cpu().numpy())) for i in ids]
     step_bytes = L * router_bytes(c) + sum(distinct) * expert_bytes(c)
     barrier(world)
@@ -544,6 +575,8 @@ def run_moe(args):
             "roofline": roofline, "e2e": e2e, "clocks": clocks,
             "gpu_launches": args.steps * L * (7 if ep else 6),  # per rank: router, top-k, grouping, 2 GEMVs, combine (+EP signal)
         }
+        if parity is not None:
+            line["parity"] = parity
         print(json.dumps(line), flush=True)
     if peers is not None:
         peers.close()
@@ -614,7 +647,10 @@ def run_ours(args):
     # ---- resident weights, generated and quantized on the device
     scratch = torch.empty(max(ffl * kin, dm * ffl), dtype=torch.float32, device=dev)
     want_cpu = (rank == 0 and world == 1 and not args.no_cpu_baseline)
-    S_cpu = 3 if want_cpu else 0
+    # parity of the timed stack: every layer's bytes kept on the host for the CPU oracle (rank 0
+    # of an unsharded run; the sharded configs hold only a shard per rank)
+    want_parity = rank == 0 and not tp and not args.no_parity
+    S_cpu = L if want_parity else (3 if want_cpu else 0)
     G, U, D, raw = [], [], [], []
     seed0 = 1_000_003 * (rank + 1)
 
@@ -690,6 +726,23 @@ def run_ours(args):
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(dev)
+    parity = None
+    if want_parity:
+        # the first row of the timed step's output (x_L = the whole stack applied to x_0)
+        # against the C oracle run on the same bytes, layer by layer
+        got = x[0, :dm].cpu().numpy().astype(np.float64)
+        xr = x0[0].cpu().numpy().copy()
+        t0 = time.perf_counter()
+        for l in range(L):
+            xr[:dm] += oracle_layer(c, *raw[l], xr)
+        ref = xr[:dm].astype(np.float64)
+        err = got - ref
+        rel = float(np.linalg.norm(err) / max(np.linalg.norm(ref), 1e-30))
+        mx = float(np.abs(err).max())
+        parity = {"rel_l2": rel, "max_abs": mx, "layers": L, "row": 0, "pass": rel <= 1e-4 and mx <= 1e-3,
+                  "tolerance": {"rel_l2": 1e-4, "max_abs": 1e-3},
+                  "vs": "oracle/ (C restatement of the reference CPU path, f32) on the same weight bytes",
+                  "oracle_s": round(time.perf_counter() - t0, 2)}
     barrier(world)
 
     sampler = ClockSampler(local)
@@ -792,7 +845,7 @@ def run_ours(args):
     cpu = None
     if want_cpu:
         x_np = x0[0].cpu().numpy()
-        cpu, ok = cpu_baseline(c, raw, x_np, args.cpu_seconds)
+        cpu, ok = cpu_baseline(c, raw[:3], x_np, args.cpu_seconds)
 
     if rank == 0:
         line = {
@@ -815,6 +868,8 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if parity is not None:
+            line["parity"] = parity
         print(json.dumps(line), flush=True)
     if peers is not None:
         peers.close()
@@ -1078,6 +1133,7 @@ def main():
     ap.add_argument("--ep", action="store_true", help="expert-parallel MoE over the ranks (qwen3moe)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed stack's output")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

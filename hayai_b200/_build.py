@@ -66,8 +66,12 @@ def gen_tables(force: bool = False) -> str:
         if force or _newer(TABLES, srcs + [script]):
             _run([sys.executable, script, REFERENCE, TABLES])
     elif not os.path.exists(TABLES):
+        missing = [s for s in srcs if not os.path.exists(s)]
         raise RuntimeError(
-            f"IQ codebook header {TABLES} is missing and the reference sources are not available at {REFERENCE}")
+            "cannot build: the IQ2/IQ3/IQ4 codebooks (GGUF format constants) are generated at build time from "
+            f"the reference's sources, and these are missing: {', '.join(missing)}.  Check out aitups/hayai "
+            f"v0.2.3 beside this repository (expected at {REFERENCE}) or set HAYAI_REFERENCE to its path; "
+            f"the generated header ({TABLES}) is not kept in the repository")
     return TABLES
 
 

@@ -25,6 +25,8 @@
 // over registers.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+
 #include "gemv_launch.h"
 #include "gemv_tma.cuh"
 
@@ -652,9 +654,22 @@ static cudaError_t launch_stack_t(const StackLaunch& s, int num_sms, int smem_li
     return cudaLaunchCooperativeKernel((const void*)kern, dim3(num_sms), dim3(kTThreads), args, smem, stream);
 }
 
+static bool flow_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("HAYAI_FLOW_KERNEL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
 // The CTA count the kernel runs with: one per SM.
 cudaError_t launch_ffn_stack(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
                              cudaStream_t stream, bool dry, size_t* scratch_bytes) {
+    if (s.tp_size <= 1 && flow_enabled()) {
+        const cudaError_t e = launch_ffn_flow(type_a, type_d, s, num_sms, smem_limit, stream, dry, scratch_bytes);
+        if (e != cudaErrorInvalidConfiguration) return e;
+        cudaGetLastError();
+    }
 #define HC_STACK_CASE(TA, FAT, TD, FDT) \
     if (type_a == TA && type_d == TD)   \
         return launch_stack_t<FAT, FDT>(s, num_sms, smem_limit, stream, dry, scratch_bytes);

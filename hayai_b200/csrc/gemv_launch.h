@@ -56,8 +56,13 @@ struct StackLaunch {
 };
 // cudaErrorInvalidConfiguration: the shapes or formats are not covered (use the per-layer
 // kernels).  dry = only check that the launch is possible and report the scratch bytes.
+// Single-GPU stacks the dataflow kernel covers (ffn_flow.cu) run on it, the others on the
+// phase-barrier kernel (ffn_stack.cu); HAYAI_FLOW_KERNEL=0 in the environment keeps every
+// stack on the latter.
 cudaError_t launch_ffn_stack(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
                              cudaStream_t stream, bool dry, size_t* scratch_bytes);
+cudaError_t launch_ffn_flow(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
+                            cudaStream_t stream, bool dry, size_t* scratch_bytes);
 
 // Batched GEMV on the tcgen05 tensor cores (gemm_tc.cu) for Q8_0, Q4_K and Q6_K, 8..128 rows of
 // x, M a multiple of 128 and K of the format's tile-block image (128 or 256).  w2 != nullptr:

@@ -38,7 +38,7 @@
 namespace hc {
 namespace flow {
 
-constexpr int kPartBlocks = 16;  // down K-part: 16 super-blocks = 4096 elements of h
+constexpr int kPartBlocks = 16;  // down K-parts: at most 16 super-blocks (4096 elements of h) each
 constexpr int kMaxS = 6;
 constexpr int kFW = 2;                            // finisher warps
 constexpr int kThreads = (kCW + 1 + kFW) * 32;    // consumers, producer, finishers
@@ -90,6 +90,7 @@ struct Geo {
     int nbk_a, nbk_d;  // kernel blocks per row
     int ta, td;        // 16-row tiles of gate/up and of down
     int np;            // down K-parts
+    int pb;            // blocks per part (the last part may hold fewer)
     int tab_a;         // gate/up table bytes
     int tab_p;         // bytes of one down table part (16 blocks)
     __host__ __device__ Geo(int dm, int ff) {
@@ -98,14 +99,15 @@ struct Geo {
         ta = ff / 16;
         td = dm / 16;
         np = (nbk_d + kPartBlocks - 1) / kPartBlocks;
+        pb = kPartBlocks;  // (parts of equal size measured slower: their stages are smaller)
         tab_a = nbk_a * table_entries_per_block<FA>(1) * 8;
-        tab_p = kPartBlocks * table_entries_per_block<FD>(1) * 8;
+        tab_p = pb * table_entries_per_block<FD>(1) * 8;
     }
     __host__ __device__ int part_blocks(int p) const {
-        return nbk_d - p * kPartBlocks < kPartBlocks ? nbk_d - p * kPartBlocks : kPartBlocks;
+        return nbk_d - p * pb < pb ? nbk_d - p * pb : pb;
     }
     __host__ __device__ int part_tiles(int p) const {  // gate/up tiles producing h of part p
-        const int t0 = p * kPartBlocks * FD::kBlockElems / 16;
+        const int t0 = p * pb * FD::kBlockElems / 16;
         const int t1 = t0 + part_blocks(p) * FD::kBlockElems / 16;
         return (t1 < ta ? t1 : ta) - t0;
     }
@@ -232,11 +234,12 @@ __device__ bool produce_layer(Prod& P, Desc* desc, const Args& a, const Geo<FA, 
     // part & 1 once the gate/up tiles of that part are done and the slot's previous part is
     // consumed
     int cur = -1;
+    unsigned next_ready = 0;  // the next part's counter, read ahead (its latency overlaps the copies)
     c = take(cnt + kCtrDn, lane);
     while (c < G.np * G.td) {
         const int nc = take(cnt + kCtrDn, lane);
         const int p = c / G.td, tile = c - p * G.td;
-        const int kb0 = p * kPartBlocks, kb1 = kb0 + G.part_blocks(p);
+        const int kb0 = p * G.pb, kb1 = kb0 + G.part_blocks(p);
         bool first = true;
         for (int kb = kb0; kb < kb1; kb += a.dsb) {
             const int n = min(a.dsb, kb1 - kb);
@@ -251,7 +254,8 @@ __device__ bool produce_layer(Prod& P, Desc* desc, const Args& a, const Geo<FA, 
                 }
                 bool ok = true;
                 if (lane == 0) {
-                    ok = wait_ge(cnt + kHcnt + p, (unsigned)G.part_tiles(p), a.err);
+                    const unsigned want = (unsigned)G.part_tiles(p);
+                    ok = (p == cur + 1 && next_ready >= want) || wait_ge(cnt + kHcnt + p, want, a.err);
                     if (ok) {
                         // h was written through the generic proxy by other SMs; the copy reads it
                         // through the async proxy
@@ -268,6 +272,7 @@ __device__ bool produce_layer(Prod& P, Desc* desc, const Args& a, const Geo<FA, 
                 if (ts) ++P.loads1;
                 else ++P.loads0;
                 cur = p;
+                if (lane == 0 && p + 1 < G.np) next_ready = ld_acq(cnt + kHcnt + p + 1);
             }
             first = false;
             const uint32_t full = r.full0 + 8 * r.slot;
@@ -362,7 +367,7 @@ __device__ void finisher(const Args& a, const Geo<FA, FD>& G, int f, uint32_t tf
             const float h = grow < a.ff ? silu_mul(inv * f0, inv * f1) : 0.f;
             pack_rows<FD>(a.htab, tile, lane, h, bad);
             __syncwarp();
-            if (lane == 0) red_rel(cnt + kHcnt + tile * 16 / (kPartBlocks * FD::kBlockElems), 1u);
+            if (lane == 0) red_rel(cnt + kHcnt + tile * 16 / (G.pb * FD::kBlockElems), 1u);
             continue;
         }
         unsigned* tc = cnt + kHcnt + G.np + tile;
@@ -616,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_flow_kernel(Args a) {
                 }
                 if (warp < d.n)
                     stage_unit<FD, 1>(r.base + r.slot * r.slot_bytes + warp * FD::kTile,
-                                      d.kb - d.part * kPartBlocks + warp, ctx, yA, yB, pA, pB);
+                                      d.kb - d.part * G.pb + warp, ctx, yA, yB, pA, pB);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(r.empty0 + 8 * r.slot);
                 r.advance();

@@ -204,7 +204,8 @@ struct TcDq<TcQ80> {
     __device__ __forceinline__ bool bad() const { return (dbits & 0x40004000u) != 0; }
 };
 
-// Q4_K image (2304 B, 256 K): [hdr: row r at 16r = d, dmin, 12 scale bytes][q0: (r,t) at
+// Q4_K image (2304 B, 256 K): [hdr: row r at 16r = d, dmin, then 24 bits per chunk c at byte
+// 4 + 3c: sc(2c) | sc(2c+1) << 6 | m(2c) << 12 | m(2c+1) << 18][q0: (r,t) at
 // 256 + 16(4r+t) = qs bytes 32t..32t+15][q1: at 1280 + 16(4r+t) = qs bytes 32t+16..32t+31].
 // qs byte 32c + l holds element 64c + l (low nibble, sub-block 2c) and 64c + 32 + l (high
 // nibble, sub-block 2c + 1), so chunk c is piece t = c of every row.  Item = (row r, piece p):
@@ -226,17 +227,15 @@ struct TcDq<TcQ4K> {
     __device__ __forceinline__ void chunk(const uint32_t* ws, int c, uint8_t* ahi, uint8_t* alo) {
         const uint4 hd = *reinterpret_cast<const uint4*>(ws + hw);
         const uint4 q = *reinterpret_cast<const uint4*>(ws + qw + 4 * c);
-        // get_scale_min_k4 of sub-blocks 2c (byte 0) and 2c + 1 (byte 1)
-        const int sh = 16 * (c & 1);
-        const uint32_t Y = hd.y >> sh, Z = hd.z >> sh, W = hd.w >> sh;
-        const uint32_t psc = c < 2 ? (Y & 0x3F3Fu) : ((W & 0x0F0Fu) | ((Y >> 2) & 0x3030u));
-        const uint32_t pm = c < 2 ? (Z & 0x3F3Fu) : (((W >> 4) & 0x0F0Fu) | ((Z >> 2) & 0x3030u));
+        // get_scale_min_k4 of sub-blocks 2c and 2c + 1 (regrouped by the repack)
+        const uint32_t V = __funnelshift_r(c < 2 ? hd.y : (c == 2 ? hd.z : hd.w), c < 2 ? hd.z : hd.w, (24 * c) & 31);
         const float2 dd = __half22float2(u32_as_h2(hd.x));
         float d1[2], m1[2];
 #pragma unroll
         for (int s = 0; s < 2; ++s) {
-            d1[s] = (dd.x * u8_to_f32(psc, s)) * kTcWScale;  // d1 = d sc, m1v = dmin m (exact)
-            m1[s] = (dd.y * u8_to_f32(pm, s)) * kTcWScale;
+            const float sc = (float)((V >> (6 * s)) & 63u), mn = (float)((V >> (12 + 6 * s)) & 63u);
+            d1[s] = (dd.x * sc) * kTcWScale;  // d1 = d sc, m1v = dmin m (exact)
+            m1[s] = (dd.y * mn) * kTcWScale;
             big = fmaxf(big, fmaf(fabsf(d1[s]), 15.f, fabsf(m1[s])));
         }
         const uint32_t words[4] = {q.x, q.y, q.z, q.w};

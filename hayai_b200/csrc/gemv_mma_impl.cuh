@@ -251,19 +251,23 @@ struct Q4KBlk {
 };
 
 // Q4_K (sc, m) of sub-blocks 2t, 2t+1 of one row, folded into the per-sub-block factors
-// c = 64 d sc and k = c + dmin m (branch-free over t: t < 2 reads the plain 6-bit fields,
-// t >= 2 the split ones).
+// c = 64 d sc and k = c + dmin m.  The header (repack.cu) holds lane t's four 6-bit fields as
+// 24 bits at byte 4 + 3t: one funnel shift brings them down, and each field becomes f32 under
+// the 2^23 magic (a LOP3 and an FADD; a field left at bits 6 or 12 comes out scaled by 64 or
+// 4096, which the factor it multiplies absorbs exactly).
 __device__ __forceinline__ void q4k_factors(const uint4& h, int t, float& c0, float& k0, float& c1, float& k1) {
-    const int sh = 16 * (t & 1);
-    const uint32_t Y = h.y >> sh, Z = h.z >> sh, W = h.w >> sh;
-    const uint32_t psc = t < 2 ? (Y & 0x3F3Fu) : ((W & 0x0F0Fu) | ((Y >> 2) & 0x3030u));
-    const uint32_t pm = t < 2 ? (Z & 0x3F3Fu) : (((W >> 4) & 0x0F0Fu) | ((Z >> 2) & 0x3030u));
+    // bits 24t.. of the 96 bits (y, z, w): t = 0, 1 from (y, z), t = 2 from (z, w), t = 3 from w
+    const uint32_t V = __funnelshift_r(t < 2 ? h.y : (t == 2 ? h.z : h.w), t < 2 ? h.z : h.w, (24 * t) & 31);
     const float2 dd = __half22float2(u32_as_h2(h.x));
-    const float d64 = 64.f * dd.x;
-    c0 = d64 * u8_to_f32(psc, 0);
-    c1 = d64 * u8_to_f32(psc, 1);
-    k0 = fmaf(dd.y, u8_to_f32(pm, 0), c0);
-    k1 = fmaf(dd.y, u8_to_f32(pm, 1), c1);
+    const float s0 = __uint_as_float((V & 0x3Fu) | 0x4B000000u) - 8388608.0f;               // sc(2t)
+    const float s1 = __uint_as_float((V & 0xFC0u) | 0x4B000000u) - 8388608.0f;              // 64 sc(2t+1)
+    const float m0 = __uint_as_float((V & 0x3F000u) | 0x4B000000u) - 8388608.0f;            // 4096 m(2t)
+    const float m1 = __uint_as_float(((V >> 6) & 0x3F000u) | 0x4B000000u) - 8388608.0f;     // 4096 m(2t+1)
+    c0 = (64.f * dd.x) * s0;
+    c1 = dd.x * s1;
+    const float dm = dd.y * (1.0f / 4096.0f);
+    k0 = fmaf(dm, m0, c0);
+    k1 = fmaf(dm, m1, c1);
 }
 
 // The 8 codes of one Q4_K word as four f16x2 registers, every code as f16(1 + n/64): low

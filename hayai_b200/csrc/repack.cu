@@ -9,7 +9,9 @@
 // consecutive pieces (conflict-free shared-memory reads) and 128-bit loads are always
 // aligned.  Rows past M are zero.
 //
-//  Q4_K image (2304 B):  [hdr: row r at 16r, the block's first 16 bytes (d, dmin, scales)]
+//  Q4_K image (2304 B):  [hdr: row r at 16r: d, dmin (f16), then the 6-bit scales and mins
+//                         regrouped per lane: bytes 4 + 3t..+2 hold sc(2t) | sc(2t+1) << 6 |
+//                         m(2t) << 12 | m(2t+1) << 18 (get_scale_min_k4, q4k.rs:34-43)]
 //                        [q0: (r,t) at 256 + 16(4r+t) = qs bytes 32t..32t+15]
 //                        [q1: (r,t) at 1280 + 16(4r+t) = qs bytes 32t+16..32t+31]
 //  Q6_K image (3360 B), lane-distributed: lane t of a row owns half h = t >> 1, l in
@@ -96,7 +98,27 @@ __device__ __forceinline__ uint32_t tiled_word(const uint8_t* __restrict__ raw, 
         int r, off;
         if (w < 64) {
             r = w >> 2;
-            off = 4 * (w & 3);
+            const int row = tile * 16 + r;
+            if (row >= M) return 0u;
+            const uint8_t* blk = raw + (size_t)row * raw_rb + (size_t)kb * 144;
+            if ((w & 3) == 0) return rd4(blk);  // d, dmin
+            // the 12 packed scale bytes, regrouped: lane t's 24 bits at byte 3t
+            const uint8_t* q = blk + 4;
+            uint8_t f[12];
+            for (int t = 0; t < 4; ++t) {
+                uint32_t v = 0;
+                for (int h = 0; h < 2; ++h) {
+                    const int j = 2 * t + h;
+                    const uint32_t sc = j < 4 ? (q[j] & 63u) : ((q[j + 4] & 0xFu) | ((q[j - 4] >> 6) << 4));
+                    const uint32_t mn = j < 4 ? (q[j + 4] & 63u) : ((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
+                    v |= sc << (6 * h);
+                    v |= mn << (12 + 6 * h);
+                }
+                f[3 * t] = (uint8_t)v;
+                f[3 * t + 1] = (uint8_t)(v >> 8);
+                f[3 * t + 2] = (uint8_t)(v >> 16);
+            }
+            return rd4(f + 4 * ((w & 3) - 1));
         } else {
             const int q = w >= 320, p = (w - (q ? 320 : 64)) >> 2, j = w & 3, t = p & 3;
             r = p >> 2;

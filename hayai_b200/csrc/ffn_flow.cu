@@ -40,7 +40,7 @@ namespace flow {
 
 constexpr int kPartBlocks = 16;  // down K-parts: at most 16 super-blocks (4096 elements of h) each
 constexpr int kMaxS = 6;
-constexpr int kFW = 2;                            // finisher warps
+constexpr int kFW = 3;                            // finisher warps
 constexpr int kThreads = (kCW + 1 + kFW) * 32;    // consumers, producer, finishers
 constexpr int kNT = 8;                            // hand-over slots (chunk partials) to the finishers
 
@@ -323,7 +323,9 @@ __device__ __forceinline__ float sum16(float v) {
     return v;
 }
 
-// Finisher warp: completes the chunks handed over in slots k = f, f + kFW, ... (in order).
+// Finisher warp: completes chunks handed over in slot k % kNT, taking the next chunk index k
+// from a shared counter whenever it is free (a finisher held up by an x tile's wait does not
+// hold up the chunks after it).
 //   gate/up chunk: g, u = the warp sums (8 + 8 warps), h = silu(inv g) * (inv u) into h's table
 //                  in global memory, then the h part's counter (release);
 //   down chunk, not the last K-part: the 16-row partial into `parts`, then the tile's counter;
@@ -334,11 +336,14 @@ __device__ __forceinline__ float sum16(float v) {
 // Global memory latency (stores, release fences, acquire waits) lands here, not on the warps
 // that consume the weight stream.
 template <class FA, class FD>
-__device__ void finisher(const Args& a, const Geo<FA, FD>& G, int f, uint32_t tfull0, uint32_t tfree0,
+__device__ void finisher(const Args& a, const Geo<FA, FD>& G, int* next, uint32_t tfull0, uint32_t tfree0,
                          const float* red, const Meta* meta, const float* s_inv, int lane) {
     bool bad = false;
     const int row = lane & 15;
-    for (int k = f;; k += kFW) {
+    while (true) {
+        int k = 0;
+        if (lane == 0) k = atomicAdd(next, 1);
+        k = __shfl_sync(kFull, k, 0);
         const int ts = k % kNT, use = k / kNT;
         if (!mbar_wait(tfull0 + 8 * ts, use & 1)) {
             if (lane == 0) atomicOr(a.err, 2);
@@ -418,6 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_flow_kernel(Args a) {
     __shared__ float s_red[32];
     __shared__ float s_inv;
     __shared__ int s_abort;
+    __shared__ int s_fnext;  // next chunk index a finisher takes
     __shared__ Desc s_desc[kMaxS];
     const Geo<FA, FD> G(a.dm, a.ff);
     const Smem L = smem_layout<FA, FD>(a.dm, a.ff, a.S, a.slot_bytes);
@@ -455,6 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_flow_kernel(Args a) {
         }
         mbar_fence_init();
         s_abort = 0;
+        s_fnext = 0;
     }
     for (int i = threadIdx.x; i < table_entries_per_block<FD>(1); i += blockDim.x) zero[i] = make_uint2(0u, 0u);
     __syncthreads();
@@ -476,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_flow_kernel(Args a) {
         return;
     }
     if (warp > kCW) {  // ------------------------------------------------ finishers
-        finisher<FA, FD>(a, G, warp - kCW - 1, tfull0, tfree0, red, meta, &s_inv, lane);
+        finisher<FA, FD>(a, G, &s_fnext, tfull0, tfree0, red, meta, &s_inv, lane);
         return;
     }
 

@@ -62,16 +62,20 @@ const char* hc_type_label(int t) {
         case T_Q5_K: return "q5_k";
         case T_IQ4_NL: return "iq4_nl";
         case T_IQ4_XS: return "iq4_xs";
+        case T_F16: return "f16";
+        case T_BF16: return "bf16";
+        case T_Q8_1: return "q8_1";
+        case T_Q8_K: return "q8_k";
         default: return "unknown";
     }
 }
 
 static int block_elems(int t) {
     switch (t) {
-        case T_F32: return 1;
-        case T_Q8_0: case T_Q4_0: case T_Q4_1: case T_Q5_0: case T_Q5_1: case T_IQ4_NL: return 32;
+        case T_F32: case T_F16: case T_BF16: return 1;
+        case T_Q8_0: case T_Q4_0: case T_Q4_1: case T_Q5_0: case T_Q5_1: case T_IQ4_NL: case T_Q8_1: return 32;
         case T_Q4_K: case T_Q6_K: case T_IQ2_XXS: case T_IQ2_XS: case T_IQ2_S: case T_IQ3_XXS: case T_IQ3_S:
-        case T_Q2_K: case T_Q3_K: case T_Q5_K: case T_IQ4_XS:
+        case T_Q2_K: case T_Q3_K: case T_Q5_K: case T_IQ4_XS: case T_Q8_K:
             return 256;
         default: return 0;
     }

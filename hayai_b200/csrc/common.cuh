@@ -31,6 +31,10 @@ enum GgmlType : int {
     T_IQ3_S = 21,
     T_IQ2_S = 22,
     T_IQ4_XS = 23,
+    T_F16 = 1,
+    T_Q8_1 = 9,
+    T_Q8_K = 15,
+    T_BF16 = 30,
 };
 
 constexpr int QK_K = 256;

@@ -1,12 +1,13 @@
-// gemv_simple.cu -- CUDA-core kernels on the raw GGUF layout: F32, the IQ2/IQ3/IQ4 codebook
-// formats, the other GGML block formats (Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q5_K), the toy
-// LUT-Q4 matmul, and the elementwise SwiGLU combine.
+// gemv_simple.cu -- CUDA-core kernels on the raw GGUF layout: F32, F16, BF16, the IQ2/IQ3/IQ4
+// codebook formats, the other GGML block formats (Q4_0, Q4_1, Q5_0, Q5_1, Q8_1, Q2_K, Q3_K,
+// Q5_K, Q8_K), the toy LUT-Q4 matmul, and the elementwise SwiGLU combine.
 //
 // Reference semantics: gemv_f32 (crates/hayai-model/src/quant.rs:358-369), the IQ2 block
 // decoders (crates/hayai-model/src/iq2.rs:504-573, gemv macro :591-626), the IQ3 block
 // decoders (crates/hayai-model/src/iq3.rs:147-220, gemv :258-331), IQ4_NL / IQ4_XS
 // (iq4.rs:36-42, :121-138), Q4_0 / Q4_1 (quant.rs:538-596, :617-650), Q5_0 / Q5_1
 // (q5.rs:26-158), Q2_K (q2k.rs:26-58), Q3_K (q3k.rs:10-30, :52-84), Q5_K (q5k.rs:10-66),
+// gemv_f16 / gemv_bf16 / gemv_q8_1 / gemv_q8_k (quant.rs:371-395, :458-501),
 // cpu_lut_matmul_q4 (crates/hayai-cpu/src/matmul.rs:48-82).
 #include "common.cuh"
 #include "gemv_launch.h"
@@ -276,6 +277,16 @@ __device__ __forceinline__ float group_dot4(const uint8_t* blk, int ib32, int e,
             const uint32_t v = (hi ? ql >> 4 : ql & 0x0Fu) + ((ldb(blk + 16 + e + i) & u) ? 16u : 0u);
             w[i] = d1 * (float)v - m1;
         }
+    } else if constexpr (TYPE == T_Q8_1) {
+        // {f16 d, f16 s, int8 qs[32]}: element j = qs[j] d (s is not read)
+        const float d = ld_f16u(blk);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[i] = (float)(int8_t)ldb(blk + 4 + e + i) * d;
+    } else if constexpr (TYPE == T_Q8_K) {
+        // {f32 d, int8 qs[256], int16 bsums[16]}: element j = qs[j] d (bsums are not read)
+        const float d = __uint_as_float(ld_u32u(blk));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[i] = (float)(int8_t)ldb(blk + 4 + 32 * ib32 + e + i) * d;
     } else if constexpr (TYPE == T_IQ4_XS) {
         const uint32_t sh = ld_u16u(blk + 2);
         const int ls = (int)(((ldb(blk + 4 + ib32 / 2) >> (4 * (ib32 & 1))) & 0x0Fu) | (((sh >> (2 * ib32)) & 3u) << 4));
@@ -400,6 +411,49 @@ __global__ void __launch_bounds__(256) gemv_f32_kernel(const float* __restrict__
     }
 }
 
+// F16 / BF16 rows (quant.rs:371-395): one warp per (row, vector); with K a multiple of 8 every
+// lane reads 16 bytes (8 elements) per step, the warp 512 contiguous bytes; otherwise one
+// element per lane per step.  BF16 is the upper half of an f32 (exact widening).
+template <bool BF>
+__device__ __forceinline__ float half_to_f32(uint32_t h) {
+    return BF ? __uint_as_float(h << 16) : h2f((uint16_t)h);
+}
+
+template <bool BF>
+__global__ void __launch_bounds__(256) gemv_half_kernel(const uint16_t* __restrict__ w, size_t row_elems, int M, int K,
+                                                        const float* __restrict__ x, int ldx, float* __restrict__ y,
+                                                        int ldy, const float* resid, int ldr, int nvec) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    const bool vec = (K & 7) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 && (ldx & 3) == 0 &&
+                     (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    for (int rv = warp; rv < M * nvec; rv += nwarps) {
+        const int row = rv % M, v = rv / M;
+        const uint16_t* wr = w + (size_t)row * row_elems;
+        const float* xv = x + (size_t)v * ldx;
+        float s = 0.f;
+        if (vec) {
+            for (int c = 8 * lane; c < K; c += 256) {
+                const uint4 q = ldg_stream128(wr + c);
+                const float4 xa = __ldg(reinterpret_cast<const float4*>(xv + c));
+                const float4 xb = __ldg(reinterpret_cast<const float4*>(xv + c + 4));
+                s += half_to_f32<BF>(q.x & 0xFFFFu) * xa.x;
+                s += half_to_f32<BF>(q.x >> 16) * xa.y;
+                s += half_to_f32<BF>(q.y & 0xFFFFu) * xa.z;
+                s += half_to_f32<BF>(q.y >> 16) * xa.w;
+                s += half_to_f32<BF>(q.z & 0xFFFFu) * xb.x;
+                s += half_to_f32<BF>(q.z >> 16) * xb.y;
+                s += half_to_f32<BF>(q.w & 0xFFFFu) * xb.z;
+                s += half_to_f32<BF>(q.w >> 16) * xb.w;
+            }
+        } else {
+            for (int c = lane; c < K; c += 32) s += half_to_f32<BF>(__ldg(wr + c)) * __ldg(xv + c);
+        }
+        s = warp_sum(s);
+        if (lane == 0) y[(size_t)v * ldy + row] = (resid ? resid[(size_t)v * ldr + row] : 0.f) + s;
+    }
+}
+
 static int grid_for(int work_warps) {
     int blocks = (work_warps + 7) / 8;
     return blocks < 1 ? 1 : (blocks > 65535 ? 65535 : blocks);
@@ -409,6 +463,7 @@ bool gemv_simple_supported(int type) {
     switch (type) {
         case T_F32: case T_IQ2_XXS: case T_IQ2_XS: case T_IQ2_S: case T_IQ3_XXS: case T_IQ3_S: case T_Q4_0:
         case T_Q4_1: case T_Q5_0: case T_Q5_1: case T_Q2_K: case T_Q3_K: case T_Q5_K: case T_IQ4_NL: case T_IQ4_XS:
+        case T_F16: case T_BF16: case T_Q8_1: case T_Q8_K:
             return true;
         default:
             return false;
@@ -422,6 +477,14 @@ cudaError_t launch_gemv_simple(int type, const uint8_t* w, size_t row_bytes, int
         case T_F32:
             gemv_f32_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const float*>(w), row_bytes / 4, M, K, x, ldx,
                                                       y, ldy, resid, ldr, nvec);
+            break;
+        case T_F16:
+            gemv_half_kernel<false><<<grid, 256, 0, stream>>>(reinterpret_cast<const uint16_t*>(w), row_bytes / 2, M, K,
+                                                             x, ldx, y, ldy, resid, ldr, nvec);
+            break;
+        case T_BF16:
+            gemv_half_kernel<true><<<grid, 256, 0, stream>>>(reinterpret_cast<const uint16_t*>(w), row_bytes / 2, M, K,
+                                                            x, ldx, y, ldy, resid, ldr, nvec);
             break;
         case T_IQ2_XXS:
             gemv_group_kernel<T_IQ2_XXS, 256, 66><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
@@ -452,6 +515,8 @@ cudaError_t launch_gemv_simple(int type, const uint8_t* w, size_t row_bytes, int
         HC_GROUP_CASE(T_Q3_K, 256, 110)
         HC_GROUP_CASE(T_Q5_K, 256, 176)
         HC_GROUP_CASE(T_IQ4_XS, 256, 136)
+        HC_GROUP_CASE(T_Q8_1, 32, 36)
+        HC_GROUP_CASE(T_Q8_K, 256, 292)
 #undef HC_GROUP_CASE
         default:
             return cudaErrorInvalidValue;

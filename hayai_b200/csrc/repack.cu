@@ -54,6 +54,9 @@ size_t raw_row_bytes(int type, int K) {
         case T_Q3_K: return (size_t)K / 256 * 110;
         case T_Q5_K: return (size_t)K / 256 * 176;
         case T_IQ4_XS: return (size_t)K / 256 * 136;
+        case T_F16: case T_BF16: return (size_t)K * 2;
+        case T_Q8_1: return (size_t)K / 32 * 36;
+        case T_Q8_K: return (size_t)K / 256 * 292;
         default: return 0;
     }
 }

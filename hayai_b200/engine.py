@@ -25,14 +25,17 @@ from ._lib import lib
 # GgmlType ids (crates/hayai-model/src/gguf_types.rs:6-40)
 F32, Q8_0, Q4_K, Q6_K, IQ2_XXS, IQ2_XS, IQ3_XXS, IQ3_S, IQ2_S = 0, 8, 12, 14, 16, 17, 18, 21, 22
 Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q5_K, IQ4_NL, IQ4_XS = 2, 3, 6, 7, 10, 11, 13, 20, 23
+F16, Q8_1, Q8_K, BF16 = 1, 9, 15, 30
 TYPE_LABELS = {F32: "f32", Q8_0: "q8_0", Q4_K: "q4_k", Q6_K: "q6_k", IQ2_XXS: "iq2_xxs", IQ2_XS: "iq2_xs",
                IQ2_S: "iq2_s", IQ3_XXS: "iq3_xxs", IQ3_S: "iq3_s", Q4_0: "q4_0", Q4_1: "q4_1", Q5_0: "q5_0",
-               Q5_1: "q5_1", Q2_K: "q2_k", Q3_K: "q3_k", Q5_K: "q5_k", IQ4_NL: "iq4_nl", IQ4_XS: "iq4_xs"}
+               Q5_1: "q5_1", Q2_K: "q2_k", Q3_K: "q3_k", Q5_K: "q5_k", IQ4_NL: "iq4_nl", IQ4_XS: "iq4_xs",
+               F16: "f16", BF16: "bf16", Q8_1: "q8_1", Q8_K: "q8_k"}
 LABEL_TYPES = {v: k for k, v in TYPE_LABELS.items()}
 # (elements, bytes) per block: gemv_row_bytes (compute.rs:877-907)
 BLOCK = {F32: (1, 4), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), IQ2_XXS: (256, 66), IQ2_XS: (256, 74),
          IQ2_S: (256, 82), IQ3_XXS: (256, 98), IQ3_S: (256, 110), Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22),
-         Q5_1: (32, 24), Q2_K: (256, 84), Q3_K: (256, 110), Q5_K: (256, 176), IQ4_NL: (32, 18), IQ4_XS: (256, 136)}
+         Q5_1: (32, 24), Q2_K: (256, 84), Q3_K: (256, 110), Q5_K: (256, 176), IQ4_NL: (32, 18), IQ4_XS: (256, 136),
+         F16: (1, 2), BF16: (1, 2), Q8_1: (32, 36), Q8_K: (256, 292)}
 
 
 class CudaError(RuntimeError):

@@ -14,8 +14,9 @@
  *
  * Conventions
  *  - ggml_type uses GGUF's GgmlType ids (crates/hayai-model/src/gguf_types.rs:6-40):
- *    F32=0, Q4_0=2, Q4_1=3, Q5_0=6, Q5_1=7, Q8_0=8, Q2_K=10, Q3_K=11, Q4_K=12, Q5_K=13,
- *    Q6_K=14, IQ2_XXS=16, IQ2_XS=17, IQ3_XXS=18, IQ4_NL=20, IQ3_S=21, IQ2_S=22, IQ4_XS=23.
+ *    F32=0, F16=1, Q4_0=2, Q4_1=3, Q5_0=6, Q5_1=7, Q8_0=8, Q8_1=9, Q2_K=10, Q3_K=11, Q4_K=12,
+ *    Q5_K=13, Q6_K=14, Q8_K=15, IQ2_XXS=16, IQ2_XS=17, IQ3_XXS=18, IQ4_NL=20, IQ3_S=21, IQ2_S=22,
+ *    IQ4_XS=23, BF16=30 (the formats of gemv_row_bytes, compute.rs:877-907).
  *    Q4_K, Q6_K and Q8_0 run on the tensor-core kernels (tile-major upload); the others on
  *    CUDA-core kernels over the raw GGUF rows.  Any other id is HC_ERR_UNSUPPORTED.
  *  - A weight matrix is GGUF-layout: nrows = m rows of ncols = n columns, each row

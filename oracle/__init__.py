@@ -20,6 +20,7 @@ LIB_PATH = os.path.join(_HERE, "_build", "liboracle.so")
 # GgmlType ids (crates/hayai-model/src/gguf_types.rs:6-40)
 F32, Q8_0, Q4_K, Q6_K, IQ2_XXS, IQ2_XS, IQ3_XXS, IQ3_S, IQ2_S = 0, 8, 12, 14, 16, 17, 18, 21, 22
 Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q5_K, IQ4_NL, IQ4_XS = 2, 3, 6, 7, 10, 11, 13, 20, 23
+F16, Q8_1, Q8_K, BF16 = 1, 9, 15, 30
 
 # (elements per block, bytes per block), crates/hayai-opencl/src/compute.rs:877-907; q5.rs:8-9,
 # q5k.rs:8, q2k.rs:8, q3k.rs:8, iq4.rs:8-11
@@ -28,6 +29,7 @@ BLOCK = {
     IQ2_XS: (256, 74), IQ2_S: (256, 82), IQ3_XXS: (256, 98), IQ3_S: (256, 110),
     Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22), Q5_1: (32, 24), Q2_K: (256, 84), Q3_K: (256, 110),
     Q5_K: (256, 176), IQ4_NL: (32, 18), IQ4_XS: (256, 136),
+    F16: (1, 2), BF16: (1, 2), Q8_1: (32, 36), Q8_K: (256, 292),
 }
 
 _lib = None
@@ -153,7 +155,7 @@ def dequant(ggml_type: int, w: np.ndarray, n: int) -> np.ndarray:
 def gemv(ggml_type: int, m: int, n: int, w: np.ndarray, x: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.float32)
     w = np.ascontiguousarray(w)
-    if ggml_type == F32:
+    if w.dtype != np.uint8:  # F32 / F16 / BF16 element arrays: their bytes
         w = w.view(np.uint8)
     assert w.nbytes >= m * row_bytes(ggml_type, n), "weights too small"
     y = np.empty(m, dtype=np.float32)

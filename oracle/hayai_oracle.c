@@ -67,12 +67,14 @@ int or_get_threads(void) {
 #define Q5_K_BLOCK 176
 #define IQ4_NL_BLOCK 18
 #define IQ4_XS_BLOCK 136
+#define Q8_1_BLOCK 36
+#define Q8_K_BLOCK 292
 
 /* GgmlType ids, crates/hayai-model/src/gguf_types.rs:6-40 */
 enum {
     T_F32 = 0, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q2_K = 10, T_Q3_K = 11,
     T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ2_XS = 17, T_IQ3_XXS = 18, T_IQ4_NL = 20,
-    T_IQ3_S = 21, T_IQ2_S = 22, T_IQ4_XS = 23
+    T_IQ3_S = 21, T_IQ2_S = 22, T_IQ4_XS = 23, T_F16 = 1, T_Q8_1 = 9, T_Q8_K = 15, T_BF16 = 30
 };
 
 /* ------------------------------------------------------------------------ */
@@ -505,6 +507,86 @@ int or_gemv_f32(size_t nrows, size_t ncols, const uint8_t* data, const float* in
     }
     return 0;
 }
+
+/* crates/hayai-model/src/quant.rs:371-382: w = f16_to_f32(bits), sum += w * x, sequential. */
+int or_gemv_f16(size_t nrows, size_t ncols, const uint8_t* data, const float* input, float* output) {
+    #pragma omp parallel for schedule(static)
+    for (size_t row = 0; row < nrows; row++) {
+        float sum = 0.0f;
+        for (size_t c = 0; c < ncols; c++) sum += rd_f16(data + (row * ncols + c) * 2) * input[c];
+        output[row] = sum;
+    }
+    return 0;
+}
+
+static inline float rd_bf16(const uint8_t* p) {
+    uint32_t bits = ((uint32_t)p[0] | ((uint32_t)p[1] << 8)) << 16;
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* crates/hayai-model/src/quant.rs:384-395: w = f32::from_bits(bits << 16). */
+int or_gemv_bf16(size_t nrows, size_t ncols, const uint8_t* data, const float* input, float* output) {
+    #pragma omp parallel for schedule(static)
+    for (size_t row = 0; row < nrows; row++) {
+        float sum = 0.0f;
+        for (size_t c = 0; c < ncols; c++) sum += rd_bf16(data + (row * ncols + c) * 2) * input[c];
+        output[row] = sum;
+    }
+    return 0;
+}
+
+/* crates/hayai-model/src/quant.rs:458-475: {f16 d, f16 s, int8 qs[32]}; sum += (q as f32) * d * x
+ * (s, the block's sum, is not read). */
+int or_gemv_q8_1(size_t nrows, size_t ncols, const uint8_t* data, const float* input, float* output) {
+    if (ncols % 32) return -1;
+    size_t bpr = ncols / 32, rb = bpr * Q8_1_BLOCK;
+    #pragma omp parallel for schedule(static)
+    for (size_t row = 0; row < nrows; row++) {
+        float sum = 0.0f;
+        for (size_t b = 0; b < bpr; b++) {
+            const uint8_t* base = data + row * rb + b * Q8_1_BLOCK;
+            float d = rd_f16(base);
+            for (int j = 0; j < 32; j++) sum += (float)(int8_t)base[4 + j] * d * input[b * 32 + j];
+        }
+        output[row] = sum;
+    }
+    return 0;
+}
+
+/* crates/hayai-model/src/quant.rs:477-501: {f32 d, int8 qs[256], int16 bsums[16]};
+ * sum += (q as f32) * d * x (bsums are not read). */
+int or_gemv_q8_k(size_t nrows, size_t ncols, const uint8_t* data, const float* input, float* output) {
+    if (ncols % 256) return -1;
+    size_t bpr = ncols / 256, rb = bpr * Q8_K_BLOCK;
+    #pragma omp parallel for schedule(static)
+    for (size_t row = 0; row < nrows; row++) {
+        float sum = 0.0f;
+        for (size_t b = 0; b < bpr; b++) {
+            const uint8_t* base = data + row * rb + b * Q8_K_BLOCK;
+            float d;
+            memcpy(&d, base, 4);
+            for (int j = 0; j < 256; j++) sum += (float)(int8_t)base[4 + j] * d * input[b * 256 + j];
+        }
+        output[row] = sum;
+    }
+    return 0;
+}
+
+static void dequant_q8_1_block(const uint8_t* b, float* y) {
+    float d = rd_f16(b);
+    for (int j = 0; j < 32; j++) y[j] = (float)(int8_t)b[4 + j] * d;
+}
+
+static void dequant_q8_k_block(const uint8_t* b, float* y) {
+    float d;
+    memcpy(&d, b, 4);
+    for (int j = 0; j < 256; j++) y[j] = (float)(int8_t)b[4 + j] * d;
+}
+
+static void dequant_f16_elem(const uint8_t* b, float* y) { y[0] = rd_f16(b); }
+static void dequant_bf16_elem(const uint8_t* b, float* y) { y[0] = rd_bf16(b); }
 
 /* ------------------------------------------------------------------------ */
 /* IQ2 / IQ3 codebook formats                                                */
@@ -1018,6 +1100,10 @@ int or_dequant(int type, const uint8_t* bytes, size_t n, float* out) {
         case T_Q3_K: fn = dequant_q3_k_block; blk = Q3_K_BLOCK; break;
         case T_Q5_K: fn = dequant_q5_k_block; blk = Q5_K_BLOCK; break;
         case T_IQ4_XS: fn = dequant_iq4_xs_block; blk = IQ4_XS_BLOCK; break;
+        case T_Q8_1: fn = dequant_q8_1_block; blk = Q8_1_BLOCK; qk = 32; break;
+        case T_Q8_K: fn = dequant_q8_k_block; blk = Q8_K_BLOCK; break;
+        case T_F16: fn = dequant_f16_elem; blk = 2; qk = 1; break;
+        case T_BF16: fn = dequant_bf16_elem; blk = 2; qk = 1; break;
         default: return -2;
     }
     if (n % qk) return -1;
@@ -1046,6 +1132,10 @@ int or_gemv(int type, size_t nrows, size_t ncols, const uint8_t* w, const float*
         case T_Q5_K: return or_gemv_q5_k(nrows, ncols, w, x, y);
         case T_IQ4_NL: return or_gemv_iq4_nl(nrows, ncols, w, x, y);
         case T_IQ4_XS: return or_gemv_iq4_xs(nrows, ncols, w, x, y);
+        case T_F16: return or_gemv_f16(nrows, ncols, w, x, y);
+        case T_BF16: return or_gemv_bf16(nrows, ncols, w, x, y);
+        case T_Q8_1: return or_gemv_q8_1(nrows, ncols, w, x, y);
+        case T_Q8_K: return or_gemv_q8_k(nrows, ncols, w, x, y);
         default: return -2;
     }
 }

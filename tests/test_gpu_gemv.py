@@ -10,7 +10,7 @@ import torch
 
 import hayai_b200 as hb
 import oracle
-from tests.helpers import BLOCK_TYPES, IQ_TYPES, MAX_ABS, REL_L2, assert_parity, quantized
+from tests.helpers import BLOCK_TYPES, ELEM_TYPES, IQ_TYPES, MAX_ABS, REL_L2, assert_parity, quantized
 
 pytestmark = pytest.mark.gpu
 
@@ -311,3 +311,67 @@ def test_golden_fixtures_on_gpu(engine):
         got = engine.ggml_gemv_dispatch(t, m, n, g[name + "_w"], g[name + "_x"])
         assert_parity(g[name + "_y"], got, what=f"golden {name}")
         assert_parity(g[name + "_y64"], got, what=f"golden {name} vs f64")
+
+
+# ---------------------------------------------------------------- F16, BF16, Q8_1, Q8_K
+def test_reference_f16_bf16_q8_1_q8_k_fixtures(engine):
+    """compute.rs:1529-1641 (opencl_f32_f16_gemv_matches_cpu / opencl_bf16_q8_1_q8_k_match_cpu):
+    the same byte patterns, inputs and tolerances, against the oracle."""
+    m = 16
+    # F16: raw masked bytes, input i * 0.01 - 0.3
+    n = 64
+    w = ((np.arange(m * n * 2) * 131 + 17) & 0x1F).astype(np.uint8)
+    x = (np.arange(n, dtype=np.float32) * np.float32(0.01) - np.float32(0.3)).astype(np.float32)
+    assert np.abs(oracle.gemv(oracle.F16, m, n, w, x) - engine.ggml_gemv_dispatch(oracle.F16, m, n, w, x)).max() < 1e-3
+    inp = (np.arange(256, dtype=np.float32) * np.float32(0.01) - np.float32(0.7)).astype(np.float32)
+    # BF16: ((i % 23) - 11) * 0.02 truncated to its upper 16 bits
+    v = ((np.arange(m * n) % 23).astype(np.float32) - np.float32(11.0)) * np.float32(0.02)
+    w = (v.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8)
+    got = engine.ggml_gemv_dispatch(oracle.BF16, m, n, w, inp[:n])
+    assert np.abs(oracle.gemv(oracle.BF16, m, n, w, inp[:n]) - got).max() < 1e-2
+    # Q8_1: d = f16 0.5, codes ((r + bi + j) % 11) - 5
+    blocks = n // 32
+    w = np.zeros((m, blocks, 36), np.uint8)
+    w[:, :, 0:2] = np.frombuffer(np.uint16(0x3800).tobytes(), np.uint8)
+    r, bi, j = np.meshgrid(np.arange(m), np.arange(blocks), np.arange(32), indexing="ij")
+    w[:, :, 4:] = (((r + bi + j) % 11) - 5).astype(np.int8).view(np.uint8)
+    w = w.reshape(-1)
+    got = engine.ggml_gemv_dispatch(oracle.Q8_1, m, n, w, inp[:n])
+    assert np.abs(oracle.gemv(oracle.Q8_1, m, n, w, inp[:n]) - got).max() < 1e-2
+    # Q8_K: d = 0.013, codes ((r * 7 + j) % 13) - 6
+    n = 256
+    w = np.zeros((m, 292), np.uint8)
+    w[:, 0:4] = np.frombuffer(np.float32(0.013).tobytes(), np.uint8)
+    r, j = np.meshgrid(np.arange(m), np.arange(256), indexing="ij")
+    w[:, 4:260] = (((r * 7 + j) % 13) - 6).astype(np.int8).view(np.uint8)
+    w = w.reshape(-1)
+    got = engine.ggml_gemv_dispatch(oracle.Q8_K, m, n, w, inp)
+    assert np.abs(oracle.gemv(oracle.Q8_K, m, n, w, inp) - got).max() < 1e-2
+
+
+@pytest.mark.parametrize("t", ELEM_TYPES)
+@pytest.mark.parametrize("m,n", [(300, 4096), (37, 2816)])
+def test_elem_types_match_oracle(engine, t, m, n):
+    w = quantized(t, m, n, seed=40 + t)
+    x = oracle.normal(41 + t, n)
+    assert_parity(oracle.gemv(t, m, n, w, x), engine.ggml_gemv_dispatch(t, m, n, w, x), what=hb.TYPE_LABELS[t])
+
+
+@pytest.mark.parametrize("t", [oracle.F16, oracle.BF16])
+def test_half_rows_not_multiple_of_8(engine, t):
+    # K % 8 != 0: rows are not 16-byte aligned, the kernel takes one element per lane
+    m, n = 45, 1001
+    w = quantized(t, m, n, seed=3)
+    x = oracle.normal(4, n)
+    assert_parity(oracle.gemv(t, m, n, w, x), engine.ggml_gemv_dispatch(t, m, n, w, x), what=hb.TYPE_LABELS[t])
+
+
+@pytest.mark.parametrize("t", ELEM_TYPES)
+def test_elem_types_batched(engine, t):
+    m, n, batch = 64, 1024, 3
+    w = quantized(t, m, n, seed=50 + t)
+    xs = oracle.normal(51, batch * n)
+    rw = engine.upload(t, m, n, w)
+    got = engine.ggml_gemv_batched(rw, xs, batch)
+    ref = np.concatenate([oracle.gemv(t, m, n, w, xs[b * n:(b + 1) * n]) for b in range(batch)])
+    assert_parity(ref, got, what=f"{hb.TYPE_LABELS[t]} batch {batch}")

@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 import oracle
-from tests.helpers import BLOCK_TYPES, IQ_TYPES, quantized
+from tests.helpers import BLOCK_TYPES, ELEM_TYPES, IQ_TYPES, quantized
 
 LUT = np.array([-0.5, -0.4, -0.3, -0.2, -0.1, 0.0, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 1.0],
                dtype=np.float32)
@@ -165,7 +165,7 @@ def test_dequant_matches_gguf_py(t):
     assert np.array_equal(ref, got)
 
 
-@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, *IQ_TYPES, *BLOCK_TYPES])
+@pytest.mark.parametrize("t", [oracle.Q4_K, oracle.Q6_K, oracle.Q8_0, *IQ_TYPES, *BLOCK_TYPES, *ELEM_TYPES])
 def test_gemv_matches_dequant_dot(t):
     m, n = 48, 1024
     w = quantized(t, m, n, seed=200 + t)
@@ -246,3 +246,37 @@ def test_dequant_matches_gguf_py_on_arbitrary_blocks():
 
     assert hyp is not None
     check()
+
+
+def test_q8_1_and_q8_k_known_answers():
+    # quant.rs:743-770 (q8_1_and_q8_k_gemv): d = 1, all codes 1, x = 1
+    b = np.frombuffer(bytes([0x00, 0x3C, 0, 0]) + bytes([1] * 32), np.uint8)
+    assert abs(oracle.gemv(oracle.Q8_1, 1, 32, b, np.ones(32, np.float32))[0] - 32.0) < 1e-3
+    b = np.frombuffer(np.float32(1.0).tobytes() + bytes([1] * 256) + bytes(32), np.uint8)
+    assert abs(oracle.gemv(oracle.Q8_K, 1, 256, b, np.ones(256, np.float32))[0] - 256.0) < 1e-3
+    d = oracle.dequant(oracle.Q8_K, b, 256)
+    assert d.size == 256 and abs(d[0] - 1.0) < 1e-6
+
+
+@pytest.mark.parametrize("t", [oracle.F16, oracle.BF16])
+def test_half_decoders_match_gguf_py(t):
+    gguf = pytest.importorskip("gguf")
+    from gguf.quants import dequantize
+
+    w = quantized(t, 8, 1024, seed=100 + t)
+    raw = w.view(np.uint16).reshape(8, 1024) if t == oracle.F16 else w.reshape(8, 2048)  # gguf-py's own input forms
+    ref = dequantize(raw, gguf.GGMLQuantizationType(t)).reshape(-1).astype(np.float32)
+    assert np.array_equal(ref, oracle.dequant(t, w, 8 * 1024))
+
+
+@pytest.mark.parametrize("t", [oracle.Q8_1, oracle.Q8_K])
+def test_q8_1_q8_k_decoders_match_numpy(t):
+    """gguf-py has no decoder for these two; numpy's own int8 and f16/f32 views are the check
+    ({f16 d, f16 s, int8 qs[32]} and {f32 d, int8 qs[256], int16 bsums[16]})."""
+    qk, bs = oracle.BLOCK[t]
+    w = quantized(t, 4, 1024, seed=7 + t)
+    blk = w.reshape(-1, bs)
+    d = (blk[:, 0:2].copy().view(np.float16).astype(np.float32) if t == oracle.Q8_1
+         else blk[:, 0:4].copy().view(np.float32))
+    q = blk[:, 4:4 + qk].view(np.int8).astype(np.float32)
+    assert np.array_equal((q * d).reshape(-1), oracle.dequant(t, w, 4 * 1024))

@@ -390,14 +390,9 @@ def run_moe(args):
     import torch
 
     world, rank, local = dist_setup(args)
+    result = None
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     import hayai_b200 as hb
     import oracle
     from hayai_b200.tp import PeerGroup, expert_range
@@ -577,18 +572,14 @@ def run_moe(args):
         }
         if parity is not None:
             line["parity"] = parity
-        print(json.dumps(line), flush=True)
+        result = line
     if peers is not None:
         peers.close()
     for group in G + U + D:
         for w in group:
             w.free()
     eng.close()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
-    return 0
+    return result
 
 
 def c_dtype(c):
@@ -602,14 +593,9 @@ def run_ours(args):
     import torch
 
     world, rank, local = dist_setup(args)
+    result = None
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     import hayai_b200 as hb
 
     c = dict(CONFIGS[args.config])
@@ -647,10 +633,14 @@ def run_ours(args):
     # ---- resident weights, generated and quantized on the device
     scratch = torch.empty(max(ffl * kin, dm * ffl), dtype=torch.float32, device=dev)
     want_cpu = (rank == 0 and world == 1 and not args.no_cpu_baseline)
-    # parity of the timed stack: every layer's bytes kept on the host for the CPU oracle (rank 0
-    # of an unsharded run; the sharded configs hold only a shard per rank)
-    want_parity = rank == 0 and not tp and not args.no_parity
-    S_cpu = L if want_parity else (3 if want_cpu else 0)
+    # parity: the whole timed stack when its weights fit the host comfortably (the 8B stack:
+    # 3.7 GB), else its first two layers run alone through the same entry point.  Rank 0 keeps
+    # the layers' bytes for the CPU oracle; under tensor parallelism it regenerates the other
+    # ranks' shards instead (same seeds, same device quantizer: the same bytes).
+    parity_on = not args.no_parity and not (tp and args.tp_impl == "nccl")
+    whole = L * layer_bytes(c) <= 6e9
+    Lp = L if whole else min(L, 2)
+    S_cpu = Lp if (parity_on and rank == 0 and not tp) else (3 if want_cpu else 0)
     G, U, D, raw = [], [], [], []
     seed0 = 1_000_003 * (rank + 1)
 
@@ -727,22 +717,72 @@ def run_ours(args):
         step()
     torch.cuda.synchronize(dev)
     parity = None
-    if want_parity:
-        # the first row of the timed step's output (x_L = the whole stack applied to x_0)
-        # against the C oracle run on the same bytes, layer by layer
-        got = x[0, :dm].cpu().numpy().astype(np.float64)
+    if parity_on:
+        # Every layer is run alone through the same entry point on the GPU's own x_l, and the
+        # oracle takes the same x_l: the tolerance is stated per FFN call.  Then row 0 of x_Lp (the
+        # timed step's output when the whole stack is checked) against the oracle chained from
+        # x_0.  Over the depth the two f32 paths' summation orders drift apart (about 2e-5
+        # relative per layer, the size of the oracle's own distance from exact arithmetic), so
+        # the chained figure is held to the relative bound.
+        def run_sub(xx, lo, hi):
+            if tp:
+                eng.ffn_stack_tp_dev(G[lo:hi], U[lo:hi], D[lo:hi], xx, B, norms=NW[lo:hi], eps=EPS)
+            else:
+                eng.ffn_stack_dev(G[lo:hi], U[lo:hi], D[lo:hi], xx, B, norms=NW[lo:hi], eps=EPS)
+
+        def regen(t, m, n, seed):
+            qk, bs = BLK[t]
+            src = torch.empty(m * n, dtype=torch.float32, device=dev)
+            eng.synth_normal_dev(seed, src, 0.0, 0.02)
+            q = torch.empty(m * n // qk * bs, dtype=torch.uint8, device=dev)
+            eng.quantize_dev(t, src, q)
+            return q.cpu().numpy()
+
+        def full_layer(l):  # rank 0: the whole layer's bytes
+            if not tp:
+                return raw[l]
+            gs, us, ds = [], [], []
+            for q in range(world):
+                s0 = 1_000_003 * (q + 1) + 4 * l
+                gs.append(regen(tg, ffl, kin, s0))
+                us.append(regen(tg, ffl, kin, s0 + 1))
+                ds.append(regen(td, dm, ffl, s0 + 2).reshape(dm, -1))  # column shards of each row
+            return (np.concatenate(gs), np.concatenate(us), np.hstack(ds).reshape(-1), NW[l].cpu().numpy())
+
+        xin = x0.clone()
         xr = x0[0].cpu().numpy().copy()
-        t0 = time.perf_counter()
-        for l in range(L):
-            xr[:dm] += oracle_layer(c, *raw[l], xr)
-        ref = xr[:dm].astype(np.float64)
-        err = got - ref
-        rel = float(np.linalg.norm(err) / max(np.linalg.norm(ref), 1e-30))
-        mx = float(np.abs(err).max())
-        parity = {"rel_l2": rel, "max_abs": mx, "layers": L, "row": 0, "pass": rel <= 1e-4 and mx <= 1e-3,
-                  "tolerance": {"rel_l2": 1e-4, "max_abs": 1e-3},
-                  "vs": "oracle/ (C restatement of the reference CPU path, f32) on the same weight bytes",
-                  "oracle_s": round(time.perf_counter() - t0, 2)}
+        worst_rel = worst_abs = 0.0
+        t_or = 0.0
+        for l in range(Lp):
+            xl = xin[0].cpu().numpy().copy()
+            run_sub(xin, l, l + 1)
+            if rank == 0:
+                w = full_layer(l)
+                t0 = time.perf_counter()
+                yl = xl.copy()
+                yl[:dm] += oracle_layer(c, *w, xl)
+                xr[:dm] += oracle_layer(c, *w, xr)
+                t_or += time.perf_counter() - t0
+                el = xin[0, :dm].cpu().numpy().astype(np.float64) - yl[:dm].astype(np.float64)
+                worst_rel = max(worst_rel, float(np.linalg.norm(el) / max(np.linalg.norm(yl[:dm]), 1e-30)))
+                worst_abs = max(worst_abs, float(np.abs(el).max()))
+        torch.cuda.synchronize(dev)
+        if rank == 0:
+            got = (x if whole else xin)[0, :dm].cpu().numpy().astype(np.float64)
+            ref = xr[:dm].astype(np.float64)
+            err = got - ref
+            rel = float(np.linalg.norm(err) / max(np.linalg.norm(ref), 1e-30))
+            mx = float(np.abs(err).max())
+            per_ok = worst_rel <= 1e-4 and worst_abs <= 1e-3
+            parity = {"rel_l2": rel, "max_abs": mx, "layers": Lp, "of_layers": L, "row": 0,
+                      "checked": "the timed stack's output" if whole else f"the first {Lp} layers run alone",
+                      "per_layer": {"worst_rel_l2": worst_rel, "worst_max_abs": worst_abs, "pass": per_ok},
+                      "pass": per_ok and rel <= 1e-4,
+                      "tolerance": {"rel_l2": 1e-4, "max_abs": 1e-3,
+                                    "applies_to": "each FFN call (every layer); rel_l2 also over the chain"},
+                      "vs": "oracle/ (C restatement of the reference CPU path, f32) on the same weight bytes"
+                            + (f", every rank's shards joined ({world} ranks)" if tp else ""),
+                      "oracle_s": round(t_or, 2)}
     barrier(world)
 
     sampler = ClockSampler(local)
@@ -870,17 +910,13 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         if parity is not None:
             line["parity"] = parity
-        print(json.dumps(line), flush=True)
+        result = line
     if peers is not None:
         peers.close()
     for w in G + U + D:
         w.free()
     eng.close()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
-    return 0
+    return result
 
 
 def run_gemv(args):
@@ -894,12 +930,6 @@ def run_gemv(args):
     world, rank, local = dist_setup(args)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     t, M, K = c["t"], c["m"], c["k"]
     mbytes = mat_bytes(t, M, K)
     copies = max(2, -(-400_000_000 // mbytes))  # > L2 between reuses of one copy
@@ -995,10 +1025,6 @@ def run_gemv(args):
     for w in W:
         w.free()
     eng.close()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
     return 0
 
 
@@ -1015,12 +1041,6 @@ def run_lut(args):
     world, rank, local = dist_setup(args)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     M, N = c["m"], c["n"]
     wbytes = M * N // 2
     copies = -(-400_000_000 // wbytes)
@@ -1111,11 +1131,52 @@ def run_lut(args):
         print(json.dumps(line))
     del graph, W
     eng.close()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
     return 0
+
+
+def nvlink_bytes_per_layer(name, a, world):
+    """Bytes one rank stores into its peers' exchange regions per layer (the in-kernel exchange),
+    0 with one GPU."""
+    if world == 1:
+        return 0
+    c = CONFIGS[a.config]
+    if name.startswith("tp"):
+        if a.batch == 1:  # every down chunk's 16 partial sums go to every rank (16-block chunks)
+            nbk = c["d_ff"] // world // 256
+            return (world - 1) * c["d_model"] * (-(-nbk // 16)) * 4
+        return (world - 1) * a.batch * c["d_model"] * 4  # the all-reduce kernel's slices
+    # EP: each routed row computed here goes to every other rank (T k / P rows on average)
+    return round((world - 1) * c["tokens"] * c["top_k"] / world * c["d_model"] * 4)
+
+
+def run_sharded(args):
+    """The two configs that shard (BASELINE configs[4] and [3]) at this run's GPU count: the
+    Llama-3-70B FFN stack tensor-parallel over the ranks at batch 1 and 16, and the Qwen3-30B-A3B
+    MoE stack expert-parallel.  With one GPU they run unsharded (the start of each curve).
+    Returns {name: summary} on rank 0."""
+    world, rank, local = dist_setup(args)
+    peak, _ = measured_peak()
+    out = {}
+    base = dict(vars(args))
+    for name, kw in (("tp_llama70b_b1", dict(config="llama70b", tp=True, ep=False, batch=1, steps=20)),
+                     ("tp_llama70b_b16", dict(config="llama70b", tp=True, ep=False, batch=16, steps=6)),
+                     ("ep_qwen3moe", dict(config="qwen3moe", tp=False, ep=True, batch=1, steps=20))):
+        a = argparse.Namespace(**{**base, **kw, "warmup": 3, "layers": 0, "no_cpu_baseline": True,
+                                  "no_parity": False, "tp_impl": "ours"})
+        line = (run_moe if "n_expert" in CONFIGS[a.config] else run_ours)(a)
+        barrier(world)
+        if rank == 0 and line:
+            out[name] = {"value": line["value"], "unit": "GB/s", "ms_per_step": line["ms_per_step"],
+                         "tokens_per_s": line["tokens_per_s"],
+                         "per_gpu_hbm_frac": round(line["value"] / world / peak, 4),
+                         "workload": line["config"]["workload"], "batch": line["config"]["batch"],
+                         "parallelism": line["config"]["parallelism"], "scaling": line["scaling"],
+                         "nvlink_bytes_per_layer_per_gpu": nvlink_bytes_per_layer(name, a, world),
+                         "kernel_path": line["config"].get("kernel_path"), "roofline": line["roofline"],
+                         "e2e": line["e2e"]}
+            if "parity" in line:
+                out[name]["parity"] = line["parity"]
+    return out
 
 
 def main():
@@ -1134,16 +1195,45 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed stack's output")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the sharded configs (70B tensor-parallel, Qwen3 expert-parallel) the default "
+                         "llama8b run also measures at the same GPU count")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
-    if "n_expert" in CONFIGS[args.config]:
-        return run_moe(args)
-    if CONFIGS[args.config].get("gemv"):
-        return run_gemv(args)
-    if CONFIGS[args.config].get("lut"):
-        return run_lut(args)
-    return run_ours(args)
+    world, rank, local = dist_setup(args)
+    import torch
+
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    try:
+        c = CONFIGS[args.config]
+        if c.get("gemv"):
+            return run_gemv(args)
+        if c.get("lut"):
+            return run_lut(args)
+        line = run_moe(args) if "n_expert" in c else run_ours(args)
+        if (args.config == "llama8b" and not args.tp and args.batch == 1 and not args.layers
+                and not args.no_sharded):
+            # the headline line also carries the sharded configs at the same GPU count
+            barrier(world)
+            sharded = run_sharded(args)
+            if rank == 0:
+                line["sharded"] = sharded
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+    return 0
 
 
 if __name__ == "__main__":

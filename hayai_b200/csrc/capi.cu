@@ -419,7 +419,10 @@ int hc_launch_gemv(hc_engine* e, const hc_weights* w, const float* x, size_t ldx
     if (nvec == 0) return HC_OK;
     if (ldx < w->n || ldy < w->m || (resid && ldr < w->m))
         return hc_set_error(HC_ERR_INVALID, "leading dimension smaller than the row length");
-    if (((uintptr_t)x & 15) || (ldx & 3))
+    // the element formats take any row length (their kernels fall back to scalar loads); the
+    // block formats' kernels read x as float4
+    const bool elem = w->type == T_F32 || w->type == T_F16 || w->type == T_BF16;
+    if (!elem && (((uintptr_t)x & 15) || (ldx & 3)))
         return hc_set_error(HC_ERR_INVALID, "x must be 16-byte aligned with ldx a multiple of 4");
     cudaError_t ce;
     if (e->use_tc && tc_gemm_supported(w->type, (int)w->m, (int)w->n, (int)nvec)) {

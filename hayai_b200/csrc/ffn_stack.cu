@@ -122,16 +122,18 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
-// Cross-GPU phase end under tensor parallelism.  Every consumer thread has made its stores to
-// the peers' regions visible system-wide (fence) before the CTA's local arrival; CTA 0 waits
-// for all local CTAs, then adds one (release, system scope) to every rank's cross counter; all
-// CTAs wait (acquire, system scope) until their own rank's counter shows all ranks' signals
-// for this phase.  Both waits are bounded by one second (error bit 1, abort).
+// Cross-GPU phase end under tensor parallelism.  After the CTA barrier (which orders every
+// consumer thread's stores to the peers' regions before thread 0's next operations), thread 0
+// alone makes them visible system-wide with one fence (cumulative over what the barrier
+// ordered) before the CTA's local arrival; CTA 0 waits for all local CTAs, then adds one
+// (release, system scope) to every rank's cross counter; all CTAs wait (acquire, system scope)
+// until their own rank's counter shows all ranks' signals for this phase.  Both waits are
+// bounded by one second (error bit 1, abort).
 __device__ void tp_sync(unsigned* bar, unsigned target, char* const* regions, int tp_rank, int tp_size,
                         unsigned xtarget, int* err, int* s_abort) {
-    __threadfence_system();
     named_bar_sync(kBarGrid, kCW * 32);
     if (threadIdx.x == 0) {
+        __threadfence_system();
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
         const unsigned* xbar = reinterpret_cast<const unsigned*>(regions[tp_rank] + kPeerTpBar);
         const unsigned long long t0 = global_ns();

@@ -44,6 +44,7 @@
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "gemv_launch.h"
@@ -54,7 +55,7 @@ constexpr int kTcRows = 128;               // output rows per CTA (MMA M)
 constexpr int kTcChunk = 64;               // K per operand buffer
 constexpr int kTcABytes = kTcRows * kTcChunk * 2;  // one f16 operand buffer (16 KB)
 constexpr int kTcThreads = 480;            // 15 warps
-constexpr int kTcMaxRing = 8;
+constexpr int kTcMaxRing = 12;
 constexpr float kTcWScale = 256.f;         // w' = w * 2^8
 
 // Tile-block image of each format (repack.cu): bytes, K elements, images per weight stage
@@ -132,6 +133,29 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Registers of this thread -> consecutive 32-bit columns of its TMEM lane (lane = the warp's
+// quarter base + thread; taddr carries the quarter's base lane in bits 31:16).
+__device__ __forceinline__ void tc_st4(uint32_t taddr, const uint32_t (&r)[4]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3])
+                 : "memory");
+}
+__device__ __forceinline__ void tc_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D (+)= A B with A read from TMEM (128 lanes = rows, K packed two f16 per column), B from
+// shared memory.
+__device__ __forceinline__ void tc_mma_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc));
 }
 
 // Four int8 codes (one word) times the block scale: exact hi/lo f16 pairs, k-adjacent codes
@@ -322,7 +346,152 @@ struct TcDq<TcQ6K> {
     __device__ __forceinline__ bool bad() const { return !(big < 65504.f); }
 };
 
+// ---- dequantisers into TMEM operands (the TA form of the kernel).  Thread (row r, half jj)
+// of the 8 dequantising warps: warp w covers TMEM lanes (= rows) 32 (w % 4) + lane, and the
+// two warps of a lane quarter split each 64-K chunk's work in halves.  An operand buffer is
+// 64 columns: A_hi in columns [0, 32), A_lo in [32, 64); column n holds chunk elements 2n (low
+// half) and 2n + 1.  chunk() writes the thread's columns with tcgen05.st (tA = the buffer's
+// column address with the quarter's base lane).
 template <class F>
+struct TcDqT;
+
+// Q8_0: chunk h of an image = blocks 2h, 2h + 1 = region h (q0 / q1): row rr's 64 bytes at
+// 1024 h + 64 rr, piece t = 16 bytes: word 2bb + hw = codes 16 hw + 4t..+3 of block 2h + bb.
+// Thread jj reads pieces t = 2jj, 2jj + 1: chunk elements 32 bb + 16 hw + 4t + i, i.e. columns
+// 16 bb + 8 hw + 4 jj + [0, 4).
+template <>
+struct TcDqT<TcQ80> {
+    int pw, dwo, jj;
+    uint32_t dbits = 0;
+    __device__ __forceinline__ void init(int r, int j) {
+        const int rt = r >> 4, rr = r & 15, base = rt * (TcQ80::kGps * TcQ80::kImg / 4);
+        jj = j;
+        pw = base + 16 * rr + 8 * j;  // piece 2jj of region 0
+        dwo = base + 512 + 2 * rr;
+    }
+    __device__ __forceinline__ void chunk(const uint32_t* ws, int h, uint32_t tA) {
+        const uint4 p0 = *reinterpret_cast<const uint4*>(ws + pw + 256 * h);
+        const uint4 p1 = *reinterpret_cast<const uint4*>(ws + pw + 256 * h + 4);
+        const uint32_t dw = ws[dwo + h];
+        dbits |= dw;
+        const __half2 dd = __hmul2(u32_as_h2(dw), __float2half2_rn(kTcWScale));
+        const __half2 d0 = __low2half2(dd), d1 = __high2half2(dd);
+        const uint32_t w0[4] = {p0.x, p0.y, p0.z, p0.w}, w1[4] = {p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {  // g = 2 bb + hw
+            uint2 h0, l0, h1, l1;
+            tc_dequant4(w0[g], g < 2 ? d0 : d1, h0, l0);
+            tc_dequant4(w1[g], g < 2 ? d0 : d1, h1, l1);
+            const uint32_t hv[4] = {h0.x, h0.y, h1.x, h1.y}, lv[4] = {l0.x, l0.y, l1.x, l1.y};
+            const uint32_t col = 16 * (g >> 1) + 8 * (g & 1) + 4 * jj;
+            tc_st4(tA + col, hv);
+            tc_st4(tA + 32 + col, lv);
+        }
+    }
+    __device__ __forceinline__ bool bad() const { return (dbits & 0x40004000u) != 0; }
+};
+
+// Q4_K: chunk c = qs bytes 32c..32c+31 of the super-block; thread jj reads piece q_jj of
+// (rr, c) = bytes 32c + 16jj + [0, 16): low nibbles are chunk elements 16jj + i (sub-block 2c,
+// columns 8jj + i/2), high nibbles 32 + 16jj + i (sub-block 2c + 1, columns 16 + 8jj + i/2).
+template <>
+struct TcDqT<TcQ4K> {
+    int hw, qw, jj;
+    float big = 0.f;
+    __device__ __forceinline__ void init(int r, int j) {
+        const int rt = r >> 4, rr = r & 15, base = rt * (TcQ4K::kGps * TcQ4K::kImg / 4);
+        jj = j;
+        hw = base + 4 * rr;
+        qw = base + 64 + 16 * rr + 256 * j;
+    }
+    __device__ __forceinline__ void chunk(const uint32_t* ws, int c, uint32_t tA) {
+        const uint4 hd = *reinterpret_cast<const uint4*>(ws + hw);
+        const uint4 q = *reinterpret_cast<const uint4*>(ws + qw + 4 * c);
+        const uint32_t V = __funnelshift_r(c < 2 ? hd.y : (c == 2 ? hd.z : hd.w), c < 2 ? hd.z : hd.w, (24 * c) & 31);
+        const float2 dd = __half22float2(u32_as_h2(hd.x));
+        const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+            const float sc = (float)((V >> (6 * s)) & 63u), mn = (float)((V >> (12 + 6 * s)) & 63u);
+            const float d1 = (dd.x * sc) * kTcWScale, m1 = (dd.y * mn) * kTcWScale;
+            big = fmaxf(big, fmaf(fabsf(d1), 15.f, fabsf(m1)));
+            uint32_t hv[8], lv[8];
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+                const uint32_t n = (s ? words[wi] >> 4 : words[wi]) & 0x0F0F0F0Fu;
+                float v[4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) v[b] = fmaf(u8_to_f32(n, b), d1, -m1);
+                tc_split2(v[0], v[1], hv[2 * wi], lv[2 * wi]);
+                tc_split2(v[2], v[3], hv[2 * wi + 1], lv[2 * wi + 1]);
+            }
+            const uint32_t col = 16 * s + 8 * jj;
+            tc_st8(tA + col, hv);
+            tc_st8(tA + 32 + col, lv);
+        }
+    }
+    __device__ __forceinline__ bool bad() const { return !(big < 65504.f); }
+};
+
+// Q6_K (lane-distributed image): thread jj = s takes the pieces of lane t = 2h + s (ql l0 / l1,
+// qh, its scale word); chunk c = 2h + nib covers groups q = 2 nib + qq, elements 32 qq + 16 s + i
+// (columns 16 qq + 8 s + i/2).  The pieces serve both chunks of a half: loaded at nib = 0.
+template <>
+struct TcDqT<TcQ6K> {
+    int lw, sw, dw, dsh, jj;
+    uint4 l0, l1, qh;
+    uint32_t scw = 0;
+    float d = 0.f, big = 0.f;
+    __device__ __forceinline__ void init(int r, int j) {
+        const int rt = r >> 4, rr = r & 15, base = rt * (TcQ6K::kGps * TcQ6K::kImg / 4);
+        jj = j;
+        lw = base + 4 * (4 * rr + j);  // piece t = 2h + s: + 8h words
+        sw = base + 768 + 4 * rr + j;  // word t: + 2h
+        dw = base + 832 + (rr >> 1);
+        dsh = 16 * (rr & 1);
+    }
+    __device__ __forceinline__ void chunk(const uint32_t* ws, int c, uint32_t tA) {
+        const int h = c >> 1, nib = c & 1;
+        if (nib == 0) {
+            l0 = *reinterpret_cast<const uint4*>(ws + lw + 8 * h);
+            l1 = *reinterpret_cast<const uint4*>(ws + lw + 8 * h + 256);
+            qh = *reinterpret_cast<const uint4*>(ws + lw + 8 * h + 512);
+            scw = ws[sw + 2 * h] ^ 0x80808080u;
+            d = h2f((uint16_t)(ws[dw] >> dsh));
+        }
+        const uint32_t Q[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+        for (int qq = 0; qq < 2; ++qq) {
+            const int q = 2 * nib + qq;
+            const float ds = (d * s8_to_f32_flipped(scw, q)) * kTcWScale;
+            big = fmaxf(big, fabsf(ds) * 32.f);
+            const uint32_t L[4] = {qq ? l1.x : l0.x, qq ? l1.y : l0.y, qq ? l1.z : l0.z, qq ? l1.w : l0.w};
+            const int hs = 2 * q;
+            uint32_t hv[8], lv[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t lo4 = (nib ? L[k] >> 4 : L[k]) & 0x0F0F0F0Fu;
+                const uint32_t up = (hs <= 4 ? Q[k] << (4 - hs) : Q[k] >> (hs - 4)) & 0x30303030u;
+                const uint32_t code = lo4 | up;
+                float v[4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    uint32_t u;
+                    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(u) : "r"(code), "r"(0x4B000000u), "r"(0x7440u | b));
+                    v[b] = (__uint_as_float(u) - 8388640.0f) * ds;
+                }
+                tc_split2(v[0], v[1], hv[2 * k], lv[2 * k]);
+                tc_split2(v[2], v[3], hv[2 * k + 1], lv[2 * k + 1]);
+            }
+            const uint32_t col = 16 * qq + 8 * jj;
+            tc_st8(tA + col, hv);
+            tc_st8(tA + 32 + col, lv);
+        }
+    }
+    __device__ __forceinline__ bool bad() const { return !(big < 65504.f); }
+};
+
+template <class F, bool TA>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
     constexpr int CPI = F::kImgK / kTcChunk;  // chunks per image (= per unit)
     constexpr int WST = tc_wstage<F>();
@@ -344,9 +513,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
     uint8_t* wring = base + 1024;
     uint8_t* xring = wring + ((a.SW * WST + 1023) & ~1023);
     const int xbytes = a.N * kTcChunk * 2;
-    uint8_t* aring = xring + ((a.NX * xbytes + 1023) & ~1023);
-    // accumulator set s: A_hi products at columns s 2N + [0, N), A_lo products at + N
-    const uint32_t need = (uint32_t)(a.nsets * 2 * a.N);
+    uint8_t* aring = xring + ((a.NX * xbytes + 1023) & ~1023);  // (the smem operand form only)
+    // accumulator set s: A_hi products at columns s 2N + [0, N), A_lo products at + N; in the
+    // TA form the NA operand buffers follow (64 columns each)
+    const uint32_t accC = (uint32_t)(a.nsets * 2 * a.N);
+    const uint32_t need = accC + (TA ? 64u * (uint32_t)a.NA : 0u);
     const uint32_t ncols = need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : need <= 256 ? 256u : 512u;
 
     if (threadIdx.x == 0) {
@@ -445,19 +616,56 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
                     break;
                 }
                 tc_fence_after();
-                const uint32_t ahi = smem_addr(aring + sa * 2 * kTcABytes), alo = ahi + kTcABytes;
                 const uint32_t xs = smem_addr(xring + sx * xbytes);
+                if constexpr (TA) {
+                    const uint32_t at = tmem + accC + 64u * (uint32_t)sa;  // lane 0, the buffer's columns
 #pragma unroll
-                for (int ks = 0; ks < kTcChunk / 16; ++ks) {
-                    const uint32_t on = (first && ks == 0) ? 0u : 1u;
-                    tc_mma(acc, tc_desc(ahi + 32 * ks), tc_desc(xs + 32 * ks), idesc, on);
-                    tc_mma(acc + (uint32_t)a.N, tc_desc(alo + 32 * ks), tc_desc(xs + 32 * ks), idesc, on);
+                    for (int ks = 0; ks < kTcChunk / 16; ++ks) {
+                        const uint32_t on = (first && ks == 0) ? 0u : 1u;
+                        tc_mma_ta(acc, at + 8 * ks, tc_desc(xs + 32 * ks), idesc, on);
+                        tc_mma_ta(acc + (uint32_t)a.N, at + 32 + 8 * ks, tc_desc(xs + 32 * ks), idesc, on);
+                    }
+                } else {
+                    const uint32_t ahi = smem_addr(aring + sa * 2 * kTcABytes), alo = ahi + kTcABytes;
+#pragma unroll
+                    for (int ks = 0; ks < kTcChunk / 16; ++ks) {
+                        const uint32_t on = (first && ks == 0) ? 0u : 1u;
+                        tc_mma(acc, tc_desc(ahi + 32 * ks), tc_desc(xs + 32 * ks), idesc, on);
+                        tc_mma(acc + (uint32_t)a.N, tc_desc(alo + 32 * ks), tc_desc(xs + 32 * ks), idesc, on);
+                    }
                 }
                 tc_commit(a_empty + 8 * sa);
                 tc_commit(x_empty + 8 * sx);
                 if (last) tc_commit(acc_full + 8 * (seg % a.nsets));
             }
         }
+    } else if (warp < 10 && TA) {
+        // ---- dequantisation into TMEM operand buffers: warp w writes lanes 32 (w % 4) + lane
+        const int quarter = warp & 3;
+        TcDqT<F> dq;
+        dq.init(32 * quarter + lane, (warp - 2) >> 2);
+        const uint32_t tq = tmem + ((uint32_t)(32 * quarter) << 16) + accC;
+        for (int j = 0; j < nj && !timeout; ++j) {
+            const int i = j / CPI, sub = j % CPI, sw = i % a.SW, sa = j % a.NA;
+            if (sub == 0 && !mbar_wait(w_full + 8 * sw, (i / a.SW) & 1)) {
+                timeout = true;
+                break;
+            }
+            if (j >= a.NA && !mbar_wait(a_empty + 8 * sa, ((j / a.NA) - 1) & 1)) {
+                timeout = true;
+                break;
+            }
+            tc_fence_after();  // the MMAs that read this buffer have completed
+            dq.chunk(reinterpret_cast<const uint32_t*>(wring + sw * WST), sub, tq + 64u * (uint32_t)sa);
+            tc_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(a_full + 8 * sa);
+                if (sub == CPI - 1) mbar_arrive(w_empty + 8 * sw);
+            }
+        }
+        bad = dq.bad();
     } else if (warp < 10) {
         // ---- dequantisation: 256 threads; a thread's shared-memory offsets are the same for
         // every chunk
@@ -680,9 +888,47 @@ size_t tc_workspace_bytes(int type, int M, int K, int nvec, int num_sms, int mat
     return (xc + 255) / 256 * 256 + part;
 }
 
+// The TA form (operands dequantised into TMEM; shared memory holds only the weight and
+// activation rings) when the accumulators leave room for four 64-column operand buffers:
+// N <= 128 (batches up to 64).  HAYAI_TC_TMEM_A=0 keeps the shared-memory operand form.
+static bool tc_use_ta(int N) {
+    static const bool on = [] {
+        const char* v = std::getenv("HAYAI_TC_TMEM_A");
+        return !(v && v[0] == '0');
+    }();
+    return on && N <= 128;
+}
+
+template <class F>
+static cudaError_t tc_launch_ta(TcArgs a, int G, int smem_limit, cudaStream_t stream) {
+    constexpr int WST = tc_wstage<F>();
+    const int xbytes = a.N * kTcChunk * 2;
+    a.NA = 4;
+    a.nsets = 2 * 2 * a.N + 64 * a.NA <= 512 ? 2 : 1;
+    a.NX = 4;
+    auto smem_of = [&](const TcArgs& t) {
+        return 1024 + ((t.SW * WST + 1023) & ~1023) + ((t.NX * xbytes + 1023) & ~1023);
+    };
+    a.SW = kTcMaxRing;
+    while (smem_of(a) > smem_limit - 2048 && a.SW > 2) --a.SW;
+    if (smem_of(a) > smem_limit - 2048) return cudaErrorInvalidConfiguration;
+    const int smem = smem_of(a) + 1024;
+    static int configured[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || configured[dev] < smem) {
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<F, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) configured[dev] = smem;
+    }
+    tc_gemm_kernel<F, true><<<G, kTcThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
 // Ring depths that fit, operand buffers first, and the kernel's dynamic shared memory.
 template <class F>
 static cudaError_t tc_launch_kernel(TcArgs a, int G, int smem_limit, cudaStream_t stream) {
+    if (tc_use_ta(a.N)) return tc_launch_ta<F>(a, G, smem_limit, stream);
     constexpr int WST = tc_wstage<F>();
     const int xbytes = a.N * kTcChunk * 2;
     // The operand buffers take the shared memory first (each makes a round trip dequant ->
@@ -702,11 +948,11 @@ static cudaError_t tc_launch_kernel(TcArgs a, int G, int smem_limit, cudaStream_
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || configured[dev] < smem) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<F, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         if (dev < 64) configured[dev] = smem;
     }
-    tc_gemm_kernel<F><<<G, kTcThreads, smem, stream>>>(a);
+    tc_gemm_kernel<F, false><<<G, kTcThreads, smem, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -264,6 +264,8 @@ def test_q8_0_tensor_core_residual_dev(engine):
     (13, 256, 2048),     # ragged batch: rows padded to 16 in the MMA's N
     (16, 384, 8192),     # config-5 batch (70B d_model), several K splits
     (64, 128, 14336),    # Llama-3-8B down length, deep K split
+    (33, 256, 4096),     # N = 80: one accumulator set pair beside the TMEM operand buffers
+    (100, 128, 4096),    # N = 208: operands in shared memory (the TMEM form holds N <= 128)
 ])
 def test_kquant_tensor_core_batches(engine, t, batch, m, n):
     w = quantized(t, m, n, seed=171 + batch)

@@ -39,6 +39,11 @@ enum GgmlType : int {
 
 constexpr int QK_K = 256;
 
+// The IQ2 / IQ3 codebook formats (tile-major layout, tensor-core GEMV).
+__host__ __device__ constexpr bool is_iq_type(int t) {
+    return t == T_IQ2_XXS || t == T_IQ2_XS || t == T_IQ2_S || t == T_IQ3_XXS || t == T_IQ3_S;
+}
+
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
 // ---------------------------------------------------------------- loads

@@ -37,9 +37,9 @@ __device__ __forceinline__ void inv_q80(int e, int& mi, int& t) {
 
 template <class F>
 __device__ __forceinline__ void inv_map(int e, int& mi, int& t) {
-    if constexpr (F::kType == T_Q4_K) inv_q4k(e, mi, t);
-    else if constexpr (F::kType == T_Q6_K) inv_q6k(e, mi, t);
-    else inv_q80(e, mi, t);
+    if constexpr (F::kType == T_Q6_K) inv_q6k(e, mi, t);
+    else if constexpr (F::kType == T_Q8_0) inv_q80(e, mi, t);
+    else inv_q4k(e, mi, t);  // Q4_K and the IQ formats (the same lane-distributed slots)
 }
 
 // Table slot (single vector) of the hi part of 4-element chunk c of the activation; the lo

@@ -1,10 +1,9 @@
-// gemv_simple.cu -- CUDA-core kernels on the raw GGUF layout: F32, F16, BF16, the IQ2/IQ3/IQ4
-// codebook formats, the other GGML block formats (Q4_0, Q4_1, Q5_0, Q5_1, Q8_1, Q2_K, Q3_K,
-// Q5_K, Q8_K), the toy LUT-Q4 matmul, and the elementwise SwiGLU combine.
+// gemv_simple.cu -- CUDA-core kernels on the raw GGUF layout: F32, F16, BF16, IQ4_NL / IQ4_XS,
+// the other GGML block formats (Q4_0, Q4_1, Q5_0, Q5_1, Q8_1, Q2_K, Q3_K, Q5_K, Q8_K), the toy
+// LUT-Q4 matmul, and the elementwise SwiGLU combine.  (The IQ2 / IQ3 codebook formats run on
+// the tensor-core GEMV: gemv_iq.cuh.)
 //
-// Reference semantics: gemv_f32 (crates/hayai-model/src/quant.rs:358-369), the IQ2 block
-// decoders (crates/hayai-model/src/iq2.rs:504-573, gemv macro :591-626), the IQ3 block
-// decoders (crates/hayai-model/src/iq3.rs:147-220, gemv :258-331), IQ4_NL / IQ4_XS
+// Reference semantics: gemv_f32 (crates/hayai-model/src/quant.rs:358-369), IQ4_NL / IQ4_XS
 // (iq4.rs:36-42, :121-138), Q4_0 / Q4_1 (quant.rs:538-596, :617-650), Q5_0 / Q5_1
 // (q5.rs:26-158), Q2_K (q2k.rs:26-58), Q3_K (q3k.rs:10-30, :52-84), Q5_K (q5k.rs:10-66),
 // gemv_f16 / gemv_bf16 / gemv_q8_1 / gemv_q8_k (quant.rs:371-395, :458-501),
@@ -17,38 +16,12 @@
 
 namespace hc {
 
-// Sign byte of a 7-bit index: the index with bit 7 = its parity (iq2.rs:18-27).
-__device__ __forceinline__ uint32_t ksigns(uint32_t i) { return (i & 127u) | ((__popc(i & 127u) & 1u) << 7); }
-
 // Byte loads of a block; the group kernel stages blocks in shared memory, so these are
 // generic loads (no read-only-path form, which only addresses global memory).
 __device__ __forceinline__ uint32_t ldb(const uint8_t* p) { return *p; }
 __device__ __forceinline__ uint32_t ld_u16u(const uint8_t* p) { return ldb(p) | (ldb(p + 1) << 8); }
 __device__ __forceinline__ uint32_t ld_u32u(const uint8_t* p) { return ld_u16u(p) | (ld_u16u(p + 2) << 16); }
 __device__ __forceinline__ float ld_f16u(const uint8_t* p) { return h2f((uint16_t)ld_u16u(p)); }
-
-// sum over 8 codebook values: db * g_j * sign_j * x_j
-__device__ __forceinline__ float dot8_grid(float db, uint64_t grid, uint32_t signs, const float* x) {
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const float g = (float)((grid >> (8 * j)) & 0xffu);
-        const float v = (signs >> j) & 1u ? -db * g : db * g;
-        s += v * x[j];
-    }
-    return s;
-}
-
-__device__ __forceinline__ float dot4_grid(float db, uint32_t grid, uint32_t signs, const float* x) {
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float g = (float)((grid >> (8 * j)) & 0xffu);
-        const float v = (signs >> j) & 1u ? -db * g : db * g;
-        s += v * x[j];
-    }
-    return s;
-}
 
 // get_scale_min_k4 (q4k.rs:34-43, q5k.rs:10-18): 6-bit scale and min j of a K-quant header.
 __device__ __forceinline__ void scale_min_k4(const uint8_t* s, int j, float& sc, float& m) {
@@ -70,160 +43,9 @@ __device__ __forceinline__ float q3k_scale(const uint8_t* s12, int i) {
     return (float)((int)(lo | (hi << 4)) - 32);
 }
 
-// One 32-element group (ib32) of a block, dotted with x[0..32).
-template <int TYPE>
-__device__ __forceinline__ float group_dot(const uint8_t* blk, int ib32, const float* x) {
-    float s = 0.f;
-    if constexpr (TYPE == T_Q4_0 || TYPE == T_Q4_1 || TYPE == T_Q5_0 || TYPE == T_Q5_1 || TYPE == T_IQ4_NL) {
-        // 32-element blocks: element j from the low nibble of qs[j], j + 16 from the high one
-        const float d = ld_f16u(blk);
-        const float m = (TYPE == T_Q4_1 || TYPE == T_Q5_1) ? ld_f16u(blk + 2) : 0.f;
-        const int qoff = TYPE == T_Q4_0 || TYPE == T_IQ4_NL ? 2 : TYPE == T_Q4_1 ? 4 : TYPE == T_Q5_0 ? 6 : 8;
-        const uint32_t qh = TYPE == T_Q5_0 ? ld_u32u(blk + 2) : TYPE == T_Q5_1 ? ld_u32u(blk + 4) : 0u;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const uint32_t q = ldb(blk + qoff + j);
-            uint32_t c0 = q & 0x0Fu, c1 = q >> 4;
-            float w0, w1;
-            if constexpr (TYPE == T_Q5_0 || TYPE == T_Q5_1) {
-                c0 |= ((qh >> j) << 4) & 0x10u;
-                c1 |= (qh >> (j + 12)) & 0x10u;
-            }
-            if constexpr (TYPE == T_Q4_0) {
-                w0 = (float)((int)c0 - 8) * d;
-                w1 = (float)((int)c1 - 8) * d;
-            } else if constexpr (TYPE == T_Q5_0) {
-                w0 = (float)((int)c0 - 16) * d;
-                w1 = (float)((int)c1 - 16) * d;
-            } else if constexpr (TYPE == T_IQ4_NL) {
-                w0 = d * (float)hc_iq4nl_values[c0];
-                w1 = d * (float)hc_iq4nl_values[c1];
-            } else {  // Q4_1, Q5_1
-                w0 = (float)c0 * d + m;
-                w1 = (float)c1 * d + m;
-            }
-            s += w0 * x[j];
-            s += w1 * x[j + 16];
-        }
-        return s;
-    } else if constexpr (TYPE == T_Q2_K) {
-        // half n = ib32 / 4, shift 2 (ib32 % 4); elements 0-15 from q[l], 16-31 from q[16 + l]
-        const int n = ib32 >> 2, j = ib32 & 3;
-        const float d = ld_f16u(blk + 80), dmin = ld_f16u(blk + 82);
-        const uint8_t* q = blk + 16 + 32 * n;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const uint32_t sc = ldb(blk + 8 * n + 2 * j + h);
-            const float dl = d * (float)(sc & 0xFu), ml = dmin * (float)(sc >> 4);
-#pragma unroll
-            for (int l = 0; l < 16; ++l) s += (dl * (float)((ldb(q + 16 * h + l) >> (2 * j)) & 3u) - ml) * x[16 * h + l];
-        }
-        return s;
-    } else if constexpr (TYPE == T_Q3_K) {
-        const int n = ib32 >> 2, j = ib32 & 3;
-        const float dall = ld_f16u(blk + 108);
-        const uint8_t* q = blk + 32 + 32 * n;
-        const uint32_t mbit = 1u << (4 * n + j);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const float dl = dall * q3k_scale(blk + 96, 8 * n + 2 * j + h);
-#pragma unroll
-            for (int l = 0; l < 16; ++l) {
-                const int qv = (int)((ldb(q + 16 * h + l) >> (2 * j)) & 3u);
-                const int hm = (ldb(blk + 16 * h + l) & mbit) ? 0 : 4;
-                s += dl * (float)(qv - hm) * x[16 * h + l];
-            }
-        }
-        return s;
-    } else if constexpr (TYPE == T_Q5_K) {
-        // chunk c = ib32 / 2: low nibbles of ql[32c + l] (ib32 even) or high ones, fifth bit
-        // qh[l] & (1 or 2) << 2c, scale and min ib32
-        const int c = ib32 >> 1, hi = ib32 & 1;
-        float sc, mn;
-        scale_min_k4(blk + 4, ib32, sc, mn);
-        const float d1 = ld_f16u(blk) * sc, m1 = ld_f16u(blk + 2) * mn;
-        const uint32_t u = (hi ? 2u : 1u) << (2 * c);
-#pragma unroll
-        for (int l = 0; l < 32; ++l) {
-            const uint32_t ql = ldb(blk + 48 + 32 * c + l);
-            const uint32_t v = (hi ? ql >> 4 : ql & 0x0Fu) + ((ldb(blk + 16 + l) & u) ? 16u : 0u);
-            s += (d1 * (float)v - m1) * x[l];
-        }
-        return s;
-    } else if constexpr (TYPE == T_IQ4_XS) {
-        const float d = ld_f16u(blk);
-        const uint32_t sh = ld_u16u(blk + 2);
-        const int ls = (int)(((ldb(blk + 4 + ib32 / 2) >> (4 * (ib32 & 1))) & 0x0Fu) | (((sh >> (2 * ib32)) & 3u) << 4));
-        const float dl = d * (float)(ls - 32);
-        const uint8_t* qs = blk + 8 + 16 * ib32;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const uint32_t q = ldb(qs + j);
-            s += dl * (float)hc_iq4nl_values[q & 0x0Fu] * x[j];
-            s += dl * (float)hc_iq4nl_values[q >> 4] * x[j + 16];
-        }
-        return s;
-    }
-    const float d = ld_f16u(blk);
-    if constexpr (TYPE == T_IQ2_XXS) {
-        const uint32_t aux0 = ld_u32u(blk + 2 + 8 * ib32), aux1 = ld_u32u(blk + 2 + 8 * ib32 + 4);
-        const float db = d * (0.5f + (float)(aux1 >> 28)) * 0.25f;
-#pragma unroll
-        for (int l = 0; l < 4; ++l)
-            s += dot8_grid(db, hc_iq2xxs_grid[(aux0 >> (8 * l)) & 0xff], ksigns(aux1 >> (7 * l)), x + 8 * l);
-    } else if constexpr (TYPE == T_IQ2_XS) {
-        const uint32_t sc = ldb(blk + 66 + ib32);
-        const float db0 = d * (0.5f + (float)(sc & 0xf)) * 0.25f, db1 = d * (0.5f + (float)(sc >> 4)) * 0.25f;
-#pragma unroll
-        for (int l = 0; l < 4; ++l) {
-            const uint32_t q = ld_u16u(blk + 2 + 2 * (4 * ib32 + l));
-            s += dot8_grid(l < 2 ? db0 : db1, hc_iq2xs_grid[q & 511], ksigns(q >> 9), x + 8 * l);
-        }
-    } else if constexpr (TYPE == T_IQ2_S) {
-        const uint32_t sc = ldb(blk + 74 + ib32), qh = ldb(blk + 66 + ib32);
-        const float db0 = d * (0.5f + (float)(sc & 0xf)) * 0.25f, db1 = d * (0.5f + (float)(sc >> 4)) * 0.25f;
-#pragma unroll
-        for (int l = 0; l < 4; ++l) {
-            const uint32_t idx = ldb(blk + 2 + 4 * ib32 + l) | ((qh << (8 - 2 * l)) & 0x300u);
-            s += dot8_grid(l < 2 ? db0 : db1, hc_iq2s_grid[idx], ldb(blk + 34 + 4 * ib32 + l), x + 8 * l);
-        }
-    } else if constexpr (TYPE == T_IQ3_XXS) {
-        const uint32_t aux = ld_u32u(blk + 66 + 4 * ib32);
-        const float db = d * (0.5f + (float)(aux >> 28)) * 0.5f;
-#pragma unroll
-        for (int l = 0; l < 4; ++l) {
-            const uint32_t sg = ksigns(aux >> (7 * l));
-            s += dot4_grid(db, hc_iq3xxs_grid[ldb(blk + 2 + 8 * ib32 + 2 * l)], sg, x + 8 * l);
-            s += dot4_grid(db, hc_iq3xxs_grid[ldb(blk + 2 + 8 * ib32 + 2 * l + 1)], sg >> 4, x + 8 * l + 4);
-        }
-    } else if constexpr (TYPE == T_IQ3_S) {
-        const uint32_t sc = ldb(blk + 106 + ib32 / 2), qh = ldb(blk + 66 + ib32);
-        const float db = d * (1.0f + 2.0f * (float)((sc >> (4 * (ib32 & 1))) & 0xf));
-#pragma unroll
-        for (int l = 0; l < 4; ++l) {
-            const uint32_t i1 = ldb(blk + 2 + 8 * ib32 + 2 * l) | ((qh << (8 - 2 * l)) & 256u);
-            const uint32_t i2 = ldb(blk + 2 + 8 * ib32 + 2 * l + 1) | ((qh << (7 - 2 * l)) & 256u);
-            const uint32_t sg = ldb(blk + 74 + 4 * ib32 + l);
-            s += dot4_grid(db, hc_iq3s_grid[i1], sg, x + 8 * l);
-            s += dot4_grid(db, hc_iq3s_grid[i2], sg >> 4, x + 8 * l + 4);
-        }
-    }
-    return s;
-}
-
 // Elements e..e+3 (e a multiple of 4) of the 32-element group ib32 of a block, dotted with x4:
 // the same values as group_dot, one quarter-octet at a time, so that 8 lanes share a group and
 // a warp's activation loads are 512 contiguous bytes.
-__device__ __forceinline__ float dot4_signed(float db, uint32_t grid4, uint32_t signs, const float4& x) {
-    float v[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float g = (float)((grid4 >> (8 * j)) & 0xffu);
-        v[j] = (signs >> j) & 1u ? -db * g : db * g;
-    }
-    return v[0] * x.x + v[1] * x.y + v[2] * x.z + v[3] * x.w;
-}
-
 template <int TYPE>
 __device__ __forceinline__ float group_dot4(const uint8_t* blk, int ib32, int e, const float4& x) {
     float w[4];
@@ -297,38 +119,6 @@ __device__ __forceinline__ float group_dot4(const uint8_t* blk, int ib32, int e,
         for (int i = 0; i < 4; ++i) {
             const uint32_t q = ldb(qs + i);
             w[i] = dl * (float)hc_iq4nl_values[hi ? q >> 4 : q & 0x0Fu];
-        }
-    } else {
-        // IQ2 (8-element grid points: half (e / 4) % 2 of point e / 8) and IQ3 (4-element points)
-        const float d = ld_f16u(blk);
-        const int l = e >> 3, half = (e >> 2) & 1;
-        if constexpr (TYPE == T_IQ2_XXS) {
-            const uint32_t aux0 = ld_u32u(blk + 2 + 8 * ib32), aux1 = ld_u32u(blk + 2 + 8 * ib32 + 4);
-            const float db = d * (0.5f + (float)(aux1 >> 28)) * 0.25f;
-            const uint64_t g = hc_iq2xxs_grid[(aux0 >> (8 * l)) & 0xff];
-            return dot4_signed(db, (uint32_t)(g >> (32 * half)), ksigns(aux1 >> (7 * l)) >> (4 * half), x);
-        } else if constexpr (TYPE == T_IQ2_XS) {
-            const uint32_t sc = ldb(blk + 66 + ib32);
-            const float db = d * (0.5f + (float)(l < 2 ? sc & 0xf : sc >> 4)) * 0.25f;
-            const uint32_t q = ld_u16u(blk + 2 + 2 * (4 * ib32 + l));
-            const uint64_t g = hc_iq2xs_grid[q & 511];
-            return dot4_signed(db, (uint32_t)(g >> (32 * half)), ksigns(q >> 9) >> (4 * half), x);
-        } else if constexpr (TYPE == T_IQ2_S) {
-            const uint32_t sc = ldb(blk + 74 + ib32), qh = ldb(blk + 66 + ib32);
-            const float db = d * (0.5f + (float)(l < 2 ? sc & 0xf : sc >> 4)) * 0.25f;
-            const uint32_t idx = ldb(blk + 2 + 4 * ib32 + l) | ((qh << (8 - 2 * l)) & 0x300u);
-            const uint64_t g = hc_iq2s_grid[idx];
-            return dot4_signed(db, (uint32_t)(g >> (32 * half)), ldb(blk + 34 + 4 * ib32 + l) >> (4 * half), x);
-        } else if constexpr (TYPE == T_IQ3_XXS) {
-            const uint32_t aux = ld_u32u(blk + 66 + 4 * ib32);
-            const float db = d * (0.5f + (float)(aux >> 28)) * 0.5f;
-            const uint32_t g = hc_iq3xxs_grid[ldb(blk + 2 + 8 * ib32 + 2 * l + half)];
-            return dot4_signed(db, g, ksigns(aux >> (7 * l)) >> (4 * half), x);
-        } else {  // IQ3_S
-            const uint32_t sc = ldb(blk + 106 + ib32 / 2), qh = ldb(blk + 66 + ib32);
-            const float db = d * (1.0f + 2.0f * (float)((sc >> (4 * (ib32 & 1))) & 0xf));
-            const uint32_t idx = ldb(blk + 2 + 8 * ib32 + 2 * l + half) | ((qh << (8 - 2 * l - half)) & 256u);
-            return dot4_signed(db, hc_iq3s_grid[idx], ldb(blk + 74 + 4 * ib32 + l) >> (4 * half), x);
         }
     }
     return w[0] * x.x + w[1] * x.y + w[2] * x.z + w[3] * x.w;
@@ -461,7 +251,7 @@ static int grid_for(int work_warps) {
 
 bool gemv_simple_supported(int type) {
     switch (type) {
-        case T_F32: case T_IQ2_XXS: case T_IQ2_XS: case T_IQ2_S: case T_IQ3_XXS: case T_IQ3_S: case T_Q4_0:
+        case T_F32: case T_Q4_0:
         case T_Q4_1: case T_Q5_0: case T_Q5_1: case T_Q2_K: case T_Q3_K: case T_Q5_K: case T_IQ4_NL: case T_IQ4_XS:
         case T_F16: case T_BF16: case T_Q8_1: case T_Q8_K:
             return true;
@@ -485,21 +275,6 @@ cudaError_t launch_gemv_simple(int type, const uint8_t* w, size_t row_bytes, int
         case T_BF16:
             gemv_half_kernel<true><<<grid, 256, 0, stream>>>(reinterpret_cast<const uint16_t*>(w), row_bytes / 2, M, K,
                                                             x, ldx, y, ldy, resid, ldr, nvec);
-            break;
-        case T_IQ2_XXS:
-            gemv_group_kernel<T_IQ2_XXS, 256, 66><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
-            break;
-        case T_IQ2_XS:
-            gemv_group_kernel<T_IQ2_XS, 256, 74><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
-            break;
-        case T_IQ2_S:
-            gemv_group_kernel<T_IQ2_S, 256, 82><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
-            break;
-        case T_IQ3_XXS:
-            gemv_group_kernel<T_IQ3_XXS, 256, 98><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
-            break;
-        case T_IQ3_S:
-            gemv_group_kernel<T_IQ3_S, 256, 110><<<grid, 256, 0, stream>>>(w, row_bytes, M, K, x, ldx, y, ldy, resid, ldr, nvec);
             break;
 #define HC_GROUP_CASE(T, QK, BLK)                                                                       \
     case T:                                                                                             \

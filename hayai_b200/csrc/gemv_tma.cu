@@ -9,6 +9,7 @@
 // deterministic.
 #include "gemv_launch.h"
 #include "gemv_tma.cuh"
+#include "gemv_iq.cuh"
 
 namespace hc {
 
@@ -187,10 +188,17 @@ cudaError_t launch_gemv_mma(int type, const GemvArgs& a0, int nvec, bool fused, 
         case T_Q4_K: return tma_launch_fmt<FmtQ4K>(a, nvec, fused, num_sms, smem_limit, stream);
         case T_Q6_K: return tma_launch_fmt<FmtQ6K>(a, nvec, fused, num_sms, smem_limit, stream);
         case T_Q8_0: return tma_launch_fmt<FmtQ80>(a, nvec, fused, num_sms, smem_limit, stream);
+        case T_IQ2_XXS: return tma_launch_fmt<FmtIQ<T_IQ2_XXS>>(a, nvec, fused, num_sms, smem_limit, stream);
+        case T_IQ2_XS: return tma_launch_fmt<FmtIQ<T_IQ2_XS>>(a, nvec, fused, num_sms, smem_limit, stream);
+        case T_IQ2_S: return tma_launch_fmt<FmtIQ<T_IQ2_S>>(a, nvec, fused, num_sms, smem_limit, stream);
+        case T_IQ3_XXS: return tma_launch_fmt<FmtIQ<T_IQ3_XXS>>(a, nvec, fused, num_sms, smem_limit, stream);
+        case T_IQ3_S: return tma_launch_fmt<FmtIQ<T_IQ3_S>>(a, nvec, fused, num_sms, smem_limit, stream);
         default: return cudaErrorInvalidValue;
     }
 }
 
-bool gemv_mma_supported(int type) { return type == T_Q4_K || type == T_Q6_K || type == T_Q8_0; }
+bool gemv_mma_supported(int type) {
+    return type == T_Q4_K || type == T_Q6_K || type == T_Q8_0 || is_iq_type(type);
+}
 
 }  // namespace hc

@@ -60,8 +60,13 @@ __host__ __device__ constexpr int tile_slot_bytes(int nv) { return kCW * nv * 16
 // matrix of consumer warp w
 __host__ __device__ constexpr int warp_matrix(int w, bool fused) { return fused ? w / (kUnits / 2) : 0; }
 
-// One consumer warp's unit of a stage: rows g, g+8 of the tile-block image at tb.  Q4_K and
-// Q6_K accumulate lane shares in pA/pB, Q8_0 row sums in yA/yB.
+// The IQ formats' unit (gemv_iq.cuh; instantiated by the dense GEMV only).
+template <class F, int NV>
+__device__ __forceinline__ void iq_stage_unit(const uint8_t* tb, int kbj, const LaneCtx<NV>& ctx,
+                                              float (&pA)[1][NV], float (&pB)[1][NV]);
+
+// One consumer warp's unit of a stage: rows g, g+8 of the tile-block image at tb.  Q4_K, Q6_K
+// and the IQ formats accumulate lane shares in pA/pB, Q8_0 row sums in yA/yB.
 template <class F, int NV>
 __device__ __forceinline__ void stage_unit(const uint8_t* tb, int kbj, const LaneCtx<NV>& ctx, float& yA, float& yB,
                                            float (&pA)[1][NV], float (&pB)[1][NV]) {
@@ -74,6 +79,8 @@ __device__ __forceinline__ void stage_unit(const uint8_t* tb, int kbj, const Lan
         Q6KBlk A, B;
         tile_load<F, true>(A, B, tb, ctx.g, ctx.t);
         q6k_unit<NV>(A, B, kbj, ctx, pA, pB);
+    } else if constexpr (is_iq_type(F::kType)) {
+        iq_stage_unit<F, NV>(tb, kbj, ctx, pA, pB);
     } else {
         typename BlkOf<F>::T A, B;
         tile_load<F, true>(A, B, tb, ctx.g, ctx.t);

@@ -1050,7 +1050,8 @@ static int moe_run(hc_engine* e, const float* router_w, size_t E, size_t k, int 
     }
     const size_t dm = g0->n, ff = g0->m;
     if (d0->n != ff || d0->m != dm) return hc_set_error(HC_ERR_INVALID, "moe_ffn: down must be d_model x d_ff");
-    if (!gemv_mma_supported(g0->type) || !gemv_mma_supported(d0->type))
+    auto routed = [](int t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0; };
+    if (!routed(g0->type) || !routed(d0->type))
         return hc_set_error(HC_ERR_UNSUPPORTED, "moe_ffn: expert format %s/%s has no routed kernel",
                             hc_type_label(g0->type), hc_type_label(d0->type));
     if (((uintptr_t)x & 15) || (dm & 3)) return hc_set_error(HC_ERR_INVALID, "moe_ffn: x must be 16-byte aligned");

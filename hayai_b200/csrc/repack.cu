@@ -1,6 +1,6 @@
 // repack.cu -- one-time upload transform from raw GGUF rows to the GPU layouts.
 //
-// Q4_K, Q6_K and Q8_0 are stored tile-major: the matrix is cut into 16-row tiles, and the
+// Q4_K, Q6_K, Q8_0 and the IQ2 / IQ3 formats are stored tile-major: the matrix is cut into 16-row tiles, and the
 // 16 rows x one kernel block (256 elements; 128 for Q8_0) of a tile form one contiguous
 // "tile-block" image.  The blocks of a tile follow one another, so any run of blocks of a
 // tile is a single contiguous range: the GEMV moves a whole pipeline stage with one TMA
@@ -25,7 +25,14 @@
 //                        [q0: (r,t) at 16(4r+t)][q1: at 1024 + 16(4r+t)][d: row r at 2048 + 8r]
 //                        word wi of lane t (q0: wi < 4, q1: wi - 4) = codes 16(wi & 1) + 4t..+3 of
 //                        block 4G + wi / 2; d = the group's 4 f16 scales; missing blocks are zero.
-//  F32, IQ*: raw GGUF rows.
+//  IQ2_XXS / IQ2_XS / IQ2_S / IQ3_XXS / IQ3_S images (1056 / 1184 / 1312 / 1568 / 1760 B):
+//                        [d: row r at 2r][piece (r,t) at 32 + 16(4r+t) = lane t's groups 2t,
+//                        2t+1: block bytes 2 + 16t..+15 (IQ2_S: grid-index bytes 2 + 8t..+7,
+//                        then sign bytes 34 + 8t..+7)][extras from 1056: IQ2_XS scales (8 B
+//                        per row); IQ2_S qh, scales (16 B per row); IQ3_XXS scale-and-sign
+//                        words (32 B per row); IQ3_S signs (32 B per row), qh (8 B per row at
+//                        1568), scales (4 B per row at 1696)] (iq2.rs:504-573, iq3.rs:147-220).
+//  F32, F16, BF16 and the other block formats: raw GGUF rows.
 //
 // Layout of the GGUF blocks: q4k.rs:11-43 (Q4_K), q6k.rs:26-57 (ql/qh/scales/d),
 // quant.rs:598-615 (Q8_0).
@@ -61,13 +68,18 @@ size_t raw_row_bytes(int type, int K) {
     }
 }
 
-bool tiled_type(int type) { return type == T_Q4_K || type == T_Q6_K || type == T_Q8_0; }
+bool tiled_type(int type) { return type == T_Q4_K || type == T_Q6_K || type == T_Q8_0 || is_iq_type(type); }
 
 size_t tile_block_bytes(int type) {
     switch (type) {
         case T_Q4_K: return 2304;
         case T_Q6_K: return 3360;
         case T_Q8_0: return 2176;
+        case T_IQ2_XXS: return 1056;
+        case T_IQ2_XS: return 1184;
+        case T_IQ2_S: return 1312;
+        case T_IQ3_XXS: return 1568;
+        case T_IQ3_S: return 1760;
         default: return 0;
     }
 }
@@ -151,6 +163,49 @@ __device__ __forceinline__ uint32_t tiled_word(const uint8_t* __restrict__ raw, 
         uint32_t v = 0;  // the lane's 4 int8 scales, group q in byte q
         for (int q = 0; q < 4; ++q) v |= (uint32_t)blk[192 + 8 * h + s + 2 * q] << (8 * q);
         return v;
+    } else if constexpr (is_iq_type(kType)) {
+        // [d of 16 rows][piece (r, t): 16 B][extras], gemv_iq.cuh
+        constexpr int kBlk = kType == T_IQ2_XXS ? 66 : kType == T_IQ2_XS ? 74 : kType == T_IQ2_S ? 82
+                             : kType == T_IQ3_XXS ? 98 : 110;
+        int r, off;
+        if (w < 8) {  // d of rows 2w, 2w + 1
+            uint32_t v = 0;
+            for (int h = 0; h < 2; ++h) {
+                const int row = tile * 16 + 2 * w + h;
+                if (row < M) v |= rd2(raw + (size_t)row * raw_rb + (size_t)kb * kBlk) << (16 * h);
+            }
+            return v;
+        } else if (w < 264) {  // piece (r, t), word j
+            const int p = (w - 8) >> 2, j = w & 3, t = p & 3;
+            r = p >> 2;
+            if constexpr (kType == T_IQ2_S) off = j < 2 ? 2 + 8 * t + 4 * j : 34 + 8 * t + 4 * (j - 2);
+            else off = 2 + 16 * t + 4 * j;
+        } else {
+            const int e = w - 264;
+            if constexpr (kType == T_IQ2_XS) {  // scales: 8 B per row
+                r = e >> 1;
+                off = 66 + 4 * (e & 1);
+            } else if constexpr (kType == T_IQ2_S) {  // qh[8] then scales[8]: 16 B per row
+                r = e >> 2;
+                off = (e & 3) < 2 ? 66 + 4 * (e & 3) : 74 + 4 * ((e & 3) - 2);
+            } else if constexpr (kType == T_IQ3_XXS) {  // scale-and-sign words: 32 B per row
+                r = e >> 3;
+                off = 66 + 4 * (e & 7);
+            } else {  // IQ3_S: signs (32 B per row), qh (8 B), scales (4 B)
+                if (e < 128) {
+                    r = e >> 3;
+                    off = 74 + 4 * (e & 7);
+                } else if (e < 160) {
+                    r = (e - 128) >> 1;
+                    off = 66 + 4 * ((e - 128) & 1);
+                } else {
+                    r = e - 160;
+                    off = 106;
+                }
+            }
+        }
+        const int row = tile * 16 + r;
+        return row < M ? rd4(raw + (size_t)row * raw_rb + (size_t)kb * kBlk + off) : 0u;
     } else {  // Q8_0, kb = group of 4 blocks
         if (w >= 512) {  // d: row r = k / 2, blocks 4G + 2(k & 1) + {0, 1}
             const int k = w - 512, row = tile * 16 + (k >> 1);
@@ -194,6 +249,11 @@ cudaError_t launch_repack(int type, const uint8_t* raw, uint8_t* gpu, int M, int
     switch (type) {
         case T_Q4_K: repack_tiled_kernel<T_Q4_K><<<blocks, 256, 0, stream>>>(raw, out, M, nb, nkb, rrb, words); break;
         case T_Q6_K: repack_tiled_kernel<T_Q6_K><<<blocks, 256, 0, stream>>>(raw, out, M, nb, nkb, rrb, words); break;
+        case T_IQ2_XXS: repack_tiled_kernel<T_IQ2_XXS><<<blocks, 256, 0, stream>>>(raw, out, M, nb, nkb, rrb, words); break;
+        case T_IQ2_XS: repack_tiled_kernel<T_IQ2_XS><<<blocks, 256, 0, stream>>>(raw, out, M, nb, nkb, rrb, words); break;
+        case T_IQ2_S: repack_tiled_kernel<T_IQ2_S><<<blocks, 256, 0, stream>>>(raw, out, M, nb, nkb, rrb, words); break;
+        case T_IQ3_XXS: repack_tiled_kernel<T_IQ3_XXS><<<blocks, 256, 0, stream>>>(raw, out, M, nb, nkb, rrb, words); break;
+        case T_IQ3_S: repack_tiled_kernel<T_IQ3_S><<<blocks, 256, 0, stream>>>(raw, out, M, nb, nkb, rrb, words); break;
         default: repack_tiled_kernel<T_Q8_0><<<blocks, 256, 0, stream>>>(raw, out, M, nb, nkb, rrb, words); break;
     }
     return cudaGetLastError();

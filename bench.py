@@ -821,8 +821,9 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
         k_time = e0.elapsed_time(e1) / 1e3 / reps
         k_bytes = tok_bytes // world if tp else tok_bytes  # this GPU's shard under TP
-        kname = f"ffn_stack_kernel<{names[tg]},{names[td]}> (all {L} layers, one launch" + \
-            (f", d_ff shard 1/{world} + in-kernel exchange)" if tp else ")")
+        flow = not tp and td == Q6_K and os.environ.get("HAYAI_FLOW_KERNEL", "1") != "0" and kin == dm
+        kname = f"{'ffn_flow_kernel' if flow else 'ffn_stack_kernel'}<{names[tg]},{names[td]}> (all {L} layers, " + \
+            "one launch" + (f", d_ff shard 1/{world} + in-kernel exchange)" if tp else ")")
         kkey = f"stack_{args.config}_L{L}" + (f"_tp{world}" if tp else "")
     else:
         h = torch.empty(B, ffl, dtype=torch.float32, device=dev)
@@ -882,6 +883,57 @@ def run_ours(args):
                    "per-layer kernels + torch.distributed all_reduce" if tp else "hc_ffn_stack") + " (host buffers)"}
     assert np.isfinite(xo).all()
 
+    # ---- the per-layer path beside the persistent kernel (rank 0, unsharded, unpadded): the
+    # same layers as per-layer kernels replayed from one captured CUDA graph (the path batches
+    # take), and launched eagerly one call at a time
+    per_layer = None
+    if rank == 0 and not tp and kin == dm and not args.no_per_layer:
+        os.environ["HAYAI_STACK_KERNEL"] = "0"
+        try:
+            eng2 = hb.CudaEngine(local)
+        finally:
+            os.environ.pop("HAYAI_STACK_KERNEL", None)
+        eng2.set_stream(stream)
+        reps = max(3, min(args.steps, 20))
+        xg = x0.clone()
+
+        def graph_step():
+            xg.copy_(x0)
+            eng2.ffn_stack_dev(G, U, D, xg, B, norms=NW, eps=EPS)
+
+        hh = torch.empty(B, ffl, dtype=torch.float32, device=dev)
+        xa, xb = x0.clone(), torch.empty_like(x0)
+
+        def eager_step():
+            cur, nxt = xa, xb
+            cur.copy_(x0)
+            for l in range(L):
+                eng2.ffn_gateup_dev(G[l], U[l], cur, hh, B, norm=NW[l], norm_len=dm, eps=EPS)
+                eng2.gemv_dev(D[l], hh, nxt, resid=cur, nvec=B)
+                cur, nxt = nxt, cur
+
+        timings = {}
+        for name, fn in (("graph", graph_step), ("eager", eager_step)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize(dev)
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            timings[name] = e0.elapsed_time(e1) / reps
+        eng2.sync()
+        per_layer = {"graph_ms_per_step": round(timings["graph"], 4), "eager_ms_per_step": round(timings["eager"], 4),
+                     "persistent_ms_per_step": round(t / args.steps * 1e3, 4),
+                     "graph_GBps": round(tok_bytes / (timings["graph"] / 1e3) / 1e9, 1),
+                     "eager_GBps": round(tok_bytes / (timings["eager"] / 1e3) / 1e9, 1),
+                     "kernels_per_layer": launches_per_layer,
+                     "note": "same weights and parity contract; graph = the per-layer kernels captured once and "
+                             "replayed (hc_ffn_stack_dev with the stack kernel off), eager = one C-ABI call per "
+                             "GEMV; both include a copy of x_0 per step"}
+        del eng2
+
     cpu = None
     if want_cpu:
         x_np = x0[0].cpu().numpy()
@@ -910,6 +962,8 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         if parity is not None:
             line["parity"] = parity
+        if per_layer is not None:
+            line["per_layer_path"] = per_layer
         result = line
     if peers is not None:
         peers.close()
@@ -1162,7 +1216,7 @@ def run_sharded(args):
                      ("tp_llama70b_b16", dict(config="llama70b", tp=True, ep=False, batch=16, steps=6)),
                      ("ep_qwen3moe", dict(config="qwen3moe", tp=False, ep=True, batch=1, steps=20))):
         a = argparse.Namespace(**{**base, **kw, "warmup": 3, "layers": 0, "no_cpu_baseline": True,
-                                  "no_parity": False, "tp_impl": "ours"})
+                                  "no_parity": False, "no_per_layer": True, "tp_impl": "ours"})
         line = (run_moe if "n_expert" in CONFIGS[a.config] else run_ours)(a)
         barrier(world)
         if rank == 0 and line:
@@ -1195,6 +1249,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed stack's output")
+    ap.add_argument("--no-per-layer", action="store_true",
+                    help="skip the per-layer path timing (CUDA graph replay and eager launches)")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the sharded configs (70B tensor-parallel, Qwen3 expert-parallel) the default "
                          "llama8b run also measures at the same GPU count")

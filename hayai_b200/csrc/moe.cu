@@ -49,49 +49,65 @@ __global__ void __launch_bounds__(128) router_exact_kernel(const float* __restri
 }
 
 // The same scores with the inputs staged in shared memory: a block takes 8 experts x 16
-// tokens (thread = token * 8 + expert), copies their rows in coalesced, then every thread runs
-// its chain from shared memory (rows padded by 4 floats so the 8 experts' float4 reads fall on
-// distinct banks).  Summation order and rounding are those of router_exact_kernel.
-constexpr int kRouterE = 8, kRouterT = 16;
+// tokens (thread = token * 8 + expert).  The rows arrive in K-chunks of 256 floats, each chunk
+// on its own mbarrier, all issued at the start, so a thread's chain (2048 dependent adds for
+// d_model 2048: the floor of this kernel) starts as soon as the first chunk has landed and the
+// rest of the copy overlaps it.  Rows are padded by 4 floats so the 8 experts' float4 reads
+// fall on distinct banks.  Summation order and rounding are those of router_exact_kernel.
+constexpr int kRouterE = 8, kRouterT = 16, kRouterChunk = 256, kRouterMaxChunks = 32;
 
 __global__ void __launch_bounds__(kRouterE * kRouterT) router_staged_kernel(const float* __restrict__ W,
                                                                             const float* __restrict__ x, int E, int D,
                                                                             int T, float* __restrict__ scores,
                                                                             int* err) {
     extern __shared__ __align__(128) float rs[];
-    __shared__ __align__(8) uint64_t s_bar;
-    __shared__ int s_ok;
+    __shared__ __align__(8) uint64_t s_bar[kRouterMaxChunks];
     const int ld = D + 4;
     float* ws = rs;                  // [kRouterE][ld]
     float* xs = rs + kRouterE * ld;  // [kRouterT][ld]
     const int e0 = blockIdx.x * kRouterE, t0 = blockIdx.y * kRouterT;
-    const int ne = min(kRouterE, E - e0), nt = min(kRouterT, T - t0), d4 = D >> 2;
-    const uint32_t bar = smem_addr(&s_bar);
-    if (threadIdx.x == 0) {  // every row with one bulk copy (rows are 16-byte multiples, 16-byte aligned)
-        mbar_init(bar, 1);
+    const int ne = min(kRouterE, E - e0), nt = min(kRouterT, T - t0);
+    const int nch = (D + kRouterChunk - 1) / kRouterChunk;
+    if (threadIdx.x == 0) {  // every row's chunk c with one bulk copy, completing on s_bar[c]
+        for (int c = 0; c < nch; ++c) mbar_init(smem_addr(&s_bar[c]), 1);
         mbar_fence_init();
-        mbar_arrive_expect_tx(bar, (uint32_t)((ne + nt) * D * 4));
-        for (int r = 0; r < ne; ++r) bulk_g2s(smem_addr(ws + r * ld), W + (size_t)(e0 + r) * D, (uint32_t)(D * 4), bar);
-        for (int r = 0; r < nt; ++r) bulk_g2s(smem_addr(xs + r * ld), x + (size_t)(t0 + r) * D, (uint32_t)(D * 4), bar);
-        s_ok = mbar_wait(bar, 0) ? 1 : 0;
-        if (!s_ok) atomicOr(err, 2);
+        for (int c = 0; c < nch; ++c) {
+            const int k0 = c * kRouterChunk, len = min(kRouterChunk, D - k0);
+            const uint32_t bar = smem_addr(&s_bar[c]);
+            mbar_arrive_expect_tx(bar, (uint32_t)((ne + nt) * len * 4));
+            for (int r = 0; r < ne; ++r)
+                bulk_g2s(smem_addr(ws + r * ld + k0), W + (size_t)(e0 + r) * D + k0, (uint32_t)(len * 4), bar);
+            for (int r = 0; r < nt; ++r)
+                bulk_g2s(smem_addr(xs + r * ld + k0), x + (size_t)(t0 + r) * D + k0, (uint32_t)(len * 4), bar);
+        }
     }
-    __syncthreads();
-    if (!s_ok) return;
+    __syncthreads();  // the barriers are initialised
     const int e = threadIdx.x % kRouterE, t = threadIdx.x / kRouterE;
-    if (e >= ne || t >= nt) return;
+    const bool live = e < ne && t < nt;
     const float4* w4 = reinterpret_cast<const float4*>(ws + e * ld);
     const float4* x4 = reinterpret_cast<const float4*>(xs + t * ld);
     float s = 0.0f;
+    bool ok = true;
+    for (int c = 0; c < nch && ok; ++c) {
+        ok = mbar_wait(smem_addr(&s_bar[c]), 0);
+        if (!ok || !live) continue;
+        const int c1 = min(D, (c + 1) * kRouterChunk) >> 2;
 #pragma unroll 4
-    for (int c = 0; c < d4; ++c) {
-        const float4 a = w4[c], b = x4[c];
-        s = __fadd_rn(s, __fmul_rn(a.x, b.x));
-        s = __fadd_rn(s, __fmul_rn(a.y, b.y));
-        s = __fadd_rn(s, __fmul_rn(a.z, b.z));
-        s = __fadd_rn(s, __fmul_rn(a.w, b.w));
+        for (int q = (c * kRouterChunk) >> 2; q < c1; ++q) {
+            const float4 a = w4[q], b = x4[q];
+            s = __fadd_rn(s, __fmul_rn(a.x, b.x));
+            s = __fadd_rn(s, __fmul_rn(a.y, b.y));
+            s = __fadd_rn(s, __fmul_rn(a.z, b.z));
+            s = __fadd_rn(s, __fmul_rn(a.w, b.w));
+        }
     }
-    scores[(size_t)(t0 + t) * E + e0 + e] = s;
+    if (!ok) {
+        if (err) atomicOr(err, 2);
+        // the copies still in flight must land before the CTA's shared memory is released
+        for (int c = 0; c < nch; ++c) mbar_wait(smem_addr(&s_bar[c]), 0);
+        return;
+    }
+    if (live) scores[(size_t)(t0 + t) * E + e0 + e] = s;
 }
 
 // Router scores on the stream: the staged kernel when the rows fit shared memory.
@@ -99,7 +115,7 @@ static cudaError_t launch_router(const float* W, const float* x, int E, int D, i
                                  cudaStream_t stream, int* err) {
     const int smem = (kRouterE + kRouterT) * (D + 4) * 4 + 128;
     const bool aligned = ((((uintptr_t)W) | ((uintptr_t)x)) & 15) == 0 && (D & 3) == 0;
-    if (aligned && smem <= smem_limit) {
+    if (aligned && smem <= smem_limit && (D + kRouterChunk - 1) / kRouterChunk <= kRouterMaxChunks) {
         static int configured[64];
         int dev = 0;
         cudaGetDevice(&dev);
@@ -459,53 +475,89 @@ __device__ int moe_cost_to_tile(long long q, const int* wcum, const int* w, int 
     return lo * tps + (int)((q - (long long)wcum[lo] * tps + w[lo] - 1) / w[lo]);
 }
 
-// Group the routed pairs sid[0..P) (in shared memory): one thread per expert of [e_lo, e_hi)
-// counts its pairs, the block scans the segment counts and costs, the segments are emitted in
-// expert order, then both GEMVs' tile sequences are cut into C ranges of equal cost:
-// ranges[0..C] over tps_a tiles per segment (gate/up), ranges[C+1..2C+1] over tps_b (down).
-// nseg[0] = segments.  wcum [P + 1] and wseg [P] are shared-memory scratch.  Needs
-// blockDim.x >= e_hi - e_lo, a multiple of 32; every thread of the block calls it.
+// Group the routed pairs sid[0..P) (in shared memory) into segments of <= kMoeNV pairs of
+// one expert, experts in id order and each expert's pairs in pair order, then cut both GEMVs'
+// tile sequences into C ranges of equal cost: ranges[0..C] over tps_a tiles per segment
+// (gate/up), ranges[C+1..2C+1] over tps_b (down).  nseg[0] = segments.
+// Every pair finds its own place in O(P / 32 + 1) steps: warp w takes pairs [32w, 32w + 32)
+// in rounds; __match_any_sync gives a pair's rank among the same expert's pairs of its group
+// of 32 and the group's count per expert (hist, one byte per (group, expert)); the expert's
+// total, its rank offset from the earlier groups and, after two block scans over the experts,
+// its first segment and cost follow.  The result equals a sequential pass over the pairs.
+// Scratch in shared memory: wcum [P + 1], wseg [P], hist [ceil(P / 32) x nE] bytes, sbase and
+// swbase [nE] each.  Every thread of the block calls it (blockDim.x a multiple of 32).
 __device__ void group_pairs(const int* sid, int P, int e_lo, int e_hi, MoeSeg* __restrict__ segs, int* __restrict__ nseg,
-                            int C, int tps_a, int tps_b, int* __restrict__ ranges, int* wcum, int* wseg, int* s_warp,
-                            int* s_tot) {
-    const int e = e_lo + (int)threadIdx.x;
-    const bool mine = e < e_hi;
-    int n = 0;
-    if (mine)
-        for (int p = 0; p < P; ++p) n += sid[p] == e;
-    const int ns = (n + kMoeNV - 1) / kMoeNV;
-    const int full = n / kMoeNV, rem = n - full * kMoeNV;
-    const int wexp = full * moe_tile_cost(kMoeNV) + (rem ? moe_tile_cost(rem > 2 ? kMoeNV : rem) : 0);
-    const int sincl = block_scan_incl(ns, s_warp);
-    const int wincl = block_scan_incl(wexp, s_warp);
-    const int base = sincl - ns, wbase = wincl - wexp;
-    if (threadIdx.x == blockDim.x - 1) {
-        s_tot[0] = sincl;
-        s_tot[1] = wincl;
+                            int C, int tps_a, int tps_b, int* __restrict__ ranges, int* wcum, int* wseg, uint8_t* hist,
+                            int* sbase, int* swbase, int* s_warp, int* s_tot) {
+    const int nE = e_hi - e_lo, nG = (P + 31) >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (int)(blockDim.x >> 5);
+    for (int i = threadIdx.x; i < ((nG * nE + 3) >> 2); i += blockDim.x) reinterpret_cast<uint32_t*>(hist)[i] = 0u;
+    __syncthreads();
+    // counts per (group, expert)
+    for (int g = warp; g < nG; g += nw) {
+        const int p = 32 * g + lane;
+        int e = p < P ? sid[p] - e_lo : -1;
+        const bool held = e >= 0 && e < nE;  // (expert parallelism: other ranks' experts are skipped)
+        if (!held) e = -1 - lane;            // distinct keys for the pairs not grouped here
+        const unsigned same = __match_any_sync(kFull, e);
+        if (held && (same & ((1u << lane) - 1u)) == 0u) hist[g * nE + e] = (uint8_t)__popc(same);
     }
-    if (mine && n > 0) {
-        int j = 0, wc = wbase;
-        for (int p = 0; p < P; ++p) {
-            if (sid[p] != e) continue;
-            const int si = base + j / kMoeNV;
-            MoeSeg& sg = segs[si];
-            if (j % kMoeNV == 0) {
-                const int nv = min(kMoeNV, n - j);
-                const int cost = moe_tile_cost(nv > 2 ? kMoeNV : nv);
-                sg.expert = e;
-                sg.nv = nv;
-                wcum[si] = wc;
-                wseg[si] = cost;
-                wc += cost;
+    __syncthreads();
+    // per expert: pairs, segments and cost; block scans give each expert its first segment
+    int base_s = 0, base_w = 0;
+    for (int e0 = 0; e0 < nE; e0 += blockDim.x) {
+        const int e = e0 + (int)threadIdx.x;
+        int n = 0;
+        if (e < nE)
+            for (int g = 0; g < nG; ++g) n += hist[g * nE + e];
+        const int ns = (n + kMoeNV - 1) / kMoeNV;
+        const int full = n / kMoeNV, rem = n - full * kMoeNV;
+        const int wexp = full * moe_tile_cost(kMoeNV) + (rem ? moe_tile_cost(rem > 2 ? kMoeNV : rem) : 0);
+        const int sincl = block_scan_incl(ns, s_warp);
+        const int wincl = block_scan_incl(wexp, s_warp);
+        if (e < nE) {
+            sbase[e] = base_s + sincl - ns;
+            swbase[e] = base_w + wincl - wexp;
+        }
+        if (threadIdx.x == blockDim.x - 1) {
+            s_tot[0] = base_s + sincl;
+            s_tot[1] = base_w + wincl;
+        }
+        __syncthreads();
+        base_s = s_tot[0];
+        base_w = s_tot[1];
+        __syncthreads();
+    }
+    // every pair to its slot
+    for (int g = warp; g < nG; g += nw) {
+        const int p = 32 * g + lane;
+        int e = p < P ? sid[p] - e_lo : -1;
+        const bool held = e >= 0 && e < nE;
+        if (!held) e = -1 - lane;
+        const unsigned same = __match_any_sync(kFull, e);
+        if (held) {
+            int r = __popc(same & ((1u << lane) - 1u)), n = 0;
+            for (int h = 0; h < nG; ++h) {
+                const int c = hist[h * nE + e];
+                n += c;
+                if (h < g) r += c;
             }
-            sg.pair[j % kMoeNV] = p;
-            ++j;
+            const int si = sbase[e] + r / kMoeNV;
+            MoeSeg& sg = segs[si];
+            sg.pair[r % kMoeNV] = p;
+            if (r % kMoeNV == 0) {
+                const int nv = min(kMoeNV, n - r);
+                sg.expert = e_lo + e;
+                sg.nv = nv;
+                wcum[si] = swbase[e] + (r / kMoeNV) * moe_tile_cost(kMoeNV);
+                wseg[si] = moe_tile_cost(nv > 2 ? kMoeNV : nv);
+            }
         }
     }
     __syncthreads();
-    const int S = s_tot[0];
+    const int S = base_s;
     if (threadIdx.x == 0) {
-        wcum[S] = s_tot[1];
+        wcum[S] = base_w;
         *nseg = S;
     }
     __syncthreads();
@@ -516,14 +568,24 @@ __device__ void group_pairs(const int* sid, int P, int e_lo, int e_hi, MoeSeg* _
     }
 }
 
+// Shared memory of the grouping step for P pairs over nE experts (ids, then group_pairs'
+// scratch), in bytes.
+__host__ __device__ constexpr size_t group_smem_bytes(int P, int nE) {
+    return (size_t)(3 * P + 1) * 4 + (((size_t)((P + 31) / 32) * nE + 3) / 4) * 4 + 2 * (size_t)nE * 4;
+}
+
 __global__ void moe_group_kernel(const int32_t* __restrict__ ids, int P, int e_lo, int e_hi, MoeSeg* __restrict__ segs,
                                  int* __restrict__ nseg, int C, int tps_a, int tps_b, int* __restrict__ ranges) {
-    extern __shared__ int sh[];  // [P] ids | [P + 1] cost prefix | [P] tile costs
+    extern __shared__ int sh[];  // [P] ids | group_pairs' scratch (group_smem_bytes)
     __shared__ int s_warp[32];
     __shared__ int s_tot[2];
     for (int p = threadIdx.x; p < P; p += blockDim.x) sh[p] = ids[p];
     __syncthreads();
-    group_pairs(sh, P, e_lo, e_hi, segs, nseg, C, tps_a, tps_b, ranges, sh + P, sh + 2 * P + 1, s_warp, s_tot);
+    const int nE = e_hi - e_lo;
+    uint8_t* hist = reinterpret_cast<uint8_t*>(sh + 3 * P + 1);
+    int* sb = reinterpret_cast<int*>(hist + (((size_t)((P + 31) / 32) * nE + 3) / 4) * 4);
+    group_pairs(sh, P, e_lo, e_hi, segs, nseg, C, tps_a, tps_b, ranges, sh + P, sh + 2 * P + 1, hist, sb, sb + nE,
+                s_warp, s_tot);
 }
 
 // Routing and grouping in one block for up to 32 tokens and 256 experts (the decode-batch
@@ -537,7 +599,7 @@ __global__ void route_group_kernel(const float* __restrict__ scores, const float
                                    int32_t* __restrict__ ids, float* __restrict__ wout, int e_lo, int e_hi,
                                    MoeSeg* __restrict__ segs, int* __restrict__ nseg, int C, int tps_a, int tps_b,
                                    int* __restrict__ ranges) {
-    extern __shared__ int sh[];  // [P] ids | [P + 1] cost prefix | [P] tile costs
+    extern __shared__ int sh[];  // [P] ids | group_pairs' scratch (group_smem_bytes)
     __shared__ int s_warp[32];
     __shared__ int s_tot[2];
     const int P = T * m.k;
@@ -615,7 +677,11 @@ __global__ void route_group_kernel(const float* __restrict__ scores, const float
         }
     }
     __syncthreads();
-    group_pairs(sh, P, e_lo, e_hi, segs, nseg, C, tps_a, tps_b, ranges, sh + P, sh + 2 * P + 1, s_warp, s_tot);
+    const int nE = e_hi - e_lo;
+    uint8_t* hist = reinterpret_cast<uint8_t*>(sh + 3 * P + 1);
+    int* sb = reinterpret_cast<int*>(hist + (((size_t)((P + 31) / 32) * nE + 3) / 4) * 4);
+    group_pairs(sh, P, e_lo, e_hi, segs, nseg, C, tps_a, tps_b, ranges, sh + P, sh + 2 * P + 1, hist, sb, sb + nE,
+                s_warp, s_tot);
 }
 
 struct MoeTmaArgs {
@@ -1090,7 +1156,7 @@ static int moe_run(hc_engine* e, const float* router_w, size_t E, size_t k, int 
     // router and top-k: on every rank alike (x and the router are replicated)
     HC_CUDA(launch_router(router_w, x, (int)E, (int)dm, (int)T, scores, e->smem_optin, e->stream, e->d_err));
     const bool tma = moe_tma_fits(g0->type, true, (int)dm) && moe_tma_fits(d0->type, false, (int)ff) && n_held <= 1024 &&
-                     (3 * P + 1) * 4 <= 48 * 1024 && ff % 4 == 0 && e->num_sms <= 1024;
+                     group_smem_bytes((int)P, (int)n_held) <= 48 * 1024 && ff % 4 == 0 && e->num_sms <= 1024;
     // decode batches: routing and grouping in one block
     const bool fused_route = tma && T <= 32 && E <= 32 * kRouteRegs && k <= 16;
     if (!fused_route) {
@@ -1109,12 +1175,12 @@ static int moe_run(hc_engine* e, const float* router_w, size_t E, size_t k, int 
         if (fused_route) {
             const RouteMeta rm{(int)E, (int)k, 0, 0, 0, norm, scale};
             const size_t nthr = std::max<size_t>(32 * T, (n_held + 31) / 32 * 32);
-            route_group_kernel<<<1, (unsigned)nthr, (3 * P + 1) * 4, e->stream>>>(
+            route_group_kernel<<<1, (unsigned)nthr, group_smem_bytes((int)P, (int)n_held), e->stream>>>(
                 scores, nullptr, (int)T, rm, ids, wts, (int)lo, (int)(lo + n_held), segs, nseg, C, (int)((ff + 15) / 16),
                 (int)((dm + 15) / 16), ranges);
         } else {
-            const unsigned gthreads = (unsigned)((n_held + 31) / 32 * 32);
-            moe_group_kernel<<<1, gthreads, (3 * P + 1) * 4, e->stream>>>(ids, (int)P, (int)lo, (int)(lo + n_held),
+            const unsigned gthreads = (unsigned)std::min<size_t>(1024, std::max<size_t>(P, n_held) + 31) / 32 * 32;
+            moe_group_kernel<<<1, gthreads, group_smem_bytes((int)P, (int)n_held), e->stream>>>(ids, (int)P, (int)lo, (int)(lo + n_held),
                                                                          segs, nseg, C, (int)((ff + 15) / 16),
                                                                          (int)((dm + 15) / 16), ranges);
         }

@@ -57,6 +57,9 @@ constexpr int kTcABytes = kTcRows * kTcChunk * 2;  // one f16 operand buffer (16
 constexpr int kTcThreads = 480;            // 15 warps
 constexpr int kTcMaxRing = 12;
 constexpr float kTcWScale = 256.f;         // w' = w * 2^8
+// TMEM operand form: one hand-over (dequant -> MMA -> release) covers kTaKH 64-K chunks; a
+// buffer is kTaBuf columns: A_hi of chunk k at [32k, 32k + 32), A_lo at kTaLo + 32k.
+constexpr int kTaKH = 2, kTaLo = 32 * kTaKH, kTaBuf = 2 * kTaLo;
 
 // Tile-block image of each format (repack.cu): bytes, K elements, images per weight stage
 // (one: a stage is one work unit).
@@ -348,10 +351,10 @@ struct TcDq<TcQ6K> {
 
 // ---- dequantisers into TMEM operands (the TA form of the kernel).  Thread (row r, half jj)
 // of the 8 dequantising warps: warp w covers TMEM lanes (= rows) 32 (w % 4) + lane, and the
-// two warps of a lane quarter split each 64-K chunk's work in halves.  An operand buffer is
-// 64 columns: A_hi in columns [0, 32), A_lo in [32, 64); column n holds chunk elements 2n (low
-// half) and 2n + 1.  chunk() writes the thread's columns with tcgen05.st (tA = the buffer's
-// column address with the quarter's base lane).
+// two warps of a lane quarter split each 64-K chunk's work in halves.  A chunk's operands are
+// 32 columns of A_hi at tA and 32 of A_lo at tA + kTaLo; column n holds chunk elements 2n (low
+// half) and 2n + 1.  chunk() writes the thread's columns with tcgen05.st (tA carries the
+// quarter's base lane).
 template <class F>
 struct TcDqT;
 
@@ -385,7 +388,7 @@ struct TcDqT<TcQ80> {
             const uint32_t hv[4] = {h0.x, h0.y, h1.x, h1.y}, lv[4] = {l0.x, l0.y, l1.x, l1.y};
             const uint32_t col = 16 * (g >> 1) + 8 * (g & 1) + 4 * jj;
             tc_st4(tA + col, hv);
-            tc_st4(tA + 32 + col, lv);
+            tc_st4(tA + kTaLo + col, lv);
         }
     }
     __device__ __forceinline__ bool bad() const { return (dbits & 0x40004000u) != 0; }
@@ -427,7 +430,7 @@ struct TcDqT<TcQ4K> {
             }
             const uint32_t col = 16 * s + 8 * jj;
             tc_st8(tA + col, hv);
-            tc_st8(tA + 32 + col, lv);
+            tc_st8(tA + kTaLo + col, lv);
         }
     }
     __device__ __forceinline__ bool bad() const { return !(big < 65504.f); }
@@ -485,7 +488,7 @@ struct TcDqT<TcQ6K> {
             }
             const uint32_t col = 16 * qq + 8 * jj;
             tc_st8(tA + col, hv);
-            tc_st8(tA + 32 + col, lv);
+            tc_st8(tA + kTaLo + col, lv);
         }
     }
     __device__ __forceinline__ bool bad() const { return !(big < 65504.f); }
@@ -494,6 +497,8 @@ struct TcDqT<TcQ6K> {
 template <class F, bool TA>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
     constexpr int CPI = F::kImgK / kTcChunk;  // chunks per image (= per unit)
+    constexpr int KH = TA ? kTaKH : 1;         // chunks per hand-over
+    static_assert(CPI % KH == 0, "a hand-over stays inside one unit");
     constexpr int WST = tc_wstage<F>();
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ uint32_t s_tmem;
@@ -501,7 +506,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
     const int G = gridDim.x, c = blockIdx.x;
     const long long u0 = (long long)c * a.U / G, u1 = (long long)(c + 1) * a.U / G;
     if (u0 >= u1) return;  // (no TMEM, no barriers used yet)
-    const int nu = (int)(u1 - u0), nj = nu * CPI;
+    const int nu = (int)(u1 - u0), nj = nu * CPI, nh = nj / KH;
     // barriers: w_full, w_empty [SW], x_full, x_empty [NX], a_full, a_empty [NA],
     // acc_full, acc_empty [2]; 1024-byte aligned base for the swizzled operand buffers (the
     // launch adds 1 KB of slack)
@@ -512,12 +517,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
                    a_empty = a_full + 8 * kTcMaxRing, acc_full = a_empty + 8 * kTcMaxRing, acc_empty = acc_full + 16;
     uint8_t* wring = base + 1024;
     uint8_t* xring = wring + ((a.SW * WST + 1023) & ~1023);
-    const int xbytes = a.N * kTcChunk * 2;
-    uint8_t* aring = xring + ((a.NX * xbytes + 1023) & ~1023);  // (the smem operand form only)
+    const int xbytes = a.N * kTcChunk * 2, xslot = KH * xbytes;  // one chunk; one hand-over
+    uint8_t* aring = xring + ((a.NX * xslot + 1023) & ~1023);  // (the smem operand form only)
     // accumulator set s: A_hi products at columns s 2N + [0, N), A_lo products at + N; in the
-    // TA form the NA operand buffers follow (64 columns each)
+    // TA form the NA operand buffers follow (kTaBuf columns each)
     const uint32_t accC = (uint32_t)(a.nsets * 2 * a.N);
-    const uint32_t need = accC + (TA ? 64u * (uint32_t)a.NA : 0u);
+    const uint32_t need = accC + (TA ? (uint32_t)kTaBuf * (uint32_t)a.NA : 0u);
     const uint32_t ncols = need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : need <= 256 ? 256u : 512u;
 
     if (threadIdx.x == 0) {
@@ -575,19 +580,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
             for (int i = nu - a.SW < 0 ? 0 : nu - a.SW; i < nu && !timeout; ++i)
                 if (!mbar_wait(w_full + 8 * (i % a.SW), (i / a.SW) & 1)) timeout = true;
         } else if (warp == 14 && lane == 0) {
-            for (int j = 0; j < nj; ++j) {
-                const int sx = j % a.NX;
-                const int kc = (int)((u0 + j / CPI) % a.nimg) * CPI + j % CPI;  // the chunk's K index
-                if (j >= a.NX && !mbar_wait(x_empty + 8 * sx, ((j / a.NX) - 1) & 1)) {
+            for (int h = 0; h < nh; ++h) {  // the hand-over's KH chunks are adjacent in K
+                const int j = h * KH, sx = h % a.NX;
+                const int kc = (int)((u0 + j / CPI) % a.nimg) * CPI + j % CPI;  // the first chunk's K index
+                if (h >= a.NX && !mbar_wait(x_empty + 8 * sx, ((h / a.NX) - 1) & 1)) {
                     timeout = true;
                     break;
                 }
-                mbar_arrive_expect_tx(x_full + 8 * sx, (uint32_t)xbytes);
-                bulk_g2s(smem_addr(xring + sx * xbytes), a.xc + (size_t)kc * xbytes, (uint32_t)xbytes,
+                mbar_arrive_expect_tx(x_full + 8 * sx, (uint32_t)xslot);
+                bulk_g2s(smem_addr(xring + sx * xslot), a.xc + (size_t)kc * xbytes, (uint32_t)xslot,
                          x_full + 8 * sx);
             }
-            for (int j = nj - a.NX < 0 ? 0 : nj - a.NX; j < nj && !timeout; ++j)
-                if (!mbar_wait(x_full + 8 * (j % a.NX), (j / a.NX) & 1)) timeout = true;
+            for (int h = nh - a.NX < 0 ? 0 : nh - a.NX; h < nh && !timeout; ++h)
+                if (!mbar_wait(x_full + 8 * (h % a.NX), (h / a.NX) & 1)) timeout = true;
         }
     } else if (warp == 1) {
         // ---- MMA issuer
@@ -595,11 +600,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
             const uint32_t idesc = (1u << 4) | ((uint32_t)(a.N >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
             int seg = -1;
             uint32_t acc = 0;
-            for (int j = 0; j < nj && !timeout; ++j) {
+            for (int h = 0; h < nh && !timeout; ++h) {
+                const int j = h * KH;
                 const long long u = u0 + j / CPI;
                 const int sub = j % CPI, img = (int)(u % a.nimg);
                 const bool first = sub == 0 && (img == 0 || u == u0);
-                const bool last = sub == CPI - 1 && (img == a.nimg - 1 || u == u1 - 1);
+                const bool last = sub + KH - 1 == CPI - 1 && (img == a.nimg - 1 || u == u1 - 1);
                 if (first) {
                     ++seg;
                     const int s = seg % a.nsets;
@@ -610,21 +616,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
                         break;
                     }
                 }
-                const int sa = j % a.NA, sx = j % a.NX;
-                if (!mbar_wait(a_full + 8 * sa, (j / a.NA) & 1) || !mbar_wait(x_full + 8 * sx, (j / a.NX) & 1)) {
+                const int sa = h % a.NA, sx = h % a.NX;
+                if (!mbar_wait(a_full + 8 * sa, (h / a.NA) & 1) || !mbar_wait(x_full + 8 * sx, (h / a.NX) & 1)) {
                     timeout = true;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t xs = smem_addr(xring + sx * xbytes);
+                const uint32_t xs = smem_addr(xring + sx * xslot);
                 if constexpr (TA) {
-                    const uint32_t at = tmem + accC + 64u * (uint32_t)sa;  // lane 0, the buffer's columns
+                    const uint32_t at = tmem + accC + (uint32_t)kTaBuf * (uint32_t)sa;  // lane 0, the buffer
 #pragma unroll
-                    for (int ks = 0; ks < kTcChunk / 16; ++ks) {
-                        const uint32_t on = (first && ks == 0) ? 0u : 1u;
-                        tc_mma_ta(acc, at + 8 * ks, tc_desc(xs + 32 * ks), idesc, on);
-                        tc_mma_ta(acc + (uint32_t)a.N, at + 32 + 8 * ks, tc_desc(xs + 32 * ks), idesc, on);
-                    }
+                    for (int k = 0; k < KH; ++k)
+#pragma unroll
+                        for (int ks = 0; ks < kTcChunk / 16; ++ks) {
+                            const uint32_t on = (first && k == 0 && ks == 0) ? 0u : 1u;
+                            const uint64_t bd = tc_desc(xs + (uint32_t)(k * xbytes) + 32 * ks);
+                            tc_mma_ta(acc, at + 32 * k + 8 * ks, bd, idesc, on);
+                            tc_mma_ta(acc + (uint32_t)a.N, at + kTaLo + 32 * k + 8 * ks, bd, idesc, on);
+                        }
                 } else {
                     const uint32_t ahi = smem_addr(aring + sa * 2 * kTcABytes), alo = ahi + kTcABytes;
 #pragma unroll
@@ -645,24 +654,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
         TcDqT<F> dq;
         dq.init(32 * quarter + lane, (warp - 2) >> 2);
         const uint32_t tq = tmem + ((uint32_t)(32 * quarter) << 16) + accC;
-        for (int j = 0; j < nj && !timeout; ++j) {
-            const int i = j / CPI, sub = j % CPI, sw = i % a.SW, sa = j % a.NA;
+        for (int h = 0; h < nh && !timeout; ++h) {
+            const int j = h * KH, i = j / CPI, sub = j % CPI, sw = i % a.SW, sa = h % a.NA;
             if (sub == 0 && !mbar_wait(w_full + 8 * sw, (i / a.SW) & 1)) {
                 timeout = true;
                 break;
             }
-            if (j >= a.NA && !mbar_wait(a_empty + 8 * sa, ((j / a.NA) - 1) & 1)) {
+            if (h >= a.NA && !mbar_wait(a_empty + 8 * sa, ((h / a.NA) - 1) & 1)) {
                 timeout = true;
                 break;
             }
             tc_fence_after();  // the MMAs that read this buffer have completed
-            dq.chunk(reinterpret_cast<const uint32_t*>(wring + sw * WST), sub, tq + 64u * (uint32_t)sa);
+#pragma unroll
+            for (int k = 0; k < KH; ++k)
+                dq.chunk(reinterpret_cast<const uint32_t*>(wring + sw * WST), sub + k,
+                         tq + (uint32_t)kTaBuf * (uint32_t)sa + 32u * (uint32_t)k);
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(a_full + 8 * sa);
-                if (sub == CPI - 1) mbar_arrive(w_empty + 8 * sw);
+                if (sub + KH - 1 == CPI - 1) mbar_arrive(w_empty + 8 * sw);
             }
         }
         bad = dq.bad();
@@ -903,11 +915,11 @@ template <class F>
 static cudaError_t tc_launch_ta(TcArgs a, int G, int smem_limit, cudaStream_t stream) {
     constexpr int WST = tc_wstage<F>();
     const int xbytes = a.N * kTcChunk * 2;
-    a.NA = 4;
-    a.nsets = 2 * 2 * a.N + 64 * a.NA <= 512 ? 2 : 1;
+    a.NA = 2;
+    a.nsets = 2 * 2 * a.N + kTaBuf * a.NA <= 512 ? 2 : 1;
     a.NX = 4;
     auto smem_of = [&](const TcArgs& t) {
-        return 1024 + ((t.SW * WST + 1023) & ~1023) + ((t.NX * xbytes + 1023) & ~1023);
+        return 1024 + ((t.SW * WST + 1023) & ~1023) + ((t.NX * kTaKH * xbytes + 1023) & ~1023);
     };
     a.SW = kTcMaxRing;
     while (smem_of(a) > smem_limit - 2048 && a.SW > 2) --a.SW;

@@ -40,6 +40,11 @@
 //   warp 14    activation producer: the 64-K chunks (prepared in the MMA's operand layout by
 //              tc_prep_kernel), one copy each.  Not a second lane of warp 0: the two producers'
 //              suspended mbarrier waits then held each other up (one third of the run time).
+// TMEM operand form (TA, batches up to 64, the default): warps 2-9 dequantise straight into
+// TMEM with tcgen05.st, and every hand-over (dequant -> MMA -> release) covers two 64-K chunks
+// (the activation copies too).  One tcgen05.mma (M 128, N <= 64, K 16) takes ~60 cycles
+// whatever N is (measured), and each hand-over adds fences, commits and barrier round trips:
+// halving the hand-overs gained 29-36 %; doubling the dequantising warps lost 5 %.
 // Every wait is bounded (~1 s; error bit 1), and the TMEM columns are freed on every path.
 #include <cuda_fp16.h>
 

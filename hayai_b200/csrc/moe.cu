@@ -68,20 +68,24 @@ __global__ void __launch_bounds__(kRouterE * kRouterT) router_staged_kernel(cons
     const int e0 = blockIdx.x * kRouterE, t0 = blockIdx.y * kRouterT;
     const int ne = min(kRouterE, E - e0), nt = min(kRouterT, T - t0);
     const int nch = (D + kRouterChunk - 1) / kRouterChunk;
-    if (threadIdx.x == 0) {  // every row's chunk c with one bulk copy, completing on s_bar[c]
+    if (threadIdx.x == 0) {  // chunk c of every row completes on s_bar[c]
         for (int c = 0; c < nch; ++c) mbar_init(smem_addr(&s_bar[c]), 1);
         mbar_fence_init();
+        for (int c = 0; c < nch; ++c)
+            mbar_arrive_expect_tx(smem_addr(&s_bar[c]), (uint32_t)((ne + nt) * min(kRouterChunk, D - c * kRouterChunk) * 4));
+    }
+    __syncthreads();  // the barriers are initialised and expect their bytes
+    // one thread per row issues that row's chunk copies, in K order (the issue of ~200 small
+    // copies from a single thread would take longer than the chains)
+    if ((int)threadIdx.x < ne + nt) {
+        const int r = threadIdx.x;
+        float* dst = r < ne ? ws + r * ld : xs + (r - ne) * ld;
+        const float* src = r < ne ? W + (size_t)(e0 + r) * D : x + (size_t)(t0 + r - ne) * D;
         for (int c = 0; c < nch; ++c) {
             const int k0 = c * kRouterChunk, len = min(kRouterChunk, D - k0);
-            const uint32_t bar = smem_addr(&s_bar[c]);
-            mbar_arrive_expect_tx(bar, (uint32_t)((ne + nt) * len * 4));
-            for (int r = 0; r < ne; ++r)
-                bulk_g2s(smem_addr(ws + r * ld + k0), W + (size_t)(e0 + r) * D + k0, (uint32_t)(len * 4), bar);
-            for (int r = 0; r < nt; ++r)
-                bulk_g2s(smem_addr(xs + r * ld + k0), x + (size_t)(t0 + r) * D + k0, (uint32_t)(len * 4), bar);
+            bulk_g2s(smem_addr(dst + k0), src + k0, (uint32_t)(len * 4), smem_addr(&s_bar[c]));
         }
     }
-    __syncthreads();  // the barriers are initialised
     const int e = threadIdx.x % kRouterE, t = threadIdx.x / kRouterE;
     const bool live = e < ne && t < nt;
     const float4* w4 = reinterpret_cast<const float4*>(ws + e * ld);

@@ -872,7 +872,10 @@ static int stack_try_kernel(hc_engine* e, const StackArgs& s, float* x, size_t n
         L.tp_size = e->peer.world;
         L.tp_regions = e->peer.d_peer;
         L.tp_base = e->peer.tp_phases;
+        L.tp_flow_base = e->peer.flow_phases;
     }
+    int flow_used = 0;
+    L.flow_used = &flow_used;
     size_t bytes = 0;
     cudaError_t ce = launch_ffn_stack(ta, td, L, e->num_sms, e->smem_optin, e->stream, true, &bytes);
     if (ce == cudaErrorInvalidConfiguration) {
@@ -886,6 +889,7 @@ static int stack_try_kernel(hc_engine* e, const StackArgs& s, float* x, size_t n
     L.scratch = e->stack_bar.p;
     ce = launch_ffn_stack(ta, td, L, e->num_sms, e->smem_optin, e->stream, false, nullptr);
     if (ce != cudaSuccess) return hc_cuda_error(ce, "stack kernel launch");
+    if (tp && flow_used) e->peer.flow_phases += (uint32_t)s.L;  // its per-tile counters advanced
     *done = true;
     return HC_OK;
 }

@@ -34,6 +34,7 @@ struct PeerState {
     void** d_peer = nullptr;     // device copy of peer[]
     bool connected = false;
     uint32_t tp_phases = 0;      // cross-GPU phases of the TP stack run so far (equal on every rank)
+    uint32_t flow_phases = 0;    // of those, the phases run by the dataflow stack kernel
 };
 
 // One GPU + stream: the counterpart of OpenClEngine (crates/hayai-opencl/src/context.rs:23).

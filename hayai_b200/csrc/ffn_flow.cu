@@ -25,6 +25,16 @@
 // Every sum has a fixed order (chunk boundaries, warp order, part order), so the result is
 // deterministic and independent of which CTA ran what.
 //
+// Tensor parallelism (up to 8 GPUs, each holding a d_ff shard of every layer): the chunk of a
+// tile's last local K-part sums the local parts and stores the tile's 16 partial outputs into
+// slot [rank] of every rank's exchange region over NVLink (plain stores, one system fence, one
+// system-scope counter add per rank and tile).  An extra warp per CTA, the x-tile completer,
+// owns tiles c, c + C, ... : it waits (acquire, system scope, bounded) until the tile's counter
+// shows every rank's partial, adds them in rank order to the replicated residual (the same sum
+// on every rank) and finishes the tile as above.  The finishers never wait on another GPU, so
+// no hand-over slot can be held while a peer waits for it.  Slots alternate with the phase
+// parity; the counters only grow (their targets carry the phases of earlier launches).
+//
 // Counters (global, per layer, zeroed by the host before the launch): chunk counters of the
 // two phases, h-part readiness, per-tile down arrivals, finished x tiles, and the CTAs that
 // copied a layer's x table (a guard: the double-buffered table is only rewritten after every
@@ -42,6 +52,7 @@ constexpr int kPartBlocks = 16;  // down K-parts: at most 16 super-blocks (4096 
 constexpr int kMaxS = 6;
 constexpr int kFW = 3;                            // finisher warps
 constexpr int kThreads = (kCW + 1 + kFW) * 32;    // consumers, producer, finishers
+constexpr int kThreadsTP = kThreads + 32;          // + the x-tile completer of tensor parallelism
 constexpr int kNT = 8;                            // hand-over slots (chunk partials) to the finishers
 
 struct Layer {  // same layout as the host's per-layer pointer table
@@ -71,6 +82,13 @@ struct Args {
     float eps;
     int* err;
     int S, slot_bytes, dsb;  // ring slots, bytes per slot, down blocks per stage
+    // tensor parallelism (tp_size > 1): this rank holds a d_ff shard of every layer; each
+    // tile's partial of the down output goes to every rank's region, x is completed per tile
+    // once all ranks' partials are in (identically on every rank: rank order)
+    char* const* regions;  // every rank's exchange region as mapped here
+    int tp_rank, tp_size;
+    unsigned tp_base;      // cross-GPU phases before this launch (slot parity)
+    unsigned flow_base;    // this kernel's phases before this launch (per-tile counter targets)
 };
 
 struct Desc {
@@ -153,6 +171,30 @@ __device__ __forceinline__ void red_rel(unsigned* p, unsigned v) {
 
 __device__ __forceinline__ bool err_raised(const int* err) {
     return (*reinterpret_cast<const volatile int*>(err) & 2) != 0;
+}
+
+__device__ __forceinline__ unsigned ld_acq_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_sys(unsigned* p, unsigned v) {
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded acquire-wait (system scope: counters other GPUs raise) until *p >= target.
+__device__ bool wait_ge_sys(const unsigned* p, unsigned target, int* err) {
+    const unsigned long long t0 = now_ns();
+    for (int i = 0;; ++i) {
+        if ((int)(ld_acq_sys(p) - target) >= 0) return true;
+        if ((i & 63) == 63) {
+            if (err_raised(err) || now_ns() - t0 > 1000000000ull) {
+                atomicOr(err, 2);
+                return false;
+            }
+        }
+    }
 }
 
 // Bounded acquire-wait until *p >= target: about a second, or until another CTA raised the
@@ -335,7 +377,7 @@ __device__ __forceinline__ float sum16(float v) {
 //                  finished-tile counter.
 // Global memory latency (stores, release fences, acquire waits) lands here, not on the warps
 // that consume the weight stream.
-template <class FA, class FD>
+template <class FA, class FD, bool TP>
 __device__ void finisher(const Args& a, const Geo<FA, FD>& G, int* next, uint32_t tfull0, uint32_t tfree0,
                          const float* red, const Meta* meta, const float* s_inv, int lane) {
     bool bad = false;
@@ -384,6 +426,29 @@ __device__ void finisher(const Args& a, const Geo<FA, FD>& G, int* next, uint32_
         }
         const int l = m.layer;
         const bool last_layer = l == a.L - 1;
+        if constexpr (TP) {
+            // this rank's partial of the tile (its parts in part order) into slot [rank] of every
+            // rank's region, then one counter add per rank; the completer warps finish x
+            int okp = 1;
+            if (lane == 0) okp = wait_ge(tc, (unsigned)(G.np - 1), a.err) ? 1 : 0;
+            okp = __shfl_sync(kFull, okp, 0);
+            __syncwarp();
+            if (!okp) break;
+            float loc = 0.f;
+            for (int q = 0; q < G.np - 1; ++q) loc += __ldcg(a.parts + ((size_t)tile * G.np + q) * 16 + row);
+            loc += f0;
+            const size_t slot =
+                (((size_t)((a.tp_base + l) & 1) * G.td + tile) * a.tp_size + a.tp_rank) * 16 + row;
+            if (lane < 16)
+                for (int q = 0; q < a.tp_size; ++q) reinterpret_cast<float*>(a.regions[q] + kPeerTpParts)[slot] = loc;
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_system();  // the lanes' stores (ordered by the warp barrier) first
+                for (int q = 0; q < a.tp_size; ++q)
+                    red_sys(reinterpret_cast<unsigned*>(a.regions[q] + kPeerFlowTile) + tile, 1u);
+            }
+            continue;
+        }
         // the tile's earlier parts have arrived (acquire), and every CTA copied the table about to
         // be overwritten (layer l - 1's, same buffer)
         int ok = 1;
@@ -417,8 +482,59 @@ __device__ void finisher(const Args& a, const Geo<FA, FD>& G, int* next, uint32_
     if (bad) atomicOr(a.err, 1);
 }
 
+// Tensor parallelism: the x-tile completer warp of CTA c finishes tiles c, c + C, ... of every
+// layer once every rank's partial of the tile is in this rank's region (system-scope counter),
+// adding them in rank order to the residual (the same sum on every rank), then stores x, the
+// next layer's gate/up table entries and the tile's sums, and raises the layer's finished-tile
+// counter.  It consumes no hand-over slot, so a finisher never waits on another GPU.
 template <class FA, class FD>
-__global__ void __launch_bounds__(kThreads, 1) ffn_flow_kernel(Args a) {
+__device__ void completer(const Args& a, const Geo<FA, FD>& G, int lane) {
+    bool bad = false;
+    const int row = lane & 15;
+    const unsigned* ctr = reinterpret_cast<const unsigned*>(a.regions[a.tp_rank] + kPeerFlowTile);
+    for (int l = 0; l < a.L; ++l) {
+        unsigned* cnt = a.cnt + (size_t)l * a.cstride;
+        const bool last_layer = l == a.L - 1;
+        const unsigned target = (a.flow_base + (unsigned)l + 1u) * (unsigned)a.tp_size;
+        const float* slots = reinterpret_cast<const float*>(a.regions[a.tp_rank] + kPeerTpParts) +
+                             (size_t)((a.tp_base + l) & 1) * G.td * a.tp_size * 16;
+        for (int tile = blockIdx.x; tile < G.td; tile += gridDim.x) {
+            int ok = 1;
+            if (lane == 0) {
+                ok = wait_ge_sys(ctr + tile, target, a.err) ? 1 : 0;
+                if (ok && l >= 2 && !last_layer)
+                    ok = wait_ge(a.cnt + (size_t)(l - 1) * a.cstride + kCopied, gridDim.x, a.err) ? 1 : 0;
+            }
+            ok = __shfl_sync(kFull, ok, 0);
+            __syncwarp();  // lane 0's acquire orders the other lanes' loads below
+            if (!ok) {
+                if (bad) atomicOr(a.err, 1);
+                return;
+            }
+            const float* xprev = l == 0 ? a.x : a.xbuf + (size_t)(l & 1) * a.dm;
+            float xn = __ldcg(xprev + tile * 16 + row);
+            for (int q = 0; q < a.tp_size; ++q) xn += __ldcg(slots + ((size_t)tile * a.tp_size + q) * 16 + row);
+            if (lane < 16) a.xbuf[(size_t)((l + 1) & 1) * a.dm + tile * 16 + row] = xn;
+            if (!last_layer) {
+                const float* wnext = a.layers[l + 1].norm;
+                const float xw = wnext ? xn * __ldg(wnext + tile * 16 + row) : xn;
+                pack_rows<FA>(a.xtab + (size_t)((l + 1) & 1) * (G.tab_a / 8), tile, lane, xw, bad);
+                const float s1 = sum16(xw), s2 = sum16(xn * xn);
+                float* snext = a.xs + (size_t)((l + 1) & 1) * 2 * G.td;
+                if (lane == 0) {
+                    snext[tile] = s1;
+                    snext[G.td + tile] = s2;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) red_rel(cnt + kXcnt, 1u);
+        }
+    }
+    if (bad) atomicOr(a.err, 1);
+}
+
+template <class FA, class FD, bool TP>
+__global__ void __launch_bounds__(TP ? kThreadsTP : kThreads, 1) ffn_flow_kernel(Args a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_red[32];
     __shared__ float s_inv;
@@ -482,8 +598,12 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_flow_kernel(Args a) {
         if (!ok && lane == 0) atomicOr(a.err, 2);
         return;
     }
+    if (TP && warp == kCW + 1 + kFW) {  // ----------------------------- x-tile completer
+        completer<FA, FD>(a, G, lane);
+        return;
+    }
     if (warp > kCW) {  // ------------------------------------------------ finishers
-        finisher<FA, FD>(a, G, &s_fnext, tfull0, tfree0, red, meta, &s_inv, lane);
+        finisher<FA, FD, TP>(a, G, &s_fnext, tfull0, tfree0, red, meta, &s_inv, lane);
         return;
     }
 
@@ -696,9 +816,15 @@ template <class FA, class FD>
 cudaError_t launch_flow_t(const StackLaunch& s, int num_sms, int smem_limit, cudaStream_t stream, bool dry,
                           size_t* scratch_bytes) {
     using namespace flow;
-    if (s.tp_size > 1) return cudaErrorInvalidConfiguration;
+    const bool tp = s.tp_size > 1;
     if (s.dm % FA::kBlockElems || s.ff % (FD::kBlockElems) || s.dm % 256 || s.ff % 256)
         return cudaErrorInvalidConfiguration;
+    if (tp) {  // the exchange: per-tile counters and the double-buffered tile partials
+        const Geo<FA, FD> g(s.dm, s.ff);
+        if (s.tp_size > 8 || (size_t)g.td * 4 > kPeerTpParts - kPeerFlowTile ||
+            (size_t)2 * g.td * s.tp_size * 16 * 4 > kPeerTpPartsBytes)
+            return cudaErrorInvalidConfiguration;
+    }
     (void)num_sms;  // any shape: CTAs without chunks of a phase pass its end marker
     // ring: slots of the larger stage; down stages of dsb blocks (16, else 12 or 8 to keep 3 slots)
     const int sa = 2 * stage_blocks(true) * FA::kTile;
@@ -712,11 +838,12 @@ cudaError_t launch_flow_t(const StackLaunch& s, int num_sms, int smem_limit, cud
     }
     if (S < 3) return cudaErrorInvalidConfiguration;
     const Smem L = smem_layout<FA, FD>(s.dm, s.ff, S, slot);
-    auto kern = ffn_flow_kernel<FA, FD>;
+    auto kern = tp ? ffn_flow_kernel<FA, FD, true> : ffn_flow_kernel<FA, FD, false>;
+    const int threads = tp ? kThreadsTP : kThreads;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, L.total);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, L.total);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     const FlowScratch sc = flow_scratch<FA, FD>(s.L, s.dm, s.ff);
@@ -745,16 +872,24 @@ cudaError_t launch_flow_t(const StackLaunch& s, int num_sms, int smem_limit, cud
     a.S = S;
     a.slot_bytes = slot;
     a.dsb = dsb;
+    a.regions = reinterpret_cast<char* const*>(s.tp_regions);
+    a.tp_rank = tp ? s.tp_rank : 0;
+    a.tp_size = tp ? s.tp_size : 1;
+    a.tp_base = s.tp_base;
+    a.flow_base = s.tp_flow_base;
     e = cudaMemsetAsync(a.cnt, 0, (size_t)s.L * sc.cstride * 4, stream);
     if (e != cudaSuccess) return e;
     void* args[] = {&a};
-    return cudaLaunchCooperativeKernel((const void*)kern, dim3(num_sms), dim3(kThreads), args, L.total, stream);
+    e = cudaLaunchCooperativeKernel((const void*)kern, dim3(num_sms), dim3(threads), args, L.total, stream);
+    if (e == cudaSuccess && s.flow_used) *s.flow_used = 1;
+    return e;
 }
 
 }  // namespace
 
-// The dataflow stack kernel covers single-GPU stacks with a Q6_K down projection and Q4_K or
-// Q6_K gate/up (d_model and d_ff whole super-blocks); cudaErrorInvalidConfiguration otherwise.
+// The dataflow stack kernel covers stacks with a Q6_K down projection and Q4_K or Q6_K gate/up
+// (d_model and d_ff whole super-blocks), on one GPU or tensor-parallel over up to 8;
+// cudaErrorInvalidConfiguration otherwise.
 cudaError_t launch_ffn_flow(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
                             cudaStream_t stream, bool dry, size_t* scratch_bytes) {
     if (type_d != T_Q6_K) return cudaErrorInvalidConfiguration;

@@ -667,7 +667,7 @@ static bool flow_enabled() {
 // The CTA count the kernel runs with: one per SM.
 cudaError_t launch_ffn_stack(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
                              cudaStream_t stream, bool dry, size_t* scratch_bytes) {
-    if (s.tp_size <= 1 && flow_enabled()) {
+    if (flow_enabled()) {
         const cudaError_t e = launch_ffn_flow(type_a, type_d, s, num_sms, smem_limit, stream, dry, scratch_bytes);
         if (e != cudaErrorInvalidConfiguration) return e;
         cudaGetLastError();

@@ -23,6 +23,8 @@ int gemv_sk_slots(int type, int M, int K, int num_sms);
 constexpr size_t kPeerTpBar = 0;                  // u32: cross-GPU counter of the TP stack
 constexpr size_t kPeerEpBar = 128;                // u32: cross-GPU counter of the EP MoE
 constexpr size_t kPeerEpEpoch = 256;              // u32: EP MoE phases this rank has signalled (local)
+constexpr size_t kPeerFlowTile = 1024;            // u32 per 16-row tile of x (<= 768 tiles): the dataflow TP
+                                                  // stack's per-tile exchange counters
 constexpr size_t kPeerTpParts = 4096;             // TP stack: down partials [2][d_model/16][parts][16] f32
 constexpr size_t kPeerTpPartsBytes = 4u << 20;    // d_model x parts (<= 8) x 2 buffers x 4 B up to 65536 x 8
 constexpr size_t kPeerEpData = kPeerTpParts + kPeerTpPartsBytes;  // EP MoE exchange data [2][T*k][d_model] f32
@@ -53,12 +55,14 @@ struct StackLaunch {
     int tp_rank, tp_size;
     void* const* tp_regions;  // device array [tp_size] of the ranks' regions as mapped here
     unsigned tp_base;         // cross-GPU phases completed before this launch
+    unsigned tp_flow_base;    // of those, the phases the dataflow kernel ran (its per-tile counters)
+    int* flow_used;           // set to 1 when the dataflow kernel took the launch (may be null)
 };
 // cudaErrorInvalidConfiguration: the shapes or formats are not covered (use the per-layer
 // kernels).  dry = only check that the launch is possible and report the scratch bytes.
-// Single-GPU stacks the dataflow kernel covers (ffn_flow.cu) run on it, the others on the
-// phase-barrier kernel (ffn_stack.cu); HAYAI_FLOW_KERNEL=0 in the environment keeps every
-// stack on the latter.
+// Stacks the dataflow kernel covers (ffn_flow.cu; one GPU or tensor-parallel) run on it, the
+// others on the phase-barrier kernel (ffn_stack.cu); HAYAI_FLOW_KERNEL=0 in the environment
+// keeps every stack on the latter.
 cudaError_t launch_ffn_stack(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,
                              cudaStream_t stream, bool dry, size_t* scratch_bytes);
 cudaError_t launch_ffn_flow(int type_a, int type_d, const StackLaunch& s, int num_sms, int smem_limit,

@@ -49,69 +49,49 @@ __global__ void __launch_bounds__(128) router_exact_kernel(const float* __restri
 }
 
 // The same scores with the inputs staged in shared memory: a block takes 8 experts x 16
-// tokens (thread = token * 8 + expert).  The rows arrive in K-chunks of 256 floats, each chunk
-// on its own mbarrier, all issued at the start, so a thread's chain (2048 dependent adds for
-// d_model 2048: the floor of this kernel) starts as soon as the first chunk has landed and the
-// rest of the copy overlaps it.  Rows are padded by 4 floats so the 8 experts' float4 reads
-// fall on distinct banks.  Summation order and rounding are those of router_exact_kernel.
-constexpr int kRouterE = 8, kRouterT = 16, kRouterChunk = 256, kRouterMaxChunks = 32;
+// tokens (thread = token * 8 + expert), copies their rows in coalesced, then every thread runs
+// its chain from shared memory (rows padded by 4 floats so the 8 experts' float4 reads fall on
+// distinct banks).  Summation order and rounding are those of router_exact_kernel.
+constexpr int kRouterE = 8, kRouterT = 16;
 
 __global__ void __launch_bounds__(kRouterE * kRouterT) router_staged_kernel(const float* __restrict__ W,
                                                                             const float* __restrict__ x, int E, int D,
                                                                             int T, float* __restrict__ scores,
                                                                             int* err) {
     extern __shared__ __align__(128) float rs[];
-    __shared__ __align__(8) uint64_t s_bar[kRouterMaxChunks];
+    __shared__ __align__(8) uint64_t s_bar;
+    __shared__ int s_ok;
     const int ld = D + 4;
     float* ws = rs;                  // [kRouterE][ld]
     float* xs = rs + kRouterE * ld;  // [kRouterT][ld]
     const int e0 = blockIdx.x * kRouterE, t0 = blockIdx.y * kRouterT;
-    const int ne = min(kRouterE, E - e0), nt = min(kRouterT, T - t0);
-    const int nch = (D + kRouterChunk - 1) / kRouterChunk;
-    if (threadIdx.x == 0) {  // chunk c of every row completes on s_bar[c]
-        for (int c = 0; c < nch; ++c) mbar_init(smem_addr(&s_bar[c]), 1);
+    const int ne = min(kRouterE, E - e0), nt = min(kRouterT, T - t0), d4 = D >> 2;
+    const uint32_t bar = smem_addr(&s_bar);
+    if (threadIdx.x == 0) {  // every row with one bulk copy (rows are 16-byte multiples, 16-byte aligned)
+        mbar_init(bar, 1);
         mbar_fence_init();
-        for (int c = 0; c < nch; ++c)
-            mbar_arrive_expect_tx(smem_addr(&s_bar[c]), (uint32_t)((ne + nt) * min(kRouterChunk, D - c * kRouterChunk) * 4));
+        mbar_arrive_expect_tx(bar, (uint32_t)((ne + nt) * D * 4));
+        for (int r = 0; r < ne; ++r) bulk_g2s(smem_addr(ws + r * ld), W + (size_t)(e0 + r) * D, (uint32_t)(D * 4), bar);
+        for (int r = 0; r < nt; ++r) bulk_g2s(smem_addr(xs + r * ld), x + (size_t)(t0 + r) * D, (uint32_t)(D * 4), bar);
+        s_ok = mbar_wait(bar, 0) ? 1 : 0;
+        if (!s_ok) atomicOr(err, 2);
     }
-    __syncthreads();  // the barriers are initialised and expect their bytes
-    // one thread per row issues that row's chunk copies, in K order (the issue of ~200 small
-    // copies from a single thread would take longer than the chains)
-    if ((int)threadIdx.x < ne + nt) {
-        const int r = threadIdx.x;
-        float* dst = r < ne ? ws + r * ld : xs + (r - ne) * ld;
-        const float* src = r < ne ? W + (size_t)(e0 + r) * D : x + (size_t)(t0 + r - ne) * D;
-        for (int c = 0; c < nch; ++c) {
-            const int k0 = c * kRouterChunk, len = min(kRouterChunk, D - k0);
-            bulk_g2s(smem_addr(dst + k0), src + k0, (uint32_t)(len * 4), smem_addr(&s_bar[c]));
-        }
-    }
+    __syncthreads();
+    if (!s_ok) return;
     const int e = threadIdx.x % kRouterE, t = threadIdx.x / kRouterE;
-    const bool live = e < ne && t < nt;
+    if (e >= ne || t >= nt) return;
     const float4* w4 = reinterpret_cast<const float4*>(ws + e * ld);
     const float4* x4 = reinterpret_cast<const float4*>(xs + t * ld);
     float s = 0.0f;
-    bool ok = true;
-    for (int c = 0; c < nch && ok; ++c) {
-        ok = mbar_wait(smem_addr(&s_bar[c]), 0);
-        if (!ok || !live) continue;
-        const int c1 = min(D, (c + 1) * kRouterChunk) >> 2;
 #pragma unroll 4
-        for (int q = (c * kRouterChunk) >> 2; q < c1; ++q) {
-            const float4 a = w4[q], b = x4[q];
-            s = __fadd_rn(s, __fmul_rn(a.x, b.x));
-            s = __fadd_rn(s, __fmul_rn(a.y, b.y));
-            s = __fadd_rn(s, __fmul_rn(a.z, b.z));
-            s = __fadd_rn(s, __fmul_rn(a.w, b.w));
-        }
+    for (int c = 0; c < d4; ++c) {
+        const float4 a = w4[c], b = x4[c];
+        s = __fadd_rn(s, __fmul_rn(a.x, b.x));
+        s = __fadd_rn(s, __fmul_rn(a.y, b.y));
+        s = __fadd_rn(s, __fmul_rn(a.z, b.z));
+        s = __fadd_rn(s, __fmul_rn(a.w, b.w));
     }
-    if (!ok) {
-        if (err) atomicOr(err, 2);
-        // the copies still in flight must land before the CTA's shared memory is released
-        for (int c = 0; c < nch; ++c) mbar_wait(smem_addr(&s_bar[c]), 0);
-        return;
-    }
-    if (live) scores[(size_t)(t0 + t) * E + e0 + e] = s;
+    scores[(size_t)(t0 + t) * E + e0 + e] = s;
 }
 
 // Router scores on the stream: the staged kernel when the rows fit shared memory.
@@ -119,7 +99,7 @@ static cudaError_t launch_router(const float* W, const float* x, int E, int D, i
                                  cudaStream_t stream, int* err) {
     const int smem = (kRouterE + kRouterT) * (D + 4) * 4 + 128;
     const bool aligned = ((((uintptr_t)W) | ((uintptr_t)x)) & 15) == 0 && (D & 3) == 0;
-    if (aligned && smem <= smem_limit && (D + kRouterChunk - 1) / kRouterChunk <= kRouterMaxChunks) {
+    if (aligned && smem <= smem_limit) {
         static int configured[64];
         int dev = 0;
         cudaGetDevice(&dev);

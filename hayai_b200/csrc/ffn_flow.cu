@@ -116,8 +116,11 @@ struct Geo {
         nbk_d = ff / FD::kBlockElems;
         ta = ff / 16;
         td = dm / 16;
-        np = (nbk_d + kPartBlocks - 1) / kPartBlocks;
-        pb = kPartBlocks;  // (parts of equal size measured slower: their stages are smaller)
+        // 16-block parts (parts of equal size measured slower: their stages are smaller); a short
+        // d_ff (a tensor-parallel shard) gets parts of a quarter of it, at least 4 blocks, so the
+        // down GEMV can still start before the last gate/up tiles are done
+        pb = nbk_d >= 3 * kPartBlocks ? kPartBlocks : ((nbk_d + 3) / 4 > 4 ? (nbk_d + 3) / 4 : 4);
+        np = (nbk_d + pb - 1) / pb;
         tab_a = nbk_a * table_entries_per_block<FA>(1) * 8;
         tab_p = pb * table_entries_per_block<FD>(1) * 8;
     }

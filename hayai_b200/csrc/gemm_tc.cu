@@ -526,7 +526,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
     uint8_t* aring = xring + ((a.NX * xslot + 1023) & ~1023);  // (the smem operand form only)
     // accumulator set s: A_hi products at columns s 2N + [0, N), A_lo products at + N; in the
     // TA form the NA operand buffers follow (kTaBuf columns each)
-    const uint32_t accC = (uint32_t)(a.nsets * 2 * a.N);
+    // columns per accumulator set: the TA form adds the A_hi and the A_lo products into one
+    // accumulator (N columns), the shared-memory form keeps them apart (2N)
+    const int accW = TA ? a.N : 2 * a.N;
+    const uint32_t accC = (uint32_t)(a.nsets * accW);
     const uint32_t need = accC + (TA ? (uint32_t)kTaBuf * (uint32_t)a.NA : 0u);
     const uint32_t ncols = need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : need <= 256 ? 256u : 512u;
 
@@ -614,7 +617,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
                 if (first) {
                     ++seg;
                     const int s = seg % a.nsets;
-                    acc = tmem + (uint32_t)(s * 2 * a.N);
+                    acc = tmem + (uint32_t)(s * accW);
                     // the set's previous segment must have been read out
                     if (seg >= a.nsets && !mbar_wait(acc_empty + 8 * s, ((seg / a.nsets) - 1) & 1)) {
                         timeout = true;
@@ -637,7 +640,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
                             const uint32_t on = (first && k == 0 && ks == 0) ? 0u : 1u;
                             const uint64_t bd = tc_desc(xs + (uint32_t)(k * xbytes) + 32 * ks);
                             tc_mma_ta(acc, at + 32 * k + 8 * ks, bd, idesc, on);
-                            tc_mma_ta(acc + (uint32_t)a.N, at + kTaLo + 32 * k + 8 * ks, bd, idesc, on);
+                            tc_mma_ta(acc, at + kTaLo + 32 * k + 8 * ks, bd, idesc, 1u);
                         }
                 } else {
                     const uint32_t ahi = smem_addr(aring + sa * 2 * kTcABytes), alo = ahi + kTcABytes;
@@ -724,19 +727,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
             tc_fence_after();
             const int slot = c - tc_owner((long long)run * a.nimg, a.U, G);
             float* out = a.out + ((size_t)run * a.slots + slot) * (size_t)a.B * kTcRows;
-            const uint32_t tb = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(s * 2 * a.N);
+            const uint32_t tb = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(s * accW);
             for (int cb = 0; cb < Bp; cb += 8) {
                 float vh[8], vl[8], wh[8], wl[8];
                 tc_ld8(tb + cb, vh);
                 tc_ld8(tb + Bp + cb, vl);
-                tc_ld8(tb + a.N + cb, wh);  // the A_lo products
-                tc_ld8(tb + a.N + Bp + cb, wl);
+                if constexpr (!TA) {
+                    tc_ld8(tb + a.N + cb, wh);  // the A_lo products
+                    tc_ld8(tb + a.N + Bp + cb, wl);
+                }
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     const int t = cb + e;
                     if (t < a.B)
                         out[(size_t)t * kTcRows + row] =
-                            ((vh[e] + wh[e]) + (vl[e] + wl[e]) * (1.0f / 2048.0f)) * (1.0f / kTcWScale);
+                            TA ? (vh[e] + vl[e] * (1.0f / 2048.0f)) * (1.0f / kTcWScale)
+                               : ((vh[e] + wh[e]) + (vl[e] + wl[e]) * (1.0f / 2048.0f)) * (1.0f / kTcWScale);
                 }
             }
             tc_fence_before();
@@ -920,8 +926,15 @@ template <class F>
 static cudaError_t tc_launch_ta(TcArgs a, int G, int smem_limit, cudaStream_t stream) {
     constexpr int WST = tc_wstage<F>();
     const int xbytes = a.N * kTcChunk * 2;
-    a.NA = 2;
-    a.nsets = 2 * 2 * a.N + kTaBuf * a.NA <= 512 ? 2 : 1;
+    // three operand buffers where TMEM holds them beside two accumulator sets (N columns each),
+    // else beside one, else two buffers
+    a.NA = 3;
+    a.nsets = 2;
+    if (2 * a.N + kTaBuf * 3 > 512) a.nsets = 1;
+    if (a.nsets * a.N + kTaBuf * 3 > 512) {
+        a.NA = 2;
+        a.nsets = 2 * a.N + kTaBuf * 2 <= 512 ? 2 : 1;
+    }
     a.NX = 4;
     auto smem_of = [&](const TcArgs& t) {
         return 1024 + ((t.SW * WST + 1023) & ~1023) + ((t.NX * kTaKH * xbytes + 1023) & ~1023);

@@ -1217,7 +1217,13 @@ def run_sharded(args):
                      ("ep_qwen3moe", dict(config="qwen3moe", tp=False, ep=True, batch=1, steps=20))):
         a = argparse.Namespace(**{**base, **kw, "warmup": 3, "layers": 0, "no_cpu_baseline": True,
                                   "no_parity": False, "no_per_layer": True, "tp_impl": "ours"})
-        line = (run_moe if "n_expert" in CONFIGS[a.config] else run_ours)(a)
+        try:
+            line = (run_moe if "n_expert" in CONFIGS[a.config] else run_ours)(a)
+        except Exception as exc:  # the headline line is still printed; the failure is reported
+            if rank == 0:
+                out[name] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+            print(f"sharded {name} failed on rank {rank}: {exc}", file=sys.stderr)
+            break  # a failed collective may leave the ranks out of step: no further sharded runs
         barrier(world)
         if rank == 0 and line:
             out[name] = {"value": line["value"], "unit": "GB/s", "ms_per_step": line["ms_per_step"],

@@ -455,6 +455,7 @@ def run_moe(args):
         if l == 0:
             y0 = y.clone()
         xr.add_(y)
+    barrier(world)  # expert parallelism: the ranks' combine kernels wait for each other (bounded)
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(dev)
@@ -713,6 +714,7 @@ def run_ours(args):
         x.copy_(x0)
         run_stack(x)
 
+    barrier(world)  # under tensor parallelism the ranks' kernels wait for each other (bounded)
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(dev)
@@ -755,6 +757,9 @@ def run_ours(args):
         t_or = 0.0
         for l in range(Lp):
             xl = xin[0].cpu().numpy().copy()
+            # the ranks' kernels wait (bounded, ~1 s) for each other inside the exchange: start
+            # them together, not while rank 0 is still busy with the oracle of the last layer
+            barrier(world)
             run_sub(xin, l, l + 1)
             if rank == 0:
                 w = full_layer(l)

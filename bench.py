@@ -1047,6 +1047,18 @@ def run_gemv(args):
     torch.cuda.synchronize(dev)
     t_e2e = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
     assert np.isfinite(yh).all()
+    parity = None
+    if rank == 0 and not args.no_parity:
+        # the first 2048 rows of the timed matrix (copy 0) against the C oracle on the same bytes
+        import oracle
+
+        prow = min(M, 2048)
+        eng.gemv_dev(W[0], x, y)
+        got = y[:prow].double().cpu().numpy()
+        ref = np.asarray(oracle.gemv(t, prow, K, raw[:prow * mbytes // M], xh.astype(np.float32)), np.float64)
+        rel = float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
+        mx = float(np.abs(got - ref).max())
+        parity = {"rel_l2": rel, "max_abs": mx, "rows": prow, "of_rows": M, "pass": rel <= 1e-4 and mx <= 1e-3}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
@@ -1080,6 +1092,8 @@ def run_gemv(args):
                 "clocks": clocks, "gpu_launches": args.steps}
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if parity is not None:
+            line["parity"] = parity
         print(json.dumps(line))
     for w in W:
         w.free()

@@ -19,9 +19,17 @@
 // in its own two columns, so every accumulator is one group's (or half-group's) dot product on
 // its own lane; the group scale is applied once per accumulator in f32.  Grid bytes enter the
 // A fragment as f16(1024 + g) by one PRMT, minus 1024 (exact), and the element signs are
-// XORed into the f16 sign bits: the sign bits of elements (0, 2) land on bits 15 / 31 by one
-// multiply of (s & 5) by 0x20008000, those of (1, 3) by (s & 10) * 0x10004000.  The codebooks
-// are read through the read-only cache (at most 8 KB each).
+// XORed into the f16 sign bits.
+//
+// Shared-memory LUTs.  Each CTA expands its format's codebook once, at kernel start, into a
+// shared-memory table of ready A-fragment registers: per grid point the f16 pairs (e0, e2),
+// (e1, e3) (and (e4, e6), (e5, e7) for the 8-element IQ2 points) of its exact small-integer
+// values, 16 B per IQ2 point, 8 B per IQ3 point (IQ2_XXS 4 KB, IQ2_XS 8 KB, IQ2_S 16 KB,
+// IQ3_XXS 2 KB, IQ3_S 4 KB).  A point then costs one shared-memory load instead of a gather
+// through L1 plus the byte-to-f16 conversion.  The 8 sign bits s of a point (bit j: element j)
+// become the f16 sign masks of its four registers by one multiply each: s * 0x20008000 puts
+// s0 on bit 15 and s2 on bit 31 (the two shifted copies of s do not overlap, so no carries),
+// s * 0x10004000 puts s1 / s3 there, s * 0x02000800 s4 / s6 and s * 0x01000400 s5 / s7.
 #pragma once
 
 #include "gemv_mma_impl.cuh"
@@ -94,44 +102,111 @@ __device__ __forceinline__ uint32_t byte_of(const uint4& p, int i) {
     return (w >> (8 * (i & 3))) & 0xFFu;
 }
 
-// Grid point l of group k (8 elements for IQ2; for IQ3 the two 4-element points 2l, 2l+1) as
-// 8 grid bytes (lo: elements 0-3, hi: 4-7) and the 8 sign bits (bit j: element j negative).
+#ifndef HC_IQ_SIGN_LUT
+#define HC_IQ_SIGN_LUT 0
+#endif
+
+// Bytes of format TYPE's grid table in the shared-memory LUT (0 for the other formats).
+__host__ __device__ constexpr int iq_grid_bytes(int type) {
+    return type == T_IQ2_XXS ? 256 * 16
+           : type == T_IQ2_XS ? 512 * 16
+           : type == T_IQ2_S  ? 1024 * 16
+           : type == T_IQ3_XXS ? 256 * 8
+           : type == T_IQ3_S   ? 512 * 8
+                               : 0;
+}
+
+// Sign-mask table entries: the 7-bit sign index of IQ2_XXS / IQ2_XS / IQ3_XXS, the sign byte
+// of IQ2_S / IQ3_S.
+__host__ __device__ constexpr int iq_sign_entries(int type) {
+    return type == T_IQ2_S || type == T_IQ3_S ? 256 : 128;
+}
+
+__host__ __device__ constexpr int iq_lut_bytes(int type) {
+    return iq_grid_bytes(type) == 0 ? 0 : iq_grid_bytes(type) + (HC_IQ_SIGN_LUT ? 16 * iq_sign_entries(type) : 0);
+}
+
+// The f16 sign masks of the four registers of an 8-element point with sign bits s8.
+__device__ __forceinline__ uint4 iq_sign_masks(uint32_t s8) {
+    return make_uint4((s8 * 0x20008000u) & 0x80008000u, (s8 * 0x10004000u) & 0x80008000u,
+                      (s8 * 0x02000800u) & 0x80008000u, (s8 * 0x01000400u) & 0x80008000u);
+}
+
+// 4 grid bytes -> the f16 pairs (e0, e2), (e1, e3) of their values (exact: 1024 + g - 1024).
+__device__ __forceinline__ uint2 iq_f16_pairs(uint32_t g4) {
+    constexpr uint32_t k1024 = 0x64006400u;
+    return make_uint2(hsub2_u32(prmt(g4, 0x64646464u, 0x4240u), k1024),
+                      hsub2_u32(prmt(g4, 0x64646464u, 0x4341u), k1024));
+}
+
+// Expand the codebook of TYPE into the shared-memory LUT (threads [0, nthr) of the CTA; the
+// caller synchronises before the first use).
 template <int TYPE>
-__device__ __forceinline__ void iq_point(const IQBlk& b, int k, int l, uint32_t& lo, uint32_t& hi, uint32_t& s8) {
+__device__ __forceinline__ void iq_fill_lut(uint8_t* lut, int tid, int nthr) {
+    if constexpr (TYPE == T_IQ3_XXS || TYPE == T_IQ3_S) {
+        const uint32_t* grid = TYPE == T_IQ3_XXS ? hc_iq3xxs_grid : hc_iq3s_grid;
+        constexpr int n = TYPE == T_IQ3_XXS ? 256 : 512;
+        for (int i = tid; i < n; i += nthr) reinterpret_cast<uint2*>(lut)[i] = iq_f16_pairs(grid[i]);
+    } else {
+        const uint64_t* grid = TYPE == T_IQ2_XXS ? hc_iq2xxs_grid : TYPE == T_IQ2_XS ? hc_iq2xs_grid : hc_iq2s_grid;
+        constexpr int n = TYPE == T_IQ2_XXS ? 256 : TYPE == T_IQ2_XS ? 512 : 1024;
+        for (int i = tid; i < n; i += nthr) {
+            const uint2 lo = iq_f16_pairs((uint32_t)grid[i]), hi = iq_f16_pairs((uint32_t)(grid[i] >> 32));
+            reinterpret_cast<uint4*>(lut)[i] = make_uint4(lo.x, lo.y, hi.x, hi.y);
+        }
+    }
+    if constexpr (HC_IQ_SIGN_LUT) {
+        constexpr bool kByte = TYPE == T_IQ2_S || TYPE == T_IQ3_S;
+        uint4* sg = reinterpret_cast<uint4*>(lut + iq_grid_bytes(TYPE));
+        for (int i = tid; i < iq_sign_entries(TYPE); i += nthr)
+            sg[i] = iq_sign_masks(kByte ? (uint32_t)i : iq_ksigns((uint32_t)i));
+    }
+}
+
+// Point l of group k (8 elements: for IQ3 the two 4-element points 2l, 2l+1) as its four
+// A-fragment registers (e0, e2), (e1, e3), (e4, e6), (e5, e7) from the LUT, signs applied.
+template <int TYPE>
+__device__ __forceinline__ void iq_point(const IQBlk& b, const uint8_t* lut, int k, int l, uint4& f) {
+    uint32_t s8;  // sign byte, or the 7-bit sign index of the ksigns formats
+    const uint4* lut4 = reinterpret_cast<const uint4*>(lut);
+    const uint2* lut2 = reinterpret_cast<const uint2*>(lut);
     if constexpr (TYPE == T_IQ2_XXS) {
         const uint32_t aux0 = k ? b.p.z : b.p.x, aux1 = k ? b.p.w : b.p.y;
-        const uint2 g = __ldg(reinterpret_cast<const uint2*>(hc_iq2xxs_grid) + ((aux0 >> (8 * l)) & 0xFFu));
-        lo = g.x;
-        hi = g.y;
-        s8 = iq_ksigns(aux1 >> (7 * l));
+        f = lut4[(aux0 >> (8 * l)) & 0xFFu];
+        s8 = (aux1 >> (7 * l)) & 127u;
     } else if constexpr (TYPE == T_IQ2_XS) {
         const int i = 4 * k + l;  // u16 i of the piece
         const uint32_t w = i < 2 ? b.p.x : (i < 4 ? b.p.y : (i < 6 ? b.p.z : b.p.w));
         const uint32_t q = (w >> (16 * (i & 1))) & 0xFFFFu;
-        const uint2 g = __ldg(reinterpret_cast<const uint2*>(hc_iq2xs_grid) + (q & 511u));
-        lo = g.x;
-        hi = g.y;
-        s8 = iq_ksigns(q >> 9);
+        f = lut4[q & 511u];
+        s8 = q >> 9;
     } else if constexpr (TYPE == T_IQ2_S) {
         const uint32_t qh = (b.s >> (8 * k)) & 0xFFu;
-        const uint32_t idx = byte_of(b.p, 4 * k + l) | (((qh >> (2 * l)) & 3u) << 8);
-        const uint2 g = __ldg(reinterpret_cast<const uint2*>(hc_iq2s_grid) + idx);
-        lo = g.x;
-        hi = g.y;
+        f = lut4[byte_of(b.p, 4 * k + l) | (((qh >> (2 * l)) & 3u) << 8)];
         s8 = byte_of(b.p, 8 + 4 * k + l);
     } else if constexpr (TYPE == T_IQ3_XXS) {
         const uint32_t aux = k ? b.x.y : b.x.x;
-        lo = __ldg(hc_iq3xxs_grid + byte_of(b.p, 8 * k + 2 * l));
-        hi = __ldg(hc_iq3xxs_grid + byte_of(b.p, 8 * k + 2 * l + 1));
-        s8 = iq_ksigns(aux >> (7 * l));
+        const uint2 p0 = lut2[byte_of(b.p, 8 * k + 2 * l)], p1 = lut2[byte_of(b.p, 8 * k + 2 * l + 1)];
+        f = make_uint4(p0.x, p0.y, p1.x, p1.y);
+        s8 = (aux >> (7 * l)) & 127u;
     } else {  // IQ3_S
         const uint32_t qh = (b.s >> (8 * k)) & 0xFFu;
-        const uint32_t i0 = byte_of(b.p, 8 * k + 2 * l) | (((qh >> (2 * l)) & 1u) << 8);
-        const uint32_t i1 = byte_of(b.p, 8 * k + 2 * l + 1) | (((qh >> (2 * l + 1)) & 1u) << 8);
-        lo = __ldg(hc_iq3s_grid + i0);
-        hi = __ldg(hc_iq3s_grid + i1);
+        const uint2 p0 = lut2[byte_of(b.p, 8 * k + 2 * l) | (((qh >> (2 * l)) & 1u) << 8)];
+        const uint2 p1 = lut2[byte_of(b.p, 8 * k + 2 * l + 1) | (((qh >> (2 * l + 1)) & 1u) << 8)];
+        f = make_uint4(p0.x, p0.y, p1.x, p1.y);
         s8 = ((k ? b.x.y : b.x.x) >> (8 * l)) & 0xFFu;
     }
+    uint4 m;
+    if constexpr (HC_IQ_SIGN_LUT) {
+        m = reinterpret_cast<const uint4*>(lut + iq_grid_bytes(TYPE))[s8];
+    } else {
+        constexpr bool kByte = TYPE == T_IQ2_S || TYPE == T_IQ3_S;
+        m = iq_sign_masks(kByte ? s8 : iq_ksigns(s8));
+    }
+    f.x ^= m.x;
+    f.y ^= m.y;
+    f.z ^= m.z;
+    f.w ^= m.w;
 }
 
 // Group scale db of accumulator a (group a / (kAcc / 2), half-group a % 2 for kAcc = 4).
@@ -154,18 +229,6 @@ __device__ __forceinline__ float iq_scale(const IQBlk& b, int a) {
     }
 }
 
-// 4 grid bytes and their 4 sign bits (at bit `sh` of s8) -> the A registers of elements (0, 2)
-// and (1, 3), exact signed integers in f16.
-__device__ __forceinline__ void iq_frag(uint32_t g4, uint32_t s8, int sh, uint32_t& a02, uint32_t& a13) {
-    constexpr uint32_t k1024 = 0x64006400u;
-    a02 = hsub2_u32(prmt(g4, 0x64646464u, 0x4240u), k1024);
-    a13 = hsub2_u32(prmt(g4, 0x64646464u, 0x4341u), k1024);
-    const uint32_t m02 = ((s8 & (5u << sh)) * (0x20008000u >> sh)) & 0x80008000u;
-    const uint32_t m13 = ((s8 & (10u << sh)) * (0x10004000u >> sh)) & 0x80008000u;
-    a02 ^= m02;
-    a13 ^= m13;
-}
-
 // One IQ unit: rows g (A) and g+8 (B) of one tile-block image, lane shares into pA / pB.
 template <int TYPE, int NV>
 __device__ __forceinline__ void iq_unit(const IQBlk& A, const IQBlk& B, int kb, const LaneCtx<NV>& c,
@@ -181,11 +244,11 @@ __device__ __forceinline__ void iq_unit(const IQBlk& A, const IQBlk& B, int kb, 
             for (int i = 0; i < 4; ++i) acc[a][v][i] = 0.f;
 #pragma unroll
     for (int l = 0; l < 4; ++l) {
-        uint32_t ga[2][2], gb[2][2], sa[2], sb[2];
+        uint4 ga[2], gb[2];
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
-            iq_point<TYPE>(A, k, l, ga[k][0], ga[k][1], sa[k]);
-            iq_point<TYPE>(B, k, l, gb[k][0], gb[k][1], sb[k]);
+            iq_point<TYPE>(A, c.lut, k, l, ga[k]);
+            iq_point<TYPE>(B, c.lut, k, l, gb[k]);
         }
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
@@ -195,9 +258,8 @@ __device__ __forceinline__ void iq_unit(const IQBlk& A, const IQBlk& B, int kb, 
             for (int v = 0; v < NV; ++v) f[v] = xb[(wi * 2 * NV + 2 * v) * 4];
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
-                uint32_t a0, a2, b0, b2;
-                iq_frag(ga[k][half], sa[k], 4 * half, a0, a2);
-                iq_frag(gb[k][half], sb[k], 4 * half, b0, b2);
+                const uint32_t a0 = half ? ga[k].z : ga[k].x, a2 = half ? ga[k].w : ga[k].y;
+                const uint32_t b0 = half ? gb[k].z : gb[k].x, b2 = half ? gb[k].w : gb[k].y;
                 const int ai = NA == 4 ? 2 * k + (l >> 1) : k;
 #pragma unroll
                 for (int v = 0; v < NV; ++v)

@@ -220,6 +220,7 @@ struct LaneCtx {
     const float* sx;  // Q4_K sub-block sums
     int sxs;          // Q4_K: K/32
     int g, t;
+    const uint8_t* lut = nullptr;  // IQ formats: the shared-memory codebook
 };
 
 // Lane context for format F: xt = fragment table, zero = a zeroed block of it.

@@ -13,9 +13,9 @@
 
 namespace hc {
 
-// Shared memory: [2 x kMaxStages mbarriers, 128 B][table][zero block][Sx][tile slots][ring]
+// Shared memory: [2 x kMaxStages mbarriers, 128 B][table][zero block][Sx][tile slots][IQ LUT][ring]
 struct TmaSmem {
-    int table, zero, sx, red, ring;  // byte offsets
+    int table, zero, sx, red, lut, ring;  // byte offsets
 };
 
 template <class F>
@@ -26,8 +26,8 @@ __host__ __device__ inline TmaSmem tma_smem_layout(int K, int nv, int stages, bo
     s.zero = s.table + g.table_bytes;
     s.sx = s.zero + g.zero_bytes;
     s.red = s.sx + g.sx_bytes;
-    s.ring = s.red + (stages + 2) * tile_slot_bytes(nv);
-    s.ring = (s.ring + 127) & ~127;
+    s.lut = (s.red + (stages + 2) * tile_slot_bytes(nv) + 15) & ~15;
+    s.ring = (s.lut + iq_lut_bytes(F::kType) + 127) & ~127;
     return s;
 }
 
@@ -71,10 +71,12 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tma_kernel(GemvArgs a, int 
     float* sx = reinterpret_cast<float*>(smem + L.sx);
     float* red = reinterpret_cast<float*>(smem + L.red);
     for (int i = threadIdx.x; i < table_entries_per_block<F>(NV); i += kCW * 32) zero[i] = make_uint2(0u, 0u);
+    if constexpr (is_iq_type(F::kType)) iq_fill_lut<F::kType>(smem + L.lut, threadIdx.x, kCW * 32);
     const NormArgs nrm{a.norm_w, a.norm_len, a.norm_eps};
     build_prologue<F, NV>(xt, sx, a.x, a.ldx, a.K, nvec, nrm, s_red, a.err, kCW * 32, kBarPro);
     named_bar_sync(kBarPro, kCW * 32);
-    const LaneCtx<NV> ctx = make_ctx<F, NV>(xt, zero, sx, a.K, lane);
+    LaneCtx<NV> ctx = make_ctx<F, NV>(xt, zero, sx, a.K, lane);
+    ctx.lut = smem + L.lut;
     const TileOut o{a.y, a.ldy, a.resid, a.ldr, nvec, a.sk_ws, a.sk_cnt, a.sk_slots};
     int tslot = 0;
     bool aborted = false;

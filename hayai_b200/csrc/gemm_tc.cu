@@ -18,20 +18,20 @@
 //   Q6_K  w' = q (d sc) 2^8 (one FMUL, the reference's rounding): split as for Q4_K.
 // The activations enter as two f16 columns per row, x = x_hi + x_lo * 2^-11 (rows [0, Bp) and
 // [Bp, 2 Bp) of the B operand), so one tcgen05.mma with N = 2 Bp multiplies both, and
-// D = A_hi X + A_lo X accumulates in f32 in TMEM (two accumulators: the A_hi and the A_lo
-// products are independent MMA chains); the epilogue forms
-// y = (D[:, t] + D[:, Bp + t] * 2^-11) * 2^-8.
+// D = A_hi X + A_lo X accumulates in f32 in TMEM (both products into one accumulator); the
+// epilogue forms y = (D[:, t] + D[:, Bp + t] * 2^-11) * 2^-8.
 //
 // Persistent, stream-K: one CTA per SM walks a contiguous range of the work units (one weight
 // image = 128 or 256 K of one 128-row block of one matrix, in the order row block, matrix, K),
 // so the weight stream never pauses between row blocks.  A maximal run of units of one (row
-// block, matrix) in a CTA is a segment: it accumulates in one of two TMEM accumulator sets
-// and ends in a partial-output slot; the finishing kernel adds a row block's slots in CTA
-// order (deterministic), then SiLU(g) * u or the residual.  15 warps:
+// block, matrix) in a CTA is a segment: it accumulates in chains of at most kTcChainK K, each
+// in one of two TMEM accumulator sets in turn, which the epilogue adds in order into the
+// segment's partial-output slot; the finishing kernel adds a row block's slots in CTA order
+// (deterministic), then SiLU(g) * u or the residual.  15 warps:
 //   warp 0     weight producer: per unit one bulk copy per 16-row tile of the tile-major
 //              layout (8 copies of one image);
 //   warp 1     owns the TMEM columns; one elected lane issues the MMAs (4 K-steps x {hi, lo}
-//              per 64-K chunk), tcgen05.commit frees the operand buffers and, at a segment's
+//              per 64-K chunk), tcgen05.commit frees the operand buffers and, at a chain's
 //              end, hands its accumulator set to the epilogue;
 //   warps 2-9  dequantise each 64-K chunk into the A_hi / A_lo operand buffers (K-major,
 //              128-byte swizzle: rows of 128 B, 16-byte chunks XOR-permuted by row);
@@ -62,9 +62,16 @@ constexpr int kTcABytes = kTcRows * kTcChunk * 2;  // one f16 operand buffer (16
 constexpr int kTcThreads = 480;            // 15 warps
 constexpr int kTcMaxRing = 12;
 constexpr float kTcWScale = 256.f;         // w' = w * 2^8
+// K elements per accumulator chain: the tensor core adds each MMA's products into its f32
+// accumulator with a truncating (biased) alignment, so a chain over a whole row (up to 28672
+// K here) drifts by up to ~1e-3 absolute at the 70B shapes.  A segment is therefore cut into
+// chains of at most kTcChainK; the epilogue adds the chains of a segment in f32 (round to
+// nearest), in order, into the segment's partial slot.
+constexpr int kTcChainK = 1024;
 // TMEM operand form: one hand-over (dequant -> MMA -> release) covers kTaKH 64-K chunks; a
 // buffer is kTaBuf columns: A_hi of chunk k at [32k, 32k + 32), A_lo at kTaLo + 32k.
 constexpr int kTaKH = 2, kTaLo = 32 * kTaKH, kTaBuf = 2 * kTaLo;
+constexpr int kTaEsum = 64 * kTcRows * 4;  // the epilogue's segment sums (batches up to 64)
 
 // Tile-block image of each format (repack.cu): bytes, K elements, images per weight stage
 // (one: a stage is one work unit).
@@ -91,7 +98,7 @@ struct TcArgs {
     int mats, nimg;       // matrices (1, or 2 for gate/up); images per row block and matrix
     long long U;          // work units: (M / 128) * mats * nimg
     int slots;            // partial-output slots per (row block, matrix)
-    int nsets;            // TMEM accumulator sets (2 when 4 N <= 512 columns)
+    int nsets;            // TMEM accumulator sets (2: the epilogue drains one while the other fills)
     float* out;           // partials [(row block, matrix)][slot][B][128]
     int* err;
     int SW, NX, NA;       // ring depths: weight units, activation chunks, operand buffers
@@ -503,7 +510,9 @@ template <class F, bool TA>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
     constexpr int CPI = F::kImgK / kTcChunk;  // chunks per image (= per unit)
     constexpr int KH = TA ? kTaKH : 1;         // chunks per hand-over
+    constexpr int CHU = kTcChainK / F::kImgK;  // units per accumulator chain
     static_assert(CPI % KH == 0, "a hand-over stays inside one unit");
+    static_assert(kTcChainK % F::kImgK == 0, "chains are whole units");
     constexpr int WST = tc_wstage<F>();
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ uint32_t s_tmem;
@@ -523,12 +532,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
     uint8_t* wring = base + 1024;
     uint8_t* xring = wring + ((a.SW * WST + 1023) & ~1023);
     const int xbytes = a.N * kTcChunk * 2, xslot = KH * xbytes;  // one chunk; one hand-over
-    uint8_t* aring = xring + ((a.NX * xslot + 1023) & ~1023);  // (the smem operand form only)
-    // accumulator set s: A_hi products at columns s 2N + [0, N), A_lo products at + N; in the
-    // TA form the NA operand buffers follow (kTaBuf columns each)
-    // columns per accumulator set: the TA form adds the A_hi and the A_lo products into one
-    // accumulator (N columns), the shared-memory form keeps them apart (2N)
-    const int accW = TA ? a.N : 2 * a.N;
+    // the smem operand form's operand buffers; the TA form's epilogue sums
+    uint8_t* aring = xring + ((a.NX * xslot + 1023) & ~1023);
+    // accumulator set s: columns [s N, (s + 1) N), the A_hi and the A_lo products added into
+    // one accumulator (a chain is short, see kTcChainK); in the TA form the NA operand buffers
+    // follow (kTaBuf columns each)
+    const int accW = a.N;
     const uint32_t accC = (uint32_t)(a.nsets * accW);
     const uint32_t need = accC + (TA ? (uint32_t)kTaBuf * (uint32_t)a.NA : 0u);
     const uint32_t ncols = need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : need <= 256 ? 256u : 512u;
@@ -547,7 +556,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
             mbar_init(a_empty + 8 * i, 1);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(acc_full + 8 * i, 1);   // tcgen05.commit at a segment's end
+            mbar_init(acc_full + 8 * i, 1);   // tcgen05.commit at an accumulator chain's end
             mbar_init(acc_empty + 8 * i, 4);  // the 4 epilogue warps
         }
         mbar_fence_init();
@@ -612,13 +621,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
                 const int j = h * KH;
                 const long long u = u0 + j / CPI;
                 const int sub = j % CPI, img = (int)(u % a.nimg);
-                const bool first = sub == 0 && (img == 0 || u == u0);
-                const bool last = sub + KH - 1 == CPI - 1 && (img == a.nimg - 1 || u == u1 - 1);
+                const bool first = sub == 0 && (img % CHU == 0 || u == u0);
+                const bool last = sub + KH - 1 == CPI - 1 && (img % CHU == CHU - 1 || img == a.nimg - 1 || u == u1 - 1);
                 if (first) {
                     ++seg;
                     const int s = seg % a.nsets;
                     acc = tmem + (uint32_t)(s * accW);
-                    // the set's previous segment must have been read out
+                    // the set's previous chain must have been read out
                     if (seg >= a.nsets && !mbar_wait(acc_empty + 8 * s, ((seg / a.nsets) - 1) & 1)) {
                         timeout = true;
                         break;
@@ -648,7 +657,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
                     for (int ks = 0; ks < kTcChunk / 16; ++ks) {
                         const uint32_t on = (first && ks == 0) ? 0u : 1u;
                         tc_mma(acc, tc_desc(ahi + 32 * ks), tc_desc(xs + 32 * ks), idesc, on);
-                        tc_mma(acc + (uint32_t)a.N, tc_desc(alo + 32 * ks), tc_desc(xs + 32 * ks), idesc, on);
+                        tc_mma(acc, tc_desc(alo + 32 * ks), tc_desc(xs + 32 * ks), idesc, 1u);
                     }
                 }
                 tc_commit(a_empty + 8 * sa);
@@ -715,10 +724,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
     } else {
         // ---- epilogue: warps 10-13 read TMEM lane quarters 2, 3, 0, 1 (warp % 4)
         const int quarter = warp & 3, row = 32 * quarter + lane, Bp = a.N >> 1;
-        int seg = 0;
+        float* esum = reinterpret_cast<float*>(aring);  // TA form: the segment sums [64][128]
+        int seg = 0;  // accumulator chains so far
         for (long long u = u0; u < u1 && !timeout; ++seg) {
-            const int run = (int)(u / a.nimg);
-            const long long ue = (long long)(run + 1) * a.nimg < u1 ? (long long)(run + 1) * a.nimg : u1;
+            const int run = (int)(u / a.nimg), img = (int)(u % a.nimg);
+            long long ue = u - img % CHU + CHU;  // the chain ends at the next CHU boundary,
+            if (ue > (long long)(run + 1) * a.nimg) ue = (long long)(run + 1) * a.nimg;  // the run's end
+            if (ue > u1) ue = u1;                                                          // or the CTA's
+            const bool chain0 = img == 0 || u == u0;  // the segment's first chain stores, the others add
             const int s = seg % a.nsets;
             if (!mbar_wait(acc_full + 8 * s, (seg / a.nsets) & 1)) {
                 timeout = true;
@@ -728,26 +741,47 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcArgs a) {
             const int slot = c - tc_owner((long long)run * a.nimg, a.U, G);
             float* out = a.out + ((size_t)run * a.slots + slot) * (size_t)a.B * kTcRows;
             const uint32_t tb = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(s * accW);
-            for (int cb = 0; cb < Bp; cb += 8) {
-                float vh[8], vl[8], wh[8], wl[8];
-                tc_ld8(tb + cb, vh);
-                tc_ld8(tb + Bp + cb, vl);
-                if constexpr (!TA) {
-                    tc_ld8(tb + a.N + cb, wh);  // the A_lo products
-                    tc_ld8(tb + a.N + Bp + cb, wl);
-                }
+            if constexpr (TA) {
+                // Bp <= 64: the row's sums over the segment's chains collect in shared memory
+                // ([t][row]: a warp's lanes hit consecutive words), and the set is released as
+                // soon as it has been read (with one accumulator set the next chain's MMAs wait
+                // only for these TMEM loads)
+                for (int cb = 0; cb < Bp; cb += 8) {
+                    float vh[8], vl[8];
+                    tc_ld8(tb + cb, vh);       // A x_hi
+                    tc_ld8(tb + Bp + cb, vl);  // A x_lo
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int t = cb + e;
-                    if (t < a.B)
-                        out[(size_t)t * kTcRows + row] =
-                            TA ? (vh[e] + vl[e] * (1.0f / 2048.0f)) * (1.0f / kTcWScale)
-                               : ((vh[e] + wh[e]) + (vl[e] + wl[e]) * (1.0f / 2048.0f)) * (1.0f / kTcWScale);
+                    for (int e = 0; e < 8; ++e) {
+                        const float v = (vh[e] + vl[e] * (1.0f / 2048.0f)) * (1.0f / kTcWScale);
+                        float* o = esum + (cb + e) * kTcRows + row;
+                        *o = chain0 ? v : *o + v;
+                    }
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acc_empty + 8 * s);
+                if (ue == u1 || ue == (long long)(run + 1) * a.nimg) {  // the segment's last chain
+                    for (int t = 0; t < a.B; ++t) out[(size_t)t * kTcRows + row] = esum[t * kTcRows + row];
+                }
+            } else {
+                for (int cb = 0; cb < Bp; cb += 8) {
+                    float vh[8], vl[8];
+                    tc_ld8(tb + cb, vh);       // A x_hi
+                    tc_ld8(tb + Bp + cb, vl);  // A x_lo
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const int t = cb + e;
+                        if (t < a.B) {
+                            const float v = (vh[e] + vl[e] * (1.0f / 2048.0f)) * (1.0f / kTcWScale);
+                            float* o = out + (size_t)t * kTcRows + row;  // (this thread's own earlier store)
+                            *o = chain0 ? v : *o + v;
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acc_empty + 8 * s);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty + 8 * s);
             u = ue;
         }
     }
@@ -926,18 +960,14 @@ template <class F>
 static cudaError_t tc_launch_ta(TcArgs a, int G, int smem_limit, cudaStream_t stream) {
     constexpr int WST = tc_wstage<F>();
     const int xbytes = a.N * kTcChunk * 2;
-    // three operand buffers where TMEM holds them beside two accumulator sets (N columns each),
-    // else beside one, else two buffers
+    // three operand buffers, and two accumulator sets (N columns each: the epilogue drains
+    // one while the other fills) where TMEM holds them beside (N <= 64), else one (the
+    // epilogue then releases it right after its TMEM loads)
     a.NA = 3;
-    a.nsets = 2;
-    if (2 * a.N + kTaBuf * 3 > 512) a.nsets = 1;
-    if (a.nsets * a.N + kTaBuf * 3 > 512) {
-        a.NA = 2;
-        a.nsets = 2 * a.N + kTaBuf * 2 <= 512 ? 2 : 1;
-    }
+    a.nsets = 2 * a.N + kTaBuf * 3 <= 512 ? 2 : 1;
     a.NX = 4;
     auto smem_of = [&](const TcArgs& t) {
-        return 1024 + ((t.SW * WST + 1023) & ~1023) + ((t.NX * kTaKH * xbytes + 1023) & ~1023);
+        return 1024 + ((t.SW * WST + 1023) & ~1023) + ((t.NX * kTaKH * xbytes + 1023) & ~1023) + kTaEsum;
     };
     a.SW = kTcMaxRing;
     while (smem_of(a) > smem_limit - 2048 && a.SW > 2) --a.SW;
@@ -1015,7 +1045,7 @@ cudaError_t launch_tc_gemm(int type, const uint8_t* w, const uint8_t* w2, long l
     a.nimg = p.nimg;
     a.U = p.U;
     a.slots = p.slots;
-    a.nsets = 4 * N <= 512 ? 2 : 1;
+    a.nsets = 2;  // 2 N <= 512 TMEM columns: N <= 256
     a.out = part;
     a.err = err;
     switch (type) {

@@ -17,9 +17,9 @@
 // Compute: lane-distributed like Q4_K (same fragment table): lane t's k-slots are elements
 // 64t + 32k + 4wi + j of the block (group 2t + k, wi < 8, j < 4), and B holds lane t's x only
 // in its own two columns, so every accumulator is one group's (or half-group's) dot product on
-// its own lane; the group scale is applied once per accumulator in f32.  Grid bytes enter the
-// A fragment as f16(1024 + g) by one PRMT, minus 1024 (exact), and the element signs are
-// XORed into the f16 sign bits.
+// its own lane; the group scale is applied once per accumulator in f32.  Grid values enter the
+// A fragment as exact f16 (from the LUT below), and the element signs are XORed into the f16
+// sign bits.
 //
 // Shared-memory LUTs.  Each CTA expands its format's codebook once, at kernel start, into a
 // shared-memory table of ready A-fragment registers: per grid point the f16 pairs (e0, e2),
@@ -102,12 +102,8 @@ __device__ __forceinline__ uint32_t byte_of(const uint4& p, int i) {
     return (w >> (8 * (i & 3))) & 0xFFu;
 }
 
-#ifndef HC_IQ_SIGN_LUT
-#define HC_IQ_SIGN_LUT 0
-#endif
-
-// Bytes of format TYPE's grid table in the shared-memory LUT (0 for the other formats).
-__host__ __device__ constexpr int iq_grid_bytes(int type) {
+// Bytes of format TYPE's shared-memory LUT (0 for the other formats).
+__host__ __device__ constexpr int iq_lut_bytes(int type) {
     return type == T_IQ2_XXS ? 256 * 16
            : type == T_IQ2_XS ? 512 * 16
            : type == T_IQ2_S  ? 1024 * 16
@@ -116,23 +112,16 @@ __host__ __device__ constexpr int iq_grid_bytes(int type) {
                                : 0;
 }
 
-// Sign-mask table entries: the 7-bit sign index of IQ2_XXS / IQ2_XS / IQ3_XXS, the sign byte
-// of IQ2_S / IQ3_S.
-__host__ __device__ constexpr int iq_sign_entries(int type) {
-    return type == T_IQ2_S || type == T_IQ3_S ? 256 : 128;
-}
-
-__host__ __device__ constexpr int iq_lut_bytes(int type) {
-    return iq_grid_bytes(type) == 0 ? 0 : iq_grid_bytes(type) + (HC_IQ_SIGN_LUT ? 16 * iq_sign_entries(type) : 0);
-}
-
-// The f16 sign masks of the four registers of an 8-element point with sign bits s8.
+// The f16 sign masks of the four registers of an 8-element point with sign bits s8 (a table of
+// these masks in shared memory, one 16-byte load per point, measured 35-45 % slower: the loads
+// compete with the grid lookups for shared-memory bandwidth).
 __device__ __forceinline__ uint4 iq_sign_masks(uint32_t s8) {
     return make_uint4((s8 * 0x20008000u) & 0x80008000u, (s8 * 0x10004000u) & 0x80008000u,
                       (s8 * 0x02000800u) & 0x80008000u, (s8 * 0x01000400u) & 0x80008000u);
 }
 
-// 4 grid bytes -> the f16 pairs (e0, e2), (e1, e3) of their values (exact: 1024 + g - 1024).
+// 4 grid bytes -> the f16 pairs (e0, e2), (e1, e3) of their values: f16(1024 + g) by one PRMT
+// under the exponent byte 0x64, minus 1024 (exact).
 __device__ __forceinline__ uint2 iq_f16_pairs(uint32_t g4) {
     constexpr uint32_t k1024 = 0x64006400u;
     return make_uint2(hsub2_u32(prmt(g4, 0x64646464u, 0x4240u), k1024),
@@ -154,12 +143,6 @@ __device__ __forceinline__ void iq_fill_lut(uint8_t* lut, int tid, int nthr) {
             const uint2 lo = iq_f16_pairs((uint32_t)grid[i]), hi = iq_f16_pairs((uint32_t)(grid[i] >> 32));
             reinterpret_cast<uint4*>(lut)[i] = make_uint4(lo.x, lo.y, hi.x, hi.y);
         }
-    }
-    if constexpr (HC_IQ_SIGN_LUT) {
-        constexpr bool kByte = TYPE == T_IQ2_S || TYPE == T_IQ3_S;
-        uint4* sg = reinterpret_cast<uint4*>(lut + iq_grid_bytes(TYPE));
-        for (int i = tid; i < iq_sign_entries(TYPE); i += nthr)
-            sg[i] = iq_sign_masks(kByte ? (uint32_t)i : iq_ksigns((uint32_t)i));
     }
 }
 
@@ -196,13 +179,8 @@ __device__ __forceinline__ void iq_point(const IQBlk& b, const uint8_t* lut, int
         f = make_uint4(p0.x, p0.y, p1.x, p1.y);
         s8 = ((k ? b.x.y : b.x.x) >> (8 * l)) & 0xFFu;
     }
-    uint4 m;
-    if constexpr (HC_IQ_SIGN_LUT) {
-        m = reinterpret_cast<const uint4*>(lut + iq_grid_bytes(TYPE))[s8];
-    } else {
-        constexpr bool kByte = TYPE == T_IQ2_S || TYPE == T_IQ3_S;
-        m = iq_sign_masks(kByte ? s8 : iq_ksigns(s8));
-    }
+    constexpr bool kByte = TYPE == T_IQ2_S || TYPE == T_IQ3_S;
+    const uint4 m = iq_sign_masks(kByte ? s8 : iq_ksigns(s8));
     f.x ^= m.x;
     f.y ^= m.y;
     f.z ^= m.z;

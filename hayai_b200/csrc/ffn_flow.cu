@@ -54,6 +54,10 @@ constexpr int kFW = 3;                            // finisher warps
 constexpr int kThreads = (kCW + 1 + kFW) * 32;    // consumers, producer, finishers
 constexpr int kThreadsTP = kThreads + 32;          // + the x-tile completer of tensor parallelism
 constexpr int kNT = 8;                            // hand-over slots (chunk partials) to the finishers
+// mbarriers at the head of shared memory: ring full / empty, x table, two down-table slots,
+// hand-over full / free
+constexpr int kBarBytes = 16 * kMaxS + 8 + 16 + 16 * kNT;
+static_assert(kBarBytes <= 256, "the mbarriers fit the 256-byte head of shared memory");
 
 struct Layer {  // same layout as the host's per-layer pointer table
     const uint8_t* g;
@@ -144,7 +148,7 @@ template <class FA, class FD>
 __host__ __device__ inline Smem smem_layout(int dm, int ff, int S, int slot_bytes) {
     const Geo<FA, FD> g(dm, ff);
     Smem s;
-    s.tab_a = 256;
+    s.tab_a = 256;  // after the mbarriers (kBarBytes)
     s.sx = s.tab_a + g.tab_a;
     s.tab_d = s.sx + (FA::kNeedSx ? ((dm / 32) * 4 + 15) / 16 * 16 : 0);
     s.zero = s.tab_d + 2 * g.tab_p;

@@ -61,6 +61,7 @@ constexpr int kTcChunk = 64;               // K per operand buffer
 constexpr int kTcABytes = kTcRows * kTcChunk * 2;  // one f16 operand buffer (16 KB)
 constexpr int kTcThreads = 480;            // 15 warps
 constexpr int kTcMaxRing = 12;
+static_assert(6 * 8 * kTcMaxRing + 32 <= 1024, "the mbarriers fit the 1 KB head of shared memory");
 constexpr float kTcWScale = 256.f;         // w' = w * 2^8
 // K elements per accumulator chain: the tensor core adds each MMA's products into its f32
 // accumulator with a truncating (biased) alignment, so a chain over a whole row (up to 28672

@@ -18,6 +18,8 @@ struct TmaSmem {
     int table, zero, sx, red, lut, ring;  // byte offsets
 };
 
+static_assert(2 * kMaxStages * 8 <= 128, "the ring's mbarriers fit the 128-byte head of shared memory");
+
 template <class F>
 __host__ __device__ inline TmaSmem tma_smem_layout(int K, int nv, int stages, bool fused) {
     const GemvSmem g = gemv_smem_layout<F>(K, nv, false);

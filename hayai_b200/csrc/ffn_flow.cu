@@ -286,7 +286,6 @@ __device__ bool produce_layer(Prod& P, Desc* desc, const Args& a, const Geo<FA, 
     unsigned next_ready = 0;  // the next part's counter, read ahead (its latency overlaps the copies)
     c = take(cnt + kCtrDn, lane);
     while (c < G.np * G.td) {
-        const int nc = take(cnt + kCtrDn, lane);
         const int p = c / G.td, tile = c - p * G.td;
         const int kb0 = p * G.pb, kb1 = kb0 + G.part_blocks(p);
         bool first = true;
@@ -337,7 +336,8 @@ __device__ bool produce_layer(Prod& P, Desc* desc, const Args& a, const Geo<FA, 
             else P.last0 = P.stage_index();
             r.advance();
         }
-        c = nc;
+        if (!slot_free(r)) return false;  // claim the next chunk only once a slot is free for it
+        c = take(cnt + kCtrDn, lane);
     }
     if (!slot_free(r)) return false;
     if (lane == 0) {
@@ -386,9 +386,12 @@ __device__ __forceinline__ float sum16(float v) {
 // that consume the weight stream.
 template <class FA, class FD, bool TP>
 __device__ void finisher(const Args& a, const Geo<FA, FD>& G, int* next, uint32_t tfull0, uint32_t tfree0,
-                         const float* red, const Meta* meta, const float* s_inv, int lane) {
+                         const float* red, const Meta* meta, const float* s_inv, const float* stage, int lane) {
     bool bad = false;
     const int row = lane & 15;
+    int copied_layer = -1;  // (lane 0) the layer whose table-copied count was seen complete
+    int inv_layer = -1;     // the layer whose 1 / rms is in inv
+    float inv = 1.0f;
     while (true) {
         int k = 0;
         if (lane == 0) k = atomicAdd(next, 1);
@@ -411,7 +414,17 @@ __device__ void finisher(const Args& a, const Geo<FA, FD>& G, int* next, uint32_
 #pragma unroll
             for (int w = 0; w < kCW; ++w) f0 += rr[w * 16 + row];
         }
-        const float inv = *s_inv;
+        if (m.layer != inv_layer) {  // 1 / rms(x) of this layer's input
+            inv_layer = m.layer;
+            if (m.layer == 0) {
+                inv = *s_inv;  // (the consumers' first prologue)
+            } else {  // from the copied sums of squares of x's 16-element tiles (fixed order)
+                float q = 0.f;
+                for (int i = lane; i < G.td; i += 32) q += stage[G.td + i];
+                q = warp_sum(q);
+                inv = a.layers[m.layer].norm ? 1.0f / sqrtf(q / (float)a.dm + a.eps) : 1.0f;
+            }
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(tfree0 + 8 * ts);  // the slot may be refilled
         unsigned* cnt = a.cnt + (size_t)m.layer * a.cstride;
@@ -461,8 +474,10 @@ __device__ void finisher(const Args& a, const Geo<FA, FD>& G, int* next, uint32_
         int ok = 1;
         if (lane == 0) {
             ok = wait_ge(tc, (unsigned)(G.np - 1), a.err) ? 1 : 0;
-            if (ok && l >= 2 && !last_layer)
+            if (ok && l >= 2 && !last_layer && copied_layer != l) {
                 ok = wait_ge(a.cnt + (size_t)(l - 1) * a.cstride + kCopied, gridDim.x, a.err) ? 1 : 0;
+                copied_layer = l;
+            }
         }
         ok = __shfl_sync(kFull, ok, 0);
         __syncwarp();  // lane 0's acquire orders the other lanes' loads below
@@ -610,7 +625,7 @@ __global__ void __launch_bounds__(TP ? kThreadsTP : kThreads, 1) ffn_flow_kernel
         return;
     }
     if (warp > kCW) {  // ------------------------------------------------ finishers
-        finisher<FA, FD, TP>(a, G, &s_fnext, tfull0, tfree0, red, meta, &s_inv, lane);
+        finisher<FA, FD, TP>(a, G, &s_fnext, tfull0, tfree0, red, meta, &s_inv, stage, lane);
         return;
     }
 
@@ -692,17 +707,16 @@ __global__ void __launch_bounds__(TP ? kThreadsTP : kThreads, 1) ffn_flow_kernel
             }
             named_bar_sync(kBarPro, kStep);
             if (s_abort) aborted = true;
-            if constexpr (FA::kNeedSx)
-                for (int j = threadIdx.x; j < a.dm / 32; j += kStep) sx[j] = stage[2 * j] + stage[2 * j + 1];
-            float ssq = 0.f;
-            for (int i = threadIdx.x; i < G.td; i += kStep) ssq += stage[G.td + i];
-            const float tot = block_sum(ssq, s_red, kStep, kBarPro);
-            if (threadIdx.x == 0) s_inv = ly.norm ? 1.0f / sqrtf(tot / (float)a.dm + a.eps) : 1.0f;
-            named_bar_sync(kBarPro, kStep);
+            // the copied per-tile sums serve the Q4_K units as they are (sx16), and the finishers
+            // take 1 / rms from the copied sums of squares: nothing else to wait for
         }
         // ---- gate/up units (h is completed by the finishers)
         {
-            const LaneCtx<1> ctx = make_ctx<FA, 1>(xt, zero, sx, a.dm, lane);
+            LaneCtx<1> ctx = make_ctx<FA, 1>(xt, zero, l == 0 ? sx : stage, a.dm, lane);
+            if (l > 0) {
+                ctx.sx16 = 1;
+                ctx.sxs = a.dm / 16;
+            }
             while (!aborted) {
                 if (!mbar_wait(r.full0 + 8 * r.slot, r.round & 1)) {
                     fail();

@@ -218,9 +218,10 @@ struct LaneCtx {
     const uint2* xb0;
     int xstride;      // table entries per kernel block, or 0
     const float* sx;  // Q4_K sub-block sums
-    int sxs;          // Q4_K: K/32
+    int sxs;          // Q4_K: K/32 (K/16 with sx16)
     int g, t;
     const uint8_t* lut = nullptr;  // IQ formats: the shared-memory codebook
+    int sx16 = 0;     // Q4_K: sx holds sums over 16-element halves of the sub-blocks
 };
 
 // Lane context for format F: xt = fragment table, zero = a zeroed block of it.
@@ -341,7 +342,14 @@ __device__ __forceinline__ void q4k_unit(const Q4KBlk (&A)[NMAT], const Q4KBlk (
         const int kb = kbs[SHARE_B ? 0 : m];
         float2 s[NV];
 #pragma unroll
-        for (int v = 0; v < NV; ++v) s[v] = *reinterpret_cast<const float2*>(c.sx + v * c.sxs + kb * 8 + 2 * c.t);
+        for (int v = 0; v < NV; ++v) {
+            if (c.sx16) {
+                const float4 h = *reinterpret_cast<const float4*>(c.sx + v * c.sxs + kb * 16 + 4 * c.t);
+                s[v] = make_float2(h.x + h.y, h.z + h.w);
+            } else {
+                s[v] = *reinterpret_cast<const float2*>(c.sx + v * c.sxs + kb * 8 + 2 * c.t);
+            }
+        }
         float cA0, kA0, cA1, kA1, cB0, kB0, cB1, kB1;
         q4k_factors(A[m].h, c.t, cA0, kA0, cA1, kA1);
         q4k_factors(B[m].h, c.t, cB0, kB0, cB1, kB1);

@@ -161,6 +161,9 @@ def test_stack_kernel_matches_per_layer_kernels(engine):
     (oracle.Q6_K, oracle.Q6_K, 1024, 5120),
     (oracle.Q8_0, oracle.Q8_0, 1024, 2080),  # h table padded from 2080 to 17 x 128 elements
     (oracle.Q4_K, oracle.Q6_K, 2048, 8192),  # 2 chunks per down tile, 64 x 32 tiles
+    # short d_ff (14 and 7 down blocks; 3584 is a 70B d_ff shard at 8 ranks): down K-parts of 4 blocks
+    (oracle.Q4_K, oracle.Q6_K, 4096, 3584),
+    (oracle.Q4_K, oracle.Q6_K, 4096, 1792),
 ])
 def test_stack_kernel_formats(engine, tg, td, dm, ff):
     L = 3

@@ -525,10 +525,10 @@ def run_moe(args):
     local_experts = [len([e for e in np.unique(i.cpu().numpy()) if lo <= e < hi]) for i in ids]
     k_bytes = L * router_bytes(c) + sum(local_experts) * expert_bytes(c)
     achieved = k_bytes / k_time / 1e9
-    roofline = {"bound": "hbm", "kernel": f"MoE stack graph, {L} layers x (router_exact_kernel + "
-                "route_topk_warp_kernel + moe_group_kernel + moe_tma_kernel<FmtQ4K,true> + "
-                "moe_tma_kernel<FmtQ4K,false> + moe_combine_kernel)"
-                + (" with the expert shard and the in-kernel exchange" if ep else ""),
+    roofline = {"bound": "hbm", "kernel": f"MoE stack graph, {L} layers x (router_staged_kernel + "
+                "route_group_kernel + moe_tma_kernel<FmtQ4K,true> + moe_tma_kernel<FmtQ4K,false> + "
+                + ("ep_signal_kernel + moe_combine_wait_kernel), the expert shard with the in-kernel exchange"
+                   if ep else "moe_combine_kernel)"),
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy burst)" if peak_kind == "measured"
                 else "fallback 6.65 TB/s", "traffic": committed_traffic(f"moe_{args.config}"),

@@ -210,7 +210,9 @@ extern "C" int hc_engine_init(int device, hc_engine** out) {
     if (tc && tc[0] == '0') e->use_tc = false;
     ce = cudaMalloc(&e->d_err, 16);
     if (ce == cudaSuccess) ce = cudaMemset(e->d_err, 0, 16);
+    if (ce == cudaSuccess) ce = cudaMallocHost(&e->h_err, 16);
     if (ce != cudaSuccess) {
+        if (e->d_err) cudaFree(e->d_err);
         cudaStreamDestroy(e->own_stream);
         delete e;
         return hc_cuda_error(ce, "error flag allocation");
@@ -241,6 +243,7 @@ extern "C" int hc_engine_free(hc_engine* e) {
     e->ws_misc.release();
     e->hs_out.release();
     if (e->d_err) cudaFree(e->d_err);
+    if (e->h_err) cudaFreeHost(e->h_err);
     if (e->own_stream) cudaStreamDestroy(e->own_stream);
     delete e;
     return HC_OK;
@@ -307,9 +310,23 @@ extern "C" int hc_engine_get_stream(hc_engine* e, void** stream) {
 }
 
 // Read (and clear) the device error flag.  Call only after the stream is synchronised.
+static int flag_error(hc_engine* e, int flag);
+
 int hc_check_device_error(hc_engine* e) {
     int flag = 0;
     HC_CUDA(cudaMemcpy(&flag, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    return flag_error(e, flag);
+}
+
+// The end of a host-buffer call: the error flag travels back on the stream behind the call's
+// results, so one stream synchronisation covers both.
+int hc_finish_sync(hc_engine* e) {
+    HC_CUDA(cudaMemcpyAsync(e->h_err, e->d_err, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    HC_CUDA(cudaStreamSynchronize(e->stream));
+    return flag_error(e, *e->h_err);
+}
+
+static int flag_error(hc_engine* e, int flag) {
     if (flag) {
         HC_CUDA(cudaMemset(e->d_err, 0, sizeof(int)));
         if (flag & 1)
@@ -324,8 +341,7 @@ int hc_check_device_error(hc_engine* e) {
 extern "C" int hc_sync(hc_engine* e) {
     int rc = hc_engine_activate(e);
     if (rc) return rc;
-    HC_CUDA(cudaStreamSynchronize(e->stream));
-    return hc_check_device_error(e);
+    return hc_finish_sync(e);
 }
 
 // ------------------------------------------------------------------ weights
@@ -478,8 +494,7 @@ static int gemv_host(hc_engine* e, const hc_weights* w, const float* in, float* 
     rc = hc_launch_gemv(e, w, (const float*)e->ws_x.p, n, (float*)e->ws_y.p, m, nullptr, 0, nvec);
     if (rc) return rc;
     HC_CUDA(cudaMemcpyAsync(out, e->ws_y.p, nvec * m * 4, cudaMemcpyDeviceToHost, e->stream));
-    HC_CUDA(cudaStreamSynchronize(e->stream));
-    return hc_check_device_error(e);
+    return hc_finish_sync(e);
 }
 
 extern "C" int hc_ggml_gemv_bound(hc_engine* e, const hc_weights* w, const float* in, float* out) {
@@ -768,8 +783,7 @@ extern "C" int hc_ffn_swiglu(hc_engine* e, const hc_weights* g, const hc_weights
                        nvec, nullptr, 0, 0.f);
     if (rc) return rc;
     HC_CUDA(cudaMemcpyAsync(y, e->ws_y.p, nvec * d->m * 4, cudaMemcpyDeviceToHost, e->stream));
-    HC_CUDA(cudaStreamSynchronize(e->stream));
-    return hc_check_device_error(e);
+    return hc_finish_sync(e);
 }
 
 // ------------------------------------------------------------------ FFN stack (+ CUDA graph)
@@ -1101,8 +1115,7 @@ extern "C" int hc_ffn_stack_tp(hc_engine* e, const hc_weights* const* g, const h
     rc = hc_ffn_stack_tp_dev(e, g, u, d, norm_w, eps, L, (float*)e->ws_x.p, nvec);
     if (rc) return rc;
     HC_CUDA(cudaMemcpyAsync(x_out, e->ws_x.p, bytes, cudaMemcpyDeviceToHost, e->stream));
-    HC_CUDA(cudaStreamSynchronize(e->stream));
-    return hc_check_device_error(e);
+    return hc_finish_sync(e);
 }
 
 extern "C" int hc_ffn_stack(hc_engine* e, const hc_weights* const* g, const hc_weights* const* u,
@@ -1122,6 +1135,5 @@ extern "C" int hc_ffn_stack(hc_engine* e, const hc_weights* const* g, const hc_w
     rc = stack_run(e, s, (float*)e->ws_x.p, nvec);
     if (rc) return rc;
     HC_CUDA(cudaMemcpyAsync(x_out, e->ws_x.p, bytes, cudaMemcpyDeviceToHost, e->stream));
-    HC_CUDA(cudaStreamSynchronize(e->stream));
-    return hc_check_device_error(e);
+    return hc_finish_sync(e);
 }

@@ -45,6 +45,7 @@ struct hc_engine {
     cudaStream_t stream = nullptr;      // stream all work is enqueued on
     cudaStream_t own_stream = nullptr;  // the engine's own stream
     int* d_err = nullptr;               // device error flags (bit 0: f16 range, bit 1: wait timeout)
+    int* h_err = nullptr;               // pinned host copy of d_err, read back with a call's results
     bool use_graphs = true;
     // grow-on-demand workspaces (the reference's GemvSyncWorkspace, compute.rs:10-17)
     DevBuf ws_raw, ws_gpu, ws_x, ws_y, ws_h, ws_g, ws_u, ws_misc;
@@ -84,6 +85,9 @@ int hc_cuda_error(cudaError_t e, const char* what);
 void hc_peer_release(hc_engine* e);  // unmap the peers' regions and free this rank's
 int hc_engine_activate(hc_engine* e);
 int hc_check_device_error(hc_engine* e);
+// Synchronises the engine's stream and reports the device error flag, read back behind the
+// work already enqueued (one stream synchronisation instead of two round trips).
+int hc_finish_sync(hc_engine* e);
 int hc_launch_gemv(hc_engine* e, const hc_weights* w, const float* x, size_t ldx, float* y, size_t ldy,
                    const float* resid, size_t ldr, size_t nvec);
 int hc_launch_gateup(hc_engine* e, const hc_weights* g, const hc_weights* u, const float* x, size_t ldx, float* h,

@@ -861,12 +861,21 @@ cudaError_t launch_flow_t(const StackLaunch& s, int num_sms, int smem_limit, cud
     const Smem L = smem_layout<FA, FD>(s.dm, s.ff, S, slot);
     auto kern = tp ? ffn_flow_kernel<FA, FD, true> : ffn_flow_kernel<FA, FD, false>;
     const int threads = tp ? kThreadsTP : kThreads;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
+    // the shared-memory opt-in and the one-CTA-per-SM check, once per kernel, device and size
+    // (a stack call makes two launches of this function: the driver queries cost microseconds)
+    static int checked[2][64];  // [tp][device]: the largest size configured and found to fit
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, L.total);
-    if (e != cudaSuccess) return e;
-    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    if (dev >= 64 || checked[tp][dev] < L.total) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
+        if (e != cudaSuccess) return e;
+        int per_sm = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, L.total);
+        if (e != cudaSuccess) return e;
+        if (per_sm < 1) return cudaErrorInvalidConfiguration;
+        if (dev < 64) checked[tp][dev] = L.total;
+    }
     const FlowScratch sc = flow_scratch<FA, FD>(s.L, s.dm, s.ff);
     if (dry) {
         if (scratch_bytes) *scratch_bytes = sc.total;

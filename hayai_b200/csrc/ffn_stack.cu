@@ -617,12 +617,20 @@ static cudaError_t launch_stack_t(const StackLaunch& s, int num_sms, int smem_li
     if (S < 3) return cudaErrorInvalidConfiguration;  // too shallow to pay off: use the per-layer kernels
     const int smem = stack_smem_layout<FA, FD>(s.dm, s.ff, S).ring + S * slot_bytes;
     auto kern = ffn_stack_kernel<FA, FD>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    // the shared-memory opt-in and the one-CTA-per-SM check, once per device and size
+    static int checked[64];  // per device: the largest size configured and found to fit
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTThreads, smem);
-    if (e != cudaSuccess) return e;
-    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    if (dev >= 64 || checked[dev] < smem) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        int per_sm = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTThreads, smem);
+        if (e != cudaSuccess) return e;
+        if (per_sm < 1) return cudaErrorInvalidConfiguration;
+        if (dev < 64) checked[dev] = smem;
+    }
     const StackScratch sc = stack_scratch<FA, FD>(s.L, s.dm, s.ff);
     if (dry) {
         if (scratch_bytes) *scratch_bytes = sc.total;

@@ -147,6 +147,36 @@ def _norm_ptrs(norms):
     return (ctypes.c_void_p * len(norms))(*[_tptr(t) for t in norms])
 
 
+class BoundStack:
+    """A layer stack bound once to an engine: its handle and norm-pointer arrays are built at
+    binding, so a decode loop pays only the call (the bound-op pattern of the reference's
+    orchestrator, crates/hayai-core/src/orchestrator.rs:276-392).  Holds references to the
+    weights and norm tensors, which must stay alive and unchanged while it is used."""
+
+    def __init__(self, engine, gates, ups, downs, norms=None, eps: float = 1e-5, tp: bool = False):
+        if not (len(gates) == len(ups) == len(downs)) or not gates:
+            raise ValueError("gates, ups and downs need the same, non-zero number of layers")
+        self.engine = engine
+        self._keep = (list(gates), list(ups), list(downs), None if norms is None else list(norms))
+        self._g, self._u, self._d = _handles(gates), _handles(ups), _handles(downs)
+        self._n = _norm_ptrs(norms)
+        self.eps = float(eps)
+        self.layers = len(gates)
+        self._fn = lib().hc_ffn_stack_tp if tp else lib().hc_ffn_stack
+
+    def run(self, x, out=None, nvec: int = 1) -> np.ndarray:
+        """x <- x + FFN_l(rms_norm(x)) for every layer, host buffers (x float32 [nvec][d_model]);
+        the result goes to ``out`` (a new array when None)."""
+        xv = x if isinstance(x, np.ndarray) and x.dtype == np.float32 and x.flags.c_contiguous else _f32(x)
+        if out is None:
+            out = np.empty_like(xv)
+        elif out.dtype != np.float32 or not out.flags.c_contiguous or out.size < xv.size:
+            raise ValueError("out must be a contiguous float32 array at least the size of x")
+        _check(self._fn(self.engine.handle, self._g, self._u, self._d, self._n, self.eps, self.layers,
+                        xv.ctypes.data, out.ctypes.data, nvec))
+        return out
+
+
 class CudaEngine:
     """One GPU + stream (OpenClEngine, crates/hayai-opencl/src/context.rs:23)."""
 
@@ -283,6 +313,11 @@ class CudaEngine:
         _check(lib().hc_ffn_swiglu(self.handle, gate.handle, up.handle, down.handle, xv.ctypes.data,
                                    y.ctypes.data, nvec))
         return y
+
+    def bind_ffn_stack(self, gates, ups, downs, norms=None, eps: float = 1e-5, tp: bool = False) -> BoundStack:
+        """Bind a layer stack for repeated host-buffer calls (see BoundStack); tp: the
+        tensor-parallel stack over this rank's d_ff shard (ffn_stack_tp)."""
+        return BoundStack(self, gates, ups, downs, norms, eps, tp)
 
     def ffn_stack(self, gates, ups, downs, x, nvec: int = 1, norms=None, eps: float = 1e-5) -> np.ndarray:
         """x <- x + FFN_l(rms_norm(x, norms[l])) for every layer (host buffers in and out).

@@ -97,6 +97,27 @@ def test_stack_parity(engine):
     assert_parity(ref, got, what="stack")
 
 
+def test_bound_stack_matches_the_unbound_call(engine):
+    """A stack bound once (BoundStack) gives the unbound call's bytes, call after call, into a
+    caller's buffer or a new one, and checks its arguments."""
+    L, dm, ff = 3, 1024, 2816
+    layers, res, norms = make_stack(engine, L, oracle.Q4_K, oracle.Q6_K, dm, ff, 520)
+    nd = [torch.from_numpy(n).cuda() for n in norms]
+    x = oracle.normal(521, dm)
+    want = engine.ffn_stack(*split(res), x, norms=nd, eps=EPS)
+    bound = engine.bind_ffn_stack(*split(res), norms=nd, eps=EPS)
+    out = np.empty(dm, np.float32)
+    for _ in range(2):
+        assert bound.run(x, out) is out
+        assert np.array_equal(out, want)
+    assert np.array_equal(bound.run(x), want)
+    assert_parity(oracle_stack(layers, norms, oracle.Q4_K, oracle.Q6_K, dm, ff, x), out, what="bound stack")
+    with pytest.raises(ValueError):
+        bound.run(x, np.empty(dm - 1, np.float32))
+    with pytest.raises(ValueError):
+        engine.bind_ffn_stack(*split(res)[:2], split(res)[2][:1])
+
+
 def test_stack_padded_k(engine):
     # SmolLM shape: K 576 zero-padded to 768 for Q4_K; norm and residual cover 576 entries
     L, dm, kin, ff = 3, 576, 768, 1536
